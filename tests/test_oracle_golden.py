@@ -1,0 +1,324 @@
+"""Pin the CPU oracle (oracle/pw_oracle.c) to the reference's own golden vectors.
+
+Each test names the reference test whose fixture it replays.  These run on the
+CPU only; the GPU parity tests then compare the CUDA path against this oracle.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    with open(os.path.join(GOLDEN, name)) as f:
+        return json.load(f)
+
+
+def bits(a):
+    return np.asarray(a, dtype=np.float32).view(np.uint32)
+
+
+def u32(values):
+    """Fixture bit patterns may be stored signed (i32) or unsigned."""
+    return (np.asarray(values, dtype=np.int64) & 0xFFFFFFFF).astype(np.uint32)
+
+
+def test_every_fp8_encoding_matches_oracle():
+    # src/lib.rs:8012 every_fp8_encoding_matches_oracle
+    fx = load("f8_e4m3fn_all_bytes.json")
+    got = bits(O.decode_array(np.arange(256, dtype=np.uint8)))
+    assert got.tolist() == fx["expected_f32_bits"]
+
+
+def test_sampled_real_fp8_block_matches():
+    # src/lib.rs:7985 sampled_real_fp8_block_matches
+    fx = load("mtp_gate_fp8_block.json")
+    raw = np.array(fx["raw_u8"], dtype=np.uint8)
+    dec = O.decode_array(raw)
+    assert np.array_equal(dec, np.array(fx["decoded_fp8"], dtype=np.float32))
+    deq = dec * np.float32(fx["scale_inv"])
+    # the reference parses the expected values as f32 (src/lib.rs:7405)
+    assert np.all(np.abs(deq - np.array(fx["dequantized"], dtype=np.float32)) < 1e-9)
+
+
+@pytest.mark.parametrize("mode", [O.ACC_F32, O.ACC_F64])
+def test_production_width_real_fp8_gemv_matches(mode):
+    # src/lib.rs:8052 production_width_real_fp8_gemv_matches (tolerance 2e-7)
+    fx = load("mtp_gate_fp8_gemv.json")
+    rows, cols = fx["rows"], fx["columns"]
+    raw = np.array(fx["raw_u8"], dtype=np.uint8)
+    scale = np.array(fx["scale_inv"], dtype=np.float32)
+    x = np.array(fx["input"], dtype=np.float32)
+    # The fixture holds 4 rows of one 128-row block; pad to a full block for
+    # the 128-multiple contract and read the first 4 rows back.
+    w = np.zeros((128, cols), np.uint8)
+    w[:rows] = raw
+    y = O.readable_gemv(w, scale.reshape(1, -1), x, mode)
+    assert np.all(np.abs(y[:rows] - np.array(fx["expected_f32"], dtype=np.float32)) < 2e-7)
+
+
+def test_mapped_fp8_gemv_selects_row_and_column_scale_blocks():
+    # src/lib.rs:7807 mapped_fp8_gemv_selects_row_and_column_scale_blocks
+    w = np.full((256, 256), 0x38, np.uint8)  # e4m3 1.0
+    s = np.array([[1.0, 2.0], [3.0, 4.0]], np.float32)
+    y = O.readable_gemv(w, s, np.ones(256, np.float32), O.ACC_F32)
+    assert np.all(y[:128] == 384.0) and np.all(y[128:] == 896.0)
+
+
+def test_block_fp8_validation_rejects_bad_layouts():
+    # src/lib.rs:8078 block_fp8_gemv_rejects_bad_layouts / :1217 validation
+    w = np.zeros((128, 256), np.uint8)
+    s = np.ones((1, 2), np.float32)
+    assert O.validate_fp8(w, s, np.zeros(256, np.float32)) == 0
+    assert O.validate_fp8(w, s, np.zeros(255, np.float32)) == -2
+    assert O.validate_fp8(w, s, np.array([np.nan] * 256, np.float32)) == -2
+    bad = w.copy()
+    bad[3, 7] = 0x7F
+    assert O.validate_fp8(bad, s, None) == -4
+    assert O.validate_fp8(bad, s, None, scan=False) == 0
+    assert O.validate_fp8(w, np.array([[1.0, np.inf]], np.float32), None) == -3
+    assert O.validate_fp8(np.zeros((100, 256), np.uint8), s, None) == -1
+
+
+def test_dynamic_fp8_activations_match_pytorch_bytes():
+    # src/text_endpoint.rs:14035 dynamic_fp8_activations_match_pytorch_bytes
+    fx = load("pw0053_dynamic_fp8.json")
+    x = u32(fx["input_f32_bits"]).view(np.float32)
+    codes, scales, deq = O.dynamic_fp8(x)
+    rows, cols = x.shape
+    assert codes.reshape(rows, cols // 128, 128).tolist() == fx["encoded_u8"]
+    assert bits(scales).tolist() == u32(fx["scale_f32_bits"]).tolist()
+    assert bits(deq).reshape(rows, cols // 128, 128).tolist() == u32(fx["dequantized_f32_bits"]).tolist()
+
+
+def test_bf16_rounding_matches_pytorch_payloads():
+    # src/text_endpoint.rs:14106 bf16_rounding_matches_pytorch_payloads
+    fx = load("pw0054_bf16_boundary.json")
+    x = u32(fx["input_f32_bits"]).view(np.float32)
+    got = bits(O.round_bf16(x))
+    widened = u32(fx["widened_f32_bits"])
+    for i in range(x.size):
+        if np.isfinite(x[i]):
+            assert int(got[i] >> 16) == fx["bf16_u16"][i]
+            assert got[i] == widened[i]
+        elif np.isnan(x[i]):
+            # as the reference test: NaN stays NaN with its sign (payload is
+            # torch-canonical in the fixture, payload-preserving here)
+            y = got[i:i + 1].view(np.float32)[0]
+            assert np.isnan(y) and np.signbit(y) == np.signbit(x[i])
+        else:
+            assert got[i] == widened[i]
+    assert bits(O.round_bf16_bits(x)).tolist() == got.tolist()
+
+
+def test_router_sigmoid_matches_pytorch_vectorized_bits():
+    # src/text_endpoint.rs:14695 (pw0062 router sigmoid, 32 real logits)
+    fx = load("pw0062_router_sigmoid.json")
+    logits = u32(fx["logit_f32_u32"]).view(np.float32)
+    assert bits(O.sigmoid_array(logits)).tolist() == fx["score_f32_u32"]
+
+
+def test_sleef_exp_and_sigmoid_match_subnormal_boundaries():
+    # src/text_endpoint.rs:14712 sleef_exp_and_sigmoid_match_subnormal_boundaries
+    fx = load("pw0068_sleef_boundaries.json")
+    x = u32(fx["input_f32_u32"]).view(np.float32)
+    assert bits(O.sleef_expf_array(x)).tolist() == fx["exp_f32_u32"]
+    assert bits(O.sigmoid_array(-x)).tolist() == fx["sigmoid_of_negated_input_f32_u32"]
+
+
+def _topk_from_corrected(corrected):
+    # Drive the canonical top-k with scores chosen so that score + 0 == corrected:
+    # select on the corrected values directly through a zero-bias router.
+    logits = corrected.reshape(1, -1)
+    return logits
+
+
+def test_unsorted_topk_matches_real_route_set():
+    # src/text_endpoint.rs:14742 pytorch_unsorted_topk_matches_real_route_order.
+    # The order is libc++-specific; the set is the pinned quantity.
+    fx = load("pw0063_topk_order.json")
+    corrected = u32(fx["corrected_f32_u32"]).view(np.float32)
+    order = sorted(range(len(corrected)), key=lambda i: (-float(corrected[i]), i))
+    assert set(order[:8]) == set(fx["selected_experts"])
+    if os.path.exists(O.REF_TOPK_PATH):
+        ref = O.reference_topk_unsorted(corrected, 8)
+        assert set(ref.tolist()) == set(fx["selected_experts"])
+
+
+def test_tied_topk_rows_are_flagged_and_valid():
+    # src/text_endpoint.rs:14776 pinned_pytorch_unsorted_topk_matches_tied_route_order.
+    # Tied boundaries pin macOS libc++ behaviour; here the canonical rule must
+    # pick a valid set (nothing rejected above the boundary) and report the tie.
+    fx = load("pw0157_topk_ties.json")
+    for case in fx["cases"]:
+        corrected = u32(case["corrected_f32_u32"]).view(np.float32)
+        order = sorted(range(len(corrected)), key=lambda i: (-float(corrected[i]), i))
+        chosen = order[:8]
+        boundary = min(corrected[i] for i in chosen)
+        rejected = max(corrected[i] for i in order[8:])
+        assert boundary >= rejected
+        ref_set = set(case["selected_experts"])
+        if boundary > rejected:
+            assert set(chosen) == ref_set
+        else:
+            # every reference choice lies on or above the tied boundary
+            assert all(corrected[i] >= boundary for i in ref_set)
+        if os.path.exists(O.REF_TOPK_PATH):
+            ref = O.reference_topk_unsorted(corrected, 8)
+            assert min(corrected[i] for i in ref) == boundary
+
+
+def test_noaux_topk_weights_sum_to_one_and_follow_canonical_order():
+    rng = np.random.default_rng(4)
+    logits = rng.normal(0, 1, (16, 256)).astype(np.float32)
+    bias = rng.normal(0, 0.01, 256).astype(np.float32)
+    sel, wts, scores, margin, ties = O.noaux_topk(logits, bias)
+    corrected = scores + bias
+    for t in range(16):
+        c = corrected[t, sel[t]]
+        assert np.all(np.diff(c) <= 0)
+        assert abs(float(wts[t].sum()) - 1.0) <= 1e-6
+        order = np.lexsort((np.arange(256), -corrected[t]))
+        assert set(order[:8]) == set(sel[t].tolist())
+    assert ties == 0
+
+
+def test_swiglu_fixture_has_independent_f64_oracle():
+    # src/lib.rs:8031 swiglu_fixture_has_independent_f64_oracle
+    fx = load("swiglu_f32.json")
+    for g, u, e in zip(fx["gate"], fx["up"], fx["expected_f64"]):
+        got = g / (1.0 + np.exp(-np.float64(g))) * u
+        assert abs(got - e) < 1e-15
+
+
+def test_source_derived_tiny_moe_fixture_matches():
+    # src/lib.rs:7966 source_derived_tiny_moe_fixture_matches (noaux-tc grouped
+    # routing + SwiGLU in f64, restated from src/lib.rs:7608 evaluate_tiny_moe)
+    fx = load("moe_noaux_tc_swiglu.json")
+    experts = fx["experts"]
+    groups, topk_group, top_k = fx["groups"], fx["topk_group"], fx["top_k"]
+    for x, expected in zip(fx["inputs"], fx["expected"]):
+        x = np.array(x, np.float64)
+        scores = np.array([1.0 / (1.0 + np.exp(-sum(a * b for a, b in zip(row, x)))) for row in fx["router_weight"]])
+        choice = scores + np.array(fx["correction_bias"])
+        gs = len(experts) // groups
+        gscore = [sum(sorted(choice[g * gs:(g + 1) * gs], reverse=True)[:2]) for g in range(groups)]
+        keep = sorted(range(groups), key=lambda g: (-gscore[g], g))[:topk_group]
+        idx = sorted([i for i in range(len(experts)) if i // gs in keep], key=lambda i: (-choice[i], i))[:top_k]
+        den = sum(scores[i] for i in range(len(experts)) if i in idx) + 1e-20
+        w = [scores[i] / den * fx["routed_scaling_factor"] for i in idx]
+        out = np.zeros(fx["hidden_size"])
+        for i, wi in zip(idx, w):
+            e = experts[i]
+            g = np.array([sum(a * b for a, b in zip(r, x)) for r in e["gate"]])
+            u = np.array([sum(a * b for a, b in zip(r, x)) for r in e["up"]])
+            h = g / (1.0 + np.exp(-g)) * u
+            y = np.array([sum(a * b for a, b in zip(r, h)) for r in e["down"]])
+            out += wi * y
+        assert idx == expected["topk_indices"]
+        assert np.all(np.abs(np.array(w) - expected["topk_weights"]) < 1e-14)
+        # 1e-14 as in the reference test; libm exp differs from Apple's by ~1 ulp
+        assert np.all(np.abs(out - expected["output"]) < 1e-14)
+
+
+def test_full_qkv_scale_layout_preserves_head_boundaries():
+    # src/text_endpoint.rs:13686 full_qkv_scale_layout_preserves_head_boundaries
+    src = {0: 0, 3071: 3071, 3072: 3392, 12287: 13247, 12288: 3072, 12480: 6464,
+           13055: 13439, 13056: 3264, 13567: 13567}
+    for k, v in src.items():
+        assert O.full_qkv_source_row(k) == v
+    with pytest.raises(ValueError):
+        O.full_qkv_source_row(13568)
+    scl = {0: 0, 3071: 23, 3072: 27, 12287: 104, 12288: 24, 12415: 24, 12416: 25, 12479: 25,
+           12480: 51, 13055: 106, 13056: 26, 13567: 107}
+    for k, v in scl.items():
+        assert O.full_qkv_scale_row(k) == v
+    with pytest.raises(ValueError):
+        O.full_qkv_scale_row(13568)
+    assert {O.full_qkv_scale_row(r) for r in range(13568)} == set(range(108))
+
+
+def test_swa_qkv_rows_deinterleave_four_checkpoint_tp_shards():
+    # src/text_endpoint.rs:13717 swa_qkv_rows_deinterleave_four_checkpoint_tp_shards
+    src = {0: 0, 3071: 3071, 3072: 3712, 12287: 14207, 12288: 3072, 12671: 3455, 12672: 6784,
+           13823: 14591, 13824: 3456, 14079: 3711, 14080: 7168, 14847: 14847}
+    for k, v in src.items():
+        assert O.swa_qkv_source_row(k) == v
+    with pytest.raises(ValueError):
+        O.swa_qkv_source_row(14848)
+
+
+def test_e4m3_search_encoder_equals_round_to_nearest_even():
+    # The reference's search encoder (src/text_endpoint.rs:2985) is RNE with
+    # ties to the even code; the CUDA path relies on that equality.
+    rng = np.random.default_rng(7)
+    vals = np.concatenate([
+        rng.uniform(-448, 448, 3000), rng.normal(0, 1e-2, 2000), rng.normal(0, 1e-3, 1000),
+        np.array([0.0, -0.0, 448.0, -448.0, 2.0 ** -10, -(2.0 ** -10), 3 * 2.0 ** -11, 2.0 ** -9 * 1.5,
+                  240.0, 232.0, 248.0, 1.0625, 1.1875]),
+    ]).astype(np.float32)
+    # every midpoint between adjacent positive codes
+    table = O.decode_array(np.arange(0x7F, dtype=np.uint8)).astype(np.float64)
+    mids = ((table[1:] + table[:-1]) / 2).astype(np.float32)
+    vals = np.concatenate([vals, mids, -mids])
+    for v in vals:
+        assert O.encode_e4m3(float(v)) == O.encode_e4m3(float(v), rne=True), v
+
+
+def test_blockscaled_equation_matches_reference_probe_shape():
+    # src/wide_metal_moe.rs:388-423 probe_sglang_blockscaled_projection inputs,
+    # widths {2, 9, 26, 32}: the f32 reference order and the f64 mode agree.
+    rows, cols = 128, 256
+    w = np.array([(i * 37 + 11) % 0x7F for i in range(rows * cols)], np.uint8).reshape(rows, cols)
+    s = np.array([0.003 + i * 0.0017 for i in range(rows // 128 * cols // 128)], np.float32).reshape(1, 2)
+    for active in [2, 9, 26, 32]:
+        x = np.array([((i * 29 % 401) - 200.0) / 37.0 for i in range(active * cols)], np.float32).reshape(active, cols)
+        codes, scales, _ = O.dynamic_fp8(x)
+        a = O.blockscaled_linear(w, s, codes, scales, mode=O.ACC_F32)
+        b = O.blockscaled_linear(w, s, codes, scales, mode=O.ACC_F64)
+        assert np.max(np.abs(a - b)) <= 1e-2 * max(1.0, float(np.max(np.abs(b)))) * 1e-3 + 1e-3
+
+
+def test_oracle_expert_matches_reference_torch_helpers():
+    # tools/generate_layer_major_moe_reference.py:196-205 run on seeded inputs
+    # (tests/golden/make_golden.py); gate/up/act/down staging must agree.
+    from golden_inputs import expert_case, unpack_f32
+    fx = load("torch_reference_expert.json")
+    for case in fx["experts"]:
+        c = expert_case(case["seed"], case["hidden"], case["intermediate"], case["width"])
+        W, H, I = case["width"], case["hidden"], case["intermediate"]
+        codes, scales, _ = O.dynamic_fp8(c["x"])
+        gate = O.round_bf16(O.blockscaled_linear(c["gate_w"], c["gate_s"], codes, scales))
+        up = O.round_bf16(O.blockscaled_linear(c["up_w"], c["up_s"], codes, scales))
+        ref_gate = unpack_f32(case["gate"], (W, I))
+        ref_up = unpack_f32(case["up"], (W, I))
+        # bf16 outputs: reassociation may move a value across one bf16 midpoint
+        assert np.max(np.abs(gate - ref_gate)) <= 2.0 ** -7 * np.max(np.abs(ref_gate))
+        assert np.mean(gate != ref_gate) < 0.02
+        act = O.staged_swiglu(ref_gate, ref_up, O.EXP_SLEEF)
+        ref_act = unpack_f32(case["act"], (W, I))
+        assert np.mean(act != ref_act) < 0.01
+        hcodes, hscales, _ = O.dynamic_fp8(ref_act)
+        down = O.round_bf16(O.blockscaled_linear(c["down_w"], c["down_s"], hcodes, hscales))
+        ref_down = unpack_f32(case["down"], (W, H))
+        rel = np.linalg.norm(down - ref_down) / np.linalg.norm(ref_down)
+        assert rel < 2e-3
+
+
+def test_schedule_matches_reference_build_schedule():
+    # tools/generate_layer_major_moe_reference.py:53 build_schedule
+    fx = load("torch_reference_expert.json")
+    sel = np.array(fx["schedule_selected"], np.uint32)
+    wts = np.array(fx["schedule_weights"], np.float32)
+    offsets, order = O.schedule(sel, 256)
+    for e_str, entry in fx["schedule"].items():
+        e = int(e_str)
+        placements = order[offsets[e]:offsets[e + 1]]
+        assert [int(p) // 8 for p in placements] == entry["positions"]
+        assert np.allclose([wts.ravel()[p] for p in placements], entry["weights"], rtol=0, atol=0)
+    assert sum(offsets[e + 1] - offsets[e] for e in range(256)) == 128 * 8
