@@ -1,0 +1,225 @@
+/*
+ * pw_cuda.h -- C ABI of the B200 (sm_100a) block-FP8 routed-MoE path.
+ *
+ * This is the drop-in boundary for Prismwing's routed-MoE / projection
+ * runtime.  Each entry point names the reference interface it replaces
+ * (path:line inside the x3haloed/mimo-prismwing tree).  A Rust caller binds
+ * these with an `extern "C"` block, exactly as the reference already binds
+ * its C++ top-k bridge (src/text_endpoint.rs:2466-2472 declaring
+ * src/pytorch_topk.cpp:7).
+ *
+ * Conventions
+ *  - Every function returns an int status: PW_OK (0) or a negative PW_ERR_*.
+ *    No C++ exception crosses the boundary.  pw_last_error() gives the text.
+ *  - Weight and scale pointers inside pw_fp8_tensor / pw_router are DEVICE
+ *    pointers owned by the caller (uploaded once; never freed by the library).
+ *  - Activation inputs and outputs are host or device pointers, chosen per
+ *    call by `mem` (PW_MEM_HOST or PW_MEM_DEVICE).  With PW_MEM_HOST the call
+ *    copies inputs in, runs, copies outputs out and returns after the stream
+ *    has finished (the reference's commit + wait_until_completed).  With
+ *    PW_MEM_DEVICE the call is asynchronous on the runtime's stream unless
+ *    stats are requested (stats imply a stream synchronisation).
+ *  - One runtime per (thread, device).  Calls on one runtime are not
+ *    re-entrant.  The runtime owns its stream, its scratch arena and the
+ *    device error-flag word.
+ */
+#ifndef PW_CUDA_H
+#define PW_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PW_ABI_VERSION 1
+
+/* ---- status codes (reference: Result<_, String>, src/wide_metal_moe.rs) ---- */
+#define PW_OK 0
+#define PW_ERR_ARGUMENT (-1)     /* null pointer, bad enum, bad runtime        */
+#define PW_ERR_SHAPE (-2)        /* shape / layout / scale-grid mismatch       */
+#define PW_ERR_NONFINITE (-3)    /* non-finite input, scale, weight or output  */
+#define PW_ERR_DEVICE_FLAGS (-4) /* a kernel set a bit in the error-flag word  */
+#define PW_ERR_CUDA (-5)         /* CUDA runtime error                         */
+#define PW_ERR_NCCL (-6)         /* NCCL error (expert-parallel calls)         */
+#define PW_ERR_TIMEOUT (-7)      /* a bounded device wait gave up              */
+#define PW_ERR_SCHEDULE (-8)     /* invalid expert schedule / route table      */
+#define PW_ERR_UNSUPPORTED (-9)  /* valid request outside this build's limits  */
+
+/* ---- device error-flag bits (reference kernels/block_fp8_gemv.metal:40-229;
+ *      bits 1..128 keep the reference meanings, 256+ are new) ---- */
+#define PW_FLAG_BAD_LAUNCH 1u          /* launch geometry mismatch            */
+#define PW_FLAG_NONFINITE_INPUT 2u     /* non-finite activation               */
+#define PW_FLAG_NONFINITE_SWIGLU 4u    /* non-finite staged SwiGLU value      */
+#define PW_FLAG_BAD_EXPERT_COUNT 8u    /* schedule row count mismatch         */
+#define PW_FLAG_NONFINITE_COMBINE 16u  /* non-finite weighted combine         */
+#define PW_FLAG_NONFINITE_ROUND 32u    /* non-finite bf16-rounded output      */
+#define PW_FLAG_NONFINITE_FUSED 128u   /* non-finite fused gate/up result     */
+#define PW_FLAG_ROUTE_WEIGHTS 256u     /* route weights not finite / sum != 1 */
+#define PW_FLAG_WAIT_TIMEOUT 512u      /* bounded pipeline wait ran out       */
+#define PW_FLAG_BAD_WEIGHT 1024u       /* weight byte 0x7f/0xff or bad scale  */
+
+/* ---- runtime flags (reference: compile vs compile_with_fused_gate_up,
+ *      src/wide_metal_moe.rs:165-171) ---- */
+#define PW_RUNTIME_FUSED_GATE_UP 1u
+
+/* ---- projection layouts (reference: execute_fp8_linear's full_qkv_layout
+ *      flag and its 14848-row SWA dispatch, src/wide_metal_moe.rs:300-306) ---- */
+#define PW_LAYOUT_PLAIN 0u
+#define PW_LAYOUT_FULL_QKV 1u /* [13568,4096], 4 shards [Q3072|K192|V128], grid [108,32] */
+#define PW_LAYOUT_SWA_QKV 2u  /* [14848,4096], 4 shards [Q3072|K384|V256], grid [116,32] */
+/* OR-able with a layout in pw_fp8_linear: return the f32 pre-round projection
+ * instead of the reference's bf16-rounded one. */
+#define PW_OUTPUT_F32 0x100u
+
+/* ---- where caller activation buffers live (the `mem` argument) ---- */
+#define PW_MEM_DEVICE 0u
+#define PW_MEM_HOST 1u
+/* OR-able with PW_MEM_DEVICE: enqueue on the runtime's stream and return
+ * without waiting (CUDA-graph capturable).  Errors surface through
+ * pw_read_error_flags(); stats must be NULL. */
+#define PW_MEM_ASYNC 2u
+
+typedef struct pw_runtime pw_runtime;
+typedef struct pw_expert_bank pw_expert_bank;
+
+/* One e4m3 weight matrix with its 128x128 f32 scale grid (reference:
+ * WideProjectionBinding src/wide_metal_moe.rs:80 + GemvShape :131).  Device
+ * pointers.  scale_rows x scale_cols must be ceil(rows/128) x cols/128 for
+ * PLAIN, [108,32] for FULL_QKV and [116,32] for SWA_QKV. */
+typedef struct pw_fp8_tensor {
+  const uint8_t *weight;
+  const float *scale;
+  uint32_t rows, cols;
+  uint32_t scale_rows, scale_cols;
+} pw_fp8_tensor;
+
+/* gate [I,H], up [I,H], down [H,I] (reference: WideExpertBinding's three
+ * projections, src/wide_metal_moe.rs:88). */
+typedef struct pw_expert_weights {
+  pw_fp8_tensor gate, up, down;
+} pw_expert_weights;
+
+/* Host-built schedule entry (reference: WideExpertBinding
+ * src/wide_metal_moe.rs:88-95: expert id, positions, route weights). */
+typedef struct pw_expert_binding {
+  uint32_t expert;
+  uint32_t count;
+  const uint32_t *positions;    /* host memory, [count], < rows */
+  const float *route_weights;   /* host memory, [count] */
+  pw_expert_weights weights;    /* device pointers */
+} pw_expert_binding;
+
+/* Router (reference: route_mlp src/text_endpoint.rs:4342 with gate.weight
+ * [256,4096] and e_score_correction_bias [256]).  The weight is bf16 bits
+ * (the reference stores F32; bf16 values widen exactly). Device pointers. */
+typedef struct pw_router {
+  const uint16_t *weight_bf16; /* [experts, hidden] */
+  const float *bias;           /* [experts] */
+  uint32_t experts, hidden, top_k;
+} pw_router;
+
+/* Per-call accounting (reference: WideMoeExecution / WideLinearExecution,
+ * src/wide_metal_moe.rs:97-111). */
+typedef struct pw_stats {
+  double wall_ms;             /* host wall time of the call                */
+  float device_ms;            /* CUDA-event time of the call's device work */
+  uint32_t error_flags;       /* PW_FLAG_* bits seen                       */
+  uint32_t unique_experts;    /* experts with >= 1 placement               */
+  uint32_t expert_rows;       /* placements (rows * top_k)                 */
+  uint32_t boundary_tie_rows; /* rows whose k-th/(k+1)-th scores tie       */
+  uint64_t weight_bytes;      /* FP8 weight + scale bytes the call reads   */
+} pw_stats;
+
+/* ---------------------------------------------------------------- runtime */
+
+/* Reference: WideMetalMoeRuntime::compile / compile_with_fused_gate_up
+ * (src/wide_metal_moe.rs:165-171).  Selects `device`, creates a stream,
+ * the error-flag word and an empty scratch arena. */
+int pw_runtime_create(int device, uint32_t flags, pw_runtime **out);
+void pw_runtime_destroy(pw_runtime *rt);
+/* Text of the last error on this runtime ("" if none); valid until the next call. */
+const char *pw_last_error(const pw_runtime *rt);
+/* Run subsequent calls on a caller stream (a cudaStream_t passed as void*); NULL restores the runtime's own. */
+int pw_set_stream(pw_runtime *rt, void *cuda_stream);
+int pw_synchronize(pw_runtime *rt);
+/* Device error-flag word accumulated since the last call that reset it (0 = clean). */
+int pw_read_error_flags(pw_runtime *rt, uint32_t *flags);
+int pw_abi_version(void);
+
+/* ------------------------------------------------------------- primitives */
+
+/* Reference: dynamic_fp8_activations src/text_endpoint.rs:3008 and the
+ * kernel dynamic_fp8_quantized_group128 kernels/block_fp8_gemv.metal:84.
+ * x f32 [rows, cols] -> codes e4m3 [rows, cols], scales f32 [rows, cols/128].
+ * cols % 128 == 0.  Bit-exact with the reference. */
+int pw_quantize_fp8(pw_runtime *rt, const float *x, uint32_t rows, uint32_t cols, uint8_t *codes,
+                    float *scales, uint32_t mem);
+
+/* Reference: validate_fp8_views_internal src/lib.rs:1217 (scan of every
+ * weight byte for 0x7f/0xff and of every scale for finiteness).
+ * *bad_offset receives the first bad weight byte offset, or UINT64_MAX. */
+int pw_validate_fp8(pw_runtime *rt, const pw_fp8_tensor *w, uint64_t *bad_offset);
+
+/* Reference: mapped_fp8_gemv src/lib.rs:1272 / block_fp8_gemv src/lib.rs:7469
+ * (the readable projection: activation NOT quantized, f32 output, no bf16
+ * rounding).  x f32 [width, cols], y f32 [width, rows], width 1..=8. */
+int pw_fp8_gemv(pw_runtime *rt, const pw_fp8_tensor *w, const float *x, uint32_t width, float *y,
+                uint32_t mem, pw_stats *stats);
+
+/* Reference: WideMetalMoeRuntime::execute_fp8_linear src/wide_metal_moe.rs:241
+ * (dynamic FP8 activation quantization, block-scaled projection, bf16 round).
+ * x f32 [width, cols], y f32 [width, rows] (bf16-valued).  `layout` selects the
+ * plain, full-QKV or SWA-QKV row/scale map.  Widths 1..=8 take the width-
+ * specialised GEMV; wider inputs run in chunks of 8 (reference limit: 8). */
+int pw_fp8_linear(pw_runtime *rt, const pw_fp8_tensor *w, uint32_t layout, const float *x,
+                  uint32_t width, float *y, uint32_t mem, pw_stats *stats);
+
+/* One routed expert at weight 1: quantize -> gate/up -> staged bf16 SwiGLU ->
+ * quantize -> down -> bf16 (reference: the per-expert body of
+ * routed_mlp_traced src/text_endpoint.rs:5311-5346 and of execute_configured
+ * src/wide_metal_moe.rs:1081-1240).  x [width, H] -> y [width, H]. */
+int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x, uint32_t width,
+                      float *y, uint32_t mem, pw_stats *stats);
+
+/* Reference: route_mlp src/text_endpoint.rs:4342 + pytorch_noaux_routes :4394
+ * (f32 logits, SLEEF-u10 sigmoid, top-k of score+bias, weights = score /
+ * (pairwise sum of the k chosen + 1e-20)).  top_k must be 8.  Logits are
+ * accumulated in f64; selected experts are emitted in canonical order
+ * (corrected score descending, index ascending).  selected u32 [tokens, 8],
+ * weights f32 [tokens, 8]. */
+int pw_route(pw_runtime *rt, const pw_router *router, const float *x, uint32_t tokens,
+             uint32_t *selected, float *weights, uint32_t mem, pw_stats *stats);
+
+/* ------------------------------------------------------------ MoE layers */
+
+/* Reference: WideMetalMoeRuntime::execute / execute_fused_gate_up
+ * src/wide_metal_moe.rs:836-1316 (host-built schedule, whole routed layer
+ * in one device transaction).  x f32 [rows, H], y f32 [rows, H] bf16-valued.
+ * sum(count) must equal rows * 8; positions < rows; counts >= 1. */
+int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_expert_binding *experts,
+                   uint32_t n_experts, float *y, uint32_t mem, pw_stats *stats);
+
+/* Register an expert bank (256 experts for MiMo-V2.5) once; the library keeps
+ * a device table of the caller's weight pointers and validates every weight
+ * byte and scale (the reference's fail-closed checkpoint validation,
+ * src/lib.rs:1217).  The weights stay caller-owned. */
+int pw_bank_create(pw_runtime *rt, const pw_expert_weights *experts, uint32_t n_experts,
+                   pw_expert_bank **out);
+void pw_bank_destroy(pw_expert_bank *bank);
+
+/* Whole routed layer on the device, router included (reference:
+ * routed_mlp_metal_wide_configured src/text_endpoint.rs:4750, with route_mlp,
+ * the BTreeMap schedule :4768-4776 and execute_configured folded into one
+ * stream of kernels with no host round trip).  x [tokens, H] -> y [tokens, H].
+ * Optional selected/weights (same `mem` as x) receive the routing. */
+int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,
+                 uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem,
+                 pw_stats *stats);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PW_CUDA_H */

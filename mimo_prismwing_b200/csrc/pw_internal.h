@@ -1,0 +1,88 @@
+// pw_internal.h -- host-side declarations shared by the kernels and the C ABI.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "pw_cuda.h"
+
+namespace pw {
+
+// One group of tokens sharing one weight matrix (a projection call, or one
+// expert's placements in a routed layer).  count <= 8 per group: wider token
+// sets are split into several groups over the same weights.
+struct GemvGroup {
+  const uint8_t *w0;   // weight (gate for the fused kernel)
+  const float *s0;     // its scale grid
+  const uint8_t *w1;   // up weight (fused kernel only)
+  const float *s1;     // its scale grid
+  uint32_t tok_begin;  // first slot in the token list / output rows
+  uint32_t count;      // 1..8 tokens
+  uint32_t pad0, pad1;
+};
+
+struct GemvArgs {
+  const GemvGroup *groups;
+  const uint32_t *n_groups_dev;  // device group count (nullptr: use n_groups)
+  uint32_t n_groups;             // host group count (upper bound if n_groups_dev)
+  uint32_t rows;                 // output rows per group (multiple of 64)
+  uint32_t K;                    // input columns (multiple of 128, <= 4096)
+  uint32_t scale_cols;           // columns of the weight scale grid (K / 128)
+  uint32_t layout;               // PW_LAYOUT_*
+  const uint32_t *tok_list;      // activation row of token slot i (nullptr: i)
+  const uint8_t *x_codes;        // e4m3 activations [*, K] (quantized kernels)
+  const float *x_scales;         // [*, K/128]
+  const float *x_f32;            // f32 activations [*, K] (readable kernel)
+  float *out;                    // out[(tok_begin + t) * out_stride + row]
+  uint32_t out_stride;
+  uint32_t round_bf16;           // bf16-round the f32 result on store
+  uint32_t *flags;
+};
+
+// Kernel launchers (pw_kernels.cu).  All enqueue on `stream` and return the
+// launch status.
+cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_t *codes, float *scales,
+                            uint32_t *flags, cudaStream_t stream);
+// kind: 0 = block-scaled (quantized x) over each group's w0/s0, 1 = readable
+// (f32 x), 2 = fused gate/up SwiGLU over w0/s0 and w1/s1, 3 = block-scaled
+// over w1/s1 (the unfused up projection)
+cudaError_t launch_gemv(int kind, const GemvArgs &args, int grid, cudaStream_t stream);
+int gemv_max_ctas(int num_sms);
+cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_t stream);
+cudaError_t launch_router_logits(const float *x, uint32_t tokens, const uint16_t *w, uint32_t experts,
+                                 uint32_t hidden, float *logits, cudaStream_t stream);
+cudaError_t launch_router_topk(const float *logits, const float *bias, uint32_t tokens, uint32_t experts,
+                               uint32_t *selected, float *weights, uint32_t *tie_rows, uint32_t *flags,
+                               cudaStream_t stream);
+
+// Device-side schedule for a routed layer: from selected [tokens, 8] build
+// placements ordered by (expert asc, position asc) and the GEMV groups.
+struct ScheduleOut {
+  uint32_t *offsets;        // [experts + 1]
+  uint32_t *placement_tok;  // [tokens*8] token position of placement p
+  float *placement_w;       // [tokens*8] route weight of placement p
+  uint32_t *slot_place;     // [tokens*8] placement index of (token, slot), slots in ascending expert
+  GemvGroup *gu_groups;     // gate/up groups (<= tokens*8 + experts)
+  GemvGroup *dn_groups;     // down groups
+  uint32_t *n_groups;       // [1] number of groups
+  uint32_t *counters;       // [4] unique experts, placements, max count, tie rows (stats)
+};
+struct BankTable {
+  const uint8_t *const *gate_w;
+  const float *const *gate_s;
+  const uint8_t *const *up_w;
+  const float *const *up_s;
+  const uint8_t *const *down_w;
+  const float *const *down_s;
+};
+cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
+                            const BankTable &bank, const ScheduleOut &out, uint32_t *flags,
+                            cudaStream_t stream);
+cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const float *placement_w,
+                           uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream);
+cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t n, uint32_t *flags,
+                          cudaStream_t stream);
+cudaError_t launch_validate_fp8(const uint8_t *w, uint64_t n, const float *s, uint64_t ns,
+                                unsigned long long *first_bad, uint32_t *flags, cudaStream_t stream);
+
+}  // namespace pw

@@ -1,0 +1,469 @@
+// pw_kernels.cu -- the small kernels around the GEMV: dynamic FP8 activation
+// quantization, router logits + sigmoid no-aux top-8, the device-side expert
+// schedule, the weighted combine, bf16 rounding and weight validation.
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "pw_device.cuh"
+#include "pw_internal.h"
+
+namespace pw {
+
+// ------------------------------------------------------------ quantization
+// One warp per 128-value group (src/text_endpoint.rs:3008,
+// kernels/block_fp8_gemv.metal:84): absmax, scale = max(absmax,1e-10)/448,
+// code = RNE_e4m3(clamp(x/scale, +-448)).  IEEE divisions (__fdiv_rn) keep it
+// bit-exact with the reference; lane l holds values 4l..4l+3.
+__global__ void k_quantize(const float *__restrict__ x, uint64_t groups, uint8_t *__restrict__ codes,
+                           float *__restrict__ scales, uint32_t *flags) {
+  const uint64_t warp_global = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32u;
+  const uint32_t lane = threadIdx.x % 32u;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) / 32u;
+  for (uint64_t g = warp_global; g < groups; g += nwarps) {
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(x + g * 128u) + lane);
+    const bool ok = finite(v.x) && finite(v.y) && finite(v.z) && finite(v.w);
+    if (!ok) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
+    float m = ok ? fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))) : 0.0f;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float scale = __fdiv_rn(fmaxf(m, 1.0e-10f), 448.0f);
+    auto q = [&](float val) { return fminf(fmaxf(__fdiv_rn(val, scale), -448.0f), 448.0f); };
+    const uint32_t lo = encode2(q(v.x), q(v.y));
+    const uint32_t hi = encode2(q(v.z), q(v.w));
+    reinterpret_cast<uint32_t *>(codes + g * 128u)[lane] = lo | (hi << 16);
+    if (lane == 0) scales[g] = scale;
+  }
+}
+
+cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_t *codes, float *scales,
+                            uint32_t *flags, cudaStream_t stream) {
+  if (cols % 128u) return cudaErrorInvalidValue;
+  const uint64_t groups = (uint64_t)rows * (cols / 128u);
+  if (groups == 0) return cudaSuccess;
+  const int threads = 256;
+  uint64_t blocks = (groups * 32u + threads - 1) / threads;
+  if (blocks > 148u * 16u) blocks = 148u * 16u;
+  k_quantize<<<(unsigned)blocks, threads, 0, stream>>>(x, groups, codes, scales, flags);
+  return cudaGetLastError();
+}
+
+// --------------------------------------------------------------- bf16 round
+__global__ void k_round_bf16(float *v, uint32_t n, uint32_t *flags) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float r = round_bf16(v[i]);
+    if (!finite(r)) raise_flag(flags, PW_FLAG_NONFINITE_ROUND);
+    v[i] = r;
+  }
+}
+
+cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  unsigned blocks = (n + 255u) / 256u;
+  if (blocks > 148u * 8u) blocks = 148u * 8u;
+  k_round_bf16<<<blocks, 256, 0, stream>>>(v, n, flags);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ router logits
+// logit[t,e] = sum_c x[t,c] * w[e,c] with f64 accumulation in a fixed order
+// (the oracle's pwo_router_logits restates it): lane l owns 8-column chunks
+// 8l + 256j (j ascending), sums them in f64, then an xor butterfly 16..1.
+// x*w of a bf16 weight and an f32 activation is exact in f64, so FMA and
+// mul+add give the same bits.  One warp per expert, 8 tokens per pass.
+constexpr int kRouterTok = 8;
+
+__global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, uint32_t tokens,
+                                                       const uint16_t *__restrict__ w, uint32_t experts,
+                                                       uint32_t hidden, float *__restrict__ logits) {
+  const uint32_t lane = threadIdx.x % 32u;
+  const uint32_t e = blockIdx.x * (blockDim.x / 32u) + threadIdx.x / 32u;
+  const uint32_t t0 = blockIdx.y * kRouterTok;
+  if (e >= experts) return;
+  double acc[kRouterTok];
+#pragma unroll
+  for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0;
+  const uint16_t *wrow = w + (size_t)e * hidden;
+  for (uint32_t c0 = 8u * lane; c0 < hidden; c0 += 256u) {
+    const uint4 wq = __ldg(reinterpret_cast<const uint4 *>(wrow + c0));
+    double wd[8];
+    const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      wd[2 * i] = (double)__uint_as_float(wv[i] << 16);
+      wd[2 * i + 1] = (double)__uint_as_float(wv[i] & 0xffff0000u);
+    }
+#pragma unroll
+    for (int t = 0; t < kRouterTok; ++t) {
+      if (t0 + t < tokens) {
+        const float4 *xp = reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * hidden + c0);
+        const float4 a = __ldg(xp), b = __ldg(xp + 1);
+        const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[t] = __fma_rn((double)xv[i], wd[i], acc[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kRouterTok; ++t) {
+    double v = acc[t];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0 && t0 + t < tokens) logits[(size_t)(t0 + t) * experts + e] = __double2float_rn(v);
+  }
+}
+
+cudaError_t launch_router_logits(const float *x, uint32_t tokens, const uint16_t *w, uint32_t experts,
+                                 uint32_t hidden, float *logits, cudaStream_t stream) {
+  if (hidden % 256u || tokens == 0) return cudaErrorInvalidValue;
+  dim3 grid((experts + 7u) / 8u, (tokens + kRouterTok - 1) / kRouterTok);
+  k_router_logits<<<grid, 256, 0, stream>>>(x, tokens, w, experts, hidden, logits);
+  return cudaGetLastError();
+}
+
+// --------------------------------------------------------------- router top-k
+// One warp per token (src/text_endpoint.rs:4394 pytorch_noaux_routes):
+// score = SLEEF sigmoid(logit); corrected = score + bias; 8 rounds of warp
+// argmax (ties -> lower index) give the canonical order; a 9th round yields
+// the boundary margin.  weight_k = score_k / (pairwise sum of 8 + 1e-20)
+// (src/text_endpoint.rs:4382).  Experts <= 32 * kTopkPer.
+constexpr int kTopkPer = 32;  // experts per lane (supports up to 1024 experts)
+
+__device__ __forceinline__ bool better(float va, uint32_t ia, float vb, uint32_t ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+__global__ void k_router_topk(const float *__restrict__ logits, const float *__restrict__ bias, uint32_t tokens,
+                              uint32_t experts, uint32_t *__restrict__ selected, float *__restrict__ weights,
+                              uint32_t *tie_rows, uint32_t *flags) {
+  const uint32_t lane = threadIdx.x % 32u;
+  const uint32_t t = blockIdx.x * (blockDim.x / 32u) + threadIdx.x / 32u;
+  if (t >= tokens) return;
+  const uint32_t per = (experts + 31u) / 32u;
+  float score[kTopkPer], corr[kTopkPer];
+  uint32_t taken = 0;  // bit j: lane's j-th expert chosen
+#pragma unroll
+  for (int j = 0; j < kTopkPer; ++j) {
+    const uint32_t e = lane + 32u * j;
+    score[j] = 0.0f;
+    corr[j] = -__int_as_float(0x7f800000);
+    if (j < (int)per && e < experts) {
+      const float lg = logits[(size_t)t * experts + e];
+      const float b = __ldg(bias + e);
+      if (!finite(lg) || !finite(b)) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
+      score[j] = sigmoid_sleef(lg);
+      corr[j] = __fadd_rn(score[j], b);
+    }
+  }
+  uint32_t chosen[8];
+  float chosen_score[8];
+  float kth = 0.0f, next = 0.0f;
+#pragma unroll 1
+  for (int k = 0; k < 9; ++k) {
+    float bv = -__int_as_float(0x7f800000);
+    uint32_t bi = 0xffffffffu;
+    float bs = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kTopkPer; ++j) {
+      const uint32_t e = lane + 32u * j;
+      if (j < (int)per && e < experts && !(taken & (1u << j)) && better(corr[j], e, bv, bi)) {
+        bv = corr[j];
+        bi = e;
+        bs = score[j];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+        bs = os;
+      }
+    }
+    if (k < 8) {
+      chosen[k] = bi;
+      chosen_score[k] = bs;
+      if (k == 7) kth = bv;
+      if (bi % 32u == lane && bi != 0xffffffffu) taken |= 1u << (bi / 32u);
+    } else {
+      next = bv;
+    }
+  }
+  if (lane == 0) {
+    const float l0 = __fadd_rn(chosen_score[0], chosen_score[4]);
+    const float l1 = __fadd_rn(chosen_score[1], chosen_score[5]);
+    const float l2 = __fadd_rn(chosen_score[2], chosen_score[6]);
+    const float l3 = __fadd_rn(chosen_score[3], chosen_score[7]);
+    const float den = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, l0), l1), l2), l3), 1.0e-20f);
+    float sum = 0.0f;
+    bool ok = true;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float wk = __fdiv_rn(chosen_score[k], den);
+      ok = ok && finite(wk) && wk >= 0.0f && chosen[k] < experts;
+      sum = __fadd_rn(sum, wk);
+      selected[(size_t)t * 8 + k] = chosen[k];
+      weights[(size_t)t * 8 + k] = wk;
+    }
+    if (!ok || fabsf(__fsub_rn(sum, 1.0f)) > 1.0e-6f) raise_flag(flags, PW_FLAG_ROUTE_WEIGHTS);
+    if (kth == next && tie_rows) atomicAdd(tie_rows, 1u);
+  }
+}
+
+cudaError_t launch_router_topk(const float *logits, const float *bias, uint32_t tokens, uint32_t experts,
+                               uint32_t *selected, float *weights, uint32_t *tie_rows, uint32_t *flags,
+                               cudaStream_t stream) {
+  if (experts <= 8 || experts > 32u * kTopkPer || tokens == 0) return cudaErrorInvalidValue;
+  k_router_topk<<<(tokens + 7u) / 8u, 256, 0, stream>>>(logits, bias, tokens, experts, selected, weights,
+                                                         tie_rows, flags);
+  return cudaGetLastError();
+}
+
+// ----------------------------------------------------------------- schedule
+// Single CTA.  Placements are ordered by (expert ascending, position
+// ascending) -- the reference's BTreeMap<expert, [(position, weight)]>
+// (src/text_endpoint.rs:4768-4776, src/text_endpoint.rs:5302-5310).  The rank
+// of a token among an expert's placements comes from per-expert token
+// bitmasks, so the order is deterministic without sorting.
+constexpr uint32_t kSchedMaxTokens = 2048;
+constexpr uint32_t kSchedMaxExperts = 256;
+constexpr uint32_t kSchedWords = kSchedMaxTokens / 32u;
+
+__global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ selected,
+                                                   const float *__restrict__ weights, uint32_t tokens,
+                                                   uint32_t experts, BankTable bank, ScheduleOut out,
+                                                   uint32_t *flags) {
+  extern __shared__ uint32_t sm[];
+  uint32_t *mask = sm;                                      // [experts][words]
+  uint16_t *prefix = reinterpret_cast<uint16_t *>(mask + experts * kSchedWords);  // [experts][words]
+  uint32_t *cnt = reinterpret_cast<uint32_t *>(prefix + experts * kSchedWords);   // [experts + 1]
+  uint32_t *grp_off = cnt + experts + 1;                    // [experts + 1]
+  __shared__ uint32_t bad;
+  const uint32_t words = (tokens + 31u) / 32u;
+  const uint32_t tid = threadIdx.x, nt = blockDim.x;
+  if (tid == 0) bad = 0;
+  for (uint32_t i = tid; i < experts * words; i += nt) mask[(i / words) * kSchedWords + i % words] = 0;
+  __syncthreads();
+  for (uint32_t i = tid; i < tokens * 8u; i += nt) {
+    const uint32_t e = selected[i];
+    const uint32_t t = i / 8u;
+    if (e >= experts) {
+      bad = 1;
+      continue;
+    }
+    const uint32_t prev = atomicOr(&mask[e * kSchedWords + t / 32u], 1u << (t % 32u));
+    if (prev & (1u << (t % 32u))) bad = 1;  // duplicate expert in one row
+  }
+  __syncthreads();
+  if (bad) {
+    if (tid == 0) raise_flag(flags, PW_FLAG_BAD_EXPERT_COUNT);
+    if (tid == 0) *out.n_groups = 0;
+    return;
+  }
+  // per-expert counts and word prefixes (thread per expert)
+  for (uint32_t e = tid; e < experts; e += nt) {
+    uint32_t run = 0;
+    for (uint32_t wi = 0; wi < words; ++wi) {
+      prefix[e * kSchedWords + wi] = (uint16_t)run;
+      run += __popc(mask[e * kSchedWords + wi]);
+    }
+    cnt[e] = run;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t off = 0, goff = 0, uniq = 0, maxc = 0;
+    for (uint32_t e = 0; e < experts; ++e) {
+      const uint32_t c = cnt[e];
+      out.offsets[e] = off;
+      grp_off[e] = goff;
+      off += c;
+      goff += (c + 7u) / 8u;
+      uniq += c ? 1u : 0u;
+      maxc = c > maxc ? c : maxc;
+    }
+    out.offsets[experts] = off;
+    grp_off[experts] = goff;
+    *out.n_groups = goff;
+    out.counters[0] = uniq;
+    out.counters[1] = off;
+    out.counters[2] = maxc;
+  }
+  __syncthreads();
+  // placement index of every (token, slot)
+  for (uint32_t i = tid; i < tokens * 8u; i += nt) {
+    const uint32_t e = selected[i];
+    const uint32_t t = i / 8u;
+    const uint32_t wi = t / 32u;
+    const uint32_t below = mask[e * kSchedWords + wi] & ((1u << (t % 32u)) - 1u);
+    const uint32_t p = out.offsets[e] + prefix[e * kSchedWords + wi] + __popc(below);
+    out.placement_tok[p] = t;
+    out.placement_w[p] = weights[i];
+  }
+  // per token: its 8 placements in ascending expert order (combine order)
+  for (uint32_t t = tid; t < tokens; t += nt) {
+    uint32_t ex[8], pl[8];
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t e = selected[t * 8u + k];
+      const uint32_t wi = t / 32u;
+      const uint32_t below = mask[e * kSchedWords + wi] & ((1u << (t % 32u)) - 1u);
+      ex[k] = e;
+      pl[k] = out.offsets[e] + prefix[e * kSchedWords + wi] + __popc(below);
+    }
+    for (int a = 1; a < 8; ++a) {
+      const uint32_t ke = ex[a], kp = pl[a];
+      int b = a - 1;
+      while (b >= 0 && ex[b] > ke) {
+        ex[b + 1] = ex[b];
+        pl[b + 1] = pl[b];
+        --b;
+      }
+      ex[b + 1] = ke;
+      pl[b + 1] = kp;
+    }
+    for (int k = 0; k < 8; ++k) out.slot_place[t * 8u + k] = pl[k];
+  }
+  // GEMV groups: each expert's placements in chunks of <= 8
+  for (uint32_t e = tid; e < experts; e += nt) {
+    const uint32_t c = cnt[e];
+    for (uint32_t j = 0; j * 8u < c; ++j) {
+      GemvGroup g;
+      g.tok_begin = out.offsets[e] + 8u * j;
+      g.count = min(8u, c - 8u * j);
+      g.pad0 = e;
+      g.pad1 = 0;
+      g.w0 = bank.gate_w[e];
+      g.s0 = bank.gate_s[e];
+      g.w1 = bank.up_w[e];
+      g.s1 = bank.up_s[e];
+      out.gu_groups[grp_off[e] + j] = g;
+      GemvGroup d = g;
+      d.w0 = bank.down_w[e];
+      d.s0 = bank.down_s[e];
+      d.w1 = nullptr;
+      d.s1 = nullptr;
+      out.dn_groups[grp_off[e] + j] = d;
+    }
+  }
+}
+
+cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
+                            const BankTable &bank, const ScheduleOut &out, uint32_t *flags,
+                            cudaStream_t stream) {
+  if (tokens == 0 || tokens > kSchedMaxTokens || experts > kSchedMaxExperts || experts < 8)
+    return cudaErrorInvalidValue;
+  const size_t smem = (size_t)experts * kSchedWords * 4 + (size_t)experts * kSchedWords * 2 +
+                      (size_t)(experts + 1) * 8;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(k_schedule, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)((size_t)kSchedMaxExperts * kSchedWords * 6 +
+                                               (size_t)(kSchedMaxExperts + 1) * 8));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  k_schedule<<<1, 1024, smem, stream>>>(selected, weights, tokens, experts, bank, out, flags);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ combine
+// y[t, c] = bf16( sum over t's 8 placements in ascending expert order of
+//                 down[p, c] * w_p )   -- product rounded, then added, from 0
+// (src/text_endpoint.rs:5365-5373; the down rows are already bf16-rounded).
+__global__ void k_combine(const float *__restrict__ down, const uint32_t *__restrict__ slot_place,
+                          const float *__restrict__ placement_w, uint32_t tokens, uint32_t hidden,
+                          float *__restrict__ y, uint32_t *flags) {
+  const uint32_t t = blockIdx.y;
+  __shared__ uint32_t pl[8];
+  __shared__ float wt[8];
+  if (threadIdx.x < 8) {
+    pl[threadIdx.x] = slot_place[t * 8u + threadIdx.x];
+    wt[threadIdx.x] = placement_w[pl[threadIdx.x]];
+  }
+  __syncthreads();
+  for (uint32_t c4 = blockIdx.x * blockDim.x + threadIdx.x; c4 < hidden / 4u; c4 += gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 d = __ldg(reinterpret_cast<const float4 *>(down + (size_t)pl[k] * hidden) + c4);
+      acc.x = __fadd_rn(acc.x, __fmul_rn(d.x, wt[k]));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(d.y, wt[k]));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(d.z, wt[k]));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(d.w, wt[k]));
+    }
+    acc.x = round_bf16(acc.x);
+    acc.y = round_bf16(acc.y);
+    acc.z = round_bf16(acc.z);
+    acc.w = round_bf16(acc.w);
+    if (!finite(acc.x) || !finite(acc.y) || !finite(acc.z) || !finite(acc.w))
+      raise_flag(flags, PW_FLAG_NONFINITE_COMBINE);
+    reinterpret_cast<float4 *>(y + (size_t)t * hidden)[c4] = acc;
+  }
+}
+
+cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const float *placement_w,
+                           uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream) {
+  if (hidden % 4u || tokens == 0) return cudaErrorInvalidValue;
+  dim3 grid((hidden / 4u + 255u) / 256u, tokens);
+  k_combine<<<grid, 256, 0, stream>>>(down, slot_place, placement_w, tokens, hidden, y, flags);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------- weight validation
+// src/lib.rs:1217: every weight byte must not be 0x7f/0xff and every scale
+// must be finite.  first_bad receives the smallest bad byte offset.
+__global__ void k_validate(const uint8_t *__restrict__ w, uint64_t n, const float *__restrict__ s, uint64_t ns,
+                           unsigned long long *first_bad, uint32_t *flags) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t n16 = n / 16u;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4 *>(w) + i);
+    const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      for (int b = 0; b < 4; ++b) {
+        if (((v[k] >> (8 * b)) & 0x7fu) == 0x7fu) {  // 0x7f or 0xff
+          atomicMin(first_bad, (unsigned long long)(i * 16u + k * 4u + b));
+          raise_flag(flags, PW_FLAG_BAD_WEIGHT);
+        }
+      }
+    }
+  }
+  for (uint64_t i = n16 * 16u + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    if ((w[i] & 0x7fu) == 0x7fu) {
+      atomicMin(first_bad, (unsigned long long)i);
+      raise_flag(flags, PW_FLAG_BAD_WEIGHT);
+    }
+  }
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ns; i += stride)
+    if (!finite(s[i])) raise_flag(flags, PW_FLAG_BAD_WEIGHT);
+}
+
+cudaError_t launch_validate_fp8(const uint8_t *w, uint64_t n, const float *s, uint64_t ns,
+                                unsigned long long *first_bad, uint32_t *flags, cudaStream_t stream) {
+  k_validate<<<148u * 4u, 256, 0, stream>>>(w, n, s, ns, first_bad, flags);
+  return cudaGetLastError();
+}
+
+// ----------------------------------------------------- unfused staged SwiGLU
+// kernels/block_fp8_gemv.metal:139 bf16_staged_swiglu (the non-fused runtime).
+__global__ void k_swiglu(const float *__restrict__ gate, const float *__restrict__ up, float *__restrict__ h,
+                         uint32_t n, uint32_t *flags) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float r = staged_swiglu(gate[i], up[i]);
+    if (!finite(r)) raise_flag(flags, PW_FLAG_NONFINITE_SWIGLU);
+    h[i] = r;
+  }
+}
+
+cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t n, uint32_t *flags,
+                          cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  unsigned blocks = (n + 255u) / 256u;
+  if (blocks > 148u * 8u) blocks = 148u * 8u;
+  k_swiglu<<<blocks, 256, 0, stream>>>(gate, up, h, n, flags);
+  return cudaGetLastError();
+}
+
+}  // namespace pw

@@ -1,0 +1,332 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU oracle.
+
+Bit-exact: e4m3 dequantization, dynamic FP8 activation codes and scales,
+router logits (pinned f64 order), selected expert sets, route weights, the
+staged SwiGLU and the weighted combine.  Within relative 2e-3 (norm-wise and
+max|d|/max|ref|) of the f64-accumulated oracle: every projection and layer.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def rt():
+    from mimo_prismwing_b200.runtime import WideMoeRuntime
+    r = WideMoeRuntime.compile_with_fused_gate_up(0)
+    yield r
+    r.close()
+
+
+@pytest.fixture(scope="module")
+def rt_unfused():
+    from mimo_prismwing_b200.runtime import WideMoeRuntime
+    r = WideMoeRuntime.compile(0)
+    yield r
+    r.close()
+
+
+def H(t):
+    from gpu_helpers import host
+    return host(t)
+
+
+# ------------------------------------------------------------ quantization
+def test_dynamic_fp8_matches_pytorch_fixture_bytes(rt):
+    with open(os.path.join(GOLDEN, "pw0053_dynamic_fp8.json")) as f:
+        fx = json.load(f)
+    x = (np.asarray(fx["input_f32_bits"], dtype=np.int64) & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
+    codes, scales = rt.quantize(torch.from_numpy(x).cuda())
+    rows, cols = x.shape
+    assert H(codes).reshape(rows, cols // 128, 128).tolist() == fx["encoded_u8"]
+    exp_scales = (np.asarray(fx["scale_f32_bits"], dtype=np.int64) & 0xFFFFFFFF).astype(np.uint32)
+    assert H(scales).view(np.uint32).tolist() == exp_scales.tolist()
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 4096), (8, 4096), (37, 2048), (5, 128)])
+def test_dynamic_fp8_bit_exact_vs_oracle(rt, rows, cols):
+    rng = np.random.default_rng(rows * 1000 + cols)
+    x = rng.normal(0, 1, (rows, cols)).astype(np.float32)
+    # edge values: zeros, signed zeros, tiny, huge, exact midpoints between codes
+    x[0, :128] = 0.0
+    x[0, 1] = -0.0
+    if cols >= 256:
+        x[0, 128:256] = rng.normal(0, 1e-30, 128)
+    if rows > 1:
+        x[1, :8] = [448.0, -448.0, 1e30, -1e-30, 3.0, 3.25, 3.125, -3.375]
+    codes, scales = rt.quantize(torch.from_numpy(x).cuda())
+    oc, os_, _ = O.dynamic_fp8(x)
+    assert np.array_equal(H(codes), oc)
+    assert np.array_equal(H(scales).view(np.uint32), os_.view(np.uint32))
+    # host I/O path gives the same bytes
+    codes_h, scales_h = rt.quantize(torch.from_numpy(x))
+    assert np.array_equal(codes_h.numpy(), oc)
+
+
+def test_quantize_rejects_nonfinite_and_bad_shape(rt):
+    from mimo_prismwing_b200.runtime import PrismwingError
+    x = torch.zeros((1, 128), device="cuda")
+    x[0, 3] = float("nan")
+    with pytest.raises(PrismwingError) as e:
+        rt.quantize(x)
+    assert e.value.kind == "nonfinite"
+    with pytest.raises(PrismwingError) as e:
+        rt.quantize(torch.zeros((1, 100), device="cuda"))
+    assert e.value.kind == "shape"
+
+
+# ------------------------------------------------------- readable GEMV (C0)
+def test_production_width_real_fp8_gemv_matches(rt):
+    # src/lib.rs:8052 fixture through the GPU readable GEMV (tolerance 2e-7)
+    from mimo_prismwing_b200.runtime import WideProjectionBinding
+    with open(os.path.join(GOLDEN, "mtp_gate_fp8_gemv.json")) as f:
+        fx = json.load(f)
+    w = np.zeros((128, fx["columns"]), np.uint8)
+    w[:fx["rows"]] = np.array(fx["raw_u8"], np.uint8)
+    s = np.array(fx["scale_inv"], np.float32).reshape(1, -1)
+    b = WideProjectionBinding(torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda())
+    x = torch.tensor(fx["input"], dtype=torch.float32).cuda()
+    y = H(rt.fp8_gemv(x, b).output)[0, :fx["rows"]]
+    assert np.all(np.abs(y - np.array(fx["expected_f32"], np.float32)) < 2e-7)
+
+
+def test_mapped_fp8_gemv_selects_row_and_column_scale_blocks(rt):
+    # src/lib.rs:7807: 256x256 of e4m3 1.0, grid [[1,2],[3,4]], x = 1 -> 384 / 896
+    from mimo_prismwing_b200.runtime import WideProjectionBinding
+    w = torch.full((256, 256), 0x38, dtype=torch.uint8, device="cuda")
+    s = torch.tensor([[1.0, 2.0], [3.0, 4.0]], device="cuda")
+    y = H(rt.fp8_gemv(torch.ones(256, device="cuda"), WideProjectionBinding(w, s)).output)[0]
+    assert np.all(y[:128] == 384.0) and np.all(y[128:] == 896.0)
+
+
+@pytest.mark.parametrize("width", [1, 2, 3, 5, 8])
+def test_readable_gemv_config0_vs_oracle(rt, width):
+    from gpu_helpers import assert_close
+    from mimo_prismwing_b200 import synth
+    b = synth.projection(2048, 4096, 11, "cuda")
+    x = synth.activations(width, 4096, 12 + width, "cuda")
+    y = H(rt.fp8_gemv(x, b).output)
+    w, s, xn = H(b.weight), H(b.scale), H(x)
+    ref = np.stack([O.readable_gemv(w, s, xn[t], O.ACC_F64) for t in range(width)])
+    assert_close(y, ref, what=f"readable width {width}")
+    # host I/O gives identical bits
+    y2 = rt.fp8_gemv(x.cpu(), b).output.numpy()
+    assert np.array_equal(y, y2)
+
+
+# --------------------------------------------------- block-scaled projection
+@pytest.mark.parametrize("rows,cols,width", [(2048, 4096, 1), (2048, 4096, 4), (2048, 4096, 8),
+                                             (4096, 2048, 2), (4096, 2048, 7), (256, 512, 3),
+                                             (2048, 4096, 13), (128, 128, 1)])
+def test_fp8_linear_vs_oracle(rt, rows, cols, width):
+    from gpu_helpers import assert_close, assert_close_bf16
+    from mimo_prismwing_b200 import synth
+    b = synth.projection(rows, cols, rows + cols, "cuda")
+    x = synth.activations(width, cols, width, "cuda")
+    y = H(rt.execute_fp8_linear(x, b).output)
+    codes, scales, _ = O.dynamic_fp8(H(x))
+    pre = O.blockscaled_linear(H(b.weight), H(b.scale), codes, scales)
+    assert np.array_equal(O.round_bf16(y), y)  # the reference's output is bf16-rounded
+    assert_close_bf16(y, O.round_bf16(pre), what=f"linear {rows}x{cols} w{width}")
+    # the f32 pre-round projection meets max relative 2e-3 outright
+    y32 = H(rt.execute_fp8_linear(x, b, f32_output=True).output)
+    assert_close(y32, pre, what=f"linear f32 {rows}x{cols} w{width}")
+    assert np.array_equal(O.round_bf16(y32), y)
+
+
+def test_sglang_blockscaled_probe_widths(rt):
+    # src/wide_metal_moe.rs:1330 probe inputs (128x256, widths 2, 9, 26, 32)
+    from gpu_helpers import assert_close
+    from mimo_prismwing_b200.runtime import WideProjectionBinding
+    rows, cols = 128, 256
+    w = np.array([(i * 37 + 11) % 0x7F for i in range(rows * cols)], np.uint8).reshape(rows, cols)
+    s = np.array([0.003 + i * 0.0017 for i in range(2)], np.float32).reshape(1, 2)
+    b = WideProjectionBinding(torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda())
+    for active in [2, 9, 26, 32]:
+        x = np.array([((i * 29 % 401) - 200.0) / 37.0 for i in range(active * cols)], np.float32).reshape(active, cols)
+        codes, scales, _ = O.dynamic_fp8(x)
+        gc, gs = rt.quantize(torch.from_numpy(x).cuda())
+        assert np.array_equal(H(gc), codes) and np.array_equal(H(gs), scales)
+        y = H(rt.execute_fp8_linear(torch.from_numpy(x).cuda(), b, f32_output=True).output)
+        ref = O.blockscaled_linear(w, s, codes, scales)
+        assert_close(y, ref, what=f"probe width {active}")
+
+
+@pytest.mark.parametrize("width", [1, 8])
+def test_full_qkv_layout_vs_oracle(rt, width):
+    from gpu_helpers import assert_close
+    from mimo_prismwing_b200 import synth
+    b = synth.full_qkv(31, "cuda")
+    assert tuple(b.scale.shape) == (108, 32)
+    x = synth.activations(width, 4096, 40 + width, "cuda")
+    y = H(rt.execute_fp8_linear(x, b, full_qkv_layout=True, f32_output=True).output)
+    codes, scales, _ = O.dynamic_fp8(H(x))
+    ref = O.blockscaled_linear(H(b.weight), H(b.scale), codes, scales, layout=O.LAYOUT_FULL_QKV)
+    assert_close(y, ref, what=f"full qkv w{width}")
+
+
+def test_swa_qkv_layout_vs_oracle(rt):
+    from gpu_helpers import assert_close
+    from mimo_prismwing_b200 import synth
+    b = synth.swa_qkv(32, "cuda")
+    x = synth.activations(3, 4096, 50, "cuda")
+    y = H(rt.execute_fp8_linear(x, b, f32_output=True).output)  # [14848, 4096] selects the SWA map
+    codes, scales, _ = O.dynamic_fp8(H(x))
+    ref = O.blockscaled_linear(H(b.weight), H(b.scale), codes, scales, layout=O.LAYOUT_SWA_QKV)
+    assert_close(y, ref, what="swa qkv")
+
+
+def test_projection_rejects_bad_layouts(rt):
+    from mimo_prismwing_b200.runtime import PrismwingError, WideProjectionBinding
+    from mimo_prismwing_b200 import synth
+    b = synth.projection(256, 256, 1, "cuda")
+    bad = WideProjectionBinding(b.weight, b.scale[:, :1].contiguous())
+    with pytest.raises(PrismwingError) as e:
+        rt.execute_fp8_linear(torch.zeros((1, 256), device="cuda"), bad)
+    assert e.value.kind == "shape"
+    with pytest.raises(PrismwingError) as e:
+        rt.execute_fp8_linear(torch.zeros((1, 256), device="cuda"), b, full_qkv_layout=True)
+    assert e.value.kind == "shape"
+    x = torch.zeros((1, 256), device="cuda")
+    x[0, 0] = float("inf")
+    with pytest.raises(PrismwingError) as e:
+        rt.execute_fp8_linear(x, b)
+    assert e.value.kind == "nonfinite"
+
+
+# ------------------------------------------------------- one expert (C1)
+@pytest.mark.parametrize("width", [1, 2, 4, 8])
+def test_expert_forward_config1_vs_oracle(rt, width):
+    from gpu_helpers import assert_close_bf16, bank_arrays
+    from mimo_prismwing_b200 import synth
+    g, u, d = synth.expert(4096, 2048, 7, "cuda")
+    x = synth.activations(width, 4096, 70 + width, "cuda")
+    y = H(rt.expert_forward(x, g, u, d).output)
+    (gw, gs, uw, us, dw, ds), = bank_arrays([(g, u, d)])
+    xc, xs, _ = O.dynamic_fp8(H(x))
+    gate = O.blockscaled_linear(gw, gs, xc, xs)
+    up = O.blockscaled_linear(uw, us, xc, xs)
+    act = O.staged_swiglu(gate, up, O.EXP_SLEEF)
+    hc, hs, _ = O.dynamic_fp8(act)
+    ref = O.round_bf16(O.blockscaled_linear(dw, ds, hc, hs))
+    assert_close_bf16(y, ref, what=f"expert w{width}")
+
+
+def test_fused_gate_up_swiglu_is_exact_against_unfused(rt, rt_unfused):
+    # src/wide_metal_moe.rs:1343 fused_gate_up_swiglu_is_exact_at_narrow_and_full_expert_widths
+    from mimo_prismwing_b200 import synth
+    g, u, d = synth.expert(4096, 2048, 8, "cuda")
+    for width in [2, 9, 26, 32]:
+        x = synth.activations(width, 4096, 90 + width, "cuda")
+        a = H(rt.expert_forward(x, g, u, d).output)
+        b = H(rt_unfused.expert_forward(x, g, u, d).output)
+        assert np.array_equal(a, b), f"width {width}"
+
+
+# ----------------------------------------------------------------- router
+@pytest.mark.parametrize("tokens", [1, 8, 128])
+def test_route_bit_exact_vs_oracle(rt, tokens):
+    from mimo_prismwing_b200 import synth
+    w, bias = synth.router(256, 4096, 5, "cuda")
+    x = synth.activations(tokens, 4096, 500 + tokens, "cuda")
+    sel, wts, st = rt.route(x, w, bias)
+    wbits = H(w.view(torch.int16)).view(np.uint16)
+    logits = O.router_logits(H(x), wbits)
+    osel, owts, _, margin, ties = O.noaux_topk(logits, H(bias))
+    assert np.array_equal(H(sel).astype(np.uint32), osel)
+    assert np.array_equal(H(wts).view(np.uint32), owts.view(np.uint32))
+    assert st["boundary_tie_rows"] == ties
+
+
+def test_route_host_io_matches_device_io(rt):
+    from mimo_prismwing_b200 import synth
+    w, bias = synth.router(256, 4096, 6, "cuda")
+    x = synth.activations(8, 4096, 600, "cuda")
+    a = rt.route(x, w, bias)
+    b = rt.route(x.cpu(), w, bias)
+    assert np.array_equal(H(a[0]), H(b[0])) and np.array_equal(H(a[1]), H(b[1]))
+
+
+# ------------------------------------------------------------ routed layer
+def _small_bank(n, hidden, inter, seed):
+    from mimo_prismwing_b200 import synth
+    return [synth.expert(hidden, inter, seed * 1000 + e, "cuda") for e in range(n)]
+
+
+def test_moe_execute_host_schedule_vs_oracle(rt):
+    # WideMetalMoeRuntime::execute with a BTreeMap-style schedule (8 tokens, 24 experts)
+    from gpu_helpers import assert_close_bf16, bank_arrays
+    from mimo_prismwing_b200 import synth
+    from mimo_prismwing_b200.runtime import WideExpertBinding
+    E, Hd, I, T = 24, 4096, 2048, 8
+    bank = _small_bank(E, Hd, I, 3)
+    rng = np.random.default_rng(3)
+    sel = np.stack([rng.choice(E, 8, replace=False) for _ in range(T)]).astype(np.uint32)
+    raw = rng.random((T, 8)).astype(np.float32)
+    wts = (raw / raw.sum(1, keepdims=True)).astype(np.float32)
+    x = synth.activations(T, Hd, 33, "cuda")
+    offsets, order = O.schedule(sel, E)
+    bindings = []
+    for e in range(E):
+        pl = order[offsets[e]:offsets[e + 1]]
+        if len(pl) == 0:
+            continue
+        g, u, d = bank[e]
+        bindings.append(WideExpertBinding(e, [int(p) // 8 for p in pl], [float(wts.ravel()[p]) for p in pl], g, u, d))
+    ex = rt.execute_fused_gate_up(x, bindings)
+    ref = O.routed_layer(H(x), sel, wts, bank_arrays(bank), O.ACC_F64, O.EXP_SLEEF)
+    assert_close_bf16(H(ex.output), ref, what="moe execute")
+    assert ex.expert_rows == T * 8 and ex.unique_experts == len(bindings)
+
+
+def test_moe_execute_rejects_bad_schedule(rt):
+    from mimo_prismwing_b200.runtime import PrismwingError, WideExpertBinding
+    bank = _small_bank(1, 256, 256, 4)
+    g, u, d = bank[0]
+    x = torch.zeros((1, 256), device="cuda")
+    with pytest.raises(PrismwingError) as e:  # 7 placements for one row
+        rt.execute(x, [WideExpertBinding(0, [0] * 7, [0.125] * 7, g, u, d)])
+    assert e.value.kind == "schedule"
+    with pytest.raises(PrismwingError) as e:  # position out of range
+        rt.execute(x, [WideExpertBinding(0, [0] * 7 + [1], [0.125] * 8, g, u, d)])
+    assert e.value.kind == "schedule"
+
+
+@pytest.mark.parametrize("tokens,E,Hd,I", [(8, 256, 4096, 2048), (1, 64, 1024, 512), (40, 32, 512, 256)])
+def test_moe_layer_device_router_vs_oracle(rt, tokens, E, Hd, I):
+    from gpu_helpers import assert_close_bf16, bank_arrays
+    from mimo_prismwing_b200 import synth
+    bank = _small_bank(E, Hd, I, 9)
+    handle = rt.create_bank(bank)
+    w, bias = synth.router(E, Hd, 10, "cuda")
+    x = synth.activations(tokens, Hd, 11, "cuda")
+    ex = rt.moe_layer(x, w, bias, handle, want_routes=True)
+    logits = O.router_logits(H(x), H(w.view(torch.int16)).view(np.uint16))
+    osel, owts, _, _, _ = O.noaux_topk(logits, H(bias))
+    assert np.array_equal(H(ex.selected).astype(np.uint32), osel)
+    assert np.array_equal(H(ex.weights).view(np.uint32), owts.view(np.uint32))
+    ref = O.routed_layer(H(x), osel, owts, bank_arrays(bank), O.ACC_F64, O.EXP_SLEEF)
+    assert_close_bf16(H(ex.output), ref, what=f"moe layer T{tokens} E{E}")
+    assert ex.expert_rows == tokens * 8
+    assert ex.unique_experts == len(set(osel.ravel().tolist()))
+    # host I/O
+    ex2 = rt.moe_layer(x.cpu(), w, bias, handle)
+    assert np.array_equal(ex2.output.numpy(), H(ex.output))
+
+
+def test_bank_rejects_nonfinite_weight_byte(rt):
+    from mimo_prismwing_b200.runtime import PrismwingError
+    bank = _small_bank(9, 256, 256, 12)
+    bank[4][1].weight[17, 5] = 0x7F
+    with pytest.raises(PrismwingError) as e:
+        rt.create_bank(bank)
+    assert e.value.kind == "nonfinite" and "4" in str(e.value)
