@@ -132,6 +132,21 @@ typedef struct pw_stats {
   uint64_t weight_bytes;      /* FP8 weight + scale bytes the call reads   */
 } pw_stats;
 
+/* Device time per kernel class of the last profiled call (CUDA events on the
+ * runtime's stream around each launch; 0 for classes the call did not run).
+ * The reference's equivalent is its per-projection tomography
+ * (ProjectionTomography / ExpertTomography, src/staged_metal_expert.rs:198-236). */
+typedef struct pw_profile {
+  float quantize_ms;   /* activation quantization (input + hidden)      */
+  float router_ms;     /* router logits + sigmoid top-k                 */
+  float schedule_ms;   /* device-side expert schedule                   */
+  float gate_up_ms;    /* gate/up projection (+ SwiGLU)                 */
+  float down_ms;       /* down projection                               */
+  float combine_ms;    /* weighted combine                              */
+  float projection_ms; /* single projections (pw_fp8_linear / gemv)     */
+  uint32_t launches;   /* kernels this library launched in the call     */
+} pw_profile;
+
 /* ---------------------------------------------------------------- runtime */
 
 /* Reference: WideMetalMoeRuntime::compile / compile_with_fused_gate_up
@@ -147,6 +162,9 @@ int pw_synchronize(pw_runtime *rt);
 /* Device error-flag word accumulated since the last call that reset it (0 = clean). */
 int pw_read_error_flags(pw_runtime *rt, uint32_t *flags);
 int pw_abi_version(void);
+/* Turn per-kernel event timing on (1) or off (0) for subsequent synchronous calls. */
+int pw_set_profiling(pw_runtime *rt, int enable);
+int pw_last_profile(pw_runtime *rt, pw_profile *out);
 
 /* ------------------------------------------------------------- primitives */
 

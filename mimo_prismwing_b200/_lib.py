@@ -54,6 +54,8 @@ def _bind(L: ctypes.CDLL) -> None:
     L.pw_bank_destroy.argtypes = [vp]
     L.pw_bank_destroy.restype = None
     L.pw_moe_layer.argtypes = [vp, vp, vp, vp, u32, vp, vp, vp, u32, vp]
+    L.pw_set_profiling.argtypes = [vp, i32]
+    L.pw_last_profile.argtypes = [vp, vp]
     for name in header_symbols():
         getattr(L, name)  # raises AttributeError if an entry point is missing
 

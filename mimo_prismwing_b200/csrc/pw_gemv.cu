@@ -428,13 +428,16 @@ static cudaError_t launch_kind(const GemvArgs &a, int grid, cudaStream_t stream)
   return launch_one<8, KIND>(a, grid, stream);
 }
 
+// The block-scaled kinds (0, 2, 3) run on the FP8 tensor-core GEMV
+// (pw_gemv_mma.cu); this CUDA-core kernel keeps the readable projection,
+// whose activation is an unquantized f32 vector.
 cudaError_t launch_gemv(int kind, const GemvArgs &a, int grid, cudaStream_t stream) {
   if (a.K == 0 || a.K % 128u || a.K > 4096u || a.rows % kUnitRows || grid <= 0) return cudaErrorInvalidValue;
   switch (kind) {
-    case 0: return launch_kind<0>(a, grid, stream);
     case 1: return launch_kind<1>(a, grid, stream);
-    case 2: return launch_kind<2>(a, grid, stream);
-    case 3: return launch_kind<3>(a, grid, stream);
+    case 0:
+    case 2:
+    case 3: return launch_gemv_mma(kind, a, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "pw_cuda.h"
@@ -12,13 +13,16 @@ namespace pw {
 // expert's placements in a routed layer).  count <= 8 per group: wider token
 // sets are split into several groups over the same weights.
 struct GemvGroup {
-  const uint8_t *w0;   // weight (gate for the fused kernel)
-  const float *s0;     // its scale grid
-  const uint8_t *w1;   // up weight (fused kernel only)
-  const float *s1;     // its scale grid
-  uint32_t tok_begin;  // first slot in the token list / output rows
-  uint32_t count;      // 1..8 tokens
-  uint32_t pad0, pad1;
+  const uint8_t *w0;        // weight (gate for the fused kernel)
+  const float *s0;          // its scale grid
+  const uint8_t *w1;        // up weight (fused kernel only)
+  const float *s1;          // its scale grid
+  const CUtensorMap *tm0;   // 2-D TMA maps of w0 / w1 in device memory
+  const CUtensorMap *tm1;   //   (128 B x 128-row boxes, 64 for QKV layouts)
+  uint32_t tok_begin;       // first slot in the token list / output rows
+  uint32_t count;           // 1..8 tokens
+  uint32_t expert;          // expert id (diagnostics)
+  uint32_t pad;
 };
 
 struct GemvArgs {
@@ -48,6 +52,7 @@ cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_
 // over w1/s1 (the unfused up projection)
 cudaError_t launch_gemv(int kind, const GemvArgs &args, int grid, cudaStream_t stream);
 int gemv_max_ctas(int num_sms);
+cudaError_t launch_gemv_mma(int kind, const GemvArgs &args, int grid, cudaStream_t stream);
 cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_t stream);
 cudaError_t launch_router_logits(const float *x, uint32_t tokens, const uint16_t *w, uint32_t experts,
                                  uint32_t hidden, float *logits, cudaStream_t stream);
@@ -74,7 +79,15 @@ struct BankTable {
   const float *const *up_s;
   const uint8_t *const *down_w;
   const float *const *down_s;
+  const CUtensorMap *gate_tm;  // [experts] each
+  const CUtensorMap *up_tm;
+  const CUtensorMap *down_tm;
 };
+
+// Host: encode the 2-D TMA map of one row-major e4m3 matrix [rows, cols]
+// (box 128 B x box_rows, 128B swizzle).  Returns false on failure.
+bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows);
+uint32_t map_box_rows(uint32_t layout);
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
                             const BankTable &bank, const ScheduleOut &out, uint32_t *flags,
                             cudaStream_t stream);

@@ -331,18 +331,22 @@ __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ 
       GemvGroup g;
       g.tok_begin = out.offsets[e] + 8u * j;
       g.count = min(8u, c - 8u * j);
-      g.pad0 = e;
-      g.pad1 = 0;
+      g.expert = e;
+      g.pad = 0;
       g.w0 = bank.gate_w[e];
       g.s0 = bank.gate_s[e];
       g.w1 = bank.up_w[e];
       g.s1 = bank.up_s[e];
+      g.tm0 = bank.gate_tm + e;
+      g.tm1 = bank.up_tm + e;
       out.gu_groups[grp_off[e] + j] = g;
       GemvGroup d = g;
       d.w0 = bank.down_w[e];
       d.s0 = bank.down_s[e];
       d.w1 = nullptr;
       d.s1 = nullptr;
+      d.tm0 = bank.down_tm + e;
+      d.tm1 = nullptr;
       out.dn_groups[grp_off[e] + j] = d;
     }
   }

@@ -16,12 +16,46 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "pw_cuda.h"
 #include "pw_internal.h"
 
 using namespace pw;
+
+// ------------------------------------------------------------ TMA maps
+namespace pw {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+uint32_t map_box_rows(uint32_t layout) { return layout == PW_LAYOUT_PLAIN ? 128u : 64u; }
+
+bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {128u, box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace pw
 
 struct pw_runtime {
   int device = 0;
@@ -35,14 +69,43 @@ struct pw_runtime {
   void *scratch = nullptr;
   size_t scratch_cap = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  // profiling: an event before and after each timed launch group
+  static constexpr int kProfEvents = 32;
+  bool profiling = false;
+  cudaEvent_t pev[kProfEvents] = {};
+  int pclass[kProfEvents / 2] = {};
+  int pcount = 0;
+  uint32_t launches = 0;
+  pw_profile last_profile{};
   std::string err;
 };
+
+namespace {
+enum ProfClass { P_QUANT, P_ROUTER, P_SCHED, P_GATEUP, P_DOWN, P_COMBINE, P_PROJ };
+
+// Opens a timed launch group of class c (no-op unless profiling).
+struct ProfScope {
+  pw_runtime *rt;
+  int idx = -1;
+  ProfScope(pw_runtime *r, int c, uint32_t n_launches) : rt(r) {
+    rt->launches += n_launches;
+    if (!rt->profiling || rt->pcount >= pw_runtime::kProfEvents / 2) return;
+    idx = rt->pcount++;
+    rt->pclass[idx] = c;
+    cudaEventRecord(rt->pev[2 * idx], rt->stream);
+  }
+  ~ProfScope() {
+    if (idx >= 0) cudaEventRecord(rt->pev[2 * idx + 1], rt->stream);
+  }
+};
+}  // namespace
 
 struct pw_expert_bank {
   pw_runtime *rt = nullptr;
   uint32_t n = 0;
   uint32_t hidden = 0, inter = 0;
   void *d_table = nullptr;  // 6 arrays of n pointers
+  CUtensorMap *d_maps = nullptr;  // 3 arrays of n TMA maps (gate, up, down)
   BankTable table{};
   std::vector<pw_expert_weights> host;
 };
@@ -146,6 +209,8 @@ struct Call {
 
   int begin() {
     t0 = now_ms();
+    rt->pcount = 0;
+    rt->launches = 0;
     if (stats) memset(stats, 0, sizeof *stats);
     if (async() && stats) return fail(rt, PW_ERR_ARGUMENT, "stats cannot be returned by an asynchronous call");
     if (!async()) CK(cudaMemsetAsync(rt->d_flags, 0, sizeof(uint32_t), rt->stream));
@@ -176,6 +241,16 @@ struct Call {
       stats->error_flags = flags;
       stats->weight_bytes = weight_bytes;
     }
+    pw_profile prof{};
+    for (int i = 0; i < rt->pcount; ++i) {
+      float ms = 0.0f;
+      CK(cudaEventElapsedTime(&ms, rt->pev[2 * i], rt->pev[2 * i + 1]));
+      float *slot[] = {&prof.quantize_ms, &prof.router_ms, &prof.schedule_ms, &prof.gate_up_ms,
+                       &prof.down_ms,     &prof.combine_ms, &prof.projection_ms};
+      *slot[rt->pclass[i]] += ms;
+    }
+    prof.launches = rt->launches;
+    rt->last_profile = prof;
     if (flags & PW_FLAG_WAIT_TIMEOUT) return fail(rt, PW_ERR_TIMEOUT, "a bounded device wait gave up (flags %u)", flags);
     if (flags & (PW_FLAG_NONFINITE_INPUT))
       return fail(rt, PW_ERR_NONFINITE, "non-finite input (device flags %u)", flags);
@@ -190,7 +265,8 @@ struct Call {
 };
 
 // Projection groups for `width` tokens over one weight set (<= 8 per group).
-std::vector<GemvGroup> width_groups(uint32_t width, const pw_fp8_tensor &a, const pw_fp8_tensor *b) {
+std::vector<GemvGroup> width_groups(uint32_t width, const pw_fp8_tensor &a, const pw_fp8_tensor *b,
+                                    const CUtensorMap *ma = nullptr, const CUtensorMap *mb = nullptr) {
   std::vector<GemvGroup> gs;
   for (uint32_t t = 0; t < width; t += 8) {
     GemvGroup g{};
@@ -198,6 +274,8 @@ std::vector<GemvGroup> width_groups(uint32_t width, const pw_fp8_tensor &a, cons
     g.s0 = a.scale;
     g.w1 = b ? b->weight : nullptr;
     g.s1 = b ? b->scale : nullptr;
+    g.tm0 = ma;
+    g.tm1 = mb;
     g.tok_begin = t;
     g.count = width - t < 8 ? width - t : 8;
     gs.push_back(g);
@@ -216,6 +294,17 @@ GemvArgs gemv_args(const pw_runtime *rt, const GemvGroup *groups, uint32_t n_gro
   a.layout = layout;
   a.flags = rt->d_flags;
   return a;
+}
+
+// Encode the maps of `n` matrices on the host into `host`; false on failure.
+bool encode_maps(pw_runtime *rt, const pw_fp8_tensor *const *ts, size_t n, uint32_t layout, CUtensorMap *host) {
+  for (size_t i = 0; i < n; ++i) {
+    if (!encode_weight_map(&host[i], ts[i]->weight, ts[i]->rows, ts[i]->cols, map_box_rows(layout))) {
+      fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for a [%u, %u] weight", ts[i]->rows, ts[i]->cols);
+      return false;
+    }
+  }
+  return true;
 }
 
 int grid_for(const pw_runtime *rt, uint64_t units) {
@@ -258,6 +347,8 @@ int pw_runtime_create(int device, uint32_t flags, pw_runtime **out) {
   if ((e = cudaMemset(rt->d_flags, 0, 256)) != cudaSuccess) return bail(e);
   if ((e = cudaEventCreate(&rt->ev0)) != cudaSuccess) return bail(e);
   if ((e = cudaEventCreate(&rt->ev1)) != cudaSuccess) return bail(e);
+  for (int i = 0; i < pw_runtime::kProfEvents; ++i)
+    if ((e = cudaEventCreate(&rt->pev[i])) != cudaSuccess) return bail(e);
   *out = rt;
   return PW_OK;
 }
@@ -270,6 +361,8 @@ void pw_runtime_destroy(pw_runtime *rt) {
   if (rt->d_flags) cudaFree(rt->d_flags);
   if (rt->ev0) cudaEventDestroy(rt->ev0);
   if (rt->ev1) cudaEventDestroy(rt->ev1);
+  for (int i = 0; i < pw_runtime::kProfEvents; ++i)
+    if (rt->pev[i]) cudaEventDestroy(rt->pev[i]);
   if (rt->own_stream) cudaStreamDestroy(rt->own_stream);
   delete rt;
 }
@@ -285,6 +378,18 @@ int pw_set_stream(pw_runtime *rt, void *cuda_stream) {
 int pw_synchronize(pw_runtime *rt) {
   if (!rt) return PW_ERR_ARGUMENT;
   CK(cudaStreamSynchronize(rt->stream));
+  return PW_OK;
+}
+
+int pw_set_profiling(pw_runtime *rt, int enable) {
+  if (!rt) return PW_ERR_ARGUMENT;
+  rt->profiling = enable != 0;
+  return PW_OK;
+}
+
+int pw_last_profile(pw_runtime *rt, pw_profile *out) {
+  if (!rt || !out) return PW_ERR_ARGUMENT;
+  *out = rt->last_profile;
   return PW_OK;
 }
 
@@ -317,10 +422,14 @@ int pw_quantize_fp8(pw_runtime *rt, const float *x, uint32_t rows, uint32_t cols
     uint8_t *dc = ar.take<uint8_t>(n);
     float *ds = ar.take<float>(ng);
     if ((s = call.stage_in(dx, x, n * 4)) != PW_OK) return s;
-    CK(launch_quantize(dx, rows, cols, dc, ds, rt->d_flags, rt->stream));
+    {
+      ProfScope ps(rt, P_QUANT, 1);
+      CK(launch_quantize(dx, rows, cols, dc, ds, rt->d_flags, rt->stream));
+    }
     if ((s = call.stage_out(codes, dc, n)) != PW_OK) return s;
     if ((s = call.stage_out(scales, ds, ng * 4)) != PW_OK) return s;
   } else {
+    ProfScope ps(rt, P_QUANT, 1);
     CK(launch_quantize(x, rows, cols, codes, scales, rt->d_flags, rt->stream));
   }
   return call.finish(0);
@@ -362,7 +471,11 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
   CK(cudaSetDevice(rt->device));
   const uint32_t K = w->cols, N = w->rows;
   const size_t nx = (size_t)width * K, ny = (size_t)width * N;
-  std::vector<GemvGroup> groups = width_groups(width, *w, nullptr);
+  CUtensorMap hmap;
+  if (kind != 1) {
+    const pw_fp8_tensor *ts[1] = {w};
+    if (!encode_maps(rt, ts, 1, layout, &hmap)) return PW_ERR_CUDA;
+  }
   Call call{rt, mem, stats, 0};
   if ((s = call.begin()) != PW_OK) return s;
   Arena ar;
@@ -375,9 +488,12 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
     float *dy = call.host() ? ar.take<float>(ny) : y;
     uint8_t *dc = kind == 1 ? nullptr : ar.take<uint8_t>(nx);
     float *ds = kind == 1 ? nullptr : ar.take<float>(nx / 128u);
+    CUtensorMap *dm = ar.take<CUtensorMap>(1);
+    std::vector<GemvGroup> groups = width_groups(width, *w, nullptr, kind == 1 ? nullptr : dm);
     GemvGroup *dg = ar.take<GemvGroup>(groups.size());
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, nx * 4)) != PW_OK) return s;
+    if (kind != 1) CK(cudaMemcpyAsync(dm, &hmap, sizeof hmap, cudaMemcpyHostToDevice, rt->stream));
     CK(cudaMemcpyAsync(dg, groups.data(), groups.size() * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
     GemvArgs a = gemv_args(rt, dg, (uint32_t)groups.size(), N, K, layout);
     a.out = dy;
@@ -386,12 +502,16 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
       a.x_f32 = dx;
       a.round_bf16 = 0;
     } else {
+      ProfScope ps(rt, P_QUANT, 1);
       CK(launch_quantize(dx, width, K, dc, ds, rt->d_flags, rt->stream));
       a.x_codes = dc;
       a.x_scales = ds;
       a.round_bf16 = round;
     }
-    CK(launch_gemv(kind, a, grid_for(rt, (uint64_t)groups.size() * (N / 64u)), rt->stream));
+    {
+      ProfScope ps(rt, P_PROJ, 1);
+      CK(launch_gemv(kind, a, grid_for(rt, (uint64_t)groups.size() * (N / (kind == 1 ? 64u : 128u))), rt->stream));
+    }
     if (call.host() && (s = call.stage_out(y, dy, ny * 4)) != PW_OK) return s;
   }
   return call.finish((uint64_t)N * K + (uint64_t)w->scale_rows * w->scale_cols * 4u);
@@ -419,7 +539,9 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
                                 const uint32_t *tok_list, const uint8_t *xc, const float *xs, float *hidden,
                                 float *gate_tmp, float *up_tmp, uint8_t *hc, float *hs, float *down,
                                 uint32_t down_round, uint64_t units_hint) {
-  const int grid_gu = grid_for(rt, units_hint * (I / 64u));
+  const int grid_gu = grid_for(rt, units_hint * (I / 128u));
+  {
+  ProfScope ps(rt, P_GATEUP, (rt->flags & PW_RUNTIME_FUSED_GATE_UP) ? 1 : 3);
   if (rt->flags & PW_RUNTIME_FUSED_GATE_UP) {
     GemvArgs a = gemv_args(rt, gu, n_groups, I, H, PW_LAYOUT_PLAIN);
     a.n_groups_dev = n_groups_dev;
@@ -446,7 +568,11 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
     CK(launch_gemv(3, b, grid_gu, rt->stream));
     CK(launch_swiglu(gate_tmp, up_tmp, hidden, slots * I, rt->d_flags, rt->stream));
   }
-  CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream));
+  }
+  {
+    ProfScope ps(rt, P_QUANT, 1);
+    CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream));
+  }
   GemvArgs d = gemv_args(rt, dn, n_groups, H, I, PW_LAYOUT_PLAIN);
   d.n_groups_dev = n_groups_dev;
   d.x_codes = hc;
@@ -454,7 +580,8 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
   d.out = down;
   d.out_stride = H;
   d.round_bf16 = down_round;
-  CK(launch_gemv(0, d, grid_for(rt, units_hint * (H / 64u)), rt->stream));
+  ProfScope ps(rt, P_DOWN, 1);
+  CK(launch_gemv(0, d, grid_for(rt, units_hint * (H / 128u)), rt->stream));
   return PW_OK;
 }
 
@@ -470,8 +597,11 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
   if (width == 0) return fail(rt, PW_ERR_SHAPE, "expert width must be at least one");
   CK(cudaSetDevice(rt->device));
   const uint32_t H = w->gate.cols, I = w->gate.rows;
-  std::vector<GemvGroup> gu = width_groups(width, w->gate, &w->up);
-  std::vector<GemvGroup> dn = width_groups(width, w->down, nullptr);
+  CUtensorMap hmaps[3];
+  {
+    const pw_fp8_tensor *ts[3] = {&w->gate, &w->up, &w->down};
+    if (!encode_maps(rt, ts, 3, PW_LAYOUT_PLAIN, hmaps)) return PW_ERR_CUDA;
+  }
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   Call call{rt, mem, stats, 0};
   if ((s = call.begin()) != PW_OK) return s;
@@ -490,13 +620,20 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
     float *ut = fused ? nullptr : ar.take<float>((size_t)width * I);
     uint8_t *hc = ar.take<uint8_t>((size_t)width * I);
     float *hs = ar.take<float>((size_t)width * I / 128u);
+    CUtensorMap *dm = ar.take<CUtensorMap>(3);
+    std::vector<GemvGroup> gu = width_groups(width, w->gate, &w->up, dm, dm ? dm + 1 : nullptr);
+    std::vector<GemvGroup> dn = width_groups(width, w->down, nullptr, dm ? dm + 2 : nullptr);
     GemvGroup *dgu = ar.take<GemvGroup>(gu.size());
     GemvGroup *ddn = ar.take<GemvGroup>(dn.size());
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)width * H * 4)) != PW_OK) return s;
+    CK(cudaMemcpyAsync(dm, hmaps, sizeof hmaps, cudaMemcpyHostToDevice, rt->stream));
     CK(cudaMemcpyAsync(dgu, gu.data(), gu.size() * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
     CK(cudaMemcpyAsync(ddn, dn.data(), dn.size() * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
-    CK(launch_quantize(dx, width, H, xc, xs, rt->d_flags, rt->stream));
+    {
+      ProfScope ps(rt, P_QUANT, 1);
+      CK(launch_quantize(dx, width, H, xc, xs, rt->d_flags, rt->stream));
+    }
     if ((s = enqueue_expert_chain(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, width, H, I, nullptr, xc, xs, hid, gt,
                                   ut, hc, hs, dy, 1, gu.size())) != PW_OK)
       return s;
@@ -540,8 +677,11 @@ int pw_route(pw_runtime *rt, const pw_router *router, const float *x, uint32_t t
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)tokens * H * 4)) != PW_OK) return s;
     CK(cudaMemsetAsync(rt->d_ties, 0, 4, rt->stream));
-    CK(launch_router_logits(dx, tokens, router->weight_bf16, E, H, logits, rt->stream));
-    CK(launch_router_topk(logits, router->bias, tokens, E, dsel, dw, rt->d_ties, rt->d_flags, rt->stream));
+    {
+      ProfScope ps(rt, P_ROUTER, 2);
+      CK(launch_router_logits(dx, tokens, router->weight_bf16, E, H, logits, rt->stream));
+      CK(launch_router_topk(logits, router->bias, tokens, E, dsel, dw, rt->d_ties, rt->d_flags, rt->stream));
+    }
     if (call.host()) {
       if ((s = call.stage_out(selected, dsel, (size_t)tokens * 32)) != PW_OK) return s;
       if ((s = call.stage_out(weights, dw, (size_t)tokens * 32)) != PW_OK) return s;
@@ -571,6 +711,8 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
   std::vector<float> placement_w;
   std::vector<GemvGroup> gu, dn;
   std::vector<uint32_t> uniq;
+  std::vector<CUtensorMap> hmaps((size_t)n_experts * 3);
+  std::vector<size_t> group_binding;
   for (uint32_t i = 0; i < n_experts; ++i) {
     const pw_expert_binding &b = experts[i];
     if ((s = check_expert(rt, &b.weights)) != PW_OK) return s;
@@ -600,8 +742,9 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
       g.s1 = b.weights.up.scale;
       g.tok_begin = begin + j;
       g.count = b.count - j < 8u ? b.count - j : 8u;
-      g.pad0 = b.expert;
+      g.expert = b.expert;
       gu.push_back(g);
+      group_binding.push_back(i);
       GemvGroup d = g;
       d.w0 = b.weights.down.weight;
       d.s0 = b.weights.down.scale;
@@ -612,6 +755,10 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
   }
   for (uint32_t t = 0; t < rows; ++t)
     if (per_token[t] != 8u) return fail(rt, PW_ERR_SCHEDULE, "position %u has %u placements, expected 8", t, per_token[t]);
+  for (uint32_t i = 0; i < n_experts; ++i) {
+    const pw_fp8_tensor *ts[3] = {&experts[i].weights.gate, &experts[i].weights.up, &experts[i].weights.down};
+    if (!encode_maps(rt, ts, 3, PW_LAYOUT_PLAIN, &hmaps[(size_t)i * 3])) return PW_ERR_CUDA;
+  }
   CK(cudaSetDevice(rt->device));
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   const uint32_t P = rows * 8u;
@@ -630,8 +777,17 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
     uint32_t *dtok = ar.take<uint32_t>(P);
     float *dpw = ar.take<float>(P);
     uint32_t *dslot = ar.take<uint32_t>(P);
+    CUtensorMap *dm = ar.take<CUtensorMap>(hmaps.size());
     GemvGroup *dgu = ar.take<GemvGroup>(gu.size());
     GemvGroup *ddn = ar.take<GemvGroup>(dn.size());
+    if (pass == 1) {
+      for (size_t k = 0; k < gu.size(); ++k) {
+        gu[k].tm0 = dm + group_binding[k] * 3;
+        gu[k].tm1 = dm + group_binding[k] * 3 + 1;
+        dn[k].tm0 = dm + group_binding[k] * 3 + 2;
+        dn[k].tm1 = nullptr;
+      }
+    }
     float *hid = ar.take<float>((size_t)P * I);
     float *gt = fused ? nullptr : ar.take<float>((size_t)P * I);
     float *ut = fused ? nullptr : ar.take<float>((size_t)P * I);
@@ -640,16 +796,23 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
     float *down = ar.take<float>((size_t)P * H);
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)rows * H * 4)) != PW_OK) return s;
+    CK(cudaMemcpyAsync(dm, hmaps.data(), hmaps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, rt->stream));
     CK(cudaMemcpyAsync(dtok, placement_tok.data(), P * 4u, cudaMemcpyHostToDevice, rt->stream));
     CK(cudaMemcpyAsync(dpw, placement_w.data(), P * 4u, cudaMemcpyHostToDevice, rt->stream));
     CK(cudaMemcpyAsync(dslot, slot_place.data(), P * 4u, cudaMemcpyHostToDevice, rt->stream));
     CK(cudaMemcpyAsync(dgu, gu.data(), gu.size() * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
     CK(cudaMemcpyAsync(ddn, dn.data(), dn.size() * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
-    CK(launch_quantize(dx, rows, H, xc, xs, rt->d_flags, rt->stream));
+    {
+      ProfScope ps(rt, P_QUANT, 1);
+      CK(launch_quantize(dx, rows, H, xc, xs, rt->d_flags, rt->stream));
+    }
     if ((s = enqueue_expert_chain(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, P, H, I, dtok, xc, xs, hid, gt, ut, hc,
                                   hs, down, 1, gu.size())) != PW_OK)
       return s;
-    CK(launch_combine(down, dslot, dpw, rows, H, dy, rt->d_flags, rt->stream));
+    {
+      ProfScope ps(rt, P_COMBINE, 1);
+      CK(launch_combine(down, dslot, dpw, rows, H, dy, rt->d_flags, rt->stream));
+    }
     if (call.host() && (s = call.stage_out(y, dy, (size_t)rows * H * 4)) != PW_OK) return s;
   }
   const pw_expert_weights &w0 = experts[0].weights;
@@ -698,6 +861,28 @@ int pw_bank_create(pw_runtime *rt, const pw_expert_weights *experts, uint32_t n_
     pw_bank_destroy(bank);
     return fail(rt, PW_ERR_CUDA, "bank table: %s", cudaGetErrorString(err));
   }
+  {
+    std::vector<CUtensorMap> maps((size_t)n_experts * 3);
+    for (uint32_t e = 0; e < n_experts; ++e) {
+      const pw_fp8_tensor *ts[3] = {&experts[e].gate, &experts[e].up, &experts[e].down};
+      for (int k = 0; k < 3; ++k) {
+        if (!encode_weight_map(&maps[(size_t)k * n_experts + e], ts[k]->weight, ts[k]->rows, ts[k]->cols, 128u)) {
+          pw_bank_destroy(bank);
+          return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for expert %u", e);
+        }
+      }
+    }
+    err = cudaMalloc(&bank->d_maps, maps.size() * sizeof(CUtensorMap));
+    if (err == cudaSuccess)
+      err = cudaMemcpy(bank->d_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+      pw_bank_destroy(bank);
+      return fail(rt, PW_ERR_CUDA, "bank maps: %s", cudaGetErrorString(err));
+    }
+    bank->table.gate_tm = bank->d_maps;
+    bank->table.up_tm = bank->d_maps + n_experts;
+    bank->table.down_tm = bank->d_maps + 2 * (size_t)n_experts;
+  }
   const void **d = static_cast<const void **>(bank->d_table);
   bank->table.gate_w = reinterpret_cast<const uint8_t *const *>(d + 0 * n_experts);
   bank->table.gate_s = reinterpret_cast<const float *const *>(d + 1 * n_experts);
@@ -722,9 +907,10 @@ int pw_bank_create(pw_runtime *rt, const pw_expert_weights *experts, uint32_t n_
 
 void pw_bank_destroy(pw_expert_bank *bank) {
   if (!bank) return;
-  if (bank->d_table) {
+  if (bank->d_table || bank->d_maps) {
     cudaSetDevice(bank->rt->device);
-    cudaFree(bank->d_table);
+    if (bank->d_table) cudaFree(bank->d_table);
+    if (bank->d_maps) cudaFree(bank->d_maps);
   }
   delete bank;
 }
@@ -779,15 +965,27 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     counters = so.counters;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)tokens * H * 4)) != PW_OK) return s;
     CK(cudaMemsetAsync(rt->d_ties, 0, 4, rt->stream));
-    CK(launch_quantize(dx, tokens, H, xc, xs, rt->d_flags, rt->stream));
-    CK(launch_router_logits(dx, tokens, router->weight_bf16, E, H, logits, rt->stream));
-    CK(launch_router_topk(logits, router->bias, tokens, E, sel, wts, rt->d_ties, rt->d_flags, rt->stream));
-    CK(launch_schedule(sel, wts, tokens, E, bank->table, so, rt->d_flags, rt->stream));
+    {
+      ProfScope ps(rt, P_QUANT, 1);
+      CK(launch_quantize(dx, tokens, H, xc, xs, rt->d_flags, rt->stream));
+    }
+    {
+      ProfScope ps(rt, P_ROUTER, 2);
+      CK(launch_router_logits(dx, tokens, router->weight_bf16, E, H, logits, rt->stream));
+      CK(launch_router_topk(logits, router->bias, tokens, E, sel, wts, rt->d_ties, rt->d_flags, rt->stream));
+    }
+    {
+      ProfScope ps(rt, P_SCHED, 1);
+      CK(launch_schedule(sel, wts, tokens, E, bank->table, so, rt->d_flags, rt->stream));
+    }
     // the grid covers the worst case; CTAs read the real group count
     if ((s = enqueue_expert_chain(rt, so.gu_groups, so.dn_groups, max_groups, so.n_groups, P, H, I, so.placement_tok,
                                   xc, xs, hid, gt, ut, hc, hs, down, 1, max_groups)) != PW_OK)
       return s;
-    CK(launch_combine(down, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream));
+    {
+      ProfScope ps(rt, P_COMBINE, 1);
+      CK(launch_combine(down, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream));
+    }
     if (call.host()) {
       if ((s = call.stage_out(y, dy, (size_t)tokens * H * 4)) != PW_OK) return s;
       if (selected && (s = call.stage_out(selected, sel, (size_t)P * 4)) != PW_OK) return s;

@@ -77,6 +77,15 @@ class Stats(ctypes.Structure):
         return {k: getattr(self, k) for k, _ in self._fields_}
 
 
+class Profile(ctypes.Structure):
+    _fields_ = [("quantize_ms", ctypes.c_float), ("router_ms", ctypes.c_float), ("schedule_ms", ctypes.c_float),
+                ("gate_up_ms", ctypes.c_float), ("down_ms", ctypes.c_float), ("combine_ms", ctypes.c_float),
+                ("projection_ms", ctypes.c_float), ("launches", ctypes.c_uint32)]
+
+    def as_dict(self) -> dict:
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
 # ------------------------------------------------------------------ bindings
 @dataclass
 class WideProjectionBinding:
@@ -187,6 +196,15 @@ class WideMoeRuntime:
 
     def synchronize(self) -> None:
         self._check(self._L.pw_synchronize(self._rt))
+
+    def set_profiling(self, enable: bool) -> None:
+        """Per-kernel CUDA-event timing of subsequent synchronous calls."""
+        self._check(self._L.pw_set_profiling(self._rt, 1 if enable else 0))
+
+    def last_profile(self) -> dict:
+        p = Profile()
+        self._check(self._L.pw_last_profile(self._rt, ctypes.byref(p)))
+        return p.as_dict()
 
     def error_flags(self) -> int:
         f = ctypes.c_uint32()
