@@ -243,7 +243,6 @@ def run_ours(args, rank, world, local_rank):
         raise RuntimeError(f"device error flags {flags}")
     ms = ev0.elapsed_time(ev1)
     us_per_layer = ms * 1e3 / args.steps
-    launches = 8 * args.steps
 
     # ---- per-kernel profile + bytes (separate pass, synchronous calls)
     rt.set_profiling(True)
@@ -257,12 +256,13 @@ def run_ours(args, rank, world, local_rank):
     for i in range(args.steps):
         ex = rt.moe_layer(xs[i], w, bias, handle, stats=True, out=y)
         p = rt.last_profile()
+        launches_per_layer = p["launches"]
         for k in prof_keys:
             prof[k] += p[k]
         U = ex.unique_experts
         uniq.append(U)
         # weights + scales + activation codes/scales read + outputs written
-        gu_bytes += U * per_expert_gu + P * (HIDDEN + HIDDEN // 128 * 4) + P * INTER * 4
+        gu_bytes += U * per_expert_gu + P * (HIDDEN + HIDDEN // 128 * 4) + P * (INTER + INTER // 128 * 4)
         dn_bytes += U * per_expert_dn + P * (INTER + INTER // 128 * 4) + P * HIDDEN * 4
     rt.set_profiling(False)
     gu_ms = prof["gate_up_ms"] / args.steps
@@ -316,7 +316,7 @@ def run_ours(args, rank, world, local_rank):
                            unique_experts_mean=round(statistics.mean(uniq), 2)),
             "e2e": {"value": round(e2e_us, 3), "unit": "us", "h2d_bytes_per_step": WIDTH * HIDDEN * 4,
                     "d2h_bytes_per_step": WIDTH * HIDDEN * 4 + 4},
-            "gpu_launches": launches,
+            "gpu_launches": launches_per_layer * args.steps,
             "roofline": {"bound": "hbm", "kernel": "k_gemv fused gate/up + SwiGLU",
                          "achieved": round(gu_gbs, 1), "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(gu_gbs / hbm, 4), "traffic": None,

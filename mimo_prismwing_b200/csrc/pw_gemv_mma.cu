@@ -9,18 +9,21 @@
 //
 // B200 design.  At decode widths the kernel is a weight stream that has to
 // run at HBM rate (~6.5 TB/s, ~22 B/clk per SM).  Measured on this part with
-// one CTA per SM: achieved bandwidth tracks the bytes in flight and drops with
-// the number of copies per byte (16 x 1 KB copies per stage: 2.0 TB/s; one
-// 16 KB copy: 5.6 TB/s; 32 KB: 6.6 TB/s).  So:
+// one CTA per SM streaming through a shared-memory ring: every 16 KB TMA
+// operation shape tops out near 4.4 TB/s, while 32 KB operations reach
+// 6.5-6.9 TB/s.  So:
 //  * a CTA owns a 128-row tile of one weight matrix for the whole K; warp w
-//    owns rows 16w..16w+15 of it, so there is no cross-warp reduction;
-//  * a stage is one 128-column block of the tile: one 2-D TMA box of
-//    128 rows x 128 B (two 64-row boxes when the rows come from a QKV shard
-//    map), 128B-swizzled so ldmatrix reads are bank-conflict-free;
-//  * a ~176 KB ring (11 stages, 5 for gate+up) keeps ~160 KB in flight per SM;
-//  * lane 0 of warp 0 issues the TMA copies NST-1 stages ahead (a separate
-//    producer warp would cap registers); the 8 token slots' codes and scales
-//    sit in shared memory for the tile (rows padded to K+16 bytes).
+//    owns rows 16w..16w+15, so no cross-warp reduction is needed;
+//  * one stage = one 32 KB 3-D TMA box over the view {128 B, rows, k-block}
+//    (strides {K, 128}) of the row-major matrix: 128 rows x 2 k-blocks, or
+//    64 rows x 4 k-blocks when a QKV shard map splits the tile into two
+//    contiguous 64-row halves.  Rows land in consecutive 128-byte lines, so
+//    the 128B swizzle makes the ldmatrix reads of 8 rows bank-conflict-free;
+//  * gate and up are separate stages of one ring (fused kernel);
+//  * a ninth warp is the producer: one lane waits for free ring slots and
+//    issues the copies, decoupled from the consumer warps' progress; the 8
+//    token slots' codes and scales and each consumer warp's weight-scale row
+//    sit in shared memory for the tile.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -31,31 +34,36 @@
 namespace pw {
 namespace mma {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+constexpr int kWarps = 8;                    // consumer warps
+constexpr int kThreads = (kWarps + 1) * 32;  // + one producer warp
+constexpr int kConsumerThreads = kWarps * 32;
 constexpr int kTileRows = 128;
-constexpr int kBoxBytes = kTileRows * 128;  // one matrix, one 128-column block
-constexpr int kRingBytes = 176 * 1024;
+constexpr int kStageBytes = 32 * 1024;   // one 3-D box: 256 lines of 128 B
 constexpr int kMaxK = 4096;
-constexpr int kXStride = kMaxK + 16;        // padded activation row in smem
+constexpr int kMaxStages = 8;
 
-template <int KIND>
-struct Cfg {
-  static constexpr bool FUSED = KIND == 2;
-  static constexpr int MATS = FUSED ? 2 : 1;
-  static constexpr int SLOT = kBoxBytes * MATS;
-  static constexpr int NST = kRingBytes / SLOT;  // 11 or 5
-  static constexpr int RING = NST * SLOT;
-  static constexpr int XOFF = RING;                       // x codes [8][kXStride]
-  static constexpr int SOFF = XOFF + 8 * kXStride;        // x scales [8][32]
-  static constexpr int BOFF = SOFF + 8 * 32 * 4;          // barriers
-  static constexpr int SMEM = BOFF + 2 * NST * 8 + 16 + 1024;  // + alignment slack
+// Shared-memory carve-up (runtime: the activation tile depends on K).
+struct Layout {
+  uint32_t nst, xstride, x, xs, ws, amax, bars, total;
 };
+
+__host__ __device__ inline Layout make_layout(uint32_t K, uint32_t nst) {
+  Layout l;
+  l.nst = nst;
+  l.xstride = K + 16u;  // padded activation row: conflict-free ldmatrix
+  l.x = nst * kStageBytes;
+  l.xs = l.x + 8u * l.xstride;            // x scales [8][32]
+  l.ws = l.xs + 8u * 32u * 4u;            // weight scales [8 warps][2][32]
+  l.amax = l.ws + 8u * 2u * 32u * 4u;     // [8 warps][8 tokens]
+  l.bars = l.amax + 8u * 8u * 4u;         // full[nst], empty[nst], abort
+  l.total = l.bars + 2u * nst * 8u + 16u;
+  return l;
+}
 
 struct Ring {
   uint32_t slot = 0, phase = 0, issued = 0, parity = 0;
-  __device__ __forceinline__ void advance(int nst) {
-    if (++slot == (uint32_t)nst) {
+  __device__ __forceinline__ void advance(uint32_t nst) {
+    if (++slot == nst) {
       slot = 0;
       phase ^= 1u;
     }
@@ -66,6 +74,8 @@ struct Shared {
   uint8_t *ring;
   uint8_t *x;
   float *xs;
+  float *ws;
+  float *amax;
   uint64_t *full;
   uint64_t *empty;
   volatile int *abort;
@@ -95,13 +105,14 @@ __device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// 2-D TMA tile load: box at (x = column byte, y = row) of the tensor map.
-// x is always a multiple of 128 (16-byte rule of the tiled copy).
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+// 3-D TMA box load at (x = 0, y = row, z = k-block) of the {128 B, rows,
+// k-blocks} view.  The innermost coordinate is 0, so the 16-byte rule of the
+// tiled copy holds trivially.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int row, int kblock, uint64_t *bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
           smem_addr(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+      "l"(map), "r"(0), "r"(row), "r"(kblock), "r"(smem_addr(bar))
       : "memory");
 }
 
@@ -109,15 +120,34 @@ __device__ __forceinline__ void tensormap_acquire(const CUtensorMap *map) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
 }
 
-// Producer: walks (tile, k-block) exactly as the consumers do and issues one
+// Stage geometry of a tile: box rows BR (128, or 64 for QKV maps), k-blocks
+// per box KBS = 256 / BR, halves = 128 / BR; stages run kc-major, then half,
+// then matrix.
+struct Geo {
+  uint32_t br, kbs, halves, kcs, per_tile;
+};
+
+__device__ __forceinline__ Geo make_geo(const GemvArgs &a, int mats) {
+  Geo g;
+  g.br = a.layout == PW_LAYOUT_PLAIN ? 128u : 64u;
+  g.kbs = 256u / g.br;
+  g.halves = 128u / g.br;
+  const uint32_t kblocks = a.K / 128u;
+  g.kcs = (kblocks + g.kbs - 1u) / g.kbs;
+  g.per_tile = g.kcs * g.halves * (uint32_t)mats;
+  return g;
+}
+
+// Producer: walks (tile, stage) exactly as the consumers do and issues one
 // stage per call.  Lives in lane 0 of warp 0.
 template <int KIND>
 struct Producer {
-  using C = Cfg<KIND>;
-  uint32_t u, u_end, tpg, kb, kblocks;
+  static constexpr int MATS = KIND == 2 ? 2 : 1;
+  uint32_t u, u_end, tpg, st, nst;
+  Geo geo;
   const CUtensorMap *m0;
   const CUtensorMap *m1;
-  uint32_t src_lo, src_hi;  // source rows of the tile's two 64-row halves
+  uint32_t src0, src1;  // source rows of the tile's two 64-row halves
   Ring ring;
 
   __device__ __forceinline__ void enter_tile(const GemvArgs &a) {
@@ -128,73 +158,69 @@ struct Producer {
     // the maps were written through the generic proxy (host copy or bank
     // build); make those writes visible to the TMA unit before first use
     tensormap_acquire(m0);
-    if (C::FUSED) tensormap_acquire(m1);
+    if (MATS == 2) tensormap_acquire(m1);
     const uint32_t row0 = (u % tpg) * kTileRows;
     uint32_t s;
-    map_row(a.layout, row0, src_lo, s);
-    map_row(a.layout, row0 + 64u, src_hi, s);
-    kb = 0;
+    map_row(a.layout, row0, src0, s);
+    map_row(a.layout, row0 + 64u, src1, s);
+    st = 0;
   }
 
-  __device__ __forceinline__ void init(const GemvArgs &a, uint32_t ub, uint32_t ue, uint32_t tpg_) {
+  __device__ __forceinline__ void init(const GemvArgs &a, uint32_t ub, uint32_t ue, uint32_t tpg_, uint32_t nst_) {
     u = ub;
     u_end = ue;
     tpg = tpg_;
-    kblocks = a.K / 128u;
+    nst = nst_;
+    geo = make_geo(a, MATS);
     enter_tile(a);
   }
 
   __device__ __forceinline__ void issue_next(const GemvArgs &a, const Shared &sh) {
     if (u >= u_end) return;
     if (ring_wait(sh, &sh.empty[ring.slot], ring.phase ^ 1u, a.flags)) {
-      uint8_t *dst = sh.ring + ring.slot * C::SLOT;
-      mbar_arrive_expect_tx(&sh.full[ring.slot], kBoxBytes * C::MATS);
-      const int x = (int)(kb * 128u);
-#pragma unroll
-      for (int m = 0; m < C::MATS; ++m) {
-        const CUtensorMap *map = m == 0 ? m0 : m1;
-        if (a.layout == PW_LAYOUT_PLAIN) {
-          tma_load_2d(dst + m * kBoxBytes, map, x, (int)src_lo, &sh.full[ring.slot]);
-        } else {
-          tma_load_2d(dst + m * kBoxBytes, map, x, (int)src_lo, &sh.full[ring.slot]);
-          tma_load_2d(dst + m * kBoxBytes + kBoxBytes / 2, map, x, (int)src_hi, &sh.full[ring.slot]);
-        }
-      }
+      const uint32_t m = st % MATS, h = (st / MATS) % geo.halves, kc = st / (MATS * geo.halves);
+      mbar_arrive_expect_tx(&sh.full[ring.slot], kStageBytes);
+      tma_load_3d(sh.ring + ring.slot * kStageBytes, m == 0 ? m0 : m1, (int)(h ? src1 : src0), (int)(kc * geo.kbs),
+                  &sh.full[ring.slot]);
       ring.issued |= 1u << ring.slot;
       ring.parity = (ring.parity & ~(1u << ring.slot)) | (ring.phase << ring.slot);
     }
-    ring.advance(C::NST);
-    if (++kb == kblocks) {
+    ring.advance(nst);
+    if (++st == geo.per_tile) {
       ++u;
       enter_tile(a);
     }
   }
 
   __device__ __forceinline__ void drain(const GemvArgs &a, const Shared &sh) {
-    for (int i = 0; i < C::NST; ++i)
+    for (uint32_t i = 0; i < nst; ++i)
       if (ring.issued & (1u << i))
         if (!mbar_wait(&sh.full[i], (ring.parity >> i) & 1u)) raise_flag(a.flags, PW_FLAG_WAIT_TIMEOUT);
   }
 };
 
 template <int KIND>
-__global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a) {
-  using C = Cfg<KIND>;
+__global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, const uint32_t nst) {
+  constexpr bool FUSED = KIND == 2;
+  constexpr int MATS = FUSED ? 2 : 1;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B swizzle pattern of the TMA boxes
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Layout L = make_layout(a.K, nst);
   Shared sh;
   sh.ring = smem;
-  sh.x = smem + C::XOFF;
-  sh.xs = reinterpret_cast<float *>(smem + C::SOFF);
-  sh.full = reinterpret_cast<uint64_t *>(smem + C::BOFF);
-  sh.empty = sh.full + C::NST;
-  sh.abort = reinterpret_cast<volatile int *>(sh.empty + C::NST);
+  sh.x = smem + L.x;
+  sh.xs = reinterpret_cast<float *>(smem + L.xs);
+  sh.ws = reinterpret_cast<float *>(smem + L.ws);
+  sh.amax = reinterpret_cast<float *>(smem + L.amax);
+  sh.full = reinterpret_cast<uint64_t *>(smem + L.bars);
+  sh.empty = sh.full + nst;
+  sh.abort = reinterpret_cast<volatile int *>(sh.empty + nst);
 
   const uint32_t warp = threadIdx.x / 32u, lane = threadIdx.x % 32u;
   const uint32_t gid = lane / 4u, tig = lane % 4u;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < C::NST; ++i) {
+    for (uint32_t i = 0; i < nst; ++i) {
       mbar_init(&sh.full[i], 1);
       mbar_init(&sh.empty[i], kWarps);
     }
@@ -209,22 +235,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a) {
   const uint32_t u_begin = (uint32_t)(total * blockIdx.x / gridDim.x);
   const uint32_t u_end = (uint32_t)(total * (blockIdx.x + 1) / gridDim.x);
   const uint32_t kblocks = a.K / 128u;
+  const Geo geo = make_geo(a, MATS);
 
-  Producer<KIND> prod;
-  if (warp == 0 && lane == 0) {
-    prod.init(a, u_begin, u_end, tpg);
-    for (int i = 0; i < C::NST - 1; ++i) prod.issue_next(a, sh);
+  if (warp == kWarps) {
+    // producer warp: stream every stage of this CTA's tiles into the ring
+    if (lane == 0) {
+      Producer<KIND> prod;
+      prod.init(a, u_begin, u_end, tpg, nst);
+      const uint64_t stages = (uint64_t)(u_end - u_begin) * geo.per_tile;
+      for (uint64_t i = 0; i < stages; ++i) prod.issue_next(a, sh);
+      prod.drain(a, sh);
+    }
+    return;
   }
-  __syncwarp();
 
   Ring ring;
-  // ldmatrix lane -> (row within the warp's 16, 16-byte half of a 32-byte k-step)
-  const uint32_t arow = warp * 16u + (lane & 7u) + ((lane >> 3) & 1u) * 8u;
+  // this warp's rows within its box half and the ldmatrix lane pattern:
+  // lanes 0-7 rows 0-7 / bytes 0-15, 8-15 rows 8-15 / 0-15, 16-23 rows 0-7 /
+  // 16-31, 24-31 rows 8-15 / 16-31 of a 32-byte k-step
+  const uint32_t my_half = (warp * 16u) / geo.br;
+  const uint32_t lrow = (warp * 16u - my_half * geo.br) + (lane & 7u) + ((lane >> 3) & 1u) * 8u;
   const uint32_t ahalf = lane >> 4;
-  const uint32_t aswz = arow & 7u;
   const uint32_t ring_base = smem_addr(sh.ring);
   // B: lane -> (token row, which of {b0(j), b1(j), b0(j+1), b1(j+1)})
-  const uint32_t x_lane = smem_addr(sh.x) + (lane & 7u) * kXStride + (lane >> 3) * 16u;
+  const uint32_t x_lane = smem_addr(sh.x) + (lane & 7u) * L.xstride + (lane >> 3) * 16u;
+  float *my_ws = sh.ws + warp * 64u;
   uint32_t cur_group = 0xffffffffu;
 
   for (uint32_t u = u_begin; u < u_end; ++u) {
@@ -234,15 +269,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a) {
     if (gi != cur_group) {
       // restage this group's activation codes and scales once every warp is
       // done with the previous group's
-      if (cur_group != 0xffffffffu) named_bar_sync(1, kThreads);
+      if (cur_group != 0xffffffffu) named_bar_sync(1, kConsumerThreads);
       const uint32_t vec_per_row = a.K / 16u;
-      for (uint32_t i = threadIdx.x; i < grp.count * vec_per_row; i += kThreads) {
+      for (uint32_t i = threadIdx.x; i < grp.count * vec_per_row; i += kConsumerThreads) {
         const uint32_t t = i / vec_per_row, v = i % vec_per_row;
         const uint32_t xrow = a.tok_list ? __ldg(a.tok_list + grp.tok_begin + t) : grp.tok_begin + t;
-        *reinterpret_cast<uint4 *>(sh.x + t * kXStride + v * 16u) =
+        *reinterpret_cast<uint4 *>(sh.x + t * L.xstride + v * 16u) =
             __ldg(reinterpret_cast<const uint4 *>(a.x_codes + (size_t)xrow * a.K) + v);
       }
-      for (uint32_t i = threadIdx.x; i < 8u * kblocks; i += kThreads) {
+      for (uint32_t i = threadIdx.x; i < 8u * kblocks; i += kConsumerThreads) {
         const uint32_t t = i / kblocks, kbi = i % kblocks;
         float v = 0.0f;
         if (t < grp.count) {
@@ -252,85 +287,150 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a) {
         sh.xs[t * 32u + kbi] = v;
       }
       cur_group = gi;
-      named_bar_sync(1, kThreads);
+      named_bar_sync(1, kConsumerThreads);
     }
-    // scale row of this warp's 16 rows (one 128-row block, or one QKV segment block)
-    uint32_t wsrc, wsrow;
-    map_row(a.layout, row0 + warp * 16u, wsrc, wsrow);
-    const float *s0 = (KIND == 3 ? grp.s1 : grp.s0) + (size_t)wsrow * a.scale_cols;
-    const float *s1 = grp.s1 + (size_t)wsrow * a.scale_cols;
+    {
+      // this warp's weight-scale row (its 16 rows sit in one 128-row block,
+      // or one QKV segment block)
+      uint32_t wsrc, wsrow;
+      map_row(a.layout, row0 + warp * 16u, wsrc, wsrow);
+      const float *s0 = (KIND == 3 ? grp.s1 : grp.s0) + (size_t)wsrow * a.scale_cols;
+      if (lane < kblocks) {
+        my_ws[lane] = __ldg(s0 + lane);
+        if (FUSED) my_ws[32 + lane] = __ldg(grp.s1 + (size_t)wsrow * a.scale_cols + lane);
+      }
+      __syncwarp();
+    }
 
-    float acc[C::MATS][4];
+    float acc[MATS][4];
 #pragma unroll
-    for (int m = 0; m < C::MATS; ++m)
+    for (int m = 0; m < MATS; ++m)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[m][i] = 0.0f;
 
 #pragma unroll 1
-    for (uint32_t kb = 0; kb < kblocks; ++kb) {
-      if (warp == 0 && lane == 0) prod.issue_next(a, sh);
-      __syncwarp();
+    for (uint32_t st = 0; st < geo.per_tile; ++st) {
+      const uint32_t m = st % MATS, h = (st / MATS) % geo.halves, kc = st / (MATS * geo.halves);
       const bool ok = ring_wait(sh, &sh.full[ring.slot], ring.phase, a.flags);
-      if (ok) {
-        uint32_t b[4][2];
-        ldmatrix_x4(x_lane + kb * 128u, b[0][0], b[0][1], b[1][0], b[1][1]);
-        ldmatrix_x4(x_lane + kb * 128u + 64u, b[2][0], b[2][1], b[3][0], b[3][1]);
-        const float xs0 = sh.xs[(tig * 2u) * 32u + kb], xs1 = sh.xs[(tig * 2u + 1u) * 32u + kb];
-        const uint32_t tile = ring_base + ring.slot * C::SLOT + arow * 128u;
-#pragma unroll
-        for (int m = 0; m < C::MATS; ++m) {
+      if (ok && h == my_half) {
+        const uint32_t box = ring_base + ring.slot * kStageBytes;
+        for (uint32_t j = 0; j < geo.kbs; ++j) {
+          const uint32_t kb = kc * geo.kbs + j;
+          if (kb >= kblocks) break;
+          uint32_t b[4][2];
+          ldmatrix_x4(x_lane + kb * 128u, b[0][0], b[0][1], b[1][0], b[1][1]);
+          ldmatrix_x4(x_lane + kb * 128u + 64u, b[2][0], b[2][1], b[3][0], b[3][1]);
+          const uint32_t line = j * geo.br + lrow;
+          const uint32_t lbase = box + line * 128u;
+          const uint32_t swz = line & 7u;
           float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t chunk = (2u * j + ahalf) ^ aswz;
+          for (int s = 0; s < 4; ++s) {
             uint32_t a0, a1, a2, a3;
-            ldmatrix_x4(tile + m * kBoxBytes + chunk * 16u, a0, a1, a2, a3);
-            mma_e4m3(d, a0, a1, a2, a3, b[j][0], b[j][1]);
+            ldmatrix_x4(lbase + (((2u * s + ahalf) ^ swz) << 4), a0, a1, a2, a3);
+            mma_e4m3(d, a0, a1, a2, a3, b[s][0], b[s][1]);
           }
-          const float ws = __ldg((m == 0 ? s0 : s1) + kb);
-          const float c0 = ws * xs0, c1 = ws * xs1;
-          acc[m][0] = fmaf(d[0], c0, acc[m][0]);
-          acc[m][1] = fmaf(d[1], c1, acc[m][1]);
-          acc[m][2] = fmaf(d[2], c0, acc[m][2]);
-          acc[m][3] = fmaf(d[3], c1, acc[m][3]);
+          const float ws = my_ws[m * 32u + kb];
+          const float c0 = ws * sh.xs[(tig * 2u) * 32u + kb];
+          const float c1 = ws * sh.xs[(tig * 2u + 1u) * 32u + kb];
+          if (m == 0) {
+            acc[0][0] = fmaf(d[0], c0, acc[0][0]);
+            acc[0][1] = fmaf(d[1], c1, acc[0][1]);
+            acc[0][2] = fmaf(d[2], c0, acc[0][2]);
+            acc[0][3] = fmaf(d[3], c1, acc[0][3]);
+          } else {
+            acc[MATS - 1][0] = fmaf(d[0], c0, acc[MATS - 1][0]);
+            acc[MATS - 1][1] = fmaf(d[1], c1, acc[MATS - 1][1]);
+            acc[MATS - 1][2] = fmaf(d[2], c0, acc[MATS - 1][2]);
+            acc[MATS - 1][3] = fmaf(d[3], c1, acc[MATS - 1][3]);
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.empty[ring.slot]);
-      ring.advance(C::NST);
+      ring.advance(nst);
     }
 
     // epilogue: thread holds rows (gid, gid+8) x tokens (2 tig, 2 tig + 1)
+    float outv[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t r = row0 + warp * 16u + gid + (i >= 2 ? 8u : 0u);
       const uint32_t t = tig * 2u + (i & 1u);
+      float out = 0.0f;
       if (t < grp.count) {
-        float out;
-        if (C::FUSED) {
-          out = staged_swiglu(acc[0][i], acc[C::MATS - 1][i]);
+        if (FUSED) {
+          out = staged_swiglu(acc[0][i], acc[MATS - 1][i]);
           if (!finite(out)) raise_flag(a.flags, PW_FLAG_NONFINITE_FUSED);
         } else {
           out = a.round_bf16 ? round_bf16(acc[0][i]) : acc[0][i];
           if (!finite(out)) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
         }
-        a.out[(size_t)(grp.tok_begin + t) * a.out_stride + r] = out;
+        if (a.out) a.out[(size_t)(grp.tok_begin + t) * a.out_stride + row0 + warp * 16u + gid + (i >= 2 ? 8u : 0u)] = out;
       }
+      outv[i] = out;
+    }
+    if (FUSED && a.q_codes) {
+      // The tile's 128 rows are exactly one 128-column group of the down
+      // projection's input, so its dynamic FP8 quantization
+      // (src/text_endpoint.rs:3008) is finished here: per-token absmax over the
+      // 128 rows, scale = max(absmax, 1e-10) / 448, RNE e4m3 codes -- the
+      // same IEEE steps as the stand-alone quantizer, so the bytes match it.
+      float m0 = fmaxf(fabsf(outv[0]), fabsf(outv[2]));
+      float m1 = fmaxf(fabsf(outv[1]), fabsf(outv[3]));
+#pragma unroll
+      for (int o = 4; o <= 16; o <<= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+      }
+      if (gid == 0) {
+        sh.amax[warp * 8u + tig * 2u] = m0;
+        sh.amax[warp * 8u + tig * 2u + 1u] = m1;
+      }
+      named_bar_sync(1, kConsumerThreads);
+      float M0 = 0.0f, M1 = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        M0 = fmaxf(M0, sh.amax[w * 8 + tig * 2u]);
+        M1 = fmaxf(M1, sh.amax[w * 8 + tig * 2u + 1u]);
+      }
+      const float sc0 = __fdiv_rn(fmaxf(M0, 1.0e-10f), 448.0f);
+      const float sc1 = __fdiv_rn(fmaxf(M1, 1.0e-10f), 448.0f);
+      const uint32_t I = a.rows;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t t = tig * 2u + (i & 1u);
+        if (t < grp.count) {
+          const float sc = (i & 1) ? sc1 : sc0;
+          const float q = fminf(fmaxf(__fdiv_rn(outv[i], sc), -448.0f), 448.0f);
+          const uint32_t r = row0 + warp * 16u + gid + (i >= 2 ? 8u : 0u);
+          a.q_codes[(size_t)(grp.tok_begin + t) * I + r] = (uint8_t)(encode2(q, 0.0f) & 0xffu);
+        }
+      }
+      if (warp == 0 && gid == 0) {
+        const uint32_t t0 = tig * 2u, t1 = tig * 2u + 1u;
+        if (t0 < grp.count) a.q_scales[(size_t)(grp.tok_begin + t0) * (I / 128u) + row0 / 128u] = sc0;
+        if (t1 < grp.count) a.q_scales[(size_t)(grp.tok_begin + t1) * (I / 128u) + row0 / 128u] = sc1;
+      }
+      named_bar_sync(1, kConsumerThreads);  // amax is rewritten by the next tile
     }
   }
-  if (warp == 0 && lane == 0) prod.drain(a, sh);
 }
+
+constexpr uint32_t kSmemLimit = 227u * 1024u;
 
 template <int KIND>
 static cudaError_t launch_one(const GemvArgs &a, int grid, cudaStream_t stream) {
-  using C = Cfg<KIND>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemv_mma<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  // deepest ring that fits next to this K's activation tile
+  uint32_t nst = kMaxStages;
+  while (nst > 2 && make_layout(a.K, nst).total + 1024u > kSmemLimit) --nst;
+  const uint32_t smem = make_layout(a.K, nst).total + 1024u;
+  static uint32_t configured = 0;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv_mma<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured = kSmemLimit;
   }
-  k_gemv_mma<KIND><<<grid, kThreads, C::SMEM, stream>>>(a);
+  k_gemv_mma<KIND><<<grid, kThreads, smem, stream>>>(a, nst);
   return cudaGetLastError();
 }
 

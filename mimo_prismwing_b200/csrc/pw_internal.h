@@ -37,8 +37,10 @@ struct GemvArgs {
   const uint8_t *x_codes;        // e4m3 activations [*, K] (quantized kernels)
   const float *x_scales;         // [*, K/128]
   const float *x_f32;            // f32 activations [*, K] (readable kernel)
-  float *out;                    // out[(tok_begin + t) * out_stride + row]
+  float *out;                    // out[(tok_begin + t) * out_stride + row] (may be null for kind 2)
   uint32_t out_stride;
+  uint8_t *q_codes;              // kind 2: dynamic-FP8 codes of the SwiGLU output [*, rows]
+  float *q_scales;               //   and its per-128-row scales [*, rows / 128]
   uint32_t round_bf16;           // bf16-round the f32 result on store
   uint32_t *flags;
 };

@@ -66,40 +66,49 @@ cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_
 
 // ------------------------------------------------------------ router logits
 // logit[t,e] = sum_c x[t,c] * w[e,c] with f64 accumulation in a fixed order
-// (the oracle's pwo_router_logits restates it): lane l owns 8-column chunks
-// 8l + 256j (j ascending), sums them in f64, then an xor butterfly 16..1.
+// (the oracle's pwo_router_logits restates it):
+//   the K axis is cut into 512-column slices; warp w (of 8) owns slices
+//   s = w, w+8, ...; lane l sums, for each owned slice in ascending order,
+//   the 8-column chunks at 512s + 8l and 512s + 8l + 256, column by column;
+//   an xor butterfly (16, 8, 4, 2, 1) sums the lanes; the CTA then adds the
+//   8 warp partials in warp order starting from warp 0's.
 // x*w of a bf16 weight and an f32 activation is exact in f64, so FMA and
-// mul+add give the same bits.  One warp per expert, 8 tokens per pass.
+// mul+add give the same bits.  One CTA per (expert, 8 tokens).
 constexpr int kRouterTok = 8;
 
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, uint32_t tokens,
                                                        const uint16_t *__restrict__ w, uint32_t experts,
                                                        uint32_t hidden, float *__restrict__ logits) {
-  const uint32_t lane = threadIdx.x % 32u;
-  const uint32_t e = blockIdx.x * (blockDim.x / 32u) + threadIdx.x / 32u;
+  __shared__ double part[8][kRouterTok];
+  const uint32_t lane = threadIdx.x % 32u, warp = threadIdx.x / 32u;
+  const uint32_t e = blockIdx.x;
   const uint32_t t0 = blockIdx.y * kRouterTok;
-  if (e >= experts) return;
   double acc[kRouterTok];
 #pragma unroll
   for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0;
   const uint16_t *wrow = w + (size_t)e * hidden;
-  for (uint32_t c0 = 8u * lane; c0 < hidden; c0 += 256u) {
-    const uint4 wq = __ldg(reinterpret_cast<const uint4 *>(wrow + c0));
-    double wd[8];
-    const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
+  const uint32_t slices = hidden / 512u;
+  for (uint32_t sl = warp; sl < slices; sl += 8u) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      wd[2 * i] = (double)__uint_as_float(wv[i] << 16);
-      wd[2 * i + 1] = (double)__uint_as_float(wv[i] & 0xffff0000u);
-    }
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t c0 = 512u * sl + 8u * lane + 256u * j;
+      const uint4 wq = __ldg(reinterpret_cast<const uint4 *>(wrow + c0));
+      double wd[8];
+      const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) {
-      if (t0 + t < tokens) {
-        const float4 *xp = reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * hidden + c0);
-        const float4 a = __ldg(xp), b = __ldg(xp + 1);
-        const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      for (int i = 0; i < 4; ++i) {
+        wd[2 * i] = (double)__uint_as_float(wv[i] << 16);
+        wd[2 * i + 1] = (double)__uint_as_float(wv[i] & 0xffff0000u);
+      }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[t] = __fma_rn((double)xv[i], wd[i], acc[t]);
+      for (int t = 0; t < kRouterTok; ++t) {
+        if (t0 + t < tokens) {
+          const float4 *xp = reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * hidden + c0);
+          const float4 a = __ldg(xp), b = __ldg(xp + 1);
+          const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[t] = __fma_rn((double)xv[i], wd[i], acc[t]);
+        }
       }
     }
   }
@@ -108,116 +117,133 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     double v = acc[t];
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0 && t0 + t < tokens) logits[(size_t)(t0 + t) * experts + e] = __double2float_rn(v);
+    if (lane == 0) part[warp][t] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < kRouterTok && t0 + threadIdx.x < tokens) {
+    double s = part[0][threadIdx.x];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) s = __dadd_rn(s, part[k][threadIdx.x]);
+    logits[(size_t)(t0 + threadIdx.x) * experts + e] = __double2float_rn(s);
   }
 }
 
 cudaError_t launch_router_logits(const float *x, uint32_t tokens, const uint16_t *w, uint32_t experts,
                                  uint32_t hidden, float *logits, cudaStream_t stream) {
-  if (hidden % 256u || tokens == 0) return cudaErrorInvalidValue;
-  dim3 grid((experts + 7u) / 8u, (tokens + kRouterTok - 1) / kRouterTok);
+  if (hidden % 512u || tokens == 0) return cudaErrorInvalidValue;
+  dim3 grid(experts, (tokens + kRouterTok - 1) / kRouterTok);
   k_router_logits<<<grid, 256, 0, stream>>>(x, tokens, w, experts, hidden, logits);
   return cudaGetLastError();
 }
 
 // --------------------------------------------------------------- router top-k
-// One warp per token (src/text_endpoint.rs:4394 pytorch_noaux_routes):
-// score = SLEEF sigmoid(logit); corrected = score + bias; 8 rounds of warp
-// argmax (ties -> lower index) give the canonical order; a 9th round yields
-// the boundary margin.  weight_k = score_k / (pairwise sum of 8 + 1e-20)
-// (src/text_endpoint.rs:4382).  Experts <= 32 * kTopkPer.
-constexpr int kTopkPer = 32;  // experts per lane (supports up to 1024 experts)
+// One CTA per token (src/text_endpoint.rs:4394 pytorch_noaux_routes):
+// score = SLEEF sigmoid(logit); corrected = score + bias; 9 rounds of
+// block-wide argmax (ties -> lower index) give the 8 picks in canonical order
+// and the first rejected value (boundary margin / tie detection).
+// weight_k = score_k / (pairwise sum of the 8 + 1e-20) (src/text_endpoint.rs:4382).
+constexpr int kTopkPer = 4;  // experts per thread: up to 1024 experts
 
 __device__ __forceinline__ bool better(float va, uint32_t ia, float vb, uint32_t ib) {
   return va > vb || (va == vb && ia < ib);
 }
 
-__global__ void k_router_topk(const float *__restrict__ logits, const float *__restrict__ bias, uint32_t tokens,
-                              uint32_t experts, uint32_t *__restrict__ selected, float *__restrict__ weights,
-                              uint32_t *tie_rows, uint32_t *flags) {
-  const uint32_t lane = threadIdx.x % 32u;
-  const uint32_t t = blockIdx.x * (blockDim.x / 32u) + threadIdx.x / 32u;
-  if (t >= tokens) return;
-  const uint32_t per = (experts + 31u) / 32u;
+__device__ __forceinline__ void argmax_shfl(float &bv, uint32_t &bi, float &bs, int width) {
+  for (int o = width / 2; o >= 1; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o, width);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o, width);
+    const float os = __shfl_xor_sync(0xffffffffu, bs, o, width);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+      bs = os;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ logits, const float *__restrict__ bias,
+                                                     uint32_t tokens, uint32_t experts, uint32_t *__restrict__ selected,
+                                                     float *__restrict__ weights, uint32_t *tie_rows, uint32_t *flags) {
+  __shared__ float cv[8], cs[8];
+  __shared__ uint32_t ci[8];
+  __shared__ float pick_s[9], pick_v[9];
+  __shared__ uint32_t pick_i[9];
+  const uint32_t t = blockIdx.x;
+  const uint32_t tid = threadIdx.x, lane = tid % 32u, warp = tid / 32u;
   float score[kTopkPer], corr[kTopkPer];
-  uint32_t taken = 0;  // bit j: lane's j-th expert chosen
+  uint32_t taken = 0;
 #pragma unroll
-  for (int j = 0; j < kTopkPer; ++j) {
-    const uint32_t e = lane + 32u * j;
-    score[j] = 0.0f;
-    corr[j] = -__int_as_float(0x7f800000);
-    if (j < (int)per && e < experts) {
+  for (int k = 0; k < kTopkPer; ++k) {
+    const uint32_t e = tid + 256u * k;
+    score[k] = 0.0f;
+    corr[k] = -__int_as_float(0x7f800000);
+    if (e < experts) {
       const float lg = logits[(size_t)t * experts + e];
       const float b = __ldg(bias + e);
       if (!finite(lg) || !finite(b)) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
-      score[j] = sigmoid_sleef(lg);
-      corr[j] = __fadd_rn(score[j], b);
+      score[k] = sigmoid_sleef(lg);
+      corr[k] = __fadd_rn(score[k], b);
     }
   }
-  uint32_t chosen[8];
-  float chosen_score[8];
-  float kth = 0.0f, next = 0.0f;
-#pragma unroll 1
-  for (int k = 0; k < 9; ++k) {
-    float bv = -__int_as_float(0x7f800000);
+  for (int round = 0; round < 9; ++round) {
+    float bv = -__int_as_float(0x7f800000), bs = 0.0f;
     uint32_t bi = 0xffffffffu;
-    float bs = 0.0f;
 #pragma unroll
-    for (int j = 0; j < kTopkPer; ++j) {
-      const uint32_t e = lane + 32u * j;
-      if (j < (int)per && e < experts && !(taken & (1u << j)) && better(corr[j], e, bv, bi)) {
-        bv = corr[j];
+    for (int k = 0; k < kTopkPer; ++k) {
+      const uint32_t e = tid + 256u * k;
+      if (e < experts && !(taken & (1u << k)) && better(corr[k], e, bv, bi)) {
+        bv = corr[k];
         bi = e;
-        bs = score[j];
+        bs = score[k];
       }
     }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-      if (better(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-        bs = os;
+    argmax_shfl(bv, bi, bs, 32);
+    if (lane == 0) {
+      cv[warp] = bv;
+      ci[warp] = bi;
+      cs[warp] = bs;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      bv = lane < 8u ? cv[lane] : -__int_as_float(0x7f800000);
+      bi = lane < 8u ? ci[lane] : 0xffffffffu;
+      bs = lane < 8u ? cs[lane] : 0.0f;
+      argmax_shfl(bv, bi, bs, 32);
+      if (lane == 0) {
+        pick_v[round] = bv;
+        pick_i[round] = bi;
+        pick_s[round] = bs;
       }
     }
-    if (k < 8) {
-      chosen[k] = bi;
-      chosen_score[k] = bs;
-      if (k == 7) kth = bv;
-      if (bi % 32u == lane && bi != 0xffffffffu) taken |= 1u << (bi / 32u);
-    } else {
-      next = bv;
-    }
+    __syncthreads();
+    const uint32_t w = pick_i[round];
+    if (round < 8 && w != 0xffffffffu && w % 256u == tid) taken |= 1u << (w / 256u);
   }
-  if (lane == 0) {
-    const float l0 = __fadd_rn(chosen_score[0], chosen_score[4]);
-    const float l1 = __fadd_rn(chosen_score[1], chosen_score[5]);
-    const float l2 = __fadd_rn(chosen_score[2], chosen_score[6]);
-    const float l3 = __fadd_rn(chosen_score[3], chosen_score[7]);
+  if (tid == 0) {
+    const float l0 = __fadd_rn(pick_s[0], pick_s[4]);
+    const float l1 = __fadd_rn(pick_s[1], pick_s[5]);
+    const float l2 = __fadd_rn(pick_s[2], pick_s[6]);
+    const float l3 = __fadd_rn(pick_s[3], pick_s[7]);
     const float den = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, l0), l1), l2), l3), 1.0e-20f);
     float sum = 0.0f;
     bool ok = true;
-#pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const float wk = __fdiv_rn(chosen_score[k], den);
-      ok = ok && finite(wk) && wk >= 0.0f && chosen[k] < experts;
+      const float wk = __fdiv_rn(pick_s[k], den);
+      ok = ok && finite(wk) && wk >= 0.0f && pick_i[k] < experts;
       sum = __fadd_rn(sum, wk);
-      selected[(size_t)t * 8 + k] = chosen[k];
+      selected[(size_t)t * 8 + k] = pick_i[k];
       weights[(size_t)t * 8 + k] = wk;
     }
     if (!ok || fabsf(__fsub_rn(sum, 1.0f)) > 1.0e-6f) raise_flag(flags, PW_FLAG_ROUTE_WEIGHTS);
-    if (kth == next && tie_rows) atomicAdd(tie_rows, 1u);
+    if (pick_v[7] == pick_v[8] && tie_rows) atomicAdd(tie_rows, 1u);
   }
 }
 
 cudaError_t launch_router_topk(const float *logits, const float *bias, uint32_t tokens, uint32_t experts,
                                uint32_t *selected, float *weights, uint32_t *tie_rows, uint32_t *flags,
                                cudaStream_t stream) {
-  if (experts <= 8 || experts > 32u * kTopkPer || tokens == 0) return cudaErrorInvalidValue;
-  k_router_topk<<<(tokens + 7u) / 8u, 256, 0, stream>>>(logits, bias, tokens, experts, selected, weights,
-                                                         tie_rows, flags);
+  if (experts <= 8 || experts > 256u * kTopkPer || tokens == 0) return cudaErrorInvalidValue;
+  k_router_topk<<<tokens, 256, 0, stream>>>(logits, bias, tokens, experts, selected, weights, tie_rows, flags);
   return cudaGetLastError();
 }
 

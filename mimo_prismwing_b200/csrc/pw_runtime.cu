@@ -44,14 +44,17 @@ static EncodeTiledFn encode_fn() {
 
 uint32_t map_box_rows(uint32_t layout) { return layout == PW_LAYOUT_PLAIN ? 128u : 64u; }
 
+// The weight is viewed as {128 B, rows, k-blocks} with strides {cols, 128}:
+// a box of {128, box_rows, 256 / box_rows} is 32 KB and lands row-major in
+// shared memory (one 128-byte line per row and k-block), 128B-swizzled.
 bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols};
-  cuuint32_t box[2] = {128u, box_rows};
-  cuuint32_t estr[2] = {1u, 1u};
-  return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+  if (!fn || cols % 128u) return false;
+  cuuint64_t dims[3] = {128u, rows, cols / 128u};
+  cuuint64_t strides[2] = {cols, 128u};
+  cuuint32_t box[3] = {128u, box_rows, 256u / box_rows};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -540,16 +543,20 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
                                 float *gate_tmp, float *up_tmp, uint8_t *hc, float *hs, float *down,
                                 uint32_t down_round, uint64_t units_hint) {
   const int grid_gu = grid_for(rt, units_hint * (I / 128u));
+  const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   {
-  ProfScope ps(rt, P_GATEUP, (rt->flags & PW_RUNTIME_FUSED_GATE_UP) ? 1 : 3);
-  if (rt->flags & PW_RUNTIME_FUSED_GATE_UP) {
+  ProfScope ps(rt, P_GATEUP, fused ? 1 : 3);
+  if (fused) {
+    // gate/up + SwiGLU + the hidden's dynamic FP8 quantization in one kernel
     GemvArgs a = gemv_args(rt, gu, n_groups, I, H, PW_LAYOUT_PLAIN);
     a.n_groups_dev = n_groups_dev;
     a.tok_list = tok_list;
     a.x_codes = xc;
     a.x_scales = xs;
-    a.out = hidden;
+    a.out = hidden;  // may be null
     a.out_stride = I;
+    a.q_codes = hc;
+    a.q_scales = hs;
     CK(launch_gemv(2, a, grid_gu, rt->stream));
   } else {
     // gate and up as two block-scaled projections, then the staged SwiGLU
@@ -569,7 +576,7 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
     CK(launch_swiglu(gate_tmp, up_tmp, hidden, slots * I, rt->d_flags, rt->stream));
   }
   }
-  {
+  if (!fused) {
     ProfScope ps(rt, P_QUANT, 1);
     CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream));
   }
@@ -615,7 +622,7 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
     float *dy = call.host() ? ar.take<float>((size_t)width * H) : y;
     uint8_t *xc = ar.take<uint8_t>((size_t)width * H);
     float *xs = ar.take<float>((size_t)width * H / 128u);
-    float *hid = ar.take<float>((size_t)width * I);
+    float *hid = fused ? nullptr : ar.take<float>((size_t)width * I);
     float *gt = fused ? nullptr : ar.take<float>((size_t)width * I);
     float *ut = fused ? nullptr : ar.take<float>((size_t)width * I);
     uint8_t *hc = ar.take<uint8_t>((size_t)width * I);
@@ -648,8 +655,8 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
 static int check_router(pw_runtime *rt, const pw_router *r) {
   if (!r || !r->weight_bf16 || !r->bias) return fail(rt, PW_ERR_ARGUMENT, "router descriptor is null");
   if (r->top_k != 8) return fail(rt, PW_ERR_UNSUPPORTED, "top_k must be 8");
-  if (r->experts <= 8 || r->experts > 256 || r->hidden == 0 || r->hidden % 256u)
-    return fail(rt, PW_ERR_SHAPE, "router shape mismatch (experts 9..256, hidden a multiple of 256)");
+  if (r->experts <= 8 || r->experts > 256 || r->hidden == 0 || r->hidden % 512u)
+    return fail(rt, PW_ERR_SHAPE, "router shape mismatch (experts 9..256, hidden a multiple of 512)");
   return PW_OK;
 }
 
@@ -788,7 +795,7 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
         dn[k].tm1 = nullptr;
       }
     }
-    float *hid = ar.take<float>((size_t)P * I);
+    float *hid = fused ? nullptr : ar.take<float>((size_t)P * I);
     float *gt = fused ? nullptr : ar.take<float>((size_t)P * I);
     float *ut = fused ? nullptr : ar.take<float>((size_t)P * I);
     uint8_t *hc = ar.take<uint8_t>((size_t)P * I);
@@ -955,7 +962,7 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     so.dn_groups = ar.take<GemvGroup>(max_groups);
     so.n_groups = ar.take<uint32_t>(1);
     so.counters = ar.take<uint32_t>(4);
-    float *hid = ar.take<float>((size_t)P * I);
+    float *hid = fused ? nullptr : ar.take<float>((size_t)P * I);
     float *gt = fused ? nullptr : ar.take<float>((size_t)P * I);
     float *ut = fused ? nullptr : ar.take<float>((size_t)P * I);
     uint8_t *hc = ar.take<uint8_t>((size_t)P * I);

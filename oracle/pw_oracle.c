@@ -441,36 +441,45 @@ float pwo_staged_swiglu(float gate, float up, int exp_kind) {
 /* computes f32 logits with an SGEMM (src/text_endpoint.rs:4350 via    */
 /* f32_linear :3458) whose order is unspecified; this build pins the   */
 /* order so that CPU and GPU agree bit for bit:                         */
-/*   lane l in 0..31 owns 8-column chunks c0 = 8*l + 256*j (j ascending)*/
-/*   and sums x*w over each chunk's 8 columns in f64, in order;         */
-/*   the 32 lane sums combine by the xor butterfly 16,8,4,2,1           */
-/*   (s_l <- s_l + s_{l^o}, lower lane's value on the left).            */
-/* The weight is bf16 bits; the result is rounded to f32 once.          */
+/*   the K axis is cut into 512-column slices; "warp" w in 0..7 owns    */
+/*   slices s = w, w+8, ...; "lane" l in 0..31 sums, per owned slice in */
+/*   ascending order, the 8-column chunks at 512s+8l and 512s+8l+256,   */
+/*   column by column, in f64; the 32 lane sums combine by the xor      */
+/*   butterfly 16,8,4,2,1; the 8 warp sums are added in warp order      */
+/*   starting from warp 0's.  The weight is bf16 bits; the result is    */
+/*   rounded to f32 once.                                               */
 /* ------------------------------------------------------------------ */
 static inline float bf16_bits_to_f32(uint16_t b) { return u2f((uint32_t)b << 16); }
 
 int pwo_router_logits(const float *x, size_t tokens, const uint16_t *weight_bf16, size_t experts,
                       size_t hidden, float *logits) {
-  if (hidden % 256 != 0) return -1;
+  if (hidden % 512 != 0) return -1;
+  const size_t slices = hidden / 512;
   for (size_t t = 0; t < tokens; ++t) {
     for (size_t e = 0; e < experts; ++e) {
-      double lane[32];
-      for (int l = 0; l < 32; ++l) {
-        double s = 0.0;
-        for (size_t c0 = 8 * (size_t)l; c0 < hidden; c0 += 256)
-          for (size_t i = 0; i < 8; ++i)
-            s += (double)x[t * hidden + c0 + i] * (double)bf16_bits_to_f32(weight_bf16[e * hidden + c0 + i]);
-        lane[l] = s;
-      }
-      for (int o = 16; o >= 1; o >>= 1) {
-        double next[32];
+      double part[8];
+      for (int w = 0; w < 8; ++w) {
+        double lane[32];
         for (int l = 0; l < 32; ++l) {
-          const int p = l ^ o;
-          next[l] = l < p ? lane[l] + lane[p] : lane[p] + lane[l];
+          double s = 0.0;
+          for (size_t sl = (size_t)w; sl < slices; sl += 8)
+            for (size_t j = 0; j < 2; ++j) {
+              const size_t c0 = 512 * sl + 8 * (size_t)l + 256 * j;
+              for (size_t i = 0; i < 8; ++i)
+                s += (double)x[t * hidden + c0 + i] * (double)bf16_bits_to_f32(weight_bf16[e * hidden + c0 + i]);
+            }
+          lane[l] = s;
         }
-        memcpy(lane, next, sizeof lane);
+        for (int o = 16; o >= 1; o >>= 1) {
+          double next[32];
+          for (int l = 0; l < 32; ++l) next[l] = lane[l] + lane[l ^ o];
+          memcpy(lane, next, sizeof lane);
+        }
+        part[w] = lane[0];
       }
-      logits[t * experts + e] = (float)lane[0];
+      double s = part[0];
+      for (int w = 1; w < 8; ++w) s += part[w];
+      logits[t * experts + e] = (float)s;
     }
   }
   return 0;
