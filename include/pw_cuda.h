@@ -236,6 +236,35 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
                  uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem,
                  pw_stats *stats);
 
+/* ------------------------------------------------- allocation-free variant */
+
+/* No counterpart in the reference: an addition of this library.
+ *
+ * pw_expert_forward_static is pw_expert_forward for callers that must not
+ * allocate device memory when they call in: code running inside a memory
+ * budget that was reserved up front, plug-in hosts that own the allocator,
+ * and serving loops that must stay free of cudaMalloc/cudaFree because those
+ * calls synchronise the device.  It allocates nothing (no cudaMalloc, no
+ * cudaFree, no allocating library call) and needs no pw_runtime: its scratch
+ * (activation and hidden FP8 codes and scales, TMA descriptors, group records,
+ * the error-flag word; about 70 KB) is one fixed __device__ array in the
+ * library, which every GPU that loads the library holds until the process
+ * exits.
+ *
+ * Limits: width 1..=8 tokens; hidden and intermediate sizes multiples of 128
+ * and at most 4096; larger requests return PW_ERR_UNSUPPORTED.  x and y are
+ * DEVICE pointers ([width, H] f32); weights as in pw_expert_forward.  The call
+ * runs on `cuda_stream` (a cudaStream_t, NULL = legacy default stream) and
+ * waits for it before returning the status.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture.  All calls share the one array and it keeps the last
+ * call's contents, so calls that overlap on the GPU (different streams or
+ * threads at once) race with each other: serialise them. */
+int pw_expert_forward_static(const pw_expert_weights *w, const float *x, uint32_t width, float *y,
+                             void *cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif
