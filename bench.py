@@ -39,6 +39,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 HIDDEN, INTER, EXPERTS, WIDTH = 4096, 2048, 256, 8
+# DRAM traffic / algorithmic bytes of the fused gate/up GEMV, from one ncu
+# capture of a 32-expert layer (profiles/k_gemv_mma_c2_small.md): 507.55 MB
+# read+written for 503.84 MB of algorithmic bytes.  Traffic grows in
+# proportion to the experts streamed, so the full-size launch's traffic is
+# this ratio times its algorithmic bytes.
+GATE_UP_TRAFFIC_RATIO = 507.55 / 503.84
 METRIC = "routed FP8 MoE layer us @width 8"
 CONFIG = {
     "workload": "C2: full routed MoE layer, decode/verifier width 8 (BASELINE.json configs[2])",
@@ -319,7 +325,8 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": launches_per_layer * args.steps,
             "roofline": {"bound": "hbm", "kernel": "k_gemv fused gate/up + SwiGLU",
                          "achieved": round(gu_gbs, 1), "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(gu_gbs / hbm, 4), "traffic": None,
+                         "frac": round(gu_gbs / hbm, 4),
+                         "traffic": int(gu_bytes / args.steps * GATE_UP_TRAFFIC_RATIO),
                          "bytes_per_launch": int(gu_bytes / args.steps), "us_per_launch": round(gu_ms * 1e3, 2)},
             "layer_roofline": {"achieved": round(layer_gbs, 1), "unit": "GB/s", "frac": round(layer_gbs / hbm, 4),
                                "bytes_per_layer": int(layer_bytes)},
