@@ -101,6 +101,13 @@ __device__ __forceinline__ float staged_swiglu(float gate, float up) {
   return round_bf16(__fmul_rn(silu, u));
 }
 
+// Programmatic dependent launch: a kernel launched behind another may start
+// early; it must wait for its predecessor's completion (and memory) before
+// touching anything the predecessor, or any earlier kernel, writes.  Both are
+// no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ bool finite(float v) { return (__float_as_uint(v) & 0x7f800000u) != 0x7f800000u; }
 
 __device__ __forceinline__ void raise_flag(uint32_t *flags, uint32_t bit) {

@@ -228,6 +228,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, cons
     mbar_fence_init();
   }
   __syncthreads();
+  // Under programmatic dependent launch the previous kernel may still run.
+  // With early_weights the groups and weights are already final (they come
+  // from two launches back), so only the activations must wait: the producer
+  // streams weights at once and the consumers wait before staging x.
+  if (!a.early_weights) pdl_wait();
+  pdl_launch_dependents();
 
   const uint32_t n_groups = a.n_groups_dev ? min(*a.n_groups_dev, a.n_groups) : a.n_groups;
   const uint32_t tpg = a.rows / kTileRows;
@@ -249,6 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, cons
     return;
   }
 
+  if (a.early_weights) pdl_wait();
   Ring ring;
   // this warp's rows within its box half and the ldmatrix lane pattern:
   // lanes 0-7 rows 0-7 / bytes 0-15, 8-15 rows 8-15 / 0-15, 16-23 rows 0-7 /
@@ -430,8 +437,7 @@ static cudaError_t launch_one(const GemvArgs &a, int grid, cudaStream_t stream) 
     if (e != cudaSuccess) return e;
     configured = kSmemLimit;
   }
-  k_gemv_mma<KIND><<<grid, kThreads, smem, stream>>>(a, nst);
-  return cudaGetLastError();
+  return launch_kernel(k_gemv_mma<KIND>, dim3(grid), dim3(kThreads), smem, stream, a, nst);
 }
 
 }  // namespace mma

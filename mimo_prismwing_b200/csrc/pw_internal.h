@@ -9,6 +9,33 @@
 
 namespace pw {
 
+// Launch a kernel, marked for programmatic dependent launch when the calling
+// thread has enabled it (routed-layer chains); otherwise a plain launch.
+bool pdl_enabled();
+void set_pdl(bool on);
+struct PdlScope {
+  bool prev;
+  explicit PdlScope(bool on) : prev(pdl_enabled()) { set_pdl(on); }
+  ~PdlScope() { set_pdl(prev); }
+};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 // One group of tokens sharing one weight matrix (a projection call, or one
 // expert's placements in a routed layer).  count <= 8 per group: wider token
 // sets are split into several groups over the same weights.
@@ -43,6 +70,8 @@ struct GemvArgs {
   float *q_scales;               //   and its per-128-row scales [*, rows / 128]
   uint32_t round_bf16;           // bf16-round the f32 result on store
   uint32_t *flags;
+  uint32_t early_weights;        // PDL: weights and groups are ready before the predecessor
+                                 //   ends, so the producer may stream them before waiting
 };
 
 // Kernel launchers (pw_kernels.cu).  All enqueue on `stream` and return the

@@ -9,6 +9,10 @@
 
 namespace pw {
 
+static thread_local bool t_pdl = false;
+bool pdl_enabled() { return t_pdl; }
+void set_pdl(bool on) { t_pdl = on; }
+
 // ------------------------------------------------------------ quantization
 // One warp per 128-value group (src/text_endpoint.rs:3008,
 // kernels/block_fp8_gemv.metal:84): absmax, scale = max(absmax,1e-10)/448,
@@ -16,6 +20,8 @@ namespace pw {
 // bit-exact with the reference; lane l holds values 4l..4l+3.
 __global__ void k_quantize(const float *__restrict__ x, uint64_t groups, uint8_t *__restrict__ codes,
                            float *__restrict__ scales, uint32_t *flags) {
+  pdl_wait();
+  pdl_launch_dependents();
   const uint64_t warp_global = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32u;
   const uint32_t lane = threadIdx.x % 32u;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) / 32u;
@@ -43,8 +49,7 @@ cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_
   const int threads = 256;
   uint64_t blocks = (groups * 32u + threads - 1) / threads;
   if (blocks > 148u * 16u) blocks = 148u * 16u;
-  k_quantize<<<(unsigned)blocks, threads, 0, stream>>>(x, groups, codes, scales, flags);
-  return cudaGetLastError();
+  return launch_kernel(k_quantize, dim3((unsigned)blocks), dim3(threads), 0, stream, x, groups, codes, scales, flags);
 }
 
 // --------------------------------------------------------------- bf16 round
@@ -79,6 +84,8 @@ constexpr int kRouterTok = 8;
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, uint32_t tokens,
                                                        const uint16_t *__restrict__ w, uint32_t experts,
                                                        uint32_t hidden, float *__restrict__ logits) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ double part[8][kRouterTok];
   const uint32_t lane = threadIdx.x % 32u, warp = threadIdx.x / 32u;
   const uint32_t e = blockIdx.x;
@@ -132,8 +139,7 @@ cudaError_t launch_router_logits(const float *x, uint32_t tokens, const uint16_t
                                  uint32_t hidden, float *logits, cudaStream_t stream) {
   if (hidden % 512u || tokens == 0) return cudaErrorInvalidValue;
   dim3 grid(experts, (tokens + kRouterTok - 1) / kRouterTok);
-  k_router_logits<<<grid, 256, 0, stream>>>(x, tokens, w, experts, hidden, logits);
-  return cudaGetLastError();
+  return launch_kernel(k_router_logits, grid, dim3(256), 0, stream, x, tokens, w, experts, hidden, logits);
 }
 
 // --------------------------------------------------------------- router top-k
@@ -164,6 +170,8 @@ __device__ __forceinline__ void argmax_shfl(float &bv, uint32_t &bi, float &bs, 
 __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ logits, const float *__restrict__ bias,
                                                      uint32_t tokens, uint32_t experts, uint32_t *__restrict__ selected,
                                                      float *__restrict__ weights, uint32_t *tie_rows, uint32_t *flags) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ float cv[8], cs[8];
   __shared__ uint32_t ci[8];
   __shared__ float pick_s[9], pick_v[9];
@@ -243,8 +251,8 @@ cudaError_t launch_router_topk(const float *logits, const float *bias, uint32_t 
                                uint32_t *selected, float *weights, uint32_t *tie_rows, uint32_t *flags,
                                cudaStream_t stream) {
   if (experts <= 8 || experts > 256u * kTopkPer || tokens == 0) return cudaErrorInvalidValue;
-  k_router_topk<<<tokens, 256, 0, stream>>>(logits, bias, tokens, experts, selected, weights, tie_rows, flags);
-  return cudaGetLastError();
+  return launch_kernel(k_router_topk, dim3(tokens), dim3(256), 0, stream, logits, bias, tokens, experts, selected,
+                       weights, tie_rows, flags);
 }
 
 // ----------------------------------------------------------------- schedule
@@ -261,6 +269,8 @@ __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ 
                                                    const float *__restrict__ weights, uint32_t tokens,
                                                    uint32_t experts, BankTable bank, ScheduleOut out,
                                                    uint32_t *flags) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ uint32_t sm[];
   uint32_t *mask = sm;                                      // [experts][words]
   uint16_t *prefix = reinterpret_cast<uint16_t *>(mask + experts * kSchedWords);  // [experts][words]
@@ -393,8 +403,8 @@ cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  k_schedule<<<1, 1024, smem, stream>>>(selected, weights, tokens, experts, bank, out, flags);
-  return cudaGetLastError();
+  return launch_kernel(k_schedule, dim3(1), dim3(1024), smem, stream, selected, weights, tokens, experts, bank, out,
+                       flags);
 }
 
 // ------------------------------------------------------------------ combine
@@ -404,6 +414,8 @@ cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint
 __global__ void k_combine(const float *__restrict__ down, const uint32_t *__restrict__ slot_place,
                           const float *__restrict__ placement_w, uint32_t tokens, uint32_t hidden,
                           float *__restrict__ y, uint32_t *flags) {
+  pdl_wait();
+  pdl_launch_dependents();
   const uint32_t t = blockIdx.y;
   __shared__ uint32_t pl[8];
   __shared__ float wt[8];
@@ -436,8 +448,7 @@ cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const 
                            uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream) {
   if (hidden % 4u || tokens == 0) return cudaErrorInvalidValue;
   dim3 grid((hidden / 4u + 255u) / 256u, tokens);
-  k_combine<<<grid, 256, 0, stream>>>(down, slot_place, placement_w, tokens, hidden, y, flags);
-  return cudaGetLastError();
+  return launch_kernel(k_combine, grid, dim3(256), 0, stream, down, slot_place, placement_w, tokens, hidden, y, flags);
 }
 
 // ------------------------------------------------------- weight validation

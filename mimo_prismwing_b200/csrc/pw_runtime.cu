@@ -587,6 +587,9 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
   d.out = down;
   d.out_stride = H;
   d.round_bf16 = down_round;
+  // groups and weights were final before gate/up ran; with PDL the down
+  // kernel's producer streams weights during gate/up's last wave
+  d.early_weights = (pdl_enabled() && fused) ? 1u : 0u;
   ProfScope ps(rt, P_DOWN, 1);
   CK(launch_gemv(0, d, grid_for(rt, units_hint * (H / 128u)), rt->stream));
   return PW_OK;
@@ -972,6 +975,8 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     counters = so.counters;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)tokens * H * 4)) != PW_OK) return s;
     CK(cudaMemsetAsync(rt->d_ties, 0, 4, rt->stream));
+    // the kernel chain below runs with programmatic dependent launch
+    PdlScope pdl(!rt->profiling);
     {
       ProfScope ps(rt, P_QUANT, 1);
       CK(launch_quantize(dx, tokens, H, xc, xs, rt->d_flags, rt->stream));
