@@ -74,6 +74,19 @@ struct GemvArgs {
                                  //   ends, so the producer may stream them before waiting
 };
 
+// Wide-width grouped GEMM (tcgen05): the GEMV arguments plus a TMA map of
+// the activation codes [rows, K] (view {128 B, rows, K/128}, box {128, TN, 2}).
+struct GemmArgs {
+  GemvArgs g;
+  CUtensorMap xmap;
+};
+// Tokens per group (TN) of the tcgen05 GEMM for a kind (0: 128, 2: 64, 3: 128).
+int gemm_tc_tokens(int kind);
+cudaError_t launch_gemm_tc(int kind, const GemmArgs &args, int grid, cudaStream_t stream);
+bool encode_act_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows);
+cudaError_t launch_gather_rows(const uint8_t *codes, const float *scales, const uint32_t *idx, uint32_t n,
+                               uint32_t K, uint8_t *out_codes, float *out_scales, cudaStream_t stream);
+
 // Kernel launchers (pw_kernels.cu).  All enqueue on `stream` and return the
 // launch status.
 cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_t *codes, float *scales,
@@ -119,8 +132,9 @@ struct BankTable {
 // (box 128 B x box_rows, 128B swizzle).  Returns false on failure.
 bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows);
 uint32_t map_box_rows(uint32_t layout);
+// chunk: tokens per GEMV/GEMM group (8 for the GEMV, gemm_tc_tokens(2) for the GEMM)
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
-                            const BankTable &bank, const ScheduleOut &out, uint32_t *flags,
+                            const BankTable &bank, const ScheduleOut &out, uint32_t *flags, uint32_t chunk,
                             cudaStream_t stream);
 cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const float *placement_w,
                            uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream);

@@ -268,7 +268,7 @@ constexpr uint32_t kSchedWords = kSchedMaxTokens / 32u;
 __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ selected,
                                                    const float *__restrict__ weights, uint32_t tokens,
                                                    uint32_t experts, BankTable bank, ScheduleOut out,
-                                                   uint32_t *flags) {
+                                                   uint32_t *flags, uint32_t chunk) {
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ uint32_t sm[];
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ 
       out.offsets[e] = off;
       grp_off[e] = goff;
       off += c;
-      goff += (c + 7u) / 8u;
+      goff += (c + chunk - 1u) / chunk;
       uniq += c ? 1u : 0u;
       maxc = c > maxc ? c : maxc;
     }
@@ -360,13 +360,13 @@ __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ 
     }
     for (int k = 0; k < 8; ++k) out.slot_place[t * 8u + k] = pl[k];
   }
-  // GEMV groups: each expert's placements in chunks of <= 8
+  // GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
   for (uint32_t e = tid; e < experts; e += nt) {
     const uint32_t c = cnt[e];
-    for (uint32_t j = 0; j * 8u < c; ++j) {
+    for (uint32_t j = 0; j * chunk < c; ++j) {
       GemvGroup g;
-      g.tok_begin = out.offsets[e] + 8u * j;
-      g.count = min(8u, c - 8u * j);
+      g.tok_begin = out.offsets[e] + chunk * j;
+      g.count = min(chunk, c - chunk * j);
       g.expert = e;
       g.pad = 0;
       g.w0 = bank.gate_w[e];
@@ -389,9 +389,9 @@ __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ 
 }
 
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
-                            const BankTable &bank, const ScheduleOut &out, uint32_t *flags,
+                            const BankTable &bank, const ScheduleOut &out, uint32_t *flags, uint32_t chunk,
                             cudaStream_t stream) {
-  if (tokens == 0 || tokens > kSchedMaxTokens || experts > kSchedMaxExperts || experts < 8)
+  if (tokens == 0 || tokens > kSchedMaxTokens || experts > kSchedMaxExperts || experts < 8 || chunk == 0)
     return cudaErrorInvalidValue;
   const size_t smem = (size_t)experts * kSchedWords * 4 + (size_t)experts * kSchedWords * 2 +
                       (size_t)(experts + 1) * 8;
@@ -404,7 +404,7 @@ cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint
     configured = true;
   }
   return launch_kernel(k_schedule, dim3(1), dim3(1024), smem, stream, selected, weights, tokens, experts, bank, out,
-                       flags);
+                       flags, chunk);
 }
 
 // ------------------------------------------------------------------ combine
@@ -449,6 +449,32 @@ cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const 
   if (hidden % 4u || tokens == 0) return cudaErrorInvalidValue;
   dim3 grid((hidden / 4u + 255u) / 256u, tokens);
   return launch_kernel(k_combine, grid, dim3(256), 0, stream, down, slot_place, placement_w, tokens, hidden, y, flags);
+}
+
+// --------------------------------------------------------------- row gather
+// dst row i = src row idx[i] (codes and their per-128 scales): lays the
+// routed tokens out in placement order so a TMA box can read an expert's
+// tokens as one contiguous block.
+__global__ void k_gather_rows(const uint8_t *__restrict__ codes, const float *__restrict__ scales,
+                              const uint32_t *__restrict__ idx, uint32_t n, uint32_t K, uint8_t *__restrict__ out_codes,
+                              float *__restrict__ out_scales) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t row = blockIdx.x;
+  if (row >= n) return;
+  const uint32_t src = idx[row];
+  const uint4 *s = reinterpret_cast<const uint4 *>(codes + (size_t)src * K);
+  uint4 *d = reinterpret_cast<uint4 *>(out_codes + (size_t)row * K);
+  for (uint32_t i = threadIdx.x; i < K / 16u; i += blockDim.x) d[i] = __ldg(s + i);
+  for (uint32_t i = threadIdx.x; i < K / 128u; i += blockDim.x)
+    out_scales[(size_t)row * (K / 128u) + i] = __ldg(scales + (size_t)src * (K / 128u) + i);
+}
+
+cudaError_t launch_gather_rows(const uint8_t *codes, const float *scales, const uint32_t *idx, uint32_t n,
+                               uint32_t K, uint8_t *out_codes, float *out_scales, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  if (K % 128u) return cudaErrorInvalidValue;
+  return launch_kernel(k_gather_rows, dim3(n), dim3(128), 0, stream, codes, scales, idx, n, K, out_codes, out_scales);
 }
 
 // ------------------------------------------------------- weight validation

@@ -44,6 +44,21 @@ static EncodeTiledFn encode_fn() {
 
 uint32_t map_box_rows(uint32_t layout) { return layout == PW_LAYOUT_PLAIN ? 128u : 64u; }
 
+// Activation codes [rows, cols] for the tcgen05 GEMM: view {128 B, rows,
+// k-blocks}, box {128, box_rows tokens, 2 k-blocks}; rows past the end of the
+// buffer read as zeros.
+bool encode_act_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || cols % 128u || rows == 0) return false;
+  cuuint64_t dims[3] = {128u, rows, cols / 128u};
+  cuuint64_t strides[2] = {cols, 128u};
+  cuuint32_t box[3] = {128u, box_rows, 2u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // The weight is viewed as {128 B, rows, k-blocks} with strides {cols, 128}:
 // a box of {128, box_rows, 256 / box_rows} is 32 KB and lands row-major in
 // shared memory (one 128-byte line per row and k-block), 128B-swizzled.
@@ -269,9 +284,10 @@ struct Call {
 
 // Projection groups for `width` tokens over one weight set (<= 8 per group).
 std::vector<GemvGroup> width_groups(uint32_t width, const pw_fp8_tensor &a, const pw_fp8_tensor *b,
-                                    const CUtensorMap *ma = nullptr, const CUtensorMap *mb = nullptr) {
+                                    const CUtensorMap *ma = nullptr, const CUtensorMap *mb = nullptr,
+                                    uint32_t chunk = 8) {
   std::vector<GemvGroup> gs;
-  for (uint32_t t = 0; t < width; t += 8) {
+  for (uint32_t t = 0; t < width; t += chunk) {
     GemvGroup g{};
     g.w0 = a.weight;
     g.s0 = a.scale;
@@ -280,7 +296,7 @@ std::vector<GemvGroup> width_groups(uint32_t width, const pw_fp8_tensor &a, cons
     g.tm0 = ma;
     g.tm1 = mb;
     g.tok_begin = t;
-    g.count = width - t < 8 ? width - t : 8;
+    g.count = width - t < chunk ? width - t : chunk;
     gs.push_back(g);
   }
   return gs;
@@ -309,6 +325,12 @@ bool encode_maps(pw_runtime *rt, const pw_fp8_tensor *const *ts, size_t n, uint3
   }
   return true;
 }
+
+// Width thresholds for the tcgen05 grouped GEMM: at or above these widths the
+// weights are read once per group of up to 64-128 tokens instead of once per
+// 8 tokens.
+constexpr uint32_t kWideProjection = 32;   // pw_fp8_linear / pw_expert_forward widths
+constexpr uint32_t kWideLayerTokens = 256; // routed-layer tokens (8 x tokens / experts >= 8)
 
 int grid_for(const pw_runtime *rt, uint64_t units) {
   const uint64_t g = units < (uint64_t)rt->num_sms ? units : (uint64_t)rt->num_sms;
@@ -479,6 +501,8 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
     const pw_fp8_tensor *ts[1] = {w};
     if (!encode_maps(rt, ts, 1, layout, &hmap)) return PW_ERR_CUDA;
   }
+  // wide block-scaled projections run on the tcgen05 GEMM (plain layout)
+  const bool wide = kind != 1 && layout == PW_LAYOUT_PLAIN && width >= kWideProjection;
   Call call{rt, mem, stats, 0};
   if ((s = call.begin()) != PW_OK) return s;
   Arena ar;
@@ -492,7 +516,8 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
     uint8_t *dc = kind == 1 ? nullptr : ar.take<uint8_t>(nx);
     float *ds = kind == 1 ? nullptr : ar.take<float>(nx / 128u);
     CUtensorMap *dm = ar.take<CUtensorMap>(1);
-    std::vector<GemvGroup> groups = width_groups(width, *w, nullptr, kind == 1 ? nullptr : dm);
+    std::vector<GemvGroup> groups =
+        width_groups(width, *w, nullptr, kind == 1 ? nullptr : dm, nullptr, wide ? (uint32_t)gemm_tc_tokens(0) : 8u);
     GemvGroup *dg = ar.take<GemvGroup>(groups.size());
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, nx * 4)) != PW_OK) return s;
@@ -513,7 +538,16 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
     }
     {
       ProfScope ps(rt, P_PROJ, 1);
-      CK(launch_gemv(kind, a, grid_for(rt, (uint64_t)groups.size() * (N / (kind == 1 ? 64u : 128u))), rt->stream));
+      const int grid = grid_for(rt, (uint64_t)groups.size() * (N / (kind == 1 ? 64u : 128u)));
+      if (wide) {
+        GemmArgs A{};
+        A.g = a;
+        if (!encode_act_map(&A.xmap, dc, width, K, (uint32_t)gemm_tc_tokens(0)))
+          return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activations");
+        CK(launch_gemm_tc(0, A, grid, rt->stream));
+      } else {
+        CK(launch_gemv(kind, a, grid, rt->stream));
+      }
     }
     if (call.host() && (s = call.stage_out(y, dy, ny * 4)) != PW_OK) return s;
   }
@@ -596,6 +630,60 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
 }
 
 
+// The expert chain on the tcgen05 GEMM.  xg / xsg are the gate/up input codes
+// and scales laid out by group (tok_begin indexes rows directly).
+static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const GemvGroup *dn, uint32_t n_groups,
+                                     const uint32_t *n_groups_dev, uint32_t slots, uint32_t H, uint32_t I,
+                                     const uint8_t *xg, const float *xsg, float *hidden, float *gate_tmp,
+                                     float *up_tmp, uint8_t *hc, float *hs, float *down, uint32_t down_round,
+                                     uint64_t units_hint) {
+  const int grid_gu = grid_for(rt, units_hint * (I / 128u));
+  const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
+  {
+    ProfScope ps(rt, P_GATEUP, fused ? 1 : 3);
+    GemmArgs A{};
+    A.g = gemv_args(rt, gu, n_groups, I, H, PW_LAYOUT_PLAIN);
+    A.g.n_groups_dev = n_groups_dev;
+    A.g.x_codes = xg;
+    A.g.x_scales = xsg;
+    A.g.out_stride = I;
+    if (fused) {
+      if (!encode_act_map(&A.xmap, xg, slots, H, (uint32_t)gemm_tc_tokens(2)))
+        return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activations");
+      A.g.out = hidden;  // may be null
+      A.g.q_codes = hc;
+      A.g.q_scales = hs;
+      CK(launch_gemm_tc(2, A, grid_gu, rt->stream));
+    } else {
+      if (!encode_act_map(&A.xmap, xg, slots, H, (uint32_t)gemm_tc_tokens(0)))
+        return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activations");
+      A.g.out = gate_tmp;
+      CK(launch_gemm_tc(0, A, grid_gu, rt->stream));
+      GemmArgs B = A;
+      B.g.out = up_tmp;
+      CK(launch_gemm_tc(3, B, grid_gu, rt->stream));
+      CK(launch_swiglu(gate_tmp, up_tmp, hidden, slots * I, rt->d_flags, rt->stream));
+    }
+  }
+  if (!fused) {
+    ProfScope ps(rt, P_QUANT, 1);
+    CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream));
+  }
+  GemmArgs D{};
+  D.g = gemv_args(rt, dn, n_groups, H, I, PW_LAYOUT_PLAIN);
+  D.g.n_groups_dev = n_groups_dev;
+  D.g.x_codes = hc;
+  D.g.x_scales = hs;
+  D.g.out = down;
+  D.g.out_stride = H;
+  D.g.round_bf16 = down_round;
+  if (!encode_act_map(&D.xmap, hc, slots, I, (uint32_t)gemm_tc_tokens(0)))
+    return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the hidden codes");
+  ProfScope ps(rt, P_DOWN, 1);
+  CK(launch_gemm_tc(0, D, grid_for(rt, units_hint * (H / 128u)), rt->stream));
+  return PW_OK;
+}
+
 extern "C" {
 
 int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x, uint32_t width, float *y,
@@ -631,8 +719,10 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
     uint8_t *hc = ar.take<uint8_t>((size_t)width * I);
     float *hs = ar.take<float>((size_t)width * I / 128u);
     CUtensorMap *dm = ar.take<CUtensorMap>(3);
-    std::vector<GemvGroup> gu = width_groups(width, w->gate, &w->up, dm, dm ? dm + 1 : nullptr);
-    std::vector<GemvGroup> dn = width_groups(width, w->down, nullptr, dm ? dm + 2 : nullptr);
+    const bool wide = width >= kWideProjection;
+    const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
+    std::vector<GemvGroup> gu = width_groups(width, w->gate, &w->up, dm, dm ? dm + 1 : nullptr, chunk);
+    std::vector<GemvGroup> dn = width_groups(width, w->down, nullptr, dm ? dm + 2 : nullptr, nullptr, chunk);
     GemvGroup *dgu = ar.take<GemvGroup>(gu.size());
     GemvGroup *ddn = ar.take<GemvGroup>(dn.size());
     if (pass == 0) continue;
@@ -644,9 +734,13 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
       ProfScope ps(rt, P_QUANT, 1);
       CK(launch_quantize(dx, width, H, xc, xs, rt->d_flags, rt->stream));
     }
-    if ((s = enqueue_expert_chain(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, width, H, I, nullptr, xc, xs, hid, gt,
-                                  ut, hc, hs, dy, 1, gu.size())) != PW_OK)
-      return s;
+    if (wide)
+      s = enqueue_expert_chain_wide(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, width, H, I, xc, xs, hid, gt, ut, hc,
+                                    hs, dy, 1, gu.size());
+    else
+      s = enqueue_expert_chain(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, width, H, I, nullptr, xc, xs, hid, gt, ut,
+                               hc, hs, dy, 1, gu.size());
+    if (s != PW_OK) return s;
     if (call.host() && (s = call.stage_out(y, dy, (size_t)width * H * 4)) != PW_OK) return s;
   }
   const uint64_t wb = 3ull * H * I + 4ull * (w->gate.scale_rows * w->gate.scale_cols * 2u +
@@ -713,8 +807,15 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
   int s;
   // schedule validation (src/wide_metal_moe.rs:858-868, 919-935)
   uint64_t total = 0;
-  for (uint32_t i = 0; i < n_experts; ++i) total += experts[i].count;
+  uint32_t max_count = 0;
+  for (uint32_t i = 0; i < n_experts; ++i) {
+    total += experts[i].count;
+    max_count = experts[i].count > max_count ? experts[i].count : max_count;
+  }
   if (total != (uint64_t)rows * 8u) return fail(rt, PW_ERR_SCHEDULE, "wide MoE input or schedule mismatch");
+  // experts with many placements run on the tcgen05 GEMM (groups of up to 64)
+  const bool wide = max_count > 16u;
+  const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
   const uint32_t H = experts[0].weights.gate.cols, I = experts[0].weights.gate.rows;
   std::vector<uint32_t> per_token(rows, 0);
   std::vector<uint32_t> placement_tok, slot_place((size_t)rows * 8u);
@@ -744,14 +845,14 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
       placement_tok.push_back(pos);
       placement_w.push_back(wt);
     }
-    for (uint32_t j = 0; j < b.count; j += 8u) {
+    for (uint32_t j = 0; j < b.count; j += chunk) {
       GemvGroup g{};
       g.w0 = b.weights.gate.weight;
       g.s0 = b.weights.gate.scale;
       g.w1 = b.weights.up.weight;
       g.s1 = b.weights.up.scale;
       g.tok_begin = begin + j;
-      g.count = b.count - j < 8u ? b.count - j : 8u;
+      g.count = b.count - j < chunk ? b.count - j : chunk;
       g.expert = b.expert;
       gu.push_back(g);
       group_binding.push_back(i);
@@ -804,6 +905,8 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
     uint8_t *hc = ar.take<uint8_t>((size_t)P * I);
     float *hs = ar.take<float>((size_t)P * I / 128u);
     float *down = ar.take<float>((size_t)P * H);
+    uint8_t *xg = wide ? ar.take<uint8_t>((size_t)P * H) : nullptr;
+    float *xsg = wide ? ar.take<float>((size_t)P * H / 128u) : nullptr;
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)rows * H * 4)) != PW_OK) return s;
     CK(cudaMemcpyAsync(dm, hmaps.data(), hmaps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, rt->stream));
@@ -816,9 +919,18 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
       ProfScope ps(rt, P_QUANT, 1);
       CK(launch_quantize(dx, rows, H, xc, xs, rt->d_flags, rt->stream));
     }
-    if ((s = enqueue_expert_chain(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, P, H, I, dtok, xc, xs, hid, gt, ut, hc,
-                                  hs, down, 1, gu.size())) != PW_OK)
-      return s;
+    if (wide) {
+      {
+        ProfScope ps(rt, P_QUANT, 1);
+        CK(launch_gather_rows(xc, xs, dtok, P, H, xg, xsg, rt->stream));
+      }
+      s = enqueue_expert_chain_wide(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, P, H, I, xg, xsg, hid, gt, ut, hc, hs,
+                                    down, 1, gu.size());
+    } else {
+      s = enqueue_expert_chain(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, P, H, I, dtok, xc, xs, hid, gt, ut, hc, hs,
+                               down, 1, gu.size());
+    }
+    if (s != PW_OK) return s;
     {
       ProfScope ps(rt, P_COMBINE, 1);
       CK(launch_combine(down, dslot, dpw, rows, H, dy, rt->d_flags, rt->stream));
@@ -938,7 +1050,11 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
   if (tokens > 2048u) return fail(rt, PW_ERR_UNSUPPORTED, "routed layer supports at most 2048 tokens per call");
   CK(cudaSetDevice(rt->device));
   const uint32_t H = bank->hidden, I = bank->inter, E = bank->n, P = tokens * 8u;
-  const uint32_t max_groups = P + E;  // sum over experts of ceil(count/8)
+  // wide layers (prefill) run the experts on the tcgen05 GEMM in groups of up
+  // to 64 placements; decode widths on the GEMV in groups of up to 8
+  const bool wide = tokens >= kWideLayerTokens;
+  const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
+  const uint32_t max_groups = P / chunk + E;  // >= sum over experts of ceil(count / chunk)
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   Call call{rt, mem, stats, 0};
   if ((s = call.begin()) != PW_OK) return s;
@@ -971,6 +1087,8 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     uint8_t *hc = ar.take<uint8_t>((size_t)P * I);
     float *hs = ar.take<float>((size_t)P * I / 128u);
     float *down = ar.take<float>((size_t)P * H);
+    uint8_t *xg = wide ? ar.take<uint8_t>((size_t)P * H) : nullptr;
+    float *xsg = wide ? ar.take<float>((size_t)P * H / 128u) : nullptr;
     if (pass == 0) continue;
     counters = so.counters;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)tokens * H * 4)) != PW_OK) return s;
@@ -988,12 +1106,21 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     }
     {
       ProfScope ps(rt, P_SCHED, 1);
-      CK(launch_schedule(sel, wts, tokens, E, bank->table, so, rt->d_flags, rt->stream));
+      CK(launch_schedule(sel, wts, tokens, E, bank->table, so, rt->d_flags, chunk, rt->stream));
     }
     // the grid covers the worst case; CTAs read the real group count
-    if ((s = enqueue_expert_chain(rt, so.gu_groups, so.dn_groups, max_groups, so.n_groups, P, H, I, so.placement_tok,
-                                  xc, xs, hid, gt, ut, hc, hs, down, 1, max_groups)) != PW_OK)
-      return s;
+    if (wide) {
+      {
+        ProfScope ps(rt, P_QUANT, 1);
+        CK(launch_gather_rows(xc, xs, so.placement_tok, P, H, xg, xsg, rt->stream));
+      }
+      s = enqueue_expert_chain_wide(rt, so.gu_groups, so.dn_groups, max_groups, so.n_groups, P, H, I, xg, xsg, hid,
+                                    gt, ut, hc, hs, down, 1, max_groups);
+    } else {
+      s = enqueue_expert_chain(rt, so.gu_groups, so.dn_groups, max_groups, so.n_groups, P, H, I, so.placement_tok, xc,
+                               xs, hid, gt, ut, hc, hs, down, 1, max_groups);
+    }
+    if (s != PW_OK) return s;
     {
       ProfScope ps(rt, P_COMBINE, 1);
       CK(launch_combine(down, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream));

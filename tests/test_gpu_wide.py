@@ -1,0 +1,121 @@
+"""GPU parity of the wide (prefill) path: the tcgen05 grouped GEMM.
+
+Widths >= 32 for projections and experts, expert groups of more than 16
+placements in a host-built schedule, and routed layers of >= 256 tokens run
+on the tcgen05/TMEM grouped GEMM instead of the GEMV.  Same oracle and
+tolerances as the narrow path.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def rt():
+    from mimo_prismwing_b200.runtime import WideMoeRuntime
+    r = WideMoeRuntime.compile_with_fused_gate_up(0)
+    yield r
+    r.close()
+
+
+@pytest.fixture(scope="module")
+def rt_unfused():
+    from mimo_prismwing_b200.runtime import WideMoeRuntime
+    r = WideMoeRuntime.compile(0)
+    yield r
+    r.close()
+
+
+def H(t):
+    from gpu_helpers import host
+    return host(t)
+
+
+@pytest.mark.parametrize("rows,cols,width", [(2048, 4096, 32), (2048, 4096, 100), (4096, 2048, 256),
+                                             (256, 384, 40), (1024, 4096, 2048)])
+def test_wide_linear_vs_oracle(rt, rows, cols, width):
+    from gpu_helpers import assert_close, assert_close_bf16
+    from mimo_prismwing_b200 import synth
+    b = synth.projection(rows, cols, rows * 7 + cols, "cuda")
+    x = synth.activations(width, cols, width + 3, "cuda")
+    y32 = H(rt.execute_fp8_linear(x, b, f32_output=True).output)
+    codes, scales, _ = O.dynamic_fp8(H(x))
+    take = slice(None) if width <= 256 else slice(0, width, 7)  # keep the f64 oracle quick
+    pre = O.blockscaled_linear(H(b.weight), H(b.scale), codes[take], scales[take])
+    assert_close(y32[take], pre, what=f"wide linear {rows}x{cols} w{width}")
+    y = H(rt.execute_fp8_linear(x, b).output)
+    assert np.array_equal(O.round_bf16(y32), y)
+    assert_close_bf16(y[take], O.round_bf16(pre), what=f"wide linear bf16 w{width}")
+
+
+@pytest.mark.parametrize("width", [32, 64, 130])
+def test_wide_expert_vs_oracle(rt, width):
+    from gpu_helpers import assert_close_bf16, bank_arrays
+    from mimo_prismwing_b200 import synth
+    g, u, d = synth.expert(4096, 2048, 17, "cuda")
+    x = synth.activations(width, 4096, 170 + width, "cuda")
+    y = H(rt.expert_forward(x, g, u, d).output)
+    (gw, gs, uw, us, dw, ds), = bank_arrays([(g, u, d)])
+    xc, xs, _ = O.dynamic_fp8(H(x))
+    gate = O.blockscaled_linear(gw, gs, xc, xs)
+    up = O.blockscaled_linear(uw, us, xc, xs)
+    act = O.staged_swiglu(gate, up, O.EXP_SLEEF)
+    hc, hs, _ = O.dynamic_fp8(act)
+    ref = O.round_bf16(O.blockscaled_linear(dw, ds, hc, hs))
+    assert_close_bf16(y, ref, what=f"wide expert w{width}")
+
+
+def test_wide_fused_gate_up_is_exact_against_unfused(rt, rt_unfused):
+    # src/wide_metal_moe.rs:1343 at widths that take the tcgen05 path
+    from mimo_prismwing_b200 import synth
+    g, u, d = synth.expert(1024, 512, 18, "cuda")
+    for width in [32, 96]:
+        x = synth.activations(width, 1024, 180 + width, "cuda")
+        a = H(rt.expert_forward(x, g, u, d).output)
+        b = H(rt_unfused.expert_forward(x, g, u, d).output)
+        assert np.array_equal(a, b), f"width {width}"
+
+
+def test_wide_host_schedule_vs_oracle(rt):
+    # every token routed to all 8 experts: 64 placements per expert (> 16)
+    from gpu_helpers import assert_close_bf16, bank_arrays
+    from mimo_prismwing_b200 import synth
+    from mimo_prismwing_b200.runtime import WideExpertBinding
+    E, Hd, I, T = 8, 1024, 512, 64
+    bank = [synth.expert(Hd, I, 300 + e, "cuda") for e in range(E)]
+    rng = np.random.default_rng(5)
+    sel = np.stack([rng.permutation(E) for _ in range(T)]).astype(np.uint32)
+    raw = rng.random((T, 8)).astype(np.float32)
+    wts = (raw / raw.sum(1, keepdims=True)).astype(np.float32)
+    x = synth.activations(T, Hd, 301, "cuda")
+    offsets, order = O.schedule(sel, E)
+    bindings = []
+    for e in range(E):
+        pl = order[offsets[e]:offsets[e + 1]]
+        g, u, d = bank[e]
+        bindings.append(WideExpertBinding(e, [int(p) // 8 for p in pl], [float(wts.ravel()[p]) for p in pl], g, u, d))
+    ex = rt.execute_fused_gate_up(x, bindings)
+    ref = O.routed_layer(H(x), sel, wts, bank_arrays(bank), O.ACC_F64, O.EXP_SLEEF)
+    assert_close_bf16(H(ex.output), ref, what="wide host schedule")
+
+
+@pytest.mark.parametrize("tokens", [256, 512])
+def test_wide_moe_layer_device_router_vs_oracle(rt, tokens):
+    from gpu_helpers import assert_close_bf16, bank_arrays
+    from mimo_prismwing_b200 import synth
+    E, Hd, I = 32, 1024, 512
+    bank = [synth.expert(Hd, I, 400 + e, "cuda") for e in range(E)]
+    handle = rt.create_bank(bank)
+    w, bias = synth.router(E, Hd, 41, "cuda")
+    x = synth.activations(tokens, Hd, 42, "cuda")
+    ex = rt.moe_layer(x, w, bias, handle, want_routes=True)
+    logits = O.router_logits(H(x), H(w.view(torch.int16)).view(np.uint16))
+    osel, owts, _, _, _ = O.noaux_topk(logits, H(bias))
+    assert np.array_equal(H(ex.selected).astype(np.uint32), osel)
+    ref = O.routed_layer(H(x), osel, owts, bank_arrays(bank), O.ACC_F64, O.EXP_SLEEF)
+    assert_close_bf16(H(ex.output), ref, what=f"wide moe layer T{tokens}")
+    assert ex.expert_rows == tokens * 8
