@@ -4,25 +4,29 @@
 // same equation as the GEMV (src/wide_metal_moe.rs:404-423)
 //   y[t, r] = sum_kb ( sum_{c in kb} dec(W[r, c]) * dec(code[t, c]) ) * S[r/128, kb] * xs[t, kb]
 // runs on the 5th-generation tensor cores:
-//  * A = 128 weight rows x 32 columns, B = TN token rows x 32 columns, both
+//  * A = 128 weight rows x 32 columns, B = N token rows x 32 columns, both
 //    K-major e4m3 in shared memory (128B swizzle, written by TMA);
 //  * one elected thread issues tcgen05.mma.kind::f8f6f4 into a TMEM
 //    accumulator; every 128-column block gets a fresh accumulator (the
 //    checkpoint's f32 block scales are not power-of-two UE8M0 scales, so the
-//    hardware block-scaled MMA cannot apply them);
-//  * four epilogue warps tcgen05.ld each block's result, promote it with
-//    S[r/128, kb] * xs[t, kb] into f32 registers (one thread per row), while
-//    the MMA of the next block fills the other TMEM buffer;
+//    hardware block-scaled MMA cannot apply them).  N is the group's token
+//    count rounded up to 32, so a 40-token expert costs 64 columns, not 128;
+//  * eight epilogue warps (two per TMEM lane quarter, each owning half of the
+//    32-token chunks) tcgen05.ld each block's result and promote it into f32
+//    registers, acc += v * (S * xs) with packed f32x2 multiply/FMA, while the
+//    MMA fills the next of the rotating 128-column TMEM accumulator slots;
 //  * a producer warp streams stages of {128 rows x 2 blocks} weights (one
-//    32 KB 3-D TMA box) and {TN tokens x 2 blocks} activation codes; in the
-//    fused kernel all gate stages of a tile come first, then all up stages,
-//    and the finished gate sums wait in spare TMEM columns so only one set of
-//    accumulators occupies registers.
-// Work: persistent CTAs over (group, 128-row tile); a group is <= TN tokens
+//    32 KB 3-D TMA box) and {n tokens x 2 blocks} activation codes, n the
+//    group's tokens rounded up to 32.  The fused kind runs all gate stages of
+//    a tile, parks the finished gate sums in a spare TMEM slot (tcgen05.st),
+//    runs the up stages in the same registers and stores bf16(gate) and
+//    bf16(up) -- the first two roundings of the staged SwiGLU.  The rest of
+//    the SwiGLU and the hidden's dynamic FP8 quantization run in
+//    k_swiglu_quant at full occupancy: inside this kernel only eight warps
+//    per SM would execute them, on the pipeline's critical path (measured
+//    ~15k cycles per 128 x 64 tile, a third of the tile's HBM time).
+// Work: persistent CTAs over (group, 128-row tile); a group is <= 128 tokens
 // of one weight matrix (an expert's placements, or a chunk of a projection).
-// The fused variant alternates gate and up stages and finishes with the
-// staged bf16 SwiGLU and the hidden's dynamic FP8 quantization, exactly as
-// the GEMV does.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -33,34 +37,37 @@
 namespace pw {
 namespace tc {
 
+// Warp roles: producer (warp 0), MMA issuer and TMEM owner (warp 1), epilogue
+// (warps 2-9, two per TMEM lane quarter).
 constexpr int kProducerWarp = 0;
 constexpr int kMmaWarp = 1;
 constexpr int kEpiWarp0 = 2;
-constexpr int kEpiThreads = 128;
-constexpr int kThreads = 6 * 32;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr int kTileRows = 128;
-constexpr int kWBox = 32 * 1024;  // weights: 128 rows x 2 k-blocks x 128 B
+constexpr int kTN = 128;           // tokens per group
+constexpr int kWBox = 32 * 1024;   // weights: 128 rows x 2 k-blocks x 128 B
+constexpr int kXBox = kTN * 256;   // activations: 128 tokens x 2 k-blocks x 128 B
+constexpr int kStage = kWBox + kXBox;
+constexpr int kNst = 3;
+constexpr int kChunks = kTN / 32;              // 32-token chunks per group
+constexpr int kThreadChunks = kChunks / 2;     // chunks per epilogue thread
+constexpr int kTmemCols = 512;                 // four 128-column slots
 
-template <int KIND, int TN>
+template <int KIND>
 struct Cfg {
   static constexpr bool FUSED = KIND == 2;
   static constexpr int MATS = FUSED ? 2 : 1;
-  static constexpr int XBOX = TN * 256;  // activations: TN rows x 2 k-blocks x 128 B
-  static constexpr int STAGE = kWBox + XBOX;
-  static constexpr int NST = (200 * 1024) / STAGE;
-  // 2 k-blocks x 2 buffers x TN f32 columns, plus TN columns for the gate
-  // sums of the fused kernel; allocations are powers of two
-  static constexpr int TMEM_USED = 4 * TN + (FUSED ? TN : 0);
-  static constexpr int TMEM_COLS = TMEM_USED <= 128 ? 128 : TMEM_USED <= 256 ? 256 : 512;
-  static constexpr int RING = NST * STAGE;
-  static constexpr int XS = RING;                     // token scales [TN][32] f32
-  static constexpr int WS = XS + TN * 32 * 4;         // weight scales [2][32] f32
-  static constexpr int AMAX = WS + 2 * 32 * 4;        // [4 warps][TN] f32
-  static constexpr int BARS = AMAX + 4 * TN * 4;      // mbarriers
-  static constexpr int NBARS = 2 * NST + 4;           // full, empty, tfull[2], tempty[2]
+  static constexpr int RING = kNst * kStage;
+  static constexpr int XS = RING;                     // token scales [32 kb][kTN] f32
+  static constexpr int WS = XS + 32 * kTN * 4;        // weight scales [2 mats][32] f32
+  static constexpr int BARS = WS + 2 * 32 * 4;        // mbarriers
+  static constexpr int NACC = FUSED ? 3 : 4;          // rotating accumulator slots (fused: + gate stash)
+  static constexpr int NBARS = 2 * kNst + 2 * NACC;   // full, empty, tfull[NACC], tempty[NACC]
   static constexpr int MISC = BARS + NBARS * 8;       // tmem base, abort
   static constexpr int SMEM = MISC + 16 + 1024;       // + alignment slack
-  static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
+  static_assert((NACC + (FUSED ? 1 : 0)) * kTN <= kTmemCols, "TMEM holds 512 columns");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
@@ -92,13 +99,12 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return d;
 }
 
-// kind::f8f6f4 instruction descriptor: D f32, A/B e4m3, both K-major, M=128, N=TN.
-template <int TN>
-__device__ __forceinline__ uint32_t instr_desc() {
+// kind::f8f6f4 instruction descriptor: D f32, A/B e4m3, both K-major, M=128, N=n.
+__device__ __forceinline__ uint32_t instr_desc(uint32_t n) {
   return (1u << 4)                   // c_format F32
          | (0u << 7) | (0u << 10)    // a, b: E4M3
          | (0u << 15) | (0u << 16)   // K-major
-         | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+         | ((n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
@@ -132,25 +138,54 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 16 consecutive f32 columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // 32 lanes x 32 consecutive f32 columns from registers into TMEM.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float2 (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
       "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
-      "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
-      "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
-      "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      "f"(v[0].x), "f"(v[0].y), "f"(v[1].x), "f"(v[1].y), "f"(v[2].x), "f"(v[2].y), "f"(v[3].x), "f"(v[3].y),
+      "f"(v[4].x), "f"(v[4].y), "f"(v[5].x), "f"(v[5].y), "f"(v[6].x), "f"(v[6].y), "f"(v[7].x), "f"(v[7].y),
+      "f"(v[8].x), "f"(v[8].y), "f"(v[9].x), "f"(v[9].y), "f"(v[10].x), "f"(v[10].y), "f"(v[11].x), "f"(v[11].y),
+      "f"(v[12].x), "f"(v[12].y), "f"(v[13].x), "f"(v[13].y), "f"(v[14].x), "f"(v[14].y), "f"(v[15].x), "f"(v[15].y)
       : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// acc[t] += v[t] * (ws * xs[t]) for N tokens, two at a time (packed f32x2);
+// each product and sum rounds exactly like the scalar fmaf(v, ws * xs, acc).
+template <int N>
+__device__ __forceinline__ void promote(float2 *acc, const float (&v)[N], float ws, const float *xs) {
+  const float2 w2 = make_float2(ws, ws);
+#pragma unroll
+  for (int i = 0; i < N / 2; i += 2) {
+    const float4 x4 = *reinterpret_cast<const float4 *>(xs + 2 * i);
+    const float2 c0 = __fmul2_rn(w2, make_float2(x4.x, x4.y));
+    const float2 c1 = __fmul2_rn(w2, make_float2(x4.z, x4.w));
+    acc[i] = __ffma2_rn(make_float2(v[2 * i], v[2 * i + 1]), c0, acc[i]);
+    acc[i + 1] = __ffma2_rn(make_float2(v[2 * i + 2], v[2 * i + 3]), c1, acc[i + 1]);
+  }
+}
+
+__device__ __forceinline__ float &el(float2 (&v)[16], int i) { return (i & 1) ? v[i / 2].y : v[i / 2].x; }
+
 struct Shared {
   uint8_t *ring;
   float *xs;
   float *ws;
-  float *amax;
   uint64_t *full, *empty, *tfull, *tempty;
   uint32_t *tmem_base;
   volatile int *abort;
@@ -164,10 +199,17 @@ __device__ __forceinline__ bool bwait(const Shared &sh, uint64_t *bar, uint32_t 
   return false;
 }
 
-template <int KIND, int TN>
+// MMA columns of a group: its token count rounded up to whole 32-token chunks.
+__device__ __forceinline__ uint32_t mma_cols(uint32_t count) {
+  const uint32_t n = (min(count, (uint32_t)kTN) + 31u) & ~31u;
+  return n ? n : 32u;
+}
+
+template <int KIND>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__ GemmArgs A) {
-  using C = Cfg<KIND, TN>;
+  using C = Cfg<KIND>;
   constexpr int MATS = C::MATS;
+  constexpr uint32_t NACC = (uint32_t)C::NACC;
   const GemvArgs &a = A.g;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -175,23 +217,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   sh.ring = smem;
   sh.xs = reinterpret_cast<float *>(smem + C::XS);
   sh.ws = reinterpret_cast<float *>(smem + C::WS);
-  sh.amax = reinterpret_cast<float *>(smem + C::AMAX);
   sh.full = reinterpret_cast<uint64_t *>(smem + C::BARS);
-  sh.empty = sh.full + C::NST;
-  sh.tfull = sh.empty + C::NST;
-  sh.tempty = sh.tfull + 2;
+  sh.empty = sh.full + kNst;
+  sh.tfull = sh.empty + kNst;
+  sh.tempty = sh.tfull + NACC;
   sh.tmem_base = reinterpret_cast<uint32_t *>(smem + C::MISC);
   sh.abort = reinterpret_cast<volatile int *>(smem + C::MISC + 4);
 
   const uint32_t warp = threadIdx.x / 32u, lane = threadIdx.x % 32u;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < C::NST; ++i) {
+    for (int i = 0; i < kNst; ++i) {
       mbar_init(&sh.full[i], 1);
       mbar_init(&sh.empty[i], 1);  // arrived by the MMA warp's tcgen05.commit
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sh.tfull[i], 1);                // tcgen05.commit after a stage's MMAs
-      mbar_init(&sh.tempty[i], kEpiThreads / 32);  // one arrive per epilogue warp
+    for (uint32_t i = 0; i < NACC; ++i) {
+      mbar_init(&sh.tfull[i], 1);           // tcgen05.commit after a k-block's MMAs
+      mbar_init(&sh.tempty[i], kEpiWarps);  // one arrive per epilogue warp
     }
     *sh.abort = 0;
     mbar_fence_init();
@@ -199,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   if (warp == kMmaWarp) {
     // allocate the accumulator columns (whole warp), then let other CTAs allocate
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(sh.tmem_base)),
-                 "r"((uint32_t)C::TMEM_COLS)
+                 "r"((uint32_t)kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -217,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   const uint32_t u_end = (uint32_t)(total * (blockIdx.x + 1) / gridDim.x);
   const uint32_t kblocks = a.K / 128u;
   const uint32_t kcs = (kblocks + 1u) / 2u;          // stages per matrix per tile
-  const uint32_t per_tile = kcs * (uint32_t)MATS;   // stages per tile
+  const uint32_t per_tile = kcs * (uint32_t)MATS;   // stages per tile; fused: all gate, then all up
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
@@ -228,88 +269,103 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
         tensormap_acquire(m0);
         if (MATS == 2) tensormap_acquire(g.tm1);
         const uint32_t row0 = (u % tpg) * kTileRows;
+        const uint32_t n = mma_cols(g.count);  // token rows loaded: whole 32-token chunks
+        const CUtensorMap *xm = &A.xmap[n / 32u - 1u];
+        const uint32_t bytes = (uint32_t)kWBox + n * 256u;
         for (uint32_t st = 0; st < per_tile; ++st) {
           const uint32_t m = st / kcs, kc = st % kcs;
           if (bwait(sh, &sh.empty[slot], phase ^ 1u, a.flags)) {
-            uint8_t *dst = sh.ring + slot * C::STAGE;
-            mbar_arrive_expect_tx(&sh.full[slot], C::STAGE);
+            uint8_t *dst = sh.ring + slot * kStage;
+            mbar_arrive_expect_tx(&sh.full[slot], bytes);
             tma_load_3d(dst, m == 0 ? m0 : g.tm1, 0, (int)row0, (int)(kc * 2u), &sh.full[slot]);
-            tma_load_3d(dst + kWBox, &A.xmap, 0, (int)g.tok_begin, (int)(kc * 2u), &sh.full[slot]);
+            tma_load_3d(dst + kWBox, xm, 0, (int)g.tok_begin, (int)(kc * 2u), &sh.full[slot]);
             issued |= 1u << slot;
             parity = (parity & ~(1u << slot)) | (phase << slot);
           }
-          if (++slot == (uint32_t)C::NST) {
+          if (++slot == (uint32_t)kNst) {
             slot = 0;
             phase ^= 1u;
           }
         }
       }
-      for (int i = 0; i < C::NST; ++i)
+      for (int i = 0; i < kNst; ++i)
         if (issued & (1u << i))
           if (!mbar_wait(&sh.full[i], (parity >> i) & 1u)) raise_flag(a.flags, PW_FLAG_WAIT_TIMEOUT);
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
-      const uint32_t idesc = instr_desc<TN>();
       const uint32_t ring = smem_addr(sh.ring);
-      uint32_t slot = 0, phase = 0, buf = 0, bphase = 0;
-      bool committed = false;
-      uint32_t last_buf = 0, last_phase = 0;
+      uint32_t slot = 0, phase = 0, acc = 0, aphase = 0;
+      uint32_t pending = 0, pend_parity = 0;  // accumulator slots with a commit in flight
       for (uint32_t u = u_begin; u < u_end; ++u) {
+        const uint32_t n = mma_cols(a.groups[u / tpg].count);
+        const uint32_t idesc = instr_desc(n);
         for (uint32_t st = 0; st < per_tile; ++st) {
+          const uint32_t kc = st % kcs;
           const bool ok_full = bwait(sh, &sh.full[slot], phase, a.flags);
-          const bool ok_buf = bwait(sh, &sh.tempty[buf], bphase ^ 1u, a.flags);
           tc_fence_after();
-          if (ok_full && ok_buf) {
-            const uint32_t kc = st % kcs;
-            const uint32_t wbase = ring + slot * C::STAGE;
-            const uint32_t xbase = wbase + kWBox;
+          const uint32_t wbase = ring + slot * kStage;
+          const uint32_t xbase = wbase + kWBox;
 #pragma unroll
-            for (uint32_t j = 0; j < 2; ++j) {
-              if (kc * 2u + j >= kblocks) break;
-              const uint32_t d = tmem + buf * (2u * TN) + j * TN;
+          for (uint32_t j = 0; j < 2; ++j) {
+            if (kc * 2u + j >= kblocks) break;
+            const bool ok_acc = bwait(sh, &sh.tempty[acc], aphase ^ 1u, a.flags);
+            tc_fence_after();
+            if (ok_full && ok_acc) {
+              const uint32_t d = tmem + acc * (uint32_t)kTN;
 #pragma unroll
               for (uint32_t s = 0; s < 4; ++s) {
                 const uint64_t ad = smem_desc_sw128(wbase + j * (kTileRows * 128u) + s * 32u);
-                const uint64_t bd = smem_desc_sw128(xbase + j * (TN * 128u) + s * 32u);
+                const uint64_t bd = smem_desc_sw128(xbase + j * (n * 128u) + s * 32u);
                 mma_f8(d, ad, bd, idesc, s > 0 ? 1u : 0u);
               }
             }
+            mma_commit(&sh.tfull[acc]);  // this k-block's sums ready for the epilogue
+            pending |= 1u << acc;
+            pend_parity = (pend_parity & ~(1u << acc)) | (aphase << acc);
+            if (++acc == NACC) {
+              acc = 0;
+              aphase ^= 1u;
+            }
           }
-          mma_commit(&sh.empty[slot]);   // stage reusable once these MMAs are done
-          mma_commit(&sh.tfull[buf]);    // accumulators ready for the epilogue
-          committed = true;
-          last_buf = buf;
-          last_phase = bphase;
-          if (++slot == (uint32_t)C::NST) {
+          mma_commit(&sh.empty[slot]);  // stage reusable once these MMAs are done
+          if (++slot == (uint32_t)kNst) {
             slot = 0;
             phase ^= 1u;
-          }
-          if (++buf == 2u) {
-            buf = 0;
-            bphase ^= 1u;
           }
         }
       }
       // every MMA must be complete before the columns are freed
-      if (committed)
-        if (!mbar_wait(&sh.tfull[last_buf], last_phase)) raise_flag(a.flags, PW_FLAG_WAIT_TIMEOUT);
+      for (uint32_t i = 0; i < NACC; ++i)
+        if (pending & (1u << i))
+          if (!mbar_wait(&sh.tfull[i], (pend_parity >> i) & 1u)) raise_flag(a.flags, PW_FLAG_WAIT_TIMEOUT);
     }
   } else {
     // ---------------------------------------------------------- epilogue
-    const uint32_t ew = warp - kEpiWarp0;         // 0..3
-    const uint32_t quarter = warp % 4u;           // TMEM lane quarter this warp may access
+    const uint32_t ew = warp - kEpiWarp0;          // 0..7
+    const uint32_t quarter = warp % 4u;            // TMEM lane quarter this warp may access
+    const uint32_t half = ew / 4u;                 // owns chunks half, half + 2
     const uint32_t r_local = quarter * 32u + lane;  // tile row owned by this thread
     const uint32_t etid = ew * 32u + lane;
-    uint32_t buf = 0, bphase = 0;
+    const uint32_t lane_base = (quarter * 32u) << 16;
+    const uint32_t stash = tmem + lane_base + NACC * (uint32_t)kTN;  // fused: gate sums
+    uint32_t acc_slot = 0, aphase = 0;
+    uint32_t cur_group = 0xffffffffu;
     for (uint32_t u = u_begin; u < u_end; ++u) {
-      const GemvGroup grp = a.groups[u / tpg];
+      const uint32_t gi = u / tpg;
+      const GemvGroup grp = a.groups[gi];
       const uint32_t row0 = (u % tpg) * kTileRows;
-      // token scales and this tile's weight-scale row
+      const uint32_t cnt = min(grp.count, (uint32_t)kTN);
+      const uint32_t nch = (cnt + 31u) / 32u;
+      // token scales ([kb][t], reloaded when the group changes) and this
+      // tile's weight-scale rows
       named_bar_sync(1, kEpiThreads);
-      for (uint32_t i = etid; i < (uint32_t)TN * kblocks; i += kEpiThreads) {
-        const uint32_t t = i / kblocks, kb = i % kblocks;
-        sh.xs[t * 32u + kb] = t < grp.count ? __ldg(a.x_scales + (size_t)(grp.tok_begin + t) * kblocks + kb) : 0.0f;
+      if (gi != cur_group) {
+        for (uint32_t i = etid; i < (uint32_t)kTN * kblocks; i += kEpiThreads) {
+          const uint32_t t = i / kblocks, kb = i % kblocks;
+          sh.xs[kb * kTN + t] = t < cnt ? __ldg(a.x_scales + (size_t)(grp.tok_begin + t) * kblocks + kb) : 0.0f;
+        }
+        cur_group = gi;
       }
       {
         const uint32_t srow = row0 / 128u;
@@ -321,92 +377,87 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       }
       named_bar_sync(1, kEpiThreads);
 
-      float acc[TN];
+      float2 acc[kThreadChunks][16];
 #pragma unroll
-      for (int t = 0; t < TN; ++t) acc[t] = 0.0f;
-      const uint32_t lane_base = (quarter * 32u) << 16;
-      const uint32_t stash = tmem + lane_base + 4u * TN;  // gate sums (fused)
-
-      for (uint32_t st = 0; st < per_tile; ++st) {
-        const uint32_t m = st / kcs, kc = st % kcs;
-        if (MATS == 2 && st == kcs) {
-          // gate finished: park its sums in TMEM and start the up sums
+      for (int m = 0; m < MATS; ++m) {
+        if (m == 1) {
+          // gate finished: park its sums in the stash slot, start the up sums
 #pragma unroll
-          for (int c = 0; c < TN; c += 32) tmem_st32(stash + c, &acc[c]);
+          for (int q = 0; q < kThreadChunks; ++q) {
+            const uint32_t ch = half + 2u * (uint32_t)q;
+            if (ch < nch) tmem_st32(stash + ch * 32u, acc[q]);
+          }
           tmem_wait_st();
-#pragma unroll
-          for (int t = 0; t < TN; ++t) acc[t] = 0.0f;
         }
-        const bool ok = bwait(sh, &sh.tfull[buf], bphase, a.flags);
-        tc_fence_after();
-        if (ok) {
 #pragma unroll
-          for (uint32_t j = 0; j < 2; ++j) {
-            const uint32_t kb = kc * 2u + j;
-            if (kb >= kblocks) break;
-            const float ws = sh.ws[m * 32u + kb];
+        for (int q = 0; q < kThreadChunks; ++q)
 #pragma unroll
-            for (int c = 0; c < TN; c += 32) {
-              float v[32];
-              tmem_ld32(tmem + lane_base + buf * (2u * TN) + j * TN + c, v);
-              tmem_wait_ld();
+          for (int i = 0; i < 16; ++i) acc[q][i] = make_float2(0.0f, 0.0f);
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+          const bool ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
+          tc_fence_after();
+          if (ok) {
+            const float ws = sh.ws[m * 32 + kb];
+            const float *xrow = sh.xs + kb * kTN;
 #pragma unroll
-              for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(v[i], ws * sh.xs[(c + i) * 32u + kb], acc[c + i]);
+            for (int q = 0; q < kThreadChunks; ++q) {
+              const uint32_t ch = half + 2u * (uint32_t)q;
+              if (ch < nch) {
+                float v[32];
+                tmem_ld32(tmem + lane_base + acc_slot * (uint32_t)kTN + ch * 32u, v);
+                tmem_wait_ld();
+                promote<32>(acc[q], v, ws, xrow + ch * 32u);
+              }
             }
           }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.tempty[buf]);
-        if (++buf == 2u) {
-          buf = 0;
-          bphase ^= 1u;
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.tempty[acc_slot]);
+          if (++acc_slot == NACC) {
+            acc_slot = 0;
+            aphase ^= 1u;
+          }
         }
       }
 
-      // outputs: thread owns row row0 + r_local, all TN token columns
+      // outputs: thread owns row row0 + r_local and token chunks half, half + 2
       const uint32_t r = row0 + r_local;
       if (KIND != 2) {
 #pragma unroll
-        for (int t = 0; t < TN; ++t) {
-          if ((uint32_t)t < grp.count) {
-            const float out = a.round_bf16 ? round_bf16(acc[t]) : acc[t];
-            if (!finite(out)) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
-            a.out[(size_t)(grp.tok_begin + t) * a.out_stride + r] = out;
+        for (int q = 0; q < kThreadChunks; ++q) {
+          const uint32_t ch = half + 2u * (uint32_t)q;
+          if (ch < nch) {
+            float *dst = a.out + (size_t)(grp.tok_begin + ch * 32u) * a.out_stride + r;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (ch * 32u + (uint32_t)i < cnt) {
+                const float v = el(acc[q], i);
+                const float out = a.round_bf16 ? round_bf16(v) : v;
+                if (!finite(out)) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
+                dst[(size_t)i * a.out_stride] = out;
+              }
+            }
           }
         }
       } else {
-        // staged SwiGLU (gate sums back from TMEM, up sums in registers), then
-        // the hidden's dynamic FP8 quantization over this tile's 128 rows
-        // (one quantization group of the down input)
-#pragma unroll
-        for (int c = 0; c < TN; c += 32) {
-          float g[32];
-          tmem_ld32(stash + c, g);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int t = c + i;
-            const float h = (uint32_t)t < grp.count ? staged_swiglu(g[i], acc[t]) : 0.0f;
-            if (!finite(h)) raise_flag(a.flags, PW_FLAG_NONFINITE_FUSED);
-            acc[t] = h;
-            if (a.out && (uint32_t)t < grp.count) a.out[(size_t)(grp.tok_begin + t) * a.out_stride + r] = h;
-            float mx = fabsf(h);
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            if (lane == 0) sh.amax[ew * TN + t] = mx;
-          }
-        }
-        named_bar_sync(1, kEpiThreads);
+        // bf16(gate) (from the stash) and bf16(up) (registers): the staged
+        // SwiGLU's first roundings; k_swiglu_quant finishes the hidden
         const uint32_t I = a.rows;
 #pragma unroll
-        for (int t = 0; t < TN; ++t) {
-          if ((uint32_t)t < grp.count) {
-            const float M = fmaxf(fmaxf(sh.amax[t], sh.amax[TN + t]), fmaxf(sh.amax[2 * TN + t], sh.amax[3 * TN + t]));
-            const float sc = __fdiv_rn(fmaxf(M, 1.0e-10f), 448.0f);
-            const float q = fminf(fmaxf(__fdiv_rn(acc[t], sc), -448.0f), 448.0f);
-            a.q_codes[(size_t)(grp.tok_begin + t) * I + r] = (uint8_t)(encode2(q, 0.0f) & 0xffu);
-            if (r_local == 0) a.q_scales[(size_t)(grp.tok_begin + t) * (I / 128u) + row0 / 128u] = sc;
+        for (int q = 0; q < kThreadChunks; ++q) {
+          const uint32_t ch = half + 2u * (uint32_t)q;
+          if (ch < nch) {
+            float g[32];
+            tmem_ld32(stash + ch * 32u, g);
+            tmem_wait_ld();
+            const size_t base = (size_t)(grp.tok_begin + ch * 32u) * I + r;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (ch * 32u + (uint32_t)i < cnt) {
+                a.gate_bf16[base + (size_t)i * I] = (uint16_t)(__float_as_uint(round_bf16(g[i])) >> 16);
+                a.up_bf16[base + (size_t)i * I] = (uint16_t)(__float_as_uint(round_bf16(el(acc[q], i))) >> 16);
+              }
+            }
           }
         }
       }
@@ -418,34 +469,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   __syncthreads();
   tc_fence_after();
   if (warp == kMmaWarp)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTmemCols)
                  : "memory");
 }
 
-template <int KIND, int TN>
+template <int KIND>
 static cudaError_t launch_one(const GemmArgs &a, int grid, cudaStream_t stream) {
-  using C = Cfg<KIND, TN>;
+  using C = Cfg<KIND>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<KIND, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  return launch_kernel(k_gemm_tc<KIND, TN>, dim3(grid), dim3(kThreads), C::SMEM, stream, a);
+  return launch_kernel(k_gemm_tc<KIND>, dim3(grid), dim3(kThreads), C::SMEM, stream, a);
 }
 
 }  // namespace tc
 
-int gemm_tc_tokens(int kind) { return kind == 2 ? 64 : 128; }
+int gemm_tc_tokens(int) { return tc::kTN; }
 
 cudaError_t launch_gemm_tc(int kind, const GemmArgs &a, int grid, cudaStream_t stream) {
   const GemvArgs &g = a.g;
   if (g.K == 0 || g.K % 128u || g.K > 4096u || g.rows % tc::kTileRows || grid <= 0 || g.layout != PW_LAYOUT_PLAIN)
     return cudaErrorInvalidValue;
   switch (kind) {
-    case 0: return tc::launch_one<0, 128>(a, grid, stream);
-    case 2: return tc::launch_one<2, 64>(a, grid, stream);
-    case 3: return tc::launch_one<3, 128>(a, grid, stream);
+    case 0: return tc::launch_one<0>(a, grid, stream);
+    case 2: return tc::launch_one<2>(a, grid, stream);
+    case 3: return tc::launch_one<3>(a, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -72,18 +72,21 @@ struct GemvArgs {
   uint32_t *flags;
   uint32_t early_weights;        // PDL: weights and groups are ready before the predecessor
                                  //   ends, so the producer may stream them before waiting
+  uint16_t *gate_bf16;           // tcgen05 kind 2: bf16(gate) and bf16(up) [*, rows], the
+  uint16_t *up_bf16;             //   staged SwiGLU's inputs (k_swiglu_quant finishes it)
 };
 
-// Wide-width grouped GEMM (tcgen05): the GEMV arguments plus a TMA map of
-// the activation codes [rows, K] (view {128 B, rows, K/128}, box {128, TN, 2}).
+// Wide-width grouped GEMM (tcgen05): the GEMV arguments plus TMA maps of the
+// activation codes [rows, K] (view {128 B, rows, K/128}); map i has a box of
+// {128, 32 (i + 1) tokens, 2} so that a group loads only its own 32-token chunks.
 struct GemmArgs {
   GemvArgs g;
-  CUtensorMap xmap;
+  CUtensorMap xmap[4];
 };
 // Tokens per group (TN) of the tcgen05 GEMM for a kind (0: 128, 2: 64, 3: 128).
 int gemm_tc_tokens(int kind);
 cudaError_t launch_gemm_tc(int kind, const GemmArgs &args, int grid, cudaStream_t stream);
-bool encode_act_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows);
+bool encode_act_maps(CUtensorMap (&out)[4], const void *base, uint32_t rows, uint32_t cols);
 cudaError_t launch_gather_rows(const uint8_t *codes, const float *scales, const uint32_t *idx, uint32_t n,
                                uint32_t K, uint8_t *out_codes, float *out_scales, cudaStream_t stream);
 
@@ -138,6 +141,10 @@ cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint
                             cudaStream_t stream);
 cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const float *placement_w,
                            uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream);
+// Staged SwiGLU of bf16 gate/up [rows, cols] followed by the hidden's dynamic
+// FP8 quantization (per 128 values); h (f32, optional) receives the SwiGLU.
+cudaError_t launch_swiglu_quant(const uint16_t *gate, const uint16_t *up, uint32_t rows, uint32_t cols, float *h,
+                                uint8_t *codes, float *scales, uint32_t *flags, cudaStream_t stream);
 cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t n, uint32_t *flags,
                           cudaStream_t stream);
 cudaError_t launch_validate_fp8(const uint8_t *w, uint64_t n, const float *s, uint64_t ns,

@@ -533,4 +533,56 @@ cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t
   return cudaGetLastError();
 }
 
+// ------------------------------------- staged SwiGLU + hidden quantization
+// The wide (tcgen05) gate/up kernel stores bf16(gate) and bf16(up), the first
+// two roundings of the staged SwiGLU; this pass finishes it at full occupancy:
+// h = bf16(bf16(g / (1 + exp(-g))) * u) (kernels/block_fp8_gemv.metal:139),
+// then the down input's dynamic FP8 quantization exactly as k_quantize.  One
+// warp per 128-value group; lane l holds values 4l..4l+3.
+__global__ void k_swiglu_quant(const uint16_t *__restrict__ gate, const uint16_t *__restrict__ up, uint64_t groups,
+                               float *__restrict__ h, uint8_t *__restrict__ codes, float *__restrict__ scales,
+                               uint32_t *flags) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint64_t warp_global = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32u;
+  const uint32_t lane = threadIdx.x % 32u;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) / 32u;
+  for (uint64_t grp = warp_global; grp < groups; grp += nwarps) {
+    const uint2 gq = __ldg(reinterpret_cast<const uint2 *>(gate + grp * 128u) + lane);
+    const uint2 uq = __ldg(reinterpret_cast<const uint2 *>(up + grp * 128u) + lane);
+    const uint32_t gw[2] = {gq.x, gq.y}, uw[2] = {uq.x, uq.y};
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float g = __uint_as_float((k & 1) ? (gw[k / 2] & 0xffff0000u) : (gw[k / 2] << 16));
+      const float u = __uint_as_float((k & 1) ? (uw[k / 2] & 0xffff0000u) : (uw[k / 2] << 16));
+      v[k] = staged_swiglu(g, u);
+    }
+    const bool ok = finite(v[0]) && finite(v[1]) && finite(v[2]) && finite(v[3]);
+    if (!ok) raise_flag(flags, PW_FLAG_NONFINITE_FUSED);
+    if (h) reinterpret_cast<float4 *>(h + grp * 128u)[lane] = make_float4(v[0], v[1], v[2], v[3]);
+    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float scale = __fdiv_rn(fmaxf(m, 1.0e-10f), 448.0f);
+    auto q = [&](float val) { return fminf(fmaxf(__fdiv_rn(val, scale), -448.0f), 448.0f); };
+    const uint32_t lo = encode2(q(v[0]), q(v[1]));
+    const uint32_t hi = encode2(q(v[2]), q(v[3]));
+    reinterpret_cast<uint32_t *>(codes + grp * 128u)[lane] = lo | (hi << 16);
+    if (lane == 0) scales[grp] = scale;
+  }
+}
+
+cudaError_t launch_swiglu_quant(const uint16_t *gate, const uint16_t *up, uint32_t rows, uint32_t cols, float *h,
+                                uint8_t *codes, float *scales, uint32_t *flags, cudaStream_t stream) {
+  if (cols % 128u) return cudaErrorInvalidValue;
+  const uint64_t groups = (uint64_t)rows * (cols / 128u);
+  if (groups == 0) return cudaSuccess;
+  const int threads = 256;
+  uint64_t blocks = (groups * 32u + threads - 1) / threads;
+  if (blocks > 148u * 8u) blocks = 148u * 8u;
+  return launch_kernel(k_swiglu_quant, dim3((unsigned)blocks), dim3(threads), 0, stream, gate, up, groups, h, codes,
+                       scales, flags);
+}
+
 }  // namespace pw

@@ -45,18 +45,22 @@ static EncodeTiledFn encode_fn() {
 uint32_t map_box_rows(uint32_t layout) { return layout == PW_LAYOUT_PLAIN ? 128u : 64u; }
 
 // Activation codes [rows, cols] for the tcgen05 GEMM: view {128 B, rows,
-// k-blocks}, box {128, box_rows tokens, 2 k-blocks}; rows past the end of the
-// buffer read as zeros.
-bool encode_act_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows) {
+// k-blocks}, boxes {128, 32 / 64 / 96 / 128 tokens, 2 k-blocks}; rows past the
+// end of the buffer read as zeros.
+bool encode_act_maps(CUtensorMap (&out)[4], const void *base, uint32_t rows, uint32_t cols) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || cols % 128u || rows == 0) return false;
   cuuint64_t dims[3] = {128u, rows, cols / 128u};
   cuuint64_t strides[2] = {cols, 128u};
-  cuuint32_t box[3] = {128u, box_rows, 2u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
-  return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  for (uint32_t i = 0; i < 4; ++i) {
+    cuuint32_t box[3] = {128u, 32u * (i + 1u), 2u};
+    if (fn(&out[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  return true;
 }
 
 // The weight is viewed as {128 B, rows, k-blocks} with strides {cols, 128}:
@@ -542,7 +546,7 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
       if (wide) {
         GemmArgs A{};
         A.g = a;
-        if (!encode_act_map(&A.xmap, dc, width, K, (uint32_t)gemm_tc_tokens(0)))
+        if (!encode_act_maps(A.xmap, dc, width, K))
           return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activations");
         CK(launch_gemm_tc(0, A, grid, rt->stream));
       } else {
@@ -640,7 +644,7 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
   const int grid_gu = grid_for(rt, units_hint * (I / 128u));
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   {
-    ProfScope ps(rt, P_GATEUP, fused ? 1 : 3);
+    ProfScope ps(rt, P_GATEUP, fused ? 2 : 3);
     GemmArgs A{};
     A.g = gemv_args(rt, gu, n_groups, I, H, PW_LAYOUT_PLAIN);
     A.g.n_groups_dev = n_groups_dev;
@@ -648,14 +652,16 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
     A.g.x_scales = xsg;
     A.g.out_stride = I;
     if (fused) {
-      if (!encode_act_map(&A.xmap, xg, slots, H, (uint32_t)gemm_tc_tokens(2)))
+      // gate and up in one kernel over shared activation tiles, bf16 out; the
+      // staged SwiGLU + the hidden's quantization follow at full occupancy
+      if (!encode_act_maps(A.xmap, xg, slots, H))
         return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activations");
-      A.g.out = hidden;  // may be null
-      A.g.q_codes = hc;
-      A.g.q_scales = hs;
+      A.g.gate_bf16 = reinterpret_cast<uint16_t *>(gate_tmp);
+      A.g.up_bf16 = reinterpret_cast<uint16_t *>(up_tmp);
       CK(launch_gemm_tc(2, A, grid_gu, rt->stream));
+      CK(launch_swiglu_quant(A.g.gate_bf16, A.g.up_bf16, slots, I, hidden, hc, hs, rt->d_flags, rt->stream));
     } else {
-      if (!encode_act_map(&A.xmap, xg, slots, H, (uint32_t)gemm_tc_tokens(0)))
+      if (!encode_act_maps(A.xmap, xg, slots, H))
         return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activations");
       A.g.out = gate_tmp;
       CK(launch_gemm_tc(0, A, grid_gu, rt->stream));
@@ -677,7 +683,7 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
   D.g.out = down;
   D.g.out_stride = H;
   D.g.round_bf16 = down_round;
-  if (!encode_act_map(&D.xmap, hc, slots, I, (uint32_t)gemm_tc_tokens(0)))
+  if (!encode_act_maps(D.xmap, hc, slots, I))
     return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the hidden codes");
   ProfScope ps(rt, P_DOWN, 1);
   CK(launch_gemm_tc(0, D, grid_for(rt, units_hint * (H / 128u)), rt->stream));
@@ -713,13 +719,14 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
     float *dy = call.host() ? ar.take<float>((size_t)width * H) : y;
     uint8_t *xc = ar.take<uint8_t>((size_t)width * H);
     float *xs = ar.take<float>((size_t)width * H / 128u);
+    const bool wide = width >= kWideProjection;
     float *hid = fused ? nullptr : ar.take<float>((size_t)width * I);
-    float *gt = fused ? nullptr : ar.take<float>((size_t)width * I);
-    float *ut = fused ? nullptr : ar.take<float>((size_t)width * I);
+    // the wide fused chain stages bf16 gate/up here
+    float *gt = fused && !wide ? nullptr : ar.take<float>((size_t)width * I);
+    float *ut = fused && !wide ? nullptr : ar.take<float>((size_t)width * I);
     uint8_t *hc = ar.take<uint8_t>((size_t)width * I);
     float *hs = ar.take<float>((size_t)width * I / 128u);
     CUtensorMap *dm = ar.take<CUtensorMap>(3);
-    const bool wide = width >= kWideProjection;
     const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
     std::vector<GemvGroup> gu = width_groups(width, w->gate, &w->up, dm, dm ? dm + 1 : nullptr, chunk);
     std::vector<GemvGroup> dn = width_groups(width, w->down, nullptr, dm ? dm + 2 : nullptr, nullptr, chunk);
@@ -900,8 +907,8 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
       }
     }
     float *hid = fused ? nullptr : ar.take<float>((size_t)P * I);
-    float *gt = fused ? nullptr : ar.take<float>((size_t)P * I);
-    float *ut = fused ? nullptr : ar.take<float>((size_t)P * I);
+    float *gt = fused && !wide ? nullptr : ar.take<float>((size_t)P * I);
+    float *ut = fused && !wide ? nullptr : ar.take<float>((size_t)P * I);
     uint8_t *hc = ar.take<uint8_t>((size_t)P * I);
     float *hs = ar.take<float>((size_t)P * I / 128u);
     float *down = ar.take<float>((size_t)P * H);
@@ -1082,8 +1089,8 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     so.n_groups = ar.take<uint32_t>(1);
     so.counters = ar.take<uint32_t>(4);
     float *hid = fused ? nullptr : ar.take<float>((size_t)P * I);
-    float *gt = fused ? nullptr : ar.take<float>((size_t)P * I);
-    float *ut = fused ? nullptr : ar.take<float>((size_t)P * I);
+    float *gt = fused && !wide ? nullptr : ar.take<float>((size_t)P * I);
+    float *ut = fused && !wide ? nullptr : ar.take<float>((size_t)P * I);
     uint8_t *hc = ar.take<uint8_t>((size_t)P * I);
     float *hs = ar.take<float>((size_t)P * I / 128u);
     float *down = ar.take<float>((size_t)P * H);
