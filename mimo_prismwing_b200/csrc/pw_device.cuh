@@ -18,14 +18,13 @@
 namespace pw {
 
 // ------------------------------------------------------------ number formats
+// Branch-free (selects): an unrolled epilogue stays one basic block.
 __device__ __forceinline__ float round_bf16(float v) {
   const uint32_t bits = __float_as_uint(v);
-  if ((bits & 0x7f800000u) == 0x7f800000u) {
-    if ((bits & 0x007fffffu) == 0u) return v;
-    return __uint_as_float((((bits >> 16) & 0xffffu) | 0x0040u) << 16);
-  }
-  const uint32_t bias = 0x7fffu + ((bits >> 16) & 1u);
-  return __uint_as_float((bits + bias) & 0xffff0000u);
+  const uint32_t rn = (bits + 0x7fffu + ((bits >> 16) & 1u)) & 0xffff0000u;  // finite: RNE
+  const uint32_t qnan = (bits | 0x00400000u) & 0xffff0000u;                  // NaN: quiet, payload kept
+  const uint32_t a = bits & 0x7fffffffu;
+  return __uint_as_float(a > 0x7f800000u ? qnan : (a == 0x7f800000u ? bits : rn));
 }
 
 // 4 packed e4m3 bytes -> 4 floats (byte 0 -> out[0]).  Exact.

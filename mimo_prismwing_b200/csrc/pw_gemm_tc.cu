@@ -422,23 +422,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
 
       // outputs: thread owns row row0 + r_local and token chunks half, half + 2
       const uint32_t r = row0 + r_local;
+      // (branch-free bodies: a guard per element would split the unrolled
+      // stores into serial basic blocks, ~3x slower)
       if (KIND != 2) {
+        const bool rb = a.round_bf16 != 0u;
+        bool bad = false;
 #pragma unroll
         for (int q = 0; q < kThreadChunks; ++q) {
           const uint32_t ch = half + 2u * (uint32_t)q;
           if (ch < nch) {
             float *dst = a.out + (size_t)(grp.tok_begin + ch * 32u) * a.out_stride + r;
+            if (ch * 32u + 32u <= cnt) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              if (ch * 32u + (uint32_t)i < cnt) {
+              for (int i = 0; i < 32; ++i) {
                 const float v = el(acc[q], i);
-                const float out = a.round_bf16 ? round_bf16(v) : v;
-                if (!finite(out)) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
+                const float out = rb ? round_bf16(v) : v;
+                bad |= !finite(out);
                 dst[(size_t)i * a.out_stride] = out;
+              }
+            } else {
+              const uint32_t tend = cnt - ch * 32u;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float v = el(acc[q], i);
+                const float out = rb ? round_bf16(v) : v;
+                const bool live = (uint32_t)i < tend;
+                bad |= live && !finite(out);
+                if (live) dst[(size_t)i * a.out_stride] = out;
               }
             }
           }
         }
+        if (bad) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
       } else {
         // bf16(gate) (from the stash) and bf16(up) (registers): the staged
         // SwiGLU's first roundings; k_swiglu_quant finishes the hidden
@@ -450,12 +465,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
             float g[32];
             tmem_ld32(stash + ch * 32u, g);
             tmem_wait_ld();
-            const size_t base = (size_t)(grp.tok_begin + ch * 32u) * I + r;
+            uint16_t *gd = a.gate_bf16 + (size_t)(grp.tok_begin + ch * 32u) * I + r;
+            uint16_t *ud = a.up_bf16 + (size_t)(grp.tok_begin + ch * 32u) * I + r;
+            const uint32_t tend = min(32u, cnt - ch * 32u);
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              if (ch * 32u + (uint32_t)i < cnt) {
-                a.gate_bf16[base + (size_t)i * I] = (uint16_t)(__float_as_uint(round_bf16(g[i])) >> 16);
-                a.up_bf16[base + (size_t)i * I] = (uint16_t)(__float_as_uint(round_bf16(el(acc[q], i))) >> 16);
+              const uint16_t gb = (uint16_t)(__float_as_uint(round_bf16(g[i])) >> 16);
+              const uint16_t ub = (uint16_t)(__float_as_uint(round_bf16(el(acc[q], i))) >> 16);
+              if ((uint32_t)i < tend) {
+                gd[(size_t)i * I] = gb;
+                ud[(size_t)i * I] = ub;
               }
             }
           }

@@ -119,3 +119,19 @@ def test_wide_moe_layer_device_router_vs_oracle(rt, tokens):
     ref = O.routed_layer(H(x), osel, owts, bank_arrays(bank), O.ACC_F64, O.EXP_SLEEF)
     assert_close_bf16(H(ex.output), ref, what=f"wide moe layer T{tokens}")
     assert ex.expert_rows == tokens * 8
+
+
+@pytest.mark.parametrize("experts,hidden,tokens", [(256, 4096, 64), (256, 4096, 67), (100, 1024, 70),
+                                                   (256, 4096, 2048)])
+def test_wide_route_bit_exact_vs_oracle(rt, experts, hidden, tokens):
+    # >= 64 tokens take the tiled router (4 tokens x 8 experts per CTA);
+    # ragged token and expert tiles included
+    from mimo_prismwing_b200 import synth
+    w, bias = synth.router(experts, hidden, 51, "cuda")
+    x = synth.activations(tokens, hidden, 700 + tokens, "cuda")
+    sel, wts, st = rt.route(x, w, bias)
+    logits = O.router_logits(H(x), H(w.view(torch.int16)).view(np.uint16))
+    osel, owts, _, _, ties = O.noaux_topk(logits, H(bias))
+    assert np.array_equal(H(sel).astype(np.uint32), osel)
+    assert np.array_equal(H(wts).view(np.uint32), owts.view(np.uint32))
+    assert st["boundary_tie_rows"] == ties
