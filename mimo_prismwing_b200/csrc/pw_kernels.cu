@@ -136,15 +136,16 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
 }
 
 // Prefill-width router logits: the same per-(token, expert) order as
-// k_router_logits, for a tile of 4 tokens x 8 experts per CTA so that each
-// activation and weight chunk loaded (and converted to f64) feeds several FMA
-// chains.  Thread (warp w, lane l) runs the 32 lane chains of its columns; the
-// 32-lane xor tree is evaluated as a transpose-reduce (at each level lane l
-// adds its xor partner's value for the half of the pairs it keeps): every
-// pair gets the same tree of commutative additions as the butterfly, in 31
-// exchanges instead of 160.  Lane l ends with pair l (token l/8, expert l%8);
-// the 8 warp sums are then added in warp order.
-constexpr int kTileTok = 4, kTileExp = 8;
+// k_router_logits, for a tile of 8 tokens x 8 experts per CTA so that each
+// activation and weight value loaded (and converted to f64) feeds 8 FMA
+// chains.  Thread (warp w, lane l) runs the 64 lane chains of its columns,
+// four columns at a time; the 32-lane xor tree is evaluated as a
+// transpose-reduce (at each level lane l adds its xor partner's value for the
+// half of the pairs it keeps): every pair gets the same tree of commutative
+// additions as the butterfly, in 62 exchanges instead of 320.  Lane l ends
+// with pairs 2l and 2l+1 (token l/4, experts 2(l%4), 2(l%4)+1); the 8 warp
+// sums are then added in warp order.
+constexpr int kTileTok = 8, kTileExp = 8;
 
 __global__ void __launch_bounds__(256) k_router_logits_tiled(const float *__restrict__ x, uint32_t tokens,
                                                              const uint16_t *__restrict__ w, uint32_t experts,
@@ -162,46 +163,44 @@ __global__ void __launch_bounds__(256) k_router_logits_tiled(const float *__rest
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const uint32_t c0 = 512u * sl + 8u * lane + 256u * (uint32_t)j;
-      double xd[kTileTok][8];
+      // each 8-column chunk in two halves of 4 (the chains still run i = 0..7)
 #pragma unroll
-      for (int t = 0; t < kTileTok; ++t) {
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-        if (t0 + t < tokens) {
-          const float4 *xp = reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * hidden + c0);
-          a = __ldg(xp);
-          b = __ldg(xp + 1);
+      for (int hf = 0; hf < 2; ++hf) {
+        double xd[kTileTok][4];
+#pragma unroll
+        for (int t = 0; t < kTileTok; ++t) {
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (t0 + t < tokens) a = __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * hidden + c0) + hf);
+          xd[t][0] = a.x; xd[t][1] = a.y; xd[t][2] = a.z; xd[t][3] = a.w;
         }
-        xd[t][0] = a.x; xd[t][1] = a.y; xd[t][2] = a.z; xd[t][3] = a.w;
-        xd[t][4] = b.x; xd[t][5] = b.y; xd[t][6] = b.z; xd[t][7] = b.w;
-      }
 #pragma unroll
-      for (int e = 0; e < kTileExp; ++e) {
-        const uint4 wq = e0 + e < experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)(e0 + e) * hidden + c0))
-                                          : make_uint4(0u, 0u, 0u, 0u);
-        const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
-        double wd[8];
+        for (int e = 0; e < kTileExp; ++e) {
+          const uint2 wq = e0 + e < experts
+                               ? __ldg(reinterpret_cast<const uint2 *>(w + (size_t)(e0 + e) * hidden + c0) + hf)
+                               : make_uint2(0u, 0u);
+          const double wd[4] = {(double)__uint_as_float(wq.x << 16), (double)__uint_as_float(wq.x & 0xffff0000u),
+                                (double)__uint_as_float(wq.y << 16), (double)__uint_as_float(wq.y & 0xffff0000u)};
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          wd[i] = (double)__uint_as_float((i & 1) ? (wv[i / 2] & 0xffff0000u) : (wv[i / 2] << 16));
+          for (int t = 0; t < kTileTok; ++t)
 #pragma unroll
-        for (int t = 0; t < kTileTok; ++t)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[t * kTileExp + e] = __fma_rn(xd[t][i], wd[i], acc[t * kTileExp + e]);
+            for (int i = 0; i < 4; ++i) acc[t * kTileExp + e] = __fma_rn(xd[t][i], wd[i], acc[t * kTileExp + e]);
+        }
       }
     }
   }
-  // transpose-reduce over the 32 lanes: 32 pairs -> 1 per lane
+  // transpose-reduce over the 32 lanes: 64 pairs -> 2 per lane (pairs 2l, 2l+1)
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
+  for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
     const bool upper = (lane & (uint32_t)o) != 0u;
 #pragma unroll
-    for (int i = 0; i < o; ++i) {
-      const double send = upper ? acc[i] : acc[i + o];
-      const double keep = upper ? acc[i + o] : acc[i];
+    for (int i = 0; i < n; ++i) {
+      const double send = upper ? acc[i] : acc[i + n];
+      const double keep = upper ? acc[i + n] : acc[i];
       acc[i] = __dadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
     }
   }
-  part[warp][lane] = acc[0];
+  part[warp][2u * lane] = acc[0];
+  part[warp][2u * lane + 1u] = acc[1];
   __syncthreads();
   if (threadIdx.x < (unsigned)(kTileTok * kTileExp)) {
     const uint32_t p = threadIdx.x, t = p / kTileExp, e = p % kTileExp;
