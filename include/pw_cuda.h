@@ -236,6 +236,46 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
                  uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem,
                  pw_stats *stats);
 
+/* ------------------------------------------------- expert parallelism */
+
+/* The reference runs all experts of a layer on one device
+ * (routed_mlp_metal_wide_configured, src/text_endpoint.rs:4750); these calls
+ * split a layer's experts over the GPUs of one node, one process (and one
+ * runtime) per GPU, over NCCL.  NCCL is loaded on first use (libnccl.so.2);
+ * without it these calls return PW_ERR_UNSUPPORTED.
+ *
+ * pw_ep_unique_id: one rank creates the communicator id (128 bytes) and sends
+ * it to the others by any out-of-band channel.
+ * pw_ep_init: collective; rank `rank` of `world` joins.  `timeout_ms` (0 = 60 s)
+ * bounds every wait of this and later expert-parallel calls; a call that runs
+ * out of time, or sees an NCCL error, aborts the communicator and returns
+ * PW_ERR_TIMEOUT / PW_ERR_NCCL, after which the runtime refuses further
+ * expert-parallel calls. */
+int pw_ep_unique_id(void *id, uint32_t bytes);
+int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t bytes, uint32_t timeout_ms);
+int pw_ep_rank(const pw_runtime *rt, int *rank, int *world);
+
+/* Collective routed layer.  Every rank passes its own tokens (x [tokens, H],
+ * tokens may be 0) and a bank holding its experts: rank g owns experts
+ * [g * n, (g + 1) * n) of the router's E = n * world.  Routing is local; token
+ * codes and scales go to the expert owners and bf16 expert outputs come back;
+ * the combine runs on the token's rank in ascending expert order, so y is
+ * bit-identical to pw_moe_layer on one GPU.  Synchronous (no PW_MEM_ASYNC);
+ * stats->unique_experts / expert_rows count this rank's local work. */
+int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,
+                    uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem,
+                    pw_stats *stats);
+
+/* Host-only helper (no GPU): the transfer plan pw_ep_moe_layer derives for
+ * rank `rank` from every rank's expert offsets.  all_offsets[g * (E + 1) + e]
+ * is the first of rank g's placements (expert-major) routed to expert e, with
+ * all_offsets[g * (E + 1) + E] its placement count.  Outputs: n_send[world],
+ * n_recv[world], recv_base[world + 1] (where each source's rows land),
+ * perm[rows received] (received row of each row in expert order: local expert,
+ * then source rank, then the source's order) and expert_begin[E / world + 1]. */
+int pw_ep_plan(const uint32_t *all_offsets, uint32_t world, uint32_t rank, uint32_t experts, uint32_t *n_send,
+               uint32_t *n_recv, uint32_t *recv_base, uint32_t *perm, uint32_t *expert_begin);
+
 /* ------------------------------------------------- allocation-free variant */
 
 /* No counterpart in the reference: an addition of this library.

@@ -4,6 +4,9 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <string>
 
 #include "pw_cuda.h"
 
@@ -141,6 +144,13 @@ cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint
                             cudaStream_t stream);
 cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const float *placement_w,
                            uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream);
+// The same combine over bf16 down rows (the expert-parallel return path; the
+// rows are bf16-rounded, so the result is identical).
+cudaError_t launch_combine_bf16(const uint16_t *down, const uint32_t *slot_place, const float *placement_w,
+                                uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream);
+// out[idx[j]] = bf16 bits of rows[j] (rows already bf16-rounded), j < n.
+cudaError_t launch_scatter_rows_bf16(const float *rows, const uint32_t *idx, uint32_t n, uint32_t cols,
+                                     uint16_t *out, cudaStream_t stream);
 // Staged SwiGLU of bf16 gate/up [rows, cols] followed by the hidden's dynamic
 // FP8 quantization (per 128 values); h (f32, optional) receives the SwiGLU.
 cudaError_t launch_swiglu_quant(const uint16_t *gate, const uint16_t *up, uint32_t rows, uint32_t cols, float *h,
@@ -149,5 +159,27 @@ cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t
                           cudaStream_t stream);
 cudaError_t launch_validate_fp8(const uint8_t *w, uint64_t n, const float *s, uint64_t ns,
                                 unsigned long long *first_bad, uint32_t *flags, cudaStream_t stream);
+
+// NCCL, dlopen'ed on first use (pw_nccl.cu).  Every call that can wait takes
+// a deadline in seconds; ncclInProgress past it means "abort the comm".
+namespace nccl {
+struct Transfer {
+  const void *ptr;
+  size_t bytes;
+  int peer;
+};
+bool load(std::string &err);
+const char *error_string(ncclResult_t r);
+ncclResult_t unique_id(ncclUniqueId *id);
+ncclResult_t init_rank(ncclComm_t *comm, int world, const ncclUniqueId &id, int rank, double deadline_s);
+ncclResult_t async_error(ncclComm_t comm);
+void abort_comm(ncclComm_t comm);
+ncclResult_t destroy(ncclComm_t comm, double deadline_s);
+ncclResult_t all_gather(const void *send, void *recv, size_t count, ncclDataType_t t, ncclComm_t comm,
+                        cudaStream_t s, double deadline_s);
+// One grouped round of point-to-point byte transfers.
+ncclResult_t exchange(const Transfer *sends, int n_sends, const Transfer *recvs, int n_recvs, ncclComm_t comm,
+                      cudaStream_t s, double deadline_s);
+}  // namespace nccl
 
 }  // namespace pw

@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ 
   __syncthreads();
   if (bad) {
     if (tid == 0) raise_flag(flags, PW_FLAG_BAD_EXPERT_COUNT);
-    if (tid == 0) *out.n_groups = 0;
+    if (tid == 0 && out.n_groups) *out.n_groups = 0;
     return;
   }
   // per-expert counts and word prefixes (thread per expert)
@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ 
     }
     out.offsets[experts] = off;
     grp_off[experts] = goff;
-    *out.n_groups = goff;
+    if (out.n_groups) *out.n_groups = goff;
     out.counters[0] = uniq;
     out.counters[1] = off;
     out.counters[2] = maxc;
@@ -443,7 +443,8 @@ __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ 
     for (int k = 0; k < 8; ++k) out.slot_place[t * 8u + k] = pl[k];
   }
   // GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
-  for (uint32_t e = tid; e < experts; e += nt) {
+  // (skipped when the caller runs the experts elsewhere: no group arrays)
+  for (uint32_t e = tid; e < experts && out.gu_groups; e += nt) {
     const uint32_t c = cnt[e];
     for (uint32_t j = 0; j * chunk < c; ++j) {
       GemvGroup g;
@@ -493,7 +494,17 @@ cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint
 // y[t, c] = bf16( sum over t's 8 placements in ascending expert order of
 //                 down[p, c] * w_p )   -- product rounded, then added, from 0
 // (src/text_endpoint.rs:5365-5373; the down rows are already bf16-rounded).
-__global__ void k_combine(const float *__restrict__ down, const uint32_t *__restrict__ slot_place,
+__device__ __forceinline__ float4 load4(const float *row, uint32_t c4) {
+  return __ldg(reinterpret_cast<const float4 *>(row) + c4);
+}
+__device__ __forceinline__ float4 load4(const uint16_t *row, uint32_t c4) {
+  const uint2 q = __ldg(reinterpret_cast<const uint2 *>(row) + c4);
+  return make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xffff0000u), __uint_as_float(q.y << 16),
+                     __uint_as_float(q.y & 0xffff0000u));
+}
+
+template <typename T>
+__global__ void k_combine(const T *__restrict__ down, const uint32_t *__restrict__ slot_place,
                           const float *__restrict__ placement_w, uint32_t tokens, uint32_t hidden,
                           float *__restrict__ y, uint32_t *flags) {
   pdl_wait();
@@ -510,7 +521,7 @@ __global__ void k_combine(const float *__restrict__ down, const uint32_t *__rest
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const float4 d = __ldg(reinterpret_cast<const float4 *>(down + (size_t)pl[k] * hidden) + c4);
+      const float4 d = load4(down + (size_t)pl[k] * hidden, c4);
       acc.x = __fadd_rn(acc.x, __fmul_rn(d.x, wt[k]));
       acc.y = __fadd_rn(acc.y, __fmul_rn(d.y, wt[k]));
       acc.z = __fadd_rn(acc.z, __fmul_rn(d.z, wt[k]));
@@ -530,7 +541,43 @@ cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const 
                            uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream) {
   if (hidden % 4u || tokens == 0) return cudaErrorInvalidValue;
   dim3 grid((hidden / 4u + 255u) / 256u, tokens);
-  return launch_kernel(k_combine, grid, dim3(256), 0, stream, down, slot_place, placement_w, tokens, hidden, y, flags);
+  return launch_kernel(k_combine<float>, grid, dim3(256), 0, stream, down, slot_place, placement_w, tokens, hidden,
+                       y, flags);
+}
+
+cudaError_t launch_combine_bf16(const uint16_t *down, const uint32_t *slot_place, const float *placement_w,
+                                uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream) {
+  if (hidden % 4u || tokens == 0) return cudaErrorInvalidValue;
+  dim3 grid((hidden / 4u + 255u) / 256u, tokens);
+  return launch_kernel(k_combine<uint16_t>, grid, dim3(256), 0, stream, down, slot_place, placement_w, tokens,
+                       hidden, y, flags);
+}
+
+// ------------------------------------------------------ bf16 row scatter
+// out[idx[j]] = bf16 bits of rows[j]: puts the expert-parallel down rows
+// (computed in expert order) back in received order for the return trip.
+__global__ void k_scatter_rows_bf16(const float *__restrict__ rows, const uint32_t *__restrict__ idx, uint32_t n,
+                                    uint32_t cols, uint16_t *__restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t per_row = cols / 4u;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (uint64_t)n * per_row;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t j = (uint32_t)(i / per_row), c4 = (uint32_t)(i % per_row);
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(rows + (size_t)j * cols) + c4);
+    const uint2 q = make_uint2((__float_as_uint(v.x) >> 16) | (__float_as_uint(v.y) & 0xffff0000u),
+                               (__float_as_uint(v.z) >> 16) | (__float_as_uint(v.w) & 0xffff0000u));
+    reinterpret_cast<uint2 *>(out + (size_t)idx[j] * cols)[c4] = q;
+  }
+}
+
+cudaError_t launch_scatter_rows_bf16(const float *rows, const uint32_t *idx, uint32_t n, uint32_t cols,
+                                     uint16_t *out, cudaStream_t stream) {
+  if (cols % 4u) return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+  uint64_t blocks = ((uint64_t)n * (cols / 4u) + 255u) / 256u;
+  if (blocks > 148u * 8u) blocks = 148u * 8u;
+  return launch_kernel(k_scatter_rows_bf16, dim3((unsigned)blocks), dim3(256), 0, stream, rows, idx, n, cols, out);
 }
 
 // --------------------------------------------------------------- row gather

@@ -14,6 +14,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include <cuda.h>
@@ -79,6 +80,20 @@ bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32
 }
 }  // namespace pw
 
+// Expert-parallel state of a runtime (pw_ep_init).
+struct EpState {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+  double timeout_s = 60.0;
+  bool dead = false;                 // aborted after an error or timeout
+  void *scratch = nullptr;           // receive-side buffers, sized per call
+  size_t cap = 0;
+  uint32_t *h_off = nullptr;         // pinned: every rank's expert offsets
+  size_t h_off_cap = 0;
+  void *h_plan = nullptr;            // pinned: row permutation + expert groups
+  size_t h_plan_cap = 0;
+};
+
 struct pw_runtime {
   int device = 0;
   uint32_t flags = 0;
@@ -100,6 +115,7 @@ struct pw_runtime {
   uint32_t launches = 0;
   pw_profile last_profile{};
   std::string err;
+  EpState *ep = nullptr;
 };
 
 namespace {
@@ -386,6 +402,13 @@ void pw_runtime_destroy(pw_runtime *rt) {
   if (!rt) return;
   cudaSetDevice(rt->device);
   if (rt->stream) cudaStreamSynchronize(rt->stream);
+  if (rt->ep) {
+    if (rt->ep->comm) pw::nccl::destroy(rt->ep->comm, rt->ep->timeout_s);
+    if (rt->ep->scratch) cudaFree(rt->ep->scratch);
+    if (rt->ep->h_off) cudaFreeHost(rt->ep->h_off);
+    if (rt->ep->h_plan) cudaFreeHost(rt->ep->h_plan);
+    delete rt->ep;
+  }
   if (rt->scratch) cudaFree(rt->scratch);
   if (rt->d_flags) cudaFree(rt->d_flags);
   if (rt->ev0) cudaEventDestroy(rt->ev0);
@@ -1158,6 +1181,411 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     stats->weight_bytes = per_expert * cnt[0] + (uint64_t)E * H * 2 + E * 4;
   }
   return s;
+}
+
+}  // extern "C"
+
+// ======================================================= expert parallelism
+// One process per GPU; rank g holds experts [g L, (g + 1) L) of the layer's
+// E = L x world (src/text_endpoint.rs:4750 runs all 256 on one device; the
+// partition is this build's).  Every rank routes its own tokens, and every
+// rank takes the same collective steps in the same order:
+//   1. quantize + route + schedule all E experts (expert-major placements,
+//      so the rows for rank g are one contiguous block), gather the codes;
+//   2. all-gather the per-expert placement offsets (E + 1 words per rank)
+//      and wait for them: from here on every rank knows every transfer size;
+//   3. grouped send/recv of FP8 codes and per-128 scales (quantizing before
+//      dispatch is exact: an expert's first step is that quantization);
+//   4. permute the received rows into expert order, run the local experts
+//      (tcgen05 GEMM, or the GEMV for <= 16 rows per expert), and scatter the
+//      bf16-rounded down rows back into received order as bf16;
+//   5. grouped send/recv of the bf16 rows back to their source ranks;
+//   6. the weighted combine in ascending expert order, as on one GPU, so the
+//      layer is bit-identical to pw_moe_layer on the same tokens.
+namespace {
+
+int ep_dead(pw_runtime *rt, int code, const char *what, ncclResult_t r) {
+  pw::nccl::abort_comm(rt->ep->comm);
+  rt->ep->comm = nullptr;
+  rt->ep->dead = true;
+  return fail(rt, code, "%s: %s (communicator aborted)", what,
+              r == ncclInProgress ? "deadline passed" : pw::nccl::error_string(r));
+}
+
+#define NK(expr, what)                                                                         \
+  do {                                                                                         \
+    ncclResult_t r_ = (expr);                                                                  \
+    if (r_ != ncclSuccess) return ep_dead(rt, r_ == ncclInProgress ? PW_ERR_TIMEOUT : PW_ERR_NCCL, what, r_); \
+  } while (0)
+
+// Bounded wait for the runtime's stream; NCCL errors and the deadline abort
+// the communicator (which also ends its kernels).
+int ep_wait(pw_runtime *rt) {
+  const double t0 = now_ms();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(rt->stream);
+    if (q == cudaSuccess) return PW_OK;
+    if (q != cudaErrorNotReady) return fail(rt, PW_ERR_CUDA, "stream: %s", cudaGetErrorString(q));
+    const ncclResult_t a = pw::nccl::async_error(rt->ep->comm);
+    if (a != ncclSuccess && a != ncclInProgress) return ep_dead(rt, PW_ERR_NCCL, "expert-parallel exchange", a);
+    if (now_ms() - t0 > rt->ep->timeout_s * 1e3)
+      return ep_dead(rt, PW_ERR_TIMEOUT, "expert-parallel exchange", ncclInProgress);
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+// The transfer plan of rank r from every rank's expert offsets
+// (all_off[g * (E + 1) + e] = first placement of expert e on rank g; rank r
+// owns experts [r L, (r + 1) L), L = E / G):
+//   n_send[g]    rows r sends to g (its placements of g's experts),
+//   n_recv[g]    rows r receives from g, landing at recv_base[g] (G + 1 words),
+//   perm[j]      received row of the j-th row in expert order (expert, then
+//                source rank, then the source's placement order),
+//   e_begin[le]  first expert-order row of local expert le (L + 1 words).
+void ep_plan(const uint32_t *all_off, uint32_t G, uint32_t r, uint32_t E, uint32_t *n_send, uint32_t *n_recv,
+             uint32_t *recv_base, uint32_t *perm, uint32_t *e_begin) {
+  const uint32_t L = E / G;
+  auto off = [&](uint32_t g, uint32_t e) { return all_off[(size_t)g * (E + 1) + e]; };
+  recv_base[0] = 0;
+  for (uint32_t g = 0; g < G; ++g) {
+    n_send[g] = off(r, (g + 1) * L) - off(r, g * L);
+    n_recv[g] = off(g, (r + 1) * L) - off(g, r * L);
+    recv_base[g + 1] = recv_base[g] + n_recv[g];
+  }
+  uint32_t j = 0;
+  e_begin[0] = 0;
+  for (uint32_t le = 0; le < L; ++le) {
+    const uint32_t e = r * L + le;
+    for (uint32_t g = 0; g < G; ++g) {
+      const uint32_t base = recv_base[g] + (off(g, e) - off(g, r * L));
+      for (uint32_t k = 0; k < off(g, e + 1) - off(g, e); ++k) perm[j++] = base + k;
+    }
+    e_begin[le + 1] = j;
+  }
+}
+
+template <class T>
+int ep_pinned(pw_runtime *rt, T *&buf, size_t &cap, size_t bytes) {
+  if (bytes <= cap) return PW_OK;
+  if (buf) CK(cudaFreeHost(buf));
+  buf = nullptr;
+  cap = 0;
+  void *p = nullptr;
+  CK(cudaMallocHost(&p, bytes));
+  buf = static_cast<T *>(p);
+  cap = bytes;
+  return PW_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pw_ep_unique_id(void *id, uint32_t bytes) {
+  if (!id || bytes < sizeof(ncclUniqueId)) return PW_ERR_ARGUMENT;
+  std::string err;
+  if (!pw::nccl::load(err)) return PW_ERR_UNSUPPORTED;
+  ncclUniqueId u;
+  if (pw::nccl::unique_id(&u) != ncclSuccess) return PW_ERR_NCCL;
+  memcpy(id, &u, sizeof u);
+  return PW_OK;
+}
+
+int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t bytes, uint32_t timeout_ms) {
+  if (!rt) return PW_ERR_ARGUMENT;
+  if (!id || bytes < sizeof(ncclUniqueId)) return fail(rt, PW_ERR_ARGUMENT, "NCCL unique id must be %zu bytes",
+                                                       sizeof(ncclUniqueId));
+  if (world < 1 || rank < 0 || rank >= world) return fail(rt, PW_ERR_ARGUMENT, "rank %d of %d", rank, world);
+  if (rt->ep) return fail(rt, PW_ERR_ARGUMENT, "expert parallelism is already initialised on this runtime");
+  std::string err;
+  if (!pw::nccl::load(err)) return fail(rt, PW_ERR_UNSUPPORTED, "%s", err.c_str());
+  CK(cudaSetDevice(rt->device));
+  EpState *ep = new (std::nothrow) EpState();
+  if (!ep) return fail(rt, PW_ERR_ARGUMENT, "out of host memory");
+  ep->rank = rank;
+  ep->world = world;
+  ep->timeout_s = timeout_ms ? timeout_ms / 1e3 : 60.0;
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof u);
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = pw::nccl::init_rank(&comm, world, u, rank, ep->timeout_s);
+  if (r != ncclSuccess) {
+    pw::nccl::abort_comm(comm);
+    delete ep;
+    return fail(rt, r == ncclInProgress ? PW_ERR_TIMEOUT : PW_ERR_NCCL, "ncclCommInitRank (rank %d of %d): %s", rank,
+                world, r == ncclInProgress ? "peers did not join before the deadline" : pw::nccl::error_string(r));
+  }
+  ep->comm = comm;
+  rt->ep = ep;
+  return PW_OK;
+}
+
+int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,
+                    uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem, pw_stats *stats) {
+  if (!rt) return PW_ERR_ARGUMENT;
+  EpState *ep = rt->ep;
+  if (!ep || !ep->comm)
+    return fail(rt, PW_ERR_ARGUMENT, ep ? "the expert-parallel communicator was aborted" : "pw_ep_init was not called");
+  if (!bank || (tokens && (!x || !y))) return fail(rt, PW_ERR_ARGUMENT, "null argument");
+  int s;
+  if ((s = check_router(rt, router)) != PW_OK) return s;
+  const uint32_t G = (uint32_t)ep->world, r = (uint32_t)ep->rank;
+  const uint32_t L = bank->n, E = router->experts, H = bank->hidden, I = bank->inter;
+  if (E != L * G) return fail(rt, PW_ERR_SHAPE, "router has %u experts; %u ranks x %u local experts", E, G, L);
+  if (bank->hidden != router->hidden) return fail(rt, PW_ERR_SHAPE, "router and expert bank disagree");
+  if (tokens > 2048u) return fail(rt, PW_ERR_UNSUPPORTED, "at most 2048 tokens per rank and call");
+  if (mem & PW_MEM_ASYNC) return fail(rt, PW_ERR_ARGUMENT, "expert-parallel layers are synchronous");
+  CK(cudaSetDevice(rt->device));
+  const uint32_t P = tokens * 8u, Hs = H / 128u, Is = I / 128u;
+  Call call{rt, mem, stats, 0};
+  if ((s = call.begin()) != PW_OK) return s;
+
+  // ---- phase 1: local routing, schedule, send rows (runtime scratch)
+  Arena ar;
+  float *dx = nullptr, *dy = nullptr;
+  uint32_t *sel = nullptr, *alloff = nullptr;
+  float *wts = nullptr;
+  uint8_t *xsend = nullptr;
+  float *ssend = nullptr;
+  uint16_t *ret = nullptr;
+  ScheduleOut so{};
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1) {
+      if ((s = ensure_scratch(rt, ar.off)) != PW_OK) return s;
+      ar = Arena{static_cast<char *>(rt->scratch), 0};
+    }
+    dx = call.host() ? ar.take<float>((size_t)tokens * H) : const_cast<float *>(x);
+    dy = call.host() ? ar.take<float>((size_t)tokens * H) : y;
+    uint8_t *xc = ar.take<uint8_t>((size_t)tokens * H);
+    float *xs = ar.take<float>((size_t)tokens * Hs);
+    float *logits = ar.take<float>((size_t)tokens * E);
+    sel = ar.take<uint32_t>(P);
+    wts = ar.take<float>(P);
+    so = ScheduleOut{};
+    so.offsets = ar.take<uint32_t>(E + 1);
+    so.placement_tok = ar.take<uint32_t>(P);
+    so.placement_w = ar.take<float>(P);
+    so.slot_place = ar.take<uint32_t>(P);
+    so.counters = ar.take<uint32_t>(4);
+    xsend = ar.take<uint8_t>((size_t)P * H);
+    ssend = ar.take<float>((size_t)P * Hs);
+    ret = ar.take<uint16_t>((size_t)P * H);
+    alloff = ar.take<uint32_t>((size_t)G * (E + 1));
+    if (pass == 0) continue;
+    if (tokens == 0) {
+      CK(cudaMemsetAsync(so.offsets, 0, (E + 1) * sizeof(uint32_t), rt->stream));
+      break;
+    }
+    if (call.host() && (s = call.stage_in(dx, x, (size_t)tokens * H * 4)) != PW_OK) return s;
+    CK(cudaMemsetAsync(rt->d_ties, 0, 4, rt->stream));
+    {
+      ProfScope ps(rt, P_QUANT, 1);
+      CK(launch_quantize(dx, tokens, H, xc, xs, rt->d_flags, rt->stream));
+    }
+    {
+      ProfScope ps(rt, P_ROUTER, 2);
+      CK(launch_router_logits(dx, tokens, router->weight_bf16, E, H, logits, rt->stream));
+      CK(launch_router_topk(logits, router->bias, tokens, E, sel, wts, rt->d_ties, rt->d_flags, rt->stream));
+    }
+    {
+      ProfScope ps(rt, P_SCHED, 2);
+      CK(launch_schedule(sel, wts, tokens, E, BankTable{}, so, rt->d_flags, 1u, rt->stream));
+      CK(launch_gather_rows(xc, xs, so.placement_tok, P, H, xsend, ssend, rt->stream));
+    }
+  }
+  if ((s = ep_pinned(rt, ep->h_off, ep->h_off_cap, (size_t)G * (E + 1) * 4)) != PW_OK) return s;
+  NK(pw::nccl::all_gather(so.offsets, alloff, E + 1, ncclUint32, ep->comm, rt->stream, ep->timeout_s),
+     "ncclAllGather of expert offsets");
+  CK(cudaMemcpyAsync(ep->h_off, alloff, (size_t)G * (E + 1) * 4, cudaMemcpyDeviceToHost, rt->stream));
+  if ((s = ep_wait(rt)) != PW_OK) return s;
+
+  // ---- plan (host): transfer sizes, expert-order permutation, groups
+  std::vector<uint32_t> offs(ep->h_off, ep->h_off + (size_t)G * (E + 1));
+  auto off = [&](uint32_t rank, uint32_t e) { return offs[(size_t)rank * (E + 1) + e]; };
+  std::vector<uint32_t> n_send(G), n_recv(G), recv_base(G + 1, 0), e_begin(L + 1, 0);
+  uint32_t P_recv = 0;
+  for (uint32_t g = 0; g < G; ++g) P_recv += off(g, (r + 1) * L) - off(g, r * L);
+  std::vector<uint32_t> perm(P_recv);
+  ep_plan(offs.data(), G, r, E, n_send.data(), n_recv.data(), recv_base.data(), perm.data(), e_begin.data());
+  uint32_t max_count = 0, local_used = 0;
+  for (uint32_t le = 0; le < L; ++le) {
+    const uint32_t c = e_begin[le + 1] - e_begin[le];
+    max_count = c > max_count ? c : max_count;
+    local_used += c ? 1u : 0u;
+  }
+  const bool wide = max_count > 16u;
+  const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
+  std::vector<GemvGroup> gu, dn;
+  for (uint32_t le = 0; le < L; ++le) {
+    const pw_expert_weights &w = bank->host[le];
+    for (uint32_t b = e_begin[le]; b < e_begin[le + 1]; b += chunk) {
+      GemvGroup g{};
+      g.tok_begin = b;
+      g.count = std::min(chunk, e_begin[le + 1] - b);
+      g.expert = r * L + le;
+      g.w0 = w.gate.weight;
+      g.s0 = w.gate.scale;
+      g.w1 = w.up.weight;
+      g.s1 = w.up.scale;
+      g.tm0 = bank->d_maps + le;
+      g.tm1 = bank->d_maps + L + le;
+      gu.push_back(g);
+      GemvGroup d = g;
+      d.w0 = w.down.weight;
+      d.s0 = w.down.scale;
+      d.w1 = nullptr;
+      d.s1 = nullptr;
+      d.tm0 = bank->d_maps + 2 * (size_t)L + le;
+      d.tm1 = nullptr;
+      dn.push_back(d);
+    }
+  }
+  const uint32_t ng = (uint32_t)gu.size();
+  const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
+
+  // ---- phase 2 buffers (expert-parallel scratch, sized now)
+  Arena br;
+  uint8_t *rcodes = nullptr, *xg = nullptr, *hc = nullptr;
+  float *rscales = nullptr, *xsg = nullptr, *hid = nullptr, *gt = nullptr, *ut = nullptr, *hs = nullptr,
+        *down = nullptr;
+  uint32_t *perm_d = nullptr;
+  GemvGroup *gu_d = nullptr, *dn_d = nullptr;
+  uint16_t *ret_send = nullptr;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1 && br.off > ep->cap) {
+      if (ep->scratch) CK(cudaFree(ep->scratch));
+      ep->scratch = nullptr;
+      ep->cap = 0;
+      size_t cap = (size_t)1 << 20;
+      while (cap < br.off) cap *= 2;
+      CK(cudaMalloc(&ep->scratch, cap));
+      ep->cap = cap;
+    }
+    if (pass == 1) br = Arena{static_cast<char *>(ep->scratch), 0};
+    rcodes = br.take<uint8_t>((size_t)P_recv * H);
+    rscales = br.take<float>((size_t)P_recv * Hs);
+    perm_d = br.take<uint32_t>(P_recv);
+    gu_d = br.take<GemvGroup>(ng);
+    dn_d = br.take<GemvGroup>(ng);
+    xg = wide ? br.take<uint8_t>((size_t)P_recv * H) : nullptr;
+    xsg = wide ? br.take<float>((size_t)P_recv * Hs) : nullptr;
+    hid = fused ? nullptr : br.take<float>((size_t)P_recv * I);
+    gt = fused && !wide ? nullptr : br.take<float>((size_t)P_recv * I);
+    ut = fused && !wide ? nullptr : br.take<float>((size_t)P_recv * I);
+    hc = br.take<uint8_t>((size_t)P_recv * I);
+    hs = br.take<float>((size_t)P_recv * Is);
+    down = br.take<float>((size_t)P_recv * H);
+    ret_send = br.take<uint16_t>((size_t)P_recv * H);
+  }
+  // plan upload through pinned staging (the call waits before returning)
+  const size_t plan_bytes = (size_t)P_recv * 4 + 2 * (size_t)ng * sizeof(GemvGroup);
+  if ((s = ep_pinned(rt, ep->h_plan, ep->h_plan_cap, plan_bytes + 16)) != PW_OK) return s;
+  {
+    char *hp = static_cast<char *>(ep->h_plan);
+    if (P_recv) memcpy(hp, perm.data(), (size_t)P_recv * 4);
+    if (ng) {
+      memcpy(hp + (size_t)P_recv * 4, gu.data(), ng * sizeof(GemvGroup));
+      memcpy(hp + (size_t)P_recv * 4 + ng * sizeof(GemvGroup), dn.data(), ng * sizeof(GemvGroup));
+      CK(cudaMemcpyAsync(gu_d, hp + (size_t)P_recv * 4, ng * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
+      CK(cudaMemcpyAsync(dn_d, hp + (size_t)P_recv * 4 + ng * sizeof(GemvGroup), ng * sizeof(GemvGroup),
+                         cudaMemcpyHostToDevice, rt->stream));
+    }
+    if (P_recv) CK(cudaMemcpyAsync(perm_d, hp, (size_t)P_recv * 4, cudaMemcpyHostToDevice, rt->stream));
+  }
+
+  // ---- dispatch: codes and scales to the expert owners
+  std::vector<pw::nccl::Transfer> sends, recvs;
+  for (uint32_t g = 0; g < G; ++g) {
+    const size_t b = off(r, g * L);
+    sends.push_back({xsend + b * H, (size_t)n_send[g] * H, (int)g});
+    sends.push_back({ssend + b * Hs, (size_t)n_send[g] * Hs * 4, (int)g});
+    recvs.push_back({rcodes + (size_t)recv_base[g] * H, (size_t)n_recv[g] * H, (int)g});
+    recvs.push_back({rscales + (size_t)recv_base[g] * Hs, (size_t)n_recv[g] * Hs * 4, (int)g});
+  }
+  NK(pw::nccl::exchange(sends.data(), (int)sends.size(), recvs.data(), (int)recvs.size(), ep->comm, rt->stream,
+                        ep->timeout_s),
+     "dispatch send/recv");
+
+  // ---- local experts on the received rows
+  if (P_recv) {
+    if (wide) {
+      {
+        ProfScope ps(rt, P_QUANT, 1);
+        CK(launch_gather_rows(rcodes, rscales, perm_d, P_recv, H, xg, xsg, rt->stream));
+      }
+      s = enqueue_expert_chain_wide(rt, gu_d, dn_d, ng, nullptr, P_recv, H, I, xg, xsg, hid, gt, ut, hc, hs, down, 1,
+                                    ng);
+    } else {
+      s = enqueue_expert_chain(rt, gu_d, dn_d, ng, nullptr, P_recv, H, I, perm_d, rcodes, rscales, hid, gt, ut, hc,
+                               hs, down, 1, ng);
+    }
+    if (s != PW_OK) return s;
+    ProfScope ps(rt, P_COMBINE, 1);
+    CK(launch_scatter_rows_bf16(down, perm_d, P_recv, H, ret_send, rt->stream));
+  }
+
+  // ---- return: bf16 down rows to their source ranks
+  sends.clear();
+  recvs.clear();
+  for (uint32_t g = 0; g < G; ++g) {
+    sends.push_back({ret_send + (size_t)recv_base[g] * H, (size_t)n_recv[g] * H * 2, (int)g});
+    recvs.push_back({ret + (size_t)off(r, g * L) * H, (size_t)n_send[g] * H * 2, (int)g});
+  }
+  NK(pw::nccl::exchange(sends.data(), (int)sends.size(), recvs.data(), (int)recvs.size(), ep->comm, rt->stream,
+                        ep->timeout_s),
+     "combine send/recv");
+
+  // ---- weighted combine in ascending expert order
+  if (tokens) {
+    {
+      ProfScope ps(rt, P_COMBINE, 1);
+      CK(launch_combine_bf16(ret, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream));
+    }
+    if (call.host()) {
+      if ((s = call.stage_out(y, dy, (size_t)tokens * H * 4)) != PW_OK) return s;
+      if (selected && (s = call.stage_out(selected, sel, (size_t)P * 4)) != PW_OK) return s;
+      if (weights && (s = call.stage_out(weights, wts, (size_t)P * 4)) != PW_OK) return s;
+    } else {
+      if (selected) CK(cudaMemcpyAsync(selected, sel, (size_t)P * 4, cudaMemcpyDeviceToDevice, rt->stream));
+      if (weights) CK(cudaMemcpyAsync(weights, wts, (size_t)P * 4, cudaMemcpyDeviceToDevice, rt->stream));
+    }
+  }
+  if ((s = ep_wait(rt)) != PW_OK) return s;
+  const pw_expert_weights &w0 = bank->host[0];
+  const uint64_t per_expert = 3ull * H * I + 4ull * (w0.gate.scale_rows * w0.gate.scale_cols * 2u +
+                                                     w0.down.scale_rows * w0.down.scale_cols);
+  s = call.finish(per_expert * local_used);
+  if (stats) {
+    stats->unique_experts = local_used;
+    stats->expert_rows = P_recv;
+  }
+  return s;
+}
+
+int pw_ep_plan(const uint32_t *all_offsets, uint32_t world, uint32_t rank, uint32_t experts, uint32_t *n_send,
+               uint32_t *n_recv, uint32_t *recv_base, uint32_t *perm, uint32_t *expert_begin) {
+  if (!all_offsets || !n_send || !n_recv || !recv_base || !expert_begin || world == 0 || rank >= world ||
+      experts % world)
+    return PW_ERR_ARGUMENT;
+  const uint32_t L = experts / world;
+  for (uint32_t g = 0; g < world; ++g)
+    for (uint32_t e = 0; e < experts; ++e)
+      if (all_offsets[(size_t)g * (experts + 1) + e + 1] < all_offsets[(size_t)g * (experts + 1) + e])
+        return PW_ERR_SCHEDULE;
+  uint32_t rows = 0;
+  for (uint32_t g = 0; g < world; ++g)
+    rows += all_offsets[(size_t)g * (experts + 1) + (rank + 1) * L] - all_offsets[(size_t)g * (experts + 1) + rank * L];
+  if (rows && !perm) return PW_ERR_ARGUMENT;
+  ep_plan(all_offsets, world, rank, experts, n_send, n_recv, recv_base, perm, expert_begin);
+  return PW_OK;
+}
+
+int pw_ep_rank(const pw_runtime *rt, int *rank, int *world) {
+  if (!rt || !rank || !world) return PW_ERR_ARGUMENT;
+  if (!rt->ep || !rt->ep->comm) return PW_ERR_ARGUMENT;
+  *rank = rt->ep->rank;
+  *world = rt->ep->world;
+  return PW_OK;
 }
 
 }  // extern "C"

@@ -159,6 +159,7 @@ class WideMoeRuntime:
         self.device = device
         self.fused_gate_up = fused_gate_up
         self._banks = []
+        self._bank_refs = []
 
     # reference constructors (src/wide_metal_moe.rs:165-171)
     @classmethod
@@ -173,6 +174,7 @@ class WideMoeRuntime:
         for b in self._banks:
             self._L.pw_bank_destroy(b)
         self._banks = []
+        self._bank_refs = []
         if getattr(self, "_rt", None):
             self._L.pw_runtime_destroy(self._rt)
             self._rt = None
@@ -341,7 +343,49 @@ class WideMoeRuntime:
         bank = ctypes.c_void_p()
         self._check(self._L.pw_bank_create(self._rt, arr, len(experts), ctypes.byref(bank)))
         self._banks.append(bank)
+        # the library keeps raw device pointers: hold the tensors as long as the bank
+        self._bank_refs.append(list(experts))
         return bank
+
+    # ------------------------------------------------- expert parallelism
+    @staticmethod
+    def ep_unique_id() -> bytes:
+        """A fresh NCCL communicator id (128 bytes) for pw_ep_init; create it on
+        one rank and send it to the others."""
+        L = _lib.load()
+        buf = ctypes.create_string_buffer(128)
+        rc = L.pw_ep_unique_id(buf, 128)
+        if rc != 0:
+            raise PrismwingError(rc, "pw_ep_unique_id failed (is libnccl.so.2 loadable?)")
+        return buf.raw
+
+    def ep_init(self, rank: int, world: int, uid: bytes, timeout_ms: int = 60000) -> None:
+        """Join the expert-parallel group (collective)."""
+        buf = ctypes.create_string_buffer(bytes(uid), len(uid))
+        self._check(self._L.pw_ep_init(self._rt, rank, world, buf, len(uid), timeout_ms))
+
+    def ep_moe_layer(self, x, router_weight_bf16: torch.Tensor, bias: torch.Tensor, bank,
+                     want_routes: bool = False, stats: bool = True,
+                     out: Optional[torch.Tensor] = None) -> Execution:
+        """Collective routed layer over this rank's tokens; `bank` holds this
+        rank's experts (rank g: experts [g n, (g + 1) n))."""
+        x = _as_f32(x)
+        T, H = x.shape
+        r = self._router(router_weight_bf16, bias)
+        mem = MEM_DEVICE if x.is_cuda else MEM_HOST
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.float32, device=x.device)
+        sel = torch.empty((T, 8), dtype=torch.int32, device=x.device) if want_routes else None
+        wts = torch.empty((T, 8), dtype=torch.float32, device=x.device) if want_routes else None
+        st = Stats()
+        self._check(self._L.pw_ep_moe_layer(
+            self._rt, ctypes.byref(r), bank, ctypes.c_void_p(x.data_ptr() if T else 0), T,
+            ctypes.c_void_p(out.data_ptr() if T else 0),
+            ctypes.c_void_p(sel.data_ptr() if sel is not None and T else 0),
+            ctypes.c_void_p(wts.data_ptr() if wts is not None and T else 0), mem,
+            ctypes.byref(st) if stats else None))
+        return Execution(out, st.wall_ms, st.device_ms, st.unique_experts, st.expert_rows, st.boundary_tie_rows,
+                         st.weight_bytes, sel, wts)
 
     def moe_layer(self, x, router_weight_bf16: torch.Tensor, bias: torch.Tensor, bank,
                   want_routes: bool = False, stats: bool = True, asynchronous: bool = False,
