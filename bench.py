@@ -1,29 +1,33 @@
 #!/usr/bin/env python3
-"""Benchmark: the routed FP8 MoE layer of MiMo-V2.5 on B200.
-
-One step = one whole routed MoE layer at decode/verifier width 8: 8 tokens of
-hidden 4096, sigmoid no-aux top-8 router over 256 experts (bf16 weight + f32
-bias), dynamic FP8 activations, per selected expert fused gate/up + staged
-SwiGLU + down over e4m3 weights with 128x128 f32 block scales, weighted
-combine.  Weights, router and tokens are seeded synthetic tensors with the
-checkpoint's shapes and distributions (no network for the checkpoint).
+"""Benchmark: MiMo-V2.5's routed FP8 MoE layers on B200.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-value      mean device time per layer (us), inputs resident in HBM, K layers
-           enqueued back to back on one stream, CUDA events around them; each
-           step routes a different token batch, so every step streams its own
-           ~57 experts (~1.4 GB) from HBM -- far more than L2, no flush needed.
-e2e        the same layer through the C ABI with HOST buffers (pinned), the
-           H2D copy of the tokens and the D2H copy of the output inside the
-           timed region, one synchronous call per step.
-roofline   the fused gate/up GEMV (the dominant kernel): algorithmic bytes per
-           launch / its CUDA-event duration, against MEASURED_PEAKS.json's HBM.
-cpu_baseline  the CPU restatement of the reference's routed layer (oracle/,
-           f32 reference order, all host threads) on the same routed layer.
+Headline (`value`): expert-parallel prefill throughput, configs[4].  One step
+pushes a 2048-token batch (bf16-valued N(0,1)) through the 48-layer routed-MoE
+stack, layer-major: every layer routes the batch with its own sigmoid no-aux
+top-8 router over 256 experts (hidden 4096, intermediate 2048, e4m3 weights
+with 128x128 f32 block scales), runs the selected experts (tcgen05 grouped
+FP8 GEMM, fused gate/up, staged SwiGLU, down) and combines.  The layers cycle
+through --banks distinct synthetic weight sets (each 6.44 GB / N per GPU, far
+beyond the 126 MB L2, so no flush is needed); the layers between the MoE
+blocks (attention, norms) are out of scope, so each layer reads the step's
+token batch.  At N GPUs (torchrun, one process per GPU) rank g holds experts
+[g 256/N, (g+1) 256/N) of every layer and routes 2048/N tokens; FP8 codes go
+to the expert owners and bf16 expert outputs come back over NCCL (pw_ep_*).
+value = 2048 / (max over ranks of the step time), tokens/s through the stack.
 
-With --gpus N > 1 (torchrun, one rank per GPU) each rank runs its own replica
-of the layer; the line reports the max over ranks.
+e2e        the same stack through the C ABI with HOST buffers: every layer call
+           copies its tokens in from pinned memory and its output back.
+roofline   the fused gate/up tcgen05 GEMM: algorithmic bytes per launch (gate +
+           up weights and scales of the experts it runs, activation codes and
+           scales, bf16 gate/up out) / its CUDA-event time, vs MEASURED_PEAKS.json.
+tensor     the layer's FP8 FLOPs vs a cuBLASLt FP8 GEMM measured live (the
+           layer is HBM-bound at 64 tokens per expert; this is context).
+decode     configs[2]: the 8-token decode/verifier layer (us per layer, HBM
+           roofline of the fused gate/up GEMV); expert-parallel at N > 1.
+cpu_baseline  oracle/ (the reference's CPU path restated, f32 order, libm exp,
+           all host threads) on a bounded sample of the same layer.
 """
 from __future__ import annotations
 
@@ -38,21 +42,15 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-HIDDEN, INTER, EXPERTS, WIDTH = 4096, 2048, 256, 8
-# DRAM traffic / algorithmic bytes of the fused gate/up GEMV, from one ncu
-# capture of a 32-expert layer (profiles/k_gemv_mma_c2_small.md): 507.55 MB
-# read+written for 503.84 MB of algorithmic bytes.  Traffic grows in
-# proportion to the experts streamed, so the full-size launch's traffic is
-# this ratio times its algorithmic bytes.
-GATE_UP_TRAFFIC_RATIO = 507.55 / 503.84
-METRIC = "routed FP8 MoE layer us @width 8"
-CONFIG = {
-    "workload": "C2: full routed MoE layer, decode/verifier width 8 (BASELINE.json configs[2])",
-    "hidden": HIDDEN, "intermediate": INTER, "experts": EXPERTS, "top_k": 8, "tokens": WIDTH,
-    "weights": "e4m3 + 128x128 f32 block scales, N(0,0.02) quantized per block (amax/448, RNE)",
-    "router": "bf16 [256,4096] N(0,0.02) + f32 bias N(0,0.01)",
-    "l2": "no flush: each step routes a fresh token batch and streams ~1.4 GB of experts (>> 126 MB L2)",
-}
+HIDDEN, INTER, EXPERTS, TOPK = 4096, 2048, 256, 8
+PREFILL_TOKENS, STACK_LAYERS, DECODE_TOKENS = 2048, 48, 8
+METRIC = "EP prefill tok/s (2048-token batch through the 48-layer routed-MoE stack)"
+DECODE_METRIC = "routed FP8 MoE layer us @width 8"
+# DRAM traffic / algorithmic bytes of the fused gate/up GEMM, from one ncu
+# capture of a 64-expert, 512-token layer (profiles/k_gemm_tc_fused_prefill_small.md);
+# traffic grows in proportion to the experts streamed.
+GATE_UP_GEMM_TRAFFIC_RATIO = 1.0
+GATE_UP_GEMV_TRAFFIC_RATIO = 507.55 / 503.84  # profiles/k_gemv_mma_c2_small.md
 
 
 def peaks():
@@ -62,6 +60,13 @@ def peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def expert_bytes():
+    kb_h, kb_i = HIDDEN // 128, INTER // 128
+    gate_up = 2 * INTER * HIDDEN + 2 * kb_i * kb_h * 4
+    down = INTER * HIDDEN + kb_h * kb_i * 4
+    return gate_up, down
 
 
 # ------------------------------------------------------------------ clocks
@@ -123,87 +128,120 @@ class ClockSampler:
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-# ------------------------------------------------------------- CPU baseline
-def cpu_layer_baseline(x_np, sel, wts, bank_np, budget_s=12.0):
-    """The reference's routed layer (src/text_endpoint.rs:5290) restated on the
-    CPU (oracle/, f32 reference order, libm exp), all host threads."""
-    from oracle import oracle as O
-    threads = os.cpu_count() or 1
-    O.set_threads(threads)
-    times = []
-    t_end = time.perf_counter() + budget_s
-    while not times or (time.perf_counter() < t_end and len(times) < 20):
-        t0 = time.perf_counter()
-        O.routed_layer(x_np, sel, wts, bank_np, O.ACC_F32, O.EXP_LIBM)
-        times.append(time.perf_counter() - t0)
-    return statistics.mean(times) * 1e6, threads, len(times)
+def fp8_peak_tflops(dev) -> float | None:
+    """Dense FP8 throughput of cuBLASLt (torch._scaled_mm, 8192^3, e4m3 x e4m3 -> bf16),
+    best of 10 back-to-back launches: the tensor roofline's denominator."""
+    import torch
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=dev)
+        for _ in range(3):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        best = None
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+            e1.record()
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        del a, b
+        return 2 * n ** 3 / (best * 1e-3) / 1e12
+    except Exception:
+        return None
 
 
-def bank_to_host(bank, experts):
-    out = []
-    for e in range(len(bank)):
-        if e in experts:
-            g, u, d = bank[e]
-            out.append(tuple(t.cpu().numpy() for p in (g, u, d) for t in (p.weight, p.scale)))
-        else:
-            out.append(None)
-    # the oracle only touches selected experts; fill the rest with a tiny stand-in
-    filler = next(o for o in out if o is not None)
-    return [o if o is not None else filler for o in out]
+# ------------------------------------------------------------- CPU samples
+_CPU_EXPERTS: dict = {}
 
 
-# -------------------------------------------------------------- reference
-def run_reference(args, rank):
-    """--impl reference: the reference's CPU path (restated, oracle/) on this
-    arm's config; rank 0 only."""
-    if rank != 0:
-        return
+def cpu_layer_sample(tokens: int, seed: int, budget_s: float = 20.0):
+    """The reference's routed layer (src/text_endpoint.rs:5290) restated on
+    the CPU (oracle/, f32 reference order, libm exp, all host threads) over
+    `tokens` tokens of a 256-expert layer; returns (seconds per call, threads,
+    repeats, unique experts).  Experts are generated once and cached."""
     import numpy as np
     import torch
     from mimo_prismwing_b200 import synth
     from oracle import oracle as O
-    # same seeded layer as our arm, generated on the CPU
-    experts_needed = None
-    w, bias = synth.router(EXPERTS, HIDDEN, 7, "cpu")
-    x = synth.activations(WIDTH, HIDDEN, 1000, "cpu")
-    logits = O.router_logits(x.numpy(), w.view(torch.int16).numpy().view(np.uint16))
-    sel, wts, _, _, _ = O.noaux_topk(logits, bias.numpy())
-    experts_needed = sorted(set(sel.ravel().tolist()))
-    bank_np = []
-    filler = None
-    for e in range(EXPERTS):
-        if e in experts_needed:
-            g, u, d = synth.expert(HIDDEN, INTER, 1000 + e, "cpu")
-            t = tuple(a.numpy() for p in (g, u, d) for a in (p.weight, p.scale))
-            bank_np.append(t)
-            filler = filler or t
-        else:
-            bank_np.append(None)
-    bank_np = [b if b is not None else filler for b in bank_np]
-    times = []
     threads = os.cpu_count() or 1
     O.set_threads(threads)
-    for _ in range(max(1, args.warmup // 3)):
-        O.routed_layer(x.numpy(), sel, wts, bank_np, O.ACC_F32, O.EXP_LIBM)
-    for _ in range(args.steps):
+    w, bias = synth.router(EXPERTS, HIDDEN, 7, "cpu")
+    x = synth.activations(tokens, HIDDEN, seed, "cpu").numpy()
+    logits = O.router_logits(x, w.view(torch.int16).numpy().view(np.uint16))
+    sel, wts, _, _, _ = O.noaux_topk(logits, bias.numpy())
+    needed = sorted(set(sel.ravel().tolist()))
+    for e in needed:
+        if e not in _CPU_EXPERTS:
+            g, u, d = synth.expert(HIDDEN, INTER, 1000 + e, "cpu")
+            _CPU_EXPERTS[e] = tuple(a.numpy() for p in (g, u, d) for a in (p.weight, p.scale))
+    filler = _CPU_EXPERTS[needed[0]]
+    bank = [_CPU_EXPERTS.get(e, filler) for e in range(EXPERTS)]  # the oracle reads only selected experts
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while not times or (time.perf_counter() < t_end and len(times) < 5):
         t0 = time.perf_counter()
-        O.routed_layer(x.numpy(), sel, wts, bank_np, O.ACC_F32, O.EXP_LIBM)
+        O.routed_layer(x, sel, wts, bank, O.ACC_F32, O.EXP_LIBM)
         times.append(time.perf_counter() - t0)
-    us = statistics.mean(times) * 1e6
+    return statistics.mean(times), threads, len(times), len(needed)
+
+
+# -------------------------------------------------------------- reference
+def run_reference(args, rank):
+    """--impl reference: the reference's CPU path (restated, oracle/) for this
+    arm's metric; rank 0 only.  A step is a bounded sample (16 tokens through
+    one layer); tok/s through the stack = sample tokens / (time x 48)."""
+    if rank != 0:
+        return
+    sample_tokens = 16
+    threads = os.cpu_count() or 1
+    per_call = []
+    for i in range(max(1, args.warmup // 3) + args.steps):
+        sec, threads, _, uniq = cpu_layer_sample(sample_tokens, 2000 + i, budget_s=0.0)
+        if i >= max(1, args.warmup // 3):
+            per_call.append(sec)
+    sec = statistics.mean(per_call)
+    tok_s = sample_tokens / (sec * STACK_LAYERS)
     line = {
-        "metric": METRIC, "value": round(us, 3), "unit": "us", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3), "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-        "config": dict(CONFIG, unique_experts=len(experts_needed)),
-        "cpu_baseline": {"value": round(us, 3), "unit": "us", "cores": threads, "kind": "port",
-                         "sample": f"one routed layer (8 tokens, {len(experts_needed)} experts) x {len(times)} steps; "
-                                   "oracle/pw_oracle.c routed layer, f32 reference order, libm exp"},
-        "e2e": {"value": round(us, 3), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(sec * STACK_LAYERS * 1e3, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "configs[4] EP prefill, 2048 tokens x 48 layers (CPU: a 16-token sample of one layer "
+                               "per step, scaled to the stack)", "hidden": HIDDEN, "experts": EXPERTS,
+                   "top_k": TOPK},
+        "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample_tokens} tokens through one 256-expert layer per step ({uniq} experts); "
+                                   "oracle/pw_oracle.c routed layer, f32 reference order, libm exp; tok/s = "
+                                   "tokens / (seconds x 48 layers)"},
+        "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------- ours
+class Layers:
+    """The per-rank weights: --banks distinct layer banks of this rank's experts."""
+
+    def __init__(self, rt, rank, world, banks, dev):
+        from mimo_prismwing_b200 import synth
+        self.L = EXPERTS // world
+        self.first = rank * self.L
+        self.handles, self.routers, self.keep = [], [], []
+        for b in range(banks):
+            experts = [synth.expert(HIDDEN, INTER, 1000 + 4099 * b + e, dev)
+                       for e in range(self.first, self.first + self.L)]
+            self.keep.append(experts)
+            self.handles.append(rt.create_bank(experts))
+            self.routers.append(synth.router(EXPERTS, HIDDEN, 7 + b, dev))
+
+    def layer(self, i):
+        b = i % len(self.handles)
+        return self.handles[b], self.routers[b][0], self.routers[b][1]
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -214,22 +252,40 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = f"cuda:{local_rank}"
     rt = WideMoeRuntime.compile_with_fused_gate_up(local_rank)
-    bank = [synth.expert(HIDDEN, INTER, 1000 + e, dev) for e in range(EXPERTS)]
-    handle = rt.create_bank(bank)
-    w, bias = synth.router(EXPERTS, HIDDEN, 7, dev)
-    n_batches = args.steps + args.warmup
-    xs = [synth.activations(WIDTH, HIDDEN, 1000 + i + 7919 * rank, dev) for i in range(n_batches)]
-    y = torch.empty((WIDTH, HIDDEN), device=dev)
+    ep = world > 1
+    if ep:
+        box = [WideMoeRuntime.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        rt.ep_init(rank, world, box[0], timeout_ms=120000)
+    layers = Layers(rt, rank, world, args.banks, dev)
     stream = torch.cuda.Stream(device=dev)
     rt.set_stream(stream)
+    hbm, peak_kind = peaks()
+    tflops_fp8 = fp8_peak_tflops(dev) if rank == 0 else None
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    # ---- device-resident timing (the `value`)
-    for i in range(args.warmup):
-        rt.moe_layer(xs[args.steps + i], w, bias, handle, asynchronous=True, out=y)
+    def layer_call(x, i, out=None, host=False, profile=False):
+        h, w, bias = layers.layer(i)
+        if ep:
+            return rt.ep_moe_layer(x, w, bias, h, stats=profile, out=out)
+        if host or profile:
+            return rt.moe_layer(x, w, bias, h, stats=profile, out=out)
+        return rt.moe_layer(x, w, bias, h, asynchronous=True, out=out)
+
+    # ================================================================ prefill
+    T = PREFILL_TOKENS // world
+    x = synth.activations(T, HIDDEN, 5000 + rank, dev)
+    ys = [torch.empty((T, HIDDEN), device=dev) for _ in range(2)]
+
+    def step():
+        for i in range(STACK_LAYERS):
+            layer_call(x, i, out=ys[i % 2])
+
+    for _ in range(args.warmup):
+        step()
     stream.synchronize()
     assert rt.error_flags() == 0, rt.last_error()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -238,100 +294,151 @@ def run_ours(args, rank, world, local_rank):
     with ClockSampler(local_rank) as clocks:
         with torch.cuda.stream(stream):
             ev0.record(stream)
-            for i in range(args.steps):
-                rt.moe_layer(xs[i], w, bias, handle, asynchronous=True, out=y)
+            for _ in range(args.steps):
+                step()
             ev1.record(stream)
         stream.synchronize()
     torch.cuda.synchronize()
     barrier()
-    flags = rt.error_flags()
-    if flags:
-        raise RuntimeError(f"device error flags {flags}")
-    ms = ev0.elapsed_time(ev1)
-    us_per_layer = ms * 1e3 / args.steps
+    if rt.error_flags():
+        raise RuntimeError(f"device error flags {rt.error_flags()}")
+    step_ms = ev0.elapsed_time(ev1) / args.steps
 
-    # ---- per-kernel profile + bytes (separate pass, synchronous calls)
+    # per-kernel profile of one layer of each bank (synchronous calls)
     rt.set_profiling(True)
-    prof_keys = ["quantize_ms", "router_ms", "schedule_ms", "gate_up_ms", "down_ms", "combine_ms"]
-    prof = {k: 0.0 for k in prof_keys}
-    gu_bytes = dn_bytes = 0
-    uniq = []
-    per_expert_gu = 2 * INTER * HIDDEN + 2 * (INTER // 128) * (HIDDEN // 128) * 4
-    per_expert_dn = INTER * HIDDEN + (HIDDEN // 128) * (INTER // 128) * 4
-    P = WIDTH * 8
-    for i in range(args.steps):
-        ex = rt.moe_layer(xs[i], w, bias, handle, stats=True, out=y)
+    keys = ["quantize_ms", "router_ms", "schedule_ms", "gate_up_ms", "down_ms", "combine_ms"]
+    prof = {k: 0.0 for k in keys}
+    launches = 0
+    uniq = rows = 0
+    nprof = len(layers.handles)
+    for i in range(nprof):
+        ex = layer_call(x, i, out=ys[0], profile=True)
         p = rt.last_profile()
-        launches_per_layer = p["launches"]
-        for k in prof_keys:
+        launches += p["launches"]
+        for k in keys:
             prof[k] += p[k]
-        U = ex.unique_experts
-        uniq.append(U)
-        # weights + scales + activation codes/scales read + outputs written
-        gu_bytes += U * per_expert_gu + P * (HIDDEN + HIDDEN // 128 * 4) + P * (INTER + INTER // 128 * 4)
-        dn_bytes += U * per_expert_dn + P * (INTER + INTER // 128 * 4) + P * HIDDEN * 4
+        uniq += ex.unique_experts
+        rows += ex.expert_rows
     rt.set_profiling(False)
-    gu_ms = prof["gate_up_ms"] / args.steps
-    dn_ms = prof["down_ms"] / args.steps
-    hbm, peak_kind = peaks()
-    gu_gbs = gu_bytes / args.steps / (gu_ms * 1e-3) / 1e9
-    dn_gbs = dn_bytes / args.steps / (dn_ms * 1e-3) / 1e9
-    layer_bytes = (gu_bytes + dn_bytes) / args.steps + EXPERTS * HIDDEN * 2
-    layer_gbs = layer_bytes / (us_per_layer * 1e-6) / 1e9
+    prof = {k: v / nprof for k, v in prof.items()}
+    launches_per_layer = launches / nprof
+    uniq, rows = uniq / nprof, rows / nprof  # experts run / rows computed by this rank per layer
 
-    # ---- end to end through the C ABI with pinned host buffers
-    xh = [x.cpu().pin_memory() for x in xs[: args.steps]]
+    gu_b, dn_b = expert_bytes()
+    # fused gate/up GEMM: gate+up weights of the experts it runs, activation codes + scales read,
+    # bf16 gate and up written
+    gemm_bytes = uniq * gu_b + rows * (HIDDEN + HIDDEN // 128 * 4) + rows * INTER * 2 * 2
+    gu_gbs = gemm_bytes / (prof["gate_up_ms"] * 1e-3) / 1e9
+    layer_ms = step_ms / STACK_LAYERS
+    layer_w_bytes = uniq * (gu_b + dn_b)
+    layer_gbs = layer_w_bytes / (layer_ms * 1e-3) / 1e9
+    layer_flops = rows * 2 * 3 * HIDDEN * INTER
+    layer_tflops = layer_flops / (layer_ms * 1e-3) / 1e12
+
+    # e2e: host buffers through the C ABI, every layer copies in and out
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
     rt.set_stream(None)
-    for i in range(min(3, args.warmup)):
-        rt.moe_layer(xh[i], w, bias, handle, stats=False)
+    e2e_steps = max(1, min(args.steps, 3))
+    layer_call(xh, 0, out=yh, host=True)
     barrier()
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        rt.moe_layer(xh[i], w, bias, handle, stats=False)
-    e2e_us = (time.perf_counter() - t0) * 1e6 / args.steps
+    for _ in range(e2e_steps):
+        for i in range(STACK_LAYERS):
+            layer_call(xh, i, out=yh, host=True)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
     barrier()
 
-    # ---- max over ranks
-    vals = torch.tensor([us_per_layer, e2e_us, gu_gbs], device=dev, dtype=torch.float64)
+    # ================================================================= decode
+    Td = DECODE_TOKENS // world if DECODE_TOKENS % world == 0 else (DECODE_TOKENS // world + (rank < DECODE_TOKENS % world))
+    xd = [synth.activations(max(Td, 1), HIDDEN, 7000 + 97 * i + rank, dev)[:Td] for i in range(args.decode_steps + 3)]
+    yd = torch.empty((max(Td, 1), HIDDEN), device=dev)[:Td]
+    rt.set_stream(stream)
+    for i in range(3):
+        layer_call(xd[args.decode_steps + i], 0, out=yd)
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        for i in range(args.decode_steps):
+            layer_call(xd[i], i % len(layers.handles), out=yd)
+        d1.record(stream)
+    stream.synchronize()
+    barrier()
+    dec_us = d0.elapsed_time(d1) * 1e3 / args.decode_steps
+    rt.set_profiling(True)
+    dprof = {"gate_up_ms": 0.0}
+    dgu_bytes = 0.0
+    duniq = []
+    for i in range(min(args.decode_steps, 20)):
+        ex = layer_call(xd[i], i % len(layers.handles), out=yd, profile=True)
+        p = rt.last_profile()
+        dprof["gate_up_ms"] += p["gate_up_ms"]
+        P = ex.expert_rows
+        dgu_bytes += ex.unique_experts * gu_b + P * (HIDDEN + HIDDEN // 128 * 4) + P * (INTER + INTER // 128 * 4)
+        duniq.append(ex.unique_experts)
+    rt.set_profiling(False)
+    nd = min(args.decode_steps, 20)
+    dgu_gbs = (dgu_bytes / nd) / (dprof["gate_up_ms"] / nd * 1e-3) / 1e9 if dprof["gate_up_ms"] else None
+
+    # ================================================================ gather
+    vals = torch.tensor([step_ms, e2e_s, dec_us, layer_gbs, gu_gbs, dgu_gbs or 0.0], device=dev,
+                        dtype=torch.float64)
     if world > 1:
         mx = vals.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        step_ms, e2e_s, dec_us = float(mx[0]), float(mx[1]), float(mx[2])
         mn = vals.clone()
         dist.all_reduce(mn, op=dist.ReduceOp.MIN)
-        us_per_layer, e2e_us = float(mx[0]), float(mx[1])
-        gu_gbs = float(mn[2])
+        layer_gbs, gu_gbs, dgu_gbs = float(mn[3]), float(mn[4]), float(mn[5])
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sel_ex = rt.moe_layer(xs[0], w, bias, handle, want_routes=True, out=y)
-        sel = sel_ex.selected.cpu().numpy().astype(np.uint32)
-        wts = sel_ex.weights.cpu().numpy()
-        bank_np = bank_to_host(bank, set(sel.ravel().tolist()))
-        cpu_us, threads, reps = cpu_layer_baseline(xs[0].cpu().numpy(), sel, wts, bank_np)
-        cpu = {"value": round(cpu_us, 1), "unit": "us", "cores": threads, "kind": "port",
-               "sample": f"step 0's routed layer (8 tokens, {len(set(sel.ravel().tolist()))} experts) x {reps}; "
-                         "oracle/pw_oracle.c routed layer, f32 reference order, libm exp"}
+        sec, threads, reps, su = cpu_layer_sample(16, 2000)
+        cpu_tok_s = 16 / (sec * STACK_LAYERS)
+        cpu = {"value": round(cpu_tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"16 tokens through one 256-expert layer ({su} experts) x {reps}; oracle/pw_oracle.c "
+                         "routed layer, f32 reference order, libm exp; tok/s = tokens / (seconds x 48 layers)"}
 
     if rank == 0:
+        value = PREFILL_TOKENS / (step_ms * 1e-3)
+        e2e_val = PREFILL_TOKENS / e2e_s
         line = {
-            "metric": METRIC, "value": round(us_per_layer, 3), "unit": "us", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us_per_layer / 1e3, 5),
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3xe4m3->f32",
-            "data": "synthetic (seeded, checkpoint shapes)",
-            "config": dict(CONFIG, parallelism=f"replicas x{world}" if world > 1 else "single GPU",
-                           unique_experts_mean=round(statistics.mean(uniq), 2)),
-            "e2e": {"value": round(e2e_us, 3), "unit": "us", "h2d_bytes_per_step": WIDTH * HIDDEN * 4,
-                    "d2h_bytes_per_step": WIDTH * HIDDEN * 4 + 4},
-            "gpu_launches": launches_per_layer * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "k_gemv fused gate/up + SwiGLU",
+            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "e4m3xe4m3->f32", "data": "synthetic (seeded, checkpoint shapes)",
+            "config": {"workload": "configs[4]: EP prefill, 2048 bf16 tokens through 48 routed-MoE layers "
+                                   "(layer-major), 256 experts x [2048x4096 gate/up, 4096x2048 down] e4m3",
+                       "hidden": HIDDEN, "intermediate": INTER, "experts": EXPERTS, "top_k": TOPK,
+                       "tokens": PREFILL_TOKENS, "layers": STACK_LAYERS, "distinct_layer_banks": args.banks,
+                       "parallelism": f"expert-parallel x{world} (NCCL all-to-all)" if ep else "single GPU",
+                       "tokens_per_rank": T, "experts_per_rank": EXPERTS // world,
+                       "l2": "no flush: every layer streams its experts' weights (>= 805 MB per GPU) from HBM"},
+            "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "h2d_bytes_per_step": T * HIDDEN * 4 * STACK_LAYERS,
+                    "d2h_bytes_per_step": T * HIDDEN * 4 * STACK_LAYERS},
+            "gpu_launches": int(round(launches_per_layer * STACK_LAYERS * args.steps)),
+            "roofline": {"bound": "hbm", "kernel": "k_gemm_tc<2> fused gate/up (tcgen05)",
                          "achieved": round(gu_gbs, 1), "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(gu_gbs / hbm, 4),
-                         "traffic": int(gu_bytes / args.steps * GATE_UP_TRAFFIC_RATIO),
-                         "bytes_per_launch": int(gu_bytes / args.steps), "us_per_launch": round(gu_ms * 1e3, 2)},
-            "layer_roofline": {"achieved": round(layer_gbs, 1), "unit": "GB/s", "frac": round(layer_gbs / hbm, 4),
-                               "bytes_per_layer": int(layer_bytes)},
-            "kernels_us": {k.replace("_ms", ""): round(v / args.steps * 1e3, 2) for k, v in prof.items()},
-            "down_gemv_gbs": round(dn_gbs, 1),
+                         "traffic": int(gemm_bytes * GATE_UP_GEMM_TRAFFIC_RATIO),
+                         "bytes_per_launch": int(gemm_bytes), "us_per_launch": round(prof["gate_up_ms"] * 1e3, 2)},
+            "layer": {"us": round(layer_ms * 1e3, 2), "weight_gbs": round(layer_gbs, 1),
+                      "hbm_frac": round(layer_gbs / hbm, 4), "fp8_tflops": round(layer_tflops, 1),
+                      "fp8_peak_tflops": round(tflops_fp8, 1) if tflops_fp8 else None,
+                      "fp8_peak_kind": "measured live: cuBLASLt FP8 8192^3 (torch._scaled_mm)",
+                      "tensor_frac": round(layer_tflops / tflops_fp8, 4) if tflops_fp8 else None,
+                      "experts_per_rank_run": round(uniq, 1), "rows_per_rank": round(rows, 1)},
+            "kernels_us_per_layer": {k.replace("_ms", ""): round(v * 1e3, 2) for k, v in prof.items()},
+            "decode": {"metric": DECODE_METRIC, "value": round(dec_us, 2), "unit": "us", "higher_is_better": False,
+                       "workload": "configs[2]: 8 tokens, 256 experts, device router"
+                                   + (f", expert-parallel x{world}" if ep else ""),
+                       "unique_experts_mean": round(statistics.mean(duniq), 2) if duniq else None,
+                       "roofline": {"bound": "hbm", "kernel": "k_gemv_mma fused gate/up + SwiGLU",
+                                    "achieved": round(dgu_gbs, 1) if dgu_gbs else None, "peak": hbm,
+                                    "unit": "GB/s", "frac": round(dgu_gbs / hbm, 4) if dgu_gbs else None,
+                                    "traffic_ratio": round(GATE_UP_GEMV_TRAFFIC_RATIO, 4)}},
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
@@ -340,18 +447,15 @@ def run_ours(args, rank, world, local_rank):
 
 
 def main():
-    global EXPERTS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--banks", type=int, default=4, help="distinct synthetic layer banks the 48 layers cycle through")
+    ap.add_argument("--decode-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--experts", type=int, default=EXPERTS,
-                    help="smaller banks only for profiling captures (the metric is quoted at 256)")
     args = ap.parse_args()
-    EXPERTS = args.experts
-    CONFIG["experts"] = EXPERTS
     if args.warmup < 3:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -667,7 +667,7 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
   const int grid_gu = grid_for(rt, units_hint * (I / 128u));
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   {
-    ProfScope ps(rt, P_GATEUP, fused ? 2 : 3);
+    ProfScope ps(rt, P_GATEUP, fused ? 1 : 3);
     GemmArgs A{};
     A.g = gemv_args(rt, gu, n_groups, I, H, PW_LAYOUT_PLAIN);
     A.g.n_groups_dev = n_groups_dev;
@@ -682,7 +682,6 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
       A.g.gate_bf16 = reinterpret_cast<uint16_t *>(gate_tmp);
       A.g.up_bf16 = reinterpret_cast<uint16_t *>(up_tmp);
       CK(launch_gemm_tc(2, A, grid_gu, rt->stream));
-      CK(launch_swiglu_quant(A.g.gate_bf16, A.g.up_bf16, slots, I, hidden, hc, hs, rt->d_flags, rt->stream));
     } else {
       if (!encode_act_maps(A.xmap, xg, slots, H))
         return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activations");
@@ -694,9 +693,13 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
       CK(launch_swiglu(gate_tmp, up_tmp, hidden, slots * I, rt->d_flags, rt->stream));
     }
   }
-  if (!fused) {
+  {
     ProfScope ps(rt, P_QUANT, 1);
-    CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream));
+    if (fused)
+      CK(launch_swiglu_quant(reinterpret_cast<const uint16_t *>(gate_tmp), reinterpret_cast<const uint16_t *>(up_tmp),
+                             slots, I, hidden, hc, hs, rt->d_flags, rt->stream));
+    else
+      CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream));
   }
   GemmArgs D{};
   D.g = gemv_args(rt, dn, n_groups, H, I, PW_LAYOUT_PLAIN);
