@@ -447,6 +447,7 @@ def run_ours(args, rank, world, local_rank):
 
 
 def main():
+    global EXPERTS, PREFILL_TOKENS, STACK_LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -455,7 +456,12 @@ def main():
     ap.add_argument("--banks", type=int, default=4, help="distinct synthetic layer banks the 48 layers cycle through")
     ap.add_argument("--decode-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # smaller cases for ncu captures only; the metric is quoted at the defaults
+    ap.add_argument("--experts", type=int, default=EXPERTS)
+    ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS)
+    ap.add_argument("--layers", type=int, default=STACK_LAYERS)
     args = ap.parse_args()
+    EXPERTS, PREFILL_TOKENS, STACK_LAYERS = args.experts, args.tokens, args.layers
     if args.warmup < 3:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))

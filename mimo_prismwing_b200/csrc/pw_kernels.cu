@@ -70,29 +70,32 @@ cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_
 }
 
 // ------------------------------------------------------------ router logits
-// logit[t,e] = sum_c x[t,c] * w[e,c] with f64 accumulation in a fixed order
-// (the oracle's pwo_router_logits restates it):
+// logit[t,e] = sum_c x[t,c] * w[e,c] in f32 in a fixed order (the oracle's
+// pwo_router_logits restates it; the reference's own logits are f32 too):
 //   the K axis is cut into 512-column slices; warp w (of 8) owns slices
-//   s = w, w+8, ...; lane l sums, for each owned slice in ascending order,
-//   the 8-column chunks at 512s + 8l and 512s + 8l + 256, column by column;
-//   an xor butterfly (16, 8, 4, 2, 1) sums the lanes; the CTA then adds the
-//   8 warp partials in warp order starting from warp 0's.
-// x*w of a bf16 weight and an f32 activation is exact in f64, so FMA and
-// mul+add give the same bits.  One CTA per (expert, 8 tokens).
+//   s = w, w+8, ...; lane l accumulates, for each owned slice in ascending
+//   order, the 8-column chunks at 512s + 8l and 512s + 8l + 256, column by
+//   column, with fused multiply-adds; an xor butterfly (16, 8, 4, 2, 1) adds
+//   the lanes; the CTA then adds the 8 warp partials in warp order starting
+//   from warp 0's.  bf16 weights widen to f32 exactly (a shift).
+// Decode widths: one CTA per (expert, 8 tokens).
 constexpr int kRouterTok = 8;
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, uint32_t tokens,
                                                        const uint16_t *__restrict__ w, uint32_t experts,
                                                        uint32_t hidden, float *__restrict__ logits) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ double part[8][kRouterTok];
+  __shared__ float part[8][kRouterTok];
   const uint32_t lane = threadIdx.x % 32u, warp = threadIdx.x / 32u;
   const uint32_t e = blockIdx.x;
   const uint32_t t0 = blockIdx.y * kRouterTok;
-  double acc[kRouterTok];
+  float acc[kRouterTok];
 #pragma unroll
-  for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0;
+  for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0f;
   const uint16_t *wrow = w + (size_t)e * hidden;
   const uint32_t slices = hidden / 512u;
   for (uint32_t sl = warp; sl < slices; sl += 8u) {
@@ -100,13 +103,8 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     for (int j = 0; j < 2; ++j) {
       const uint32_t c0 = 512u * sl + 8u * lane + 256u * j;
       const uint4 wq = __ldg(reinterpret_cast<const uint4 *>(wrow + c0));
-      double wd[8];
-      const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        wd[2 * i] = (double)__uint_as_float(wv[i] << 16);
-        wd[2 * i + 1] = (double)__uint_as_float(wv[i] & 0xffff0000u);
-      }
+      const float wf[8] = {bf16lo(wq.x), bf16hi(wq.x), bf16lo(wq.y), bf16hi(wq.y),
+                           bf16lo(wq.z), bf16hi(wq.z), bf16lo(wq.w), bf16hi(wq.w)};
 #pragma unroll
       for (int t = 0; t < kRouterTok; ++t) {
         if (t0 + t < tokens) {
@@ -114,101 +112,113 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
           const float4 a = __ldg(xp), b = __ldg(xp + 1);
           const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[t] = __fma_rn((double)xv[i], wd[i], acc[t]);
+          for (int i = 0; i < 8; ++i) acc[t] = __fmaf_rn(xv[i], wf[i], acc[t]);
         }
       }
     }
   }
 #pragma unroll
   for (int t = 0; t < kRouterTok; ++t) {
-    double v = acc[t];
+    float v = acc[t];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
     if (lane == 0) part[warp][t] = v;
   }
   __syncthreads();
   if (threadIdx.x < kRouterTok && t0 + threadIdx.x < tokens) {
-    double s = part[0][threadIdx.x];
+    float s = part[0][threadIdx.x];
 #pragma unroll
-    for (int k = 1; k < 8; ++k) s = __dadd_rn(s, part[k][threadIdx.x]);
-    logits[(size_t)(t0 + threadIdx.x) * experts + e] = __double2float_rn(s);
+    for (int k = 1; k < 8; ++k) s = __fadd_rn(s, part[k][threadIdx.x]);
+    logits[(size_t)(t0 + threadIdx.x) * experts + e] = s;
   }
 }
 
 // Prefill-width router logits: the same per-(token, expert) order as
-// k_router_logits, for a tile of 8 tokens x 8 experts per CTA so that each
-// activation and weight value loaded (and converted to f64) feeds 8 FMA
-// chains.  Thread (warp w, lane l) runs the 64 lane chains of its columns,
-// four columns at a time; the 32-lane xor tree is evaluated as a
-// transpose-reduce (at each level lane l adds its xor partner's value for the
-// half of the pairs it keeps): every pair gets the same tree of commutative
-// additions as the butterfly, in 62 exchanges instead of 320.  Lane l ends
-// with pairs 2l and 2l+1 (token l/4, experts 2(l%4), 2(l%4)+1); the 8 warp
-// sums are then added in warp order.
-constexpr int kTileTok = 8, kTileExp = 8;
+// k_router_logits, for a tile of 8 tokens x 16 experts per CTA so that each
+// activation and weight value loaded feeds 16 (resp. 8) chains.  Thread
+// (warp w, lane l) runs the 128 lane chains of its columns four columns at a
+// time, two tokens per packed f32x2 FMA (each lane of the pair rounds like
+// fmaf).  The 32-lane xor tree is evaluated as a transpose-reduce (at each
+// level lane l adds its xor partner's value for the half of the pairs it
+// keeps): every pair gets the same tree of commutative additions as the
+// butterfly, in 124 exchanges instead of 640.  Lane l ends with pairs
+// 4l..4l+3; the 8 warp sums are then added in warp order.
+constexpr int kTileTok = 8, kTileExp = 16;
 
 __global__ void __launch_bounds__(256) k_router_logits_tiled(const float *__restrict__ x, uint32_t tokens,
                                                              const uint16_t *__restrict__ w, uint32_t experts,
                                                              uint32_t hidden, float *__restrict__ logits) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ double part[8][kTileTok * kTileExp];
+  constexpr int NP = kTileTok * kTileExp;  // pairs, index p = e * kTileTok + t
+  __shared__ float part[8][NP];
   const uint32_t lane = threadIdx.x % 32u, warp = threadIdx.x / 32u;
   const uint32_t e0 = blockIdx.x * kTileExp, t0 = blockIdx.y * kTileTok;
-  double acc[kTileTok * kTileExp];
+  float2 acc[kTileExp][kTileTok / 2];  // acc[e][tp] = tokens 2tp, 2tp+1
 #pragma unroll
-  for (int p = 0; p < kTileTok * kTileExp; ++p) acc[p] = 0.0;
+  for (int e = 0; e < kTileExp; ++e)
+#pragma unroll
+    for (int tp = 0; tp < kTileTok / 2; ++tp) acc[e][tp] = make_float2(0.0f, 0.0f);
   const uint32_t slices = hidden / 512u;
   for (uint32_t sl = warp; sl < slices; sl += 8u) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const uint32_t c0 = 512u * sl + 8u * lane + 256u * (uint32_t)j;
-      // each 8-column chunk in two halves of 4 (the chains still run i = 0..7)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        double xd[kTileTok][4];
+        float4 xq[kTileTok];
 #pragma unroll
-        for (int t = 0; t < kTileTok; ++t) {
-          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (t0 + t < tokens) a = __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * hidden + c0) + hf);
-          xd[t][0] = a.x; xd[t][1] = a.y; xd[t][2] = a.z; xd[t][3] = a.w;
-        }
+        for (int t = 0; t < kTileTok; ++t)
+          xq[t] = t0 + t < tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * hidden + c0) + hf)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int e = 0; e < kTileExp; ++e) {
           const uint2 wq = e0 + e < experts
                                ? __ldg(reinterpret_cast<const uint2 *>(w + (size_t)(e0 + e) * hidden + c0) + hf)
                                : make_uint2(0u, 0u);
-          const double wd[4] = {(double)__uint_as_float(wq.x << 16), (double)__uint_as_float(wq.x & 0xffff0000u),
-                                (double)__uint_as_float(wq.y << 16), (double)__uint_as_float(wq.y & 0xffff0000u)};
+          const float wf[4] = {bf16lo(wq.x), bf16hi(wq.x), bf16lo(wq.y), bf16hi(wq.y)};
 #pragma unroll
-          for (int t = 0; t < kTileTok; ++t)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[t * kTileExp + e] = __fma_rn(xd[t][i], wd[i], acc[t * kTileExp + e]);
+          for (int tp = 0; tp < kTileTok / 2; ++tp) {
+            const float4 a = xq[2 * tp], b = xq[2 * tp + 1];
+            acc[e][tp] = __ffma2_rn(make_float2(a.x, b.x), make_float2(wf[0], wf[0]), acc[e][tp]);
+            acc[e][tp] = __ffma2_rn(make_float2(a.y, b.y), make_float2(wf[1], wf[1]), acc[e][tp]);
+            acc[e][tp] = __ffma2_rn(make_float2(a.z, b.z), make_float2(wf[2], wf[2]), acc[e][tp]);
+            acc[e][tp] = __ffma2_rn(make_float2(a.w, b.w), make_float2(wf[3], wf[3]), acc[e][tp]);
+          }
         }
       }
     }
   }
-  // transpose-reduce over the 32 lanes: 64 pairs -> 2 per lane (pairs 2l, 2l+1)
+  // flatten: v[e * 8 + t]
+  float v[NP];
 #pragma unroll
-  for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+  for (int e = 0; e < kTileExp; ++e)
+#pragma unroll
+    for (int tp = 0; tp < kTileTok / 2; ++tp) {
+      v[e * kTileTok + 2 * tp] = acc[e][tp].x;
+      v[e * kTileTok + 2 * tp + 1] = acc[e][tp].y;
+    }
+  // transpose-reduce over the 32 lanes: 128 pairs -> 4 per lane
+#pragma unroll
+  for (int o = 16, n = NP / 2; o >= 1; o >>= 1, n >>= 1) {
     const bool upper = (lane & (uint32_t)o) != 0u;
 #pragma unroll
     for (int i = 0; i < n; ++i) {
-      const double send = upper ? acc[i] : acc[i + n];
-      const double keep = upper ? acc[i + n] : acc[i];
-      acc[i] = __dadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+      const float send = upper ? v[i] : v[i + n];
+      const float keep = upper ? v[i + n] : v[i];
+      v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
     }
   }
-  part[warp][2u * lane] = acc[0];
-  part[warp][2u * lane + 1u] = acc[1];
-  __syncthreads();
-  if (threadIdx.x < (unsigned)(kTileTok * kTileExp)) {
-    const uint32_t p = threadIdx.x, t = p / kTileExp, e = p % kTileExp;
-    if (t0 + t < tokens && e0 + e < experts) {
-      double s = part[0][p];
 #pragma unroll
-      for (int k = 1; k < 8; ++k) s = __dadd_rn(s, part[k][p]);
-      logits[(size_t)(t0 + t) * experts + e0 + e] = __double2float_rn(s);
+  for (int k = 0; k < NP / 32; ++k) part[warp][(NP / 32) * lane + k] = v[k];
+  __syncthreads();
+  if (threadIdx.x < (unsigned)NP) {
+    const uint32_t p = threadIdx.x, e = p / kTileTok, t = p % kTileTok;
+    if (t0 + t < tokens && e0 + e < experts) {
+      float s = part[0][p];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) s = __fadd_rn(s, part[k][p]);
+      logits[(size_t)(t0 + t) * experts + e0 + e] = s;
     }
   }
 }

@@ -86,7 +86,8 @@ static ncclResult_t settle(ncclComm_t comm, ncclResult_t first, double deadline_
     if (st != ncclInProgress) return st;
     const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     if (el > deadline_s) return ncclInProgress;  // caller aborts
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    if (el > 2e-3) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    else std::this_thread::yield();
   }
 }
 

@@ -1231,9 +1231,13 @@ int ep_wait(pw_runtime *rt) {
     if (q != cudaErrorNotReady) return fail(rt, PW_ERR_CUDA, "stream: %s", cudaGetErrorString(q));
     const ncclResult_t a = pw::nccl::async_error(rt->ep->comm);
     if (a != ncclSuccess && a != ncclInProgress) return ep_dead(rt, PW_ERR_NCCL, "expert-parallel exchange", a);
-    if (now_ms() - t0 > rt->ep->timeout_s * 1e3)
+    const double el = now_ms() - t0;
+    if (el > rt->ep->timeout_s * 1e3)
       return ep_dead(rt, PW_ERR_TIMEOUT, "expert-parallel exchange", ncclInProgress);
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
+    // spin for the first 2 ms (a sleep costs tens of microseconds of timer
+    // slack, per layer), then back off
+    if (el > 2.0) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    else std::this_thread::yield();
   }
 }
 
