@@ -106,15 +106,19 @@ ncclResult_t async_error(ncclComm_t comm) {
   return q != ncclSuccess ? q : st;
 }
 
+// Abort on a detached thread: ncclCommAbort waits for the communicator's
+// background work, which may itself be waiting on a peer that is gone; the
+// caller must get its error back within its deadline regardless.
 void abort_comm(ncclComm_t comm) {
-  if (comm && g_loaded) g_api.CommAbort(comm);
+  if (!comm || !g_loaded) return;
+  std::thread([comm]() { g_api.CommAbort(comm); }).detach();
 }
 
 ncclResult_t destroy(ncclComm_t comm, double deadline_s) {
   if (!comm) return ncclSuccess;
   ncclResult_t r = settle(comm, g_api.CommFinalize(comm), deadline_s);
   if (r != ncclSuccess) {
-    g_api.CommAbort(comm);
+    abort_comm(comm);
     return r;
   }
   return g_api.CommDestroy(comm);
@@ -129,7 +133,7 @@ ncclResult_t exchange(const Transfer *sends, int n_sends, const Transfer *recvs,
                       cudaStream_t s, double deadline_s) {
   ncclResult_t r = g_api.GroupStart();
   if (r != ncclSuccess) return r;
-  for (int i = 0; i < n_sends && r == ncclSuccess; ++i)
+  for (int i = 0; i < n_sends && (r == ncclSuccess || r == ncclInProgress); ++i)
     if (sends[i].bytes) r = g_api.Send(sends[i].ptr, sends[i].bytes, ncclUint8, sends[i].peer, comm, s);
   for (int i = 0; i < n_recvs && (r == ncclSuccess || r == ncclInProgress); ++i)
     if (recvs[i].bytes)

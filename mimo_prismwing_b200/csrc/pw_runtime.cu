@@ -403,6 +403,7 @@ void pw_runtime_destroy(pw_runtime *rt) {
   cudaSetDevice(rt->device);
   if (rt->stream) cudaStreamSynchronize(rt->stream);
   if (rt->ep) {
+    // an aborted communicator (ep->comm cleared) is never finalized or destroyed
     if (rt->ep->comm) pw::nccl::destroy(rt->ep->comm, rt->ep->timeout_s);
     if (rt->ep->scratch) cudaFree(rt->ep->scratch);
     if (rt->ep->h_off) cudaFreeHost(rt->ep->h_off);
@@ -1221,16 +1222,16 @@ int ep_dead(pw_runtime *rt, int code, const char *what, ncclResult_t r) {
     if (r_ != ncclSuccess) return ep_dead(rt, r_ == ncclInProgress ? PW_ERR_TIMEOUT : PW_ERR_NCCL, what, r_); \
   } while (0)
 
-// Bounded wait for the runtime's stream; NCCL errors and the deadline abort
-// the communicator (which also ends its kernels).
+// Bounded wait for the runtime's stream; the deadline aborts the
+// communicator (which also ends its kernels).  Only the stream and the clock
+// are polled here: a communicator query can wait on NCCL's own background
+// work, which is exactly what may be stuck when a peer is gone.
 int ep_wait(pw_runtime *rt) {
   const double t0 = now_ms();
   for (;;) {
     const cudaError_t q = cudaStreamQuery(rt->stream);
     if (q == cudaSuccess) return PW_OK;
     if (q != cudaErrorNotReady) return fail(rt, PW_ERR_CUDA, "stream: %s", cudaGetErrorString(q));
-    const ncclResult_t a = pw::nccl::async_error(rt->ep->comm);
-    if (a != ncclSuccess && a != ncclInProgress) return ep_dead(rt, PW_ERR_NCCL, "expert-parallel exchange", a);
     const double el = now_ms() - t0;
     if (el > rt->ep->timeout_s * 1e3)
       return ep_dead(rt, PW_ERR_TIMEOUT, "expert-parallel exchange", ncclInProgress);
@@ -1324,7 +1325,28 @@ int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t byt
   }
   ep->comm = comm;
   rt->ep = ep;
-  return PW_OK;
+  // Establish every connection now, while all ranks are here: one all-gather
+  // and one send/recv with each peer.  NCCL connects lazily on a
+  // communicator's first use, and that handshake runs on the calling thread;
+  // a peer lost later can then only stall kernels, which the bounded stream
+  // wait and the abort end.
+  uint32_t *probe = nullptr;
+  CK(cudaMalloc(&probe, (size_t)world * 3 * sizeof(uint32_t)));
+  CK(cudaMemsetAsync(probe, 0, (size_t)world * 3 * sizeof(uint32_t), rt->stream));
+  int s = PW_OK;
+  NK(pw::nccl::all_gather(probe, probe + world, 1, ncclUint32, ep->comm, rt->stream, ep->timeout_s),
+     "connection warm-up (all-gather)");
+  std::vector<pw::nccl::Transfer> sends, recvs;
+  for (int g = 0; g < world; ++g) {
+    sends.push_back({probe, sizeof(uint32_t), g});
+    recvs.push_back({probe + 2 * world + g, sizeof(uint32_t), g});
+  }
+  NK(pw::nccl::exchange(sends.data(), (int)sends.size(), recvs.data(), (int)recvs.size(), ep->comm, rt->stream,
+                        ep->timeout_s),
+     "connection warm-up (send/recv)");
+  s = ep_wait(rt);
+  cudaFree(probe);
+  return s;
 }
 
 int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,

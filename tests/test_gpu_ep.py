@@ -37,25 +37,28 @@ def _worker(rank, world, uid_q, res_q, tokens_per_rank, mode):
                 uid_q.put(uid)
         else:
             uid = uid_q.get(timeout=60)
-        rt.ep_init(rank, world, uid, timeout_ms=20000)
+        rt.ep_init(rank, world, uid, timeout_ms=8000 if mode == "leave" else 20000)
         L = E // world
         local = rt.create_bank(_bank(dev, range(rank * L, (rank + 1) * L)))
         w, bias = synth.router(E, HID, 77, dev)
         T = tokens_per_rank[rank]
         x = synth.activations(max(T, 1), HID, 300 + rank, dev)[:T]
         if mode == "leave":
+            def report_and_exit(val):
+                res_q.put((rank, val))
+                res_q.close()
+                res_q.join_thread()  # flush the queue's feeder thread before _exit
+                os._exit(0)
             if rank == 1:
                 torch.cuda.synchronize()
-                res_q.put((rank, "left"))
-                os._exit(0)  # between steps: nothing in flight
+                report_and_exit("left")  # between steps: nothing in flight
             import time
             time.sleep(2.0)
             try:
                 rt.ep_moe_layer(x, w, bias, local)
-                res_q.put((rank, "no error"))
+                report_and_exit("no error")
             except Exception as exc:  # expected: bounded timeout / NCCL error
-                res_q.put((rank, getattr(exc, "status", str(exc))))
-            os._exit(0)
+                report_and_exit(getattr(exc, "status", str(exc)))
         ex = rt.ep_moe_layer(x, w, bias, local, want_routes=True)
         if T == 0:
             res_q.put((rank, "ok"))
@@ -86,7 +89,7 @@ def _worker(rank, world, uid_q, res_q, tokens_per_rank, mode):
         raise
 
 
-def _run(world, tokens_per_rank, mode):
+def _run(world, tokens_per_rank, mode, wait_s=300):
     ctx = mp.get_context("spawn")
     uid_q, res_q = ctx.Queue(), ctx.Queue()
     procs = [ctx.Process(target=_worker, args=(r, world, uid_q, res_q, tokens_per_rank, mode)) for r in range(world)]
@@ -94,7 +97,7 @@ def _run(world, tokens_per_rank, mode):
         p.start()
     out = {}
     for _ in range(world):
-        rank, val = res_q.get(timeout=300)
+        rank, val = res_q.get(timeout=wait_s)
         out[rank] = val
     for p in procs:
         p.join(timeout=120)
@@ -124,6 +127,7 @@ def test_ep_layer_two_gpus(tokens_per_rank):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_peer_leaves_between_layers():
-    out = _run(2, (4, 4), "leave")
+    # the survivor's layer must end within its 8 s deadline (plus start-up)
+    out = _run(2, (4, 4), "leave", wait_s=90)
     assert out[1] == "left"
     assert out[0] in (-7, -6), out[0]  # PW_ERR_TIMEOUT or PW_ERR_NCCL, within the deadline
