@@ -270,7 +270,9 @@ def run_ours(args, rank, world, local_rank):
     def layer_call(x, i, out=None, host=False, profile=False):
         h, w, bias = layers.layer(i)
         if ep:
-            return rt.ep_moe_layer(x, w, bias, h, stats=profile, out=out)
+            if host or profile:
+                return rt.ep_moe_layer(x, w, bias, h, stats=profile, out=out)
+            return rt.ep_moe_layer(x, w, bias, h, asynchronous=True, out=out)
         if host or profile:
             return rt.moe_layer(x, w, bias, h, stats=profile, out=out)
         return rt.moe_layer(x, w, bias, h, asynchronous=True, out=out)

@@ -260,7 +260,10 @@ int pw_ep_rank(const pw_runtime *rt, int *rank, int *world);
  * [g * n, (g + 1) * n) of the router's E = n * world.  Routing is local; token
  * codes and scales go to the expert owners and bf16 expert outputs come back;
  * the combine runs on the token's rank in ascending expert order, so y is
- * bit-identical to pw_moe_layer on one GPU.  Synchronous (no PW_MEM_ASYNC);
+ * bit-identical to pw_moe_layer on one GPU.  The call waits (bounded) for the
+ * all-gathered per-expert counts; with PW_MEM_DEVICE | PW_MEM_ASYNC it returns
+ * once the rest is enqueued (the next expert-parallel call, pw_synchronize or
+ * pw_read_error_flags observes it), otherwise when the layer is done.
  * stats->unique_experts / expert_rows count this rank's local work. */
 int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,
                     uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem,

@@ -1363,7 +1363,8 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
   if (E != L * G) return fail(rt, PW_ERR_SHAPE, "router has %u experts; %u ranks x %u local experts", E, G, L);
   if (bank->hidden != router->hidden) return fail(rt, PW_ERR_SHAPE, "router and expert bank disagree");
   if (tokens > 2048u) return fail(rt, PW_ERR_UNSUPPORTED, "at most 2048 tokens per rank and call");
-  if (mem & PW_MEM_ASYNC) return fail(rt, PW_ERR_ARGUMENT, "expert-parallel layers are synchronous");
+  if ((mem & PW_MEM_ASYNC) && (mem & PW_MEM_HOST))
+    return fail(rt, PW_ERR_ARGUMENT, "asynchronous expert-parallel calls need device I/O");
   CK(cudaSetDevice(rt->device));
   const uint32_t P = tokens * 8u, Hs = H / 128u, Is = I / 128u;
   Call call{rt, mem, stats, 0};
@@ -1579,7 +1580,10 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
       if (weights) CK(cudaMemcpyAsync(weights, wts, (size_t)P * 4, cudaMemcpyDeviceToDevice, rt->stream));
     }
   }
-  if ((s = ep_wait(rt)) != PW_OK) return s;
+  // PW_MEM_ASYNC: return with the dispatch, the experts, the return trip and
+  // the combine enqueued; the next expert-parallel call's offset wait covers
+  // them, and every buffer this call used is rewritten only after that wait.
+  if (!call.async() && (s = ep_wait(rt)) != PW_OK) return s;
   const pw_expert_weights &w0 = bank->host[0];
   const uint64_t per_expert = 3ull * H * I + 4ull * (w0.gate.scale_rows * w0.gate.scale_cols * 2u +
                                                      w0.down.scale_rows * w0.down.scale_cols);

@@ -365,7 +365,7 @@ class WideMoeRuntime:
         self._check(self._L.pw_ep_init(self._rt, rank, world, buf, len(uid), timeout_ms))
 
     def ep_moe_layer(self, x, router_weight_bf16: torch.Tensor, bias: torch.Tensor, bank,
-                     want_routes: bool = False, stats: bool = True,
+                     want_routes: bool = False, stats: bool = True, asynchronous: bool = False,
                      out: Optional[torch.Tensor] = None) -> Execution:
         """Collective routed layer over this rank's tokens; `bank` holds this
         rank's experts (rank g: experts [g n, (g + 1) n))."""
@@ -373,6 +373,11 @@ class WideMoeRuntime:
         T, H = x.shape
         r = self._router(router_weight_bf16, bias)
         mem = MEM_DEVICE if x.is_cuda else MEM_HOST
+        if asynchronous:
+            if not x.is_cuda:
+                raise PrismwingError(-1, "asynchronous calls need device I/O")
+            mem |= MEM_ASYNC
+            stats = False
         if out is None:
             out = torch.empty((T, H), dtype=torch.float32, device=x.device)
         sel = torch.empty((T, 8), dtype=torch.int32, device=x.device) if want_routes else None

@@ -60,9 +60,15 @@ def _worker(rank, world, uid_q, res_q, tokens_per_rank, mode):
             except Exception as exc:  # expected: bounded timeout / NCCL error
                 report_and_exit(getattr(exc, "status", str(exc)))
         ex = rt.ep_moe_layer(x, w, bias, local, want_routes=True)
+        # the asynchronous form (enqueue and return) gives the same bits; a
+        # synchronous call after it observes its completion
+        y_async = torch.empty((T, HID), device=dev)
+        rt.ep_moe_layer(x, w, bias, local, asynchronous=True, out=y_async)
+        rt.ep_moe_layer(x, w, bias, local)
         if T == 0:
             res_q.put((rank, "ok"))
             return
+        assert torch.equal(y_async, ex.output), "asynchronous EP layer differs"
         y = ex.output.cpu().numpy()
         sel = ex.selected.cpu().numpy().astype(np.uint32)
         wts = ex.weights.cpu().numpy()
