@@ -259,6 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   const uint32_t kblocks = a.K / 128u;
   const uint32_t kcs = (kblocks + 1u) / 2u;          // stages per matrix per tile
   const uint32_t per_tile = kcs * (uint32_t)MATS;   // stages per tile; fused: all gate, then all up
+  const bool qkv = KIND == 0 && a.layout != PW_LAYOUT_PLAIN;
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
@@ -269,6 +270,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
         tensormap_acquire(m0);
         if (MATS == 2) tensormap_acquire(g.tm1);
         const uint32_t row0 = (u % tpg) * kTileRows;
+        // QKV layouts: the tile's two 64-row halves are each one run of
+        // consecutive checkpoint rows (map_row); load them as {128, 64, 1} boxes
+        uint32_t src0 = 0, src1 = 0, sr_unused = 0;
+        if (qkv) {
+          map_row(a.layout, row0, src0, sr_unused);
+          map_row(a.layout, row0 + 64u, src1, sr_unused);
+        }
         const uint32_t n = mma_cols(g.count);  // token rows loaded: whole 32-token chunks
         const CUtensorMap *xm = &A.xmap[n / 32u - 1u];
         const uint32_t bytes = (uint32_t)kWBox + n * 256u;
@@ -277,7 +285,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
           if (bwait(sh, &sh.empty[slot], phase ^ 1u, a.flags)) {
             uint8_t *dst = sh.ring + slot * kStage;
             mbar_arrive_expect_tx(&sh.full[slot], bytes);
-            tma_load_3d(dst, m == 0 ? m0 : g.tm1, 0, (int)row0, (int)(kc * 2u), &sh.full[slot]);
+            if (!qkv) {
+              tma_load_3d(dst, m == 0 ? m0 : g.tm1, 0, (int)row0, (int)(kc * 2u), &sh.full[slot]);
+            } else {
+#pragma unroll
+              for (uint32_t j = 0; j < 2; ++j) {
+                tma_load_3d(dst + j * (kTileRows * 128u), m0, 0, (int)src0, (int)(kc * 2u + j), &sh.full[slot]);
+                tma_load_3d(dst + j * (kTileRows * 128u) + 64u * 128u, m0, 0, (int)src1, (int)(kc * 2u + j),
+                            &sh.full[slot]);
+              }
+            }
             tma_load_3d(dst + kWBox, xm, 0, (int)g.tok_begin, (int)(kc * 2u), &sh.full[slot]);
             issued |= 1u << slot;
             parity = (parity & ~(1u << slot)) | (phase << slot);
@@ -368,11 +385,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
         cur_group = gi;
       }
       {
-        const uint32_t srow = row0 / 128u;
+        uint32_t srow = row0 / 128u, srow1 = srow;
+        if (qkv) {
+          uint32_t src_unused = 0;
+          map_row(a.layout, row0, src_unused, srow);
+          map_row(a.layout, row0 + 64u, src_unused, srow1);
+        }
         const float *s0 = (KIND == 3 ? grp.s1 : grp.s0) + (size_t)srow * a.scale_cols;
         for (uint32_t i = etid; i < kblocks; i += kEpiThreads) {
           sh.ws[i] = __ldg(s0 + i);
           if (MATS == 2) sh.ws[32u + i] = __ldg(grp.s1 + (size_t)srow * a.scale_cols + i);
+          if (qkv) sh.ws[32u + i] = __ldg(grp.s0 + (size_t)srow1 * a.scale_cols + i);  // rows 64..127
         }
       }
       named_bar_sync(1, kEpiThreads);
@@ -397,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
           const bool ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
           tc_fence_after();
           if (ok) {
-            const float ws = sh.ws[m * 32 + kb];
+            const float ws = sh.ws[(qkv ? quarter / 2u : (uint32_t)m) * 32u + kb];
             const float *xrow = sh.xs + kb * kTN;
 #pragma unroll
             for (int q = 0; q < kThreadChunks; ++q) {
@@ -510,7 +533,8 @@ int gemm_tc_tokens(int) { return tc::kTN; }
 
 cudaError_t launch_gemm_tc(int kind, const GemmArgs &a, int grid, cudaStream_t stream) {
   const GemvArgs &g = a.g;
-  if (g.K == 0 || g.K % 128u || g.K > 4096u || g.rows % tc::kTileRows || grid <= 0 || g.layout != PW_LAYOUT_PLAIN)
+  if (g.K == 0 || g.K % 128u || g.K > 4096u || g.rows % tc::kTileRows || grid <= 0 ||
+      (g.layout != PW_LAYOUT_PLAIN && kind != 0))
     return cudaErrorInvalidValue;
   switch (kind) {
     case 0: return tc::launch_one<0>(a, grid, stream);

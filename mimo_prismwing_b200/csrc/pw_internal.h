@@ -136,7 +136,8 @@ struct BankTable {
 
 // Host: encode the 2-D TMA map of one row-major e4m3 matrix [rows, cols]
 // (box 128 B x box_rows, 128B swizzle).  Returns false on failure.
-bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows);
+bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows,
+                       uint32_t box_kb = 0);
 uint32_t map_box_rows(uint32_t layout);
 // chunk: tokens per GEMV/GEMM group (8 for the GEMV, gemm_tc_tokens(2) for the GEMM)
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,

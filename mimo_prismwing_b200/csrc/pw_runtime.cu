@@ -67,12 +67,15 @@ bool encode_act_maps(CUtensorMap (&out)[4], const void *base, uint32_t rows, uin
 // The weight is viewed as {128 B, rows, k-blocks} with strides {cols, 128}:
 // a box of {128, box_rows, 256 / box_rows} is 32 KB and lands row-major in
 // shared memory (one 128-byte line per row and k-block), 128B-swizzled.
-bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows) {
+// box_kb != 0 overrides the k-blocks per box (the tcgen05 GEMM's QKV tiles
+// load {128, 64, 1} boxes).
+bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows,
+                       uint32_t box_kb) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || cols % 128u) return false;
   cuuint64_t dims[3] = {128u, rows, cols / 128u};
   cuuint64_t strides[2] = {cols, 128u};
-  cuuint32_t box[3] = {128u, box_rows, 256u / box_rows};
+  cuuint32_t box[3] = {128u, box_rows, box_kb ? box_kb : 256u / box_rows};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -524,13 +527,19 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
   CK(cudaSetDevice(rt->device));
   const uint32_t K = w->cols, N = w->rows;
   const size_t nx = (size_t)width * K, ny = (size_t)width * N;
+  // wide block-scaled projections run on the tcgen05 GEMM (all layouts; the
+  // QKV layouts load each 128-row tile as two 64-row source runs)
+  const bool wide = kind != 1 && width >= kWideProjection;
   CUtensorMap hmap;
   if (kind != 1) {
     const pw_fp8_tensor *ts[1] = {w};
-    if (!encode_maps(rt, ts, 1, layout, &hmap)) return PW_ERR_CUDA;
+    if (wide && layout != PW_LAYOUT_PLAIN) {
+      if (!encode_weight_map(&hmap, w->weight, w->rows, w->cols, 64u, 1u))
+        return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for a [%u, %u] weight", w->rows, w->cols);
+    } else if (!encode_maps(rt, ts, 1, layout, &hmap)) {
+      return PW_ERR_CUDA;
+    }
   }
-  // wide block-scaled projections run on the tcgen05 GEMM (plain layout)
-  const bool wide = kind != 1 && layout == PW_LAYOUT_PLAIN && width >= kWideProjection;
   Call call{rt, mem, stats, 0};
   if ((s = call.begin()) != PW_OK) return s;
   Arena ar;

@@ -135,3 +135,23 @@ def test_wide_route_bit_exact_vs_oracle(rt, experts, hidden, tokens):
     assert np.array_equal(H(sel).astype(np.uint32), osel)
     assert np.array_equal(H(wts).view(np.uint32), owts.view(np.uint32))
     assert st["boundary_tie_rows"] == ties
+
+
+@pytest.mark.parametrize("layout,width", [("full", 64), ("full", 2048), ("swa", 40), ("swa", 300)])
+def test_wide_qkv_layouts_vs_oracle(rt, layout, width):
+    # the fused QKV projection with its per-segment scale grid on
+    # the tcgen05 GEMM (each 128-row tile = two 64-row checkpoint runs)
+    from gpu_helpers import assert_close, assert_close_bf16
+    from mimo_prismwing_b200 import synth
+    b = synth.full_qkv(31, "cuda") if layout == "full" else synth.swa_qkv(32, "cuda")
+    lay = O.LAYOUT_FULL_QKV if layout == "full" else O.LAYOUT_SWA_QKV
+    x = synth.activations(width, 4096, 60 + width, "cuda")
+    full = layout == "full"
+    y32 = H(rt.execute_fp8_linear(x, b, full_qkv_layout=full, f32_output=True).output)
+    codes, scales, _ = O.dynamic_fp8(H(x))
+    take = slice(None) if width <= 300 else slice(0, width, 29)  # keep the f64 oracle quick
+    ref = O.blockscaled_linear(H(b.weight), H(b.scale), codes[take], scales[take], layout=lay)
+    assert_close(y32[take], ref, what=f"{layout} qkv w{width}")
+    y = H(rt.execute_fp8_linear(x, b, full_qkv_layout=full).output)
+    assert np.array_equal(O.round_bf16(y32), y)
+    assert_close_bf16(y[take], O.round_bf16(ref), what=f"{layout} qkv bf16 w{width}")
