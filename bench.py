@@ -26,6 +26,9 @@ tensor     the layer's FP8 FLOPs vs a cuBLASLt FP8 GEMM measured live (the
            layer is HBM-bound at 64 tokens per expert; this is context).
 decode     configs[2]: the 8-token decode/verifier layer (us per layer, HBM
            roofline of the fused gate/up GEMV); expert-parallel at N > 1.
+configs    (N = 1) configs[0] readable GEMV, configs[1] one expert at widths
+           1/2/4/8, configs[3] fused QKV at widths 1/8/2048: device time per
+           call and its HBM / FP8 tensor fraction.
 cpu_baseline  oracle/ (the reference's CPU path restated, f32 order, libm exp,
            all host threads) on a bounded sample of the same layer.
 """
@@ -187,6 +190,63 @@ def cpu_layer_sample(tokens: int, seed: int, budget_s: float = 20.0):
         O.routed_layer(x, sel, wts, bank, O.ACC_F32, O.EXP_LIBM)
         times.append(time.perf_counter() - t0)
     return statistics.mean(times), threads, len(times), len(needed)
+
+
+# ------------------------------------------------- configs[0], [1], [3]
+def bench_configs(rt, dev, hbm, tflops_fp8, iters=20):
+    """The single-projection configs on one GPU, device time per call from
+    CUDA events around each kernel class (the runtime's profiler); weights
+    rotate over copies that together exceed 2x L2 (126 MB)."""
+    import torch
+    from mimo_prismwing_b200 import synth
+    out = {}
+
+    def timed(fn, keys, n):
+        for i in range(3):
+            fn(i)
+        rt.set_profiling(True)
+        tot = 0.0
+        for i in range(n):
+            fn(i)
+            p = rt.last_profile()
+            tot += sum(p[k] for k in keys)
+        rt.set_profiling(False)
+        return tot / n * 1e3  # us
+
+    # configs[0]: readable GEMV [2048 x 4096], x [1 x 4096] f32 (src/lib.rs:1272)
+    c0 = [synth.projection(2048, 4096, 100 + i, dev) for i in range(32)]
+    x1 = synth.activations(1, 4096, 5, dev)
+    us = timed(lambda i: rt.fp8_gemv(x1, c0[i % 32]), ["projection_ms"], iters)
+    b0 = 8407040
+    out["c0_gemv_2048x4096_w1"] = {"us": round(us, 2), "gbs": round(b0 / us / 1e3, 1),
+                                   "hbm_frac": round(b0 / us / 1e3 / hbm, 4), "bytes": b0}
+    del c0
+    # configs[1]: one routed expert at widths 1, 2, 4, 8 (quantize, fused gate/up, down)
+    ex = [synth.expert(HIDDEN, INTER, 200 + i, dev) for i in range(12)]
+    gu_b, dn_b = expert_bytes()
+    for w in (1, 2, 4, 8):
+        xw = synth.activations(w, HIDDEN, 6 + w, dev)
+        us = timed(lambda i: rt.expert_forward(xw, *ex[i % 12]), ["quantize_ms", "gate_up_ms", "down_ms"], iters)
+        b = gu_b + dn_b + w * (8192 + 16384)
+        out[f"c1_expert_w{w}"] = {"us": round(us, 2), "gbs": round(b / us / 1e3, 1),
+                                  "hbm_frac": round(b / us / 1e3 / hbm, 4), "bytes": b}
+    del ex
+    # configs[3]: fused QKV [13568 x 4096] (full layout) at widths 1, 8, 2048
+    qk = [synth.full_qkv(300 + i, dev) for i in range(6)]
+    for w in (1, 8, 2048):
+        xw = synth.activations(w, HIDDEN, 9 + w, dev)
+        us = timed(lambda i: rt.execute_fp8_linear(xw, qk[i % 6], full_qkv_layout=True),
+                   ["quantize_ms", "projection_ms"], iters if w < 2048 else 10)
+        b = 55574528 + 13824 + w * (8192 + 4 * 13568)
+        flops = 2 * w * 13568 * 4096
+        row = {"us": round(us, 2), "gbs": round(b / us / 1e3, 1), "hbm_frac": round(b / us / 1e3 / hbm, 4),
+               "tflops": round(flops / us / 1e6, 1)}
+        if w == 2048 and tflops_fp8:
+            row["tensor_frac"] = round(flops / us / 1e6 / tflops_fp8, 4)
+        out[f"c3_qkv_full_w{w}"] = row
+    del qk
+    torch.cuda.empty_cache()
+    return out
 
 
 # -------------------------------------------------------------- reference
@@ -396,6 +456,10 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(mn, op=dist.ReduceOp.MIN)
         layer_gbs, gu_gbs, dgu_gbs = float(mn[3]), float(mn[4]), float(mn[5])
 
+    configs = None
+    if world == 1 and not args.skip_configs:
+        configs = bench_configs(rt, dev, hbm, tflops_fp8)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sec, threads, reps, su = cpu_layer_sample(16, 2000)
@@ -441,6 +505,7 @@ def run_ours(args, rank, world, local_rank):
                                     "achieved": round(dgu_gbs, 1) if dgu_gbs else None, "peak": hbm,
                                     "unit": "GB/s", "frac": round(dgu_gbs / hbm, 4) if dgu_gbs else None,
                                     "traffic_ratio": round(GATE_UP_GEMV_TRAFFIC_RATIO, 4)}},
+            "configs": configs,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
@@ -458,6 +523,7 @@ def main():
     ap.add_argument("--banks", type=int, default=4, help="distinct synthetic layer banks the 48 layers cycle through")
     ap.add_argument("--decode-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-configs", action="store_true", help="skip the configs[0]/[1]/[3] sub-benchmarks")
     # smaller cases for ncu captures only; the metric is quoted at the defaults
     ap.add_argument("--experts", type=int, default=EXPERTS)
     ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS)

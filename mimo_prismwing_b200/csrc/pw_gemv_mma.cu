@@ -23,7 +23,14 @@
 //  * a ninth warp is the producer: one lane waits for free ring slots and
 //    issues the copies, decoupled from the consumer warps' progress; the 8
 //    token slots' codes and scales and each consumer warp's weight-scale row
-//    sit in shared memory for the tile.
+//    sit in shared memory for the tile;
+//  * when K allows (its stages divide into 8 equal leaves), the block sums are
+//    added per leaf and the 8 leaf sums in a fixed pairwise tree
+//    ((l0+l1)+(l2+l3))+((l4+l5)+(l6+l7)).  With few tiles (a lone expert, a
+//    narrow QKV) the runtime splits each tile's K over 2, 4 or 8 CTAs, each
+//    evaluating a complete subtree; the last to arrive adds the partials with
+//    the same tree and runs the epilogue, so the result does not depend on
+//    the split.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -41,6 +48,7 @@ constexpr int kTileRows = 128;
 constexpr int kStageBytes = 32 * 1024;   // one 3-D box: 256 lines of 128 B
 constexpr int kMaxK = 4096;
 constexpr int kMaxStages = 8;
+constexpr uint32_t kLeaves = 8;  // K tree leaves
 
 // Shared-memory carve-up (runtime: the activation tile depends on K).
 struct Layout {
@@ -79,6 +87,7 @@ struct Shared {
   uint64_t *full;
   uint64_t *empty;
   volatile int *abort;
+  volatile int *last;  // this CTA finishes the tile (split-K)
 };
 
 __device__ __forceinline__ bool ring_wait(const Shared &sh, uint64_t *bar, uint32_t parity, uint32_t *flags) {
@@ -124,7 +133,7 @@ __device__ __forceinline__ void tensormap_acquire(const CUtensorMap *map) {
 // per box KBS = 256 / BR, halves = 128 / BR; stages run kc-major, then half,
 // then matrix.
 struct Geo {
-  uint32_t br, kbs, halves, kcs, per_tile;
+  uint32_t br, kbs, halves, kcs, per_kc, splits, leaves, leaf_kc;
 };
 
 __device__ __forceinline__ Geo make_geo(const GemvArgs &a, int mats) {
@@ -134,9 +143,16 @@ __device__ __forceinline__ Geo make_geo(const GemvArgs &a, int mats) {
   g.halves = 128u / g.br;
   const uint32_t kblocks = a.K / 128u;
   g.kcs = (kblocks + g.kbs - 1u) / g.kbs;
-  g.per_tile = g.kcs * g.halves * (uint32_t)mats;
+  g.per_kc = g.halves * (uint32_t)mats;  // stages per kc
+  const bool tree = g.kcs % kLeaves == 0u;
+  g.splits = tree && a.splits > 1u ? a.splits : 1u;
+  g.leaves = tree ? kLeaves / g.splits : 1u;    // leaves per unit
+  g.leaf_kc = tree ? g.kcs / kLeaves : g.kcs;   // kc per leaf
   return g;
 }
+
+// first kc of split s of a tile
+__device__ __forceinline__ uint32_t kc_first(const Geo &g, uint32_t split) { return split * g.leaves * g.leaf_kc; }
 
 // Producer: walks (tile, stage) exactly as the consumers do and issues one
 // stage per call.  Lives in lane 0 of warp 0.
@@ -150,16 +166,21 @@ struct Producer {
   uint32_t src0, src1;  // source rows of the tile's two 64-row halves
   Ring ring;
 
+  uint32_t kc0, per_unit;
+
   __device__ __forceinline__ void enter_tile(const GemvArgs &a) {
     if (u >= u_end) return;
-    const GemvGroup &g = a.groups[u / tpg];
+    const uint32_t tile = u / geo.splits;
+    kc0 = kc_first(geo, u % geo.splits);
+    per_unit = geo.leaves * geo.leaf_kc * geo.per_kc;
+    const GemvGroup &g = a.groups[tile / tpg];
     m0 = KIND == 3 ? g.tm1 : g.tm0;
     m1 = g.tm1;
     // the maps were written through the generic proxy (host copy or bank
     // build); make those writes visible to the TMA unit before first use
     tensormap_acquire(m0);
     if (MATS == 2) tensormap_acquire(m1);
-    const uint32_t row0 = (u % tpg) * kTileRows;
+    const uint32_t row0 = (tile % tpg) * kTileRows;
     uint32_t s;
     map_row(a.layout, row0, src0, s);
     map_row(a.layout, row0 + 64u, src1, s);
@@ -178,7 +199,7 @@ struct Producer {
   __device__ __forceinline__ void issue_next(const GemvArgs &a, const Shared &sh) {
     if (u >= u_end) return;
     if (ring_wait(sh, &sh.empty[ring.slot], ring.phase ^ 1u, a.flags)) {
-      const uint32_t m = st % MATS, h = (st / MATS) % geo.halves, kc = st / (MATS * geo.halves);
+      const uint32_t m = st % MATS, h = (st / MATS) % geo.halves, kc = kc0 + st / (MATS * geo.halves);
       mbar_arrive_expect_tx(&sh.full[ring.slot], kStageBytes);
       tma_load_3d(sh.ring + ring.slot * kStageBytes, m == 0 ? m0 : m1, (int)(h ? src1 : src0), (int)(kc * geo.kbs),
                   &sh.full[ring.slot]);
@@ -186,7 +207,7 @@ struct Producer {
       ring.parity = (ring.parity & ~(1u << ring.slot)) | (ring.phase << ring.slot);
     }
     ring.advance(nst);
-    if (++st == geo.per_tile) {
+    if (++st == per_unit) {
       ++u;
       enter_tile(a);
     }
@@ -198,6 +219,23 @@ struct Producer {
         if (!mbar_wait(&sh.full[i], (ring.parity >> i) & 1u)) raise_flag(a.flags, PW_FLAG_WAIT_TIMEOUT);
   }
 };
+
+// K-tree helpers: dst = src, and acc = left + acc (left subtree first).
+template <int MATS>
+__device__ __forceinline__ void tree_copy(float (&dst)[MATS][4], const float (&src)[MATS][4]) {
+#pragma unroll
+  for (int m = 0; m < MATS; ++m)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[m][i] = src[m][i];
+}
+
+template <int MATS>
+__device__ __forceinline__ void tree_add(float (&acc)[MATS][4], const float (&left)[MATS][4]) {
+#pragma unroll
+  for (int m = 0; m < MATS; ++m)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[m][i] = __fadd_rn(left[m][i], acc[m][i]);
+}
 
 template <int KIND>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, const uint32_t nst) {
@@ -216,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, cons
   sh.full = reinterpret_cast<uint64_t *>(smem + L.bars);
   sh.empty = sh.full + nst;
   sh.abort = reinterpret_cast<volatile int *>(sh.empty + nst);
+  sh.last = sh.abort + 1;
 
   const uint32_t warp = threadIdx.x / 32u, lane = threadIdx.x % 32u;
   const uint32_t gid = lane / 4u, tig = lane % 4u;
@@ -237,19 +276,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, cons
 
   const uint32_t n_groups = a.n_groups_dev ? min(*a.n_groups_dev, a.n_groups) : a.n_groups;
   const uint32_t tpg = a.rows / kTileRows;
-  const uint64_t total = (uint64_t)n_groups * tpg;
+  const Geo geo = make_geo(a, MATS);
+  const uint64_t total = (uint64_t)n_groups * tpg * geo.splits;  // units: (tile, split)
   const uint32_t u_begin = (uint32_t)(total * blockIdx.x / gridDim.x);
   const uint32_t u_end = (uint32_t)(total * (blockIdx.x + 1) / gridDim.x);
   const uint32_t kblocks = a.K / 128u;
-  const Geo geo = make_geo(a, MATS);
 
   if (warp == kWarps) {
-    // producer warp: stream every stage of this CTA's tiles into the ring
+    // producer warp: stream every stage of this CTA's units into the ring
     if (lane == 0) {
       Producer<KIND> prod;
       prod.init(a, u_begin, u_end, tpg, nst);
-      const uint64_t stages = (uint64_t)(u_end - u_begin) * geo.per_tile;
-      for (uint64_t i = 0; i < stages; ++i) prod.issue_next(a, sh);
+      while (prod.u < u_end) prod.issue_next(a, sh);
       prod.drain(a, sh);
     }
     return;
@@ -270,9 +308,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, cons
   uint32_t cur_group = 0xffffffffu;
 
   for (uint32_t u = u_begin; u < u_end; ++u) {
-    const uint32_t gi = u / tpg;
+    const uint32_t tile = u / geo.splits, split = u % geo.splits;
+    const uint32_t gi = tile / tpg;
     const GemvGroup grp = a.groups[gi];
-    const uint32_t row0 = (u % tpg) * kTileRows;
+    const uint32_t row0 = (tile % tpg) * kTileRows;
+    const uint32_t kc0 = kc_first(geo, split);
     if (gi != cur_group) {
       // restage this group's activation codes and scales once every warp is
       // done with the previous group's
@@ -309,15 +349,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, cons
       __syncwarp();
     }
 
-    float acc[MATS][4];
+    float acc[MATS][4];                           // current leaf
+    float s0[MATS][4], s1[MATS][4], s2[MATS][4];  // pending left subtrees (1, 2, 4 leaves)
+    const uint32_t st_leaf = geo.leaf_kc * geo.per_kc;
+#pragma unroll 1
+    for (uint32_t leaf = 0; leaf < geo.leaves; ++leaf) {
 #pragma unroll
     for (int m = 0; m < MATS; ++m)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[m][i] = 0.0f;
-
 #pragma unroll 1
-    for (uint32_t st = 0; st < geo.per_tile; ++st) {
-      const uint32_t m = st % MATS, h = (st / MATS) % geo.halves, kc = st / (MATS * geo.halves);
+    for (uint32_t sl = 0; sl < st_leaf; ++sl) {
+      const uint32_t st = leaf * st_leaf + sl;
+      const uint32_t m = st % MATS, h = (st / MATS) % geo.halves, kc = kc0 + st / (MATS * geo.halves);
       const bool ok = ring_wait(sh, &sh.full[ring.slot], ring.phase, a.flags);
       if (ok && h == my_half) {
         const uint32_t box = ring_base + ring.slot * kStageBytes;
@@ -356,6 +400,66 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, cons
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.empty[ring.slot]);
       ring.advance(nst);
+    }
+    // fold the leaf into the pairwise tree (left subtree + right, fixed order);
+    // after the unit's last leaf acc holds its whole subtree
+    if ((leaf & 1u) == 0u) {
+      if (leaf + 1u < geo.leaves) tree_copy<MATS>(s0, acc);
+    } else {
+      tree_add<MATS>(acc, s0);
+      if ((leaf & 2u) == 0u) {
+        if (leaf + 1u < geo.leaves) tree_copy<MATS>(s1, acc);
+      } else {
+        tree_add<MATS>(acc, s1);
+        if ((leaf & 4u) == 0u) {
+          if (leaf + 1u < geo.leaves) tree_copy<MATS>(s2, acc);
+        } else {
+          tree_add<MATS>(acc, s2);
+        }
+      }
+    }
+    }
+
+    if (geo.splits > 1u) {
+      // split-K: publish this subtree; the last CTA of the tile adds all
+      // subtrees in the same pairwise tree and runs the epilogue
+      float *mine = a.split_ws + ((size_t)(tile * geo.splits + split) * MATS) * 1024u;
+#pragma unroll
+      for (int m = 0; m < MATS; ++m)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          mine[m * 1024 + (warp * 16u + gid + (i >= 2 ? 8u : 0u)) * 8u + tig * 2u + (i & 1u)] = acc[m][i];
+      __threadfence();
+      named_bar_sync(1, kConsumerThreads);
+      if (threadIdx.x == 0) *sh.last = atomicAdd(a.split_cnt + tile, 1u) == geo.splits - 1u;
+      named_bar_sync(1, kConsumerThreads);
+      if (!*sh.last) continue;
+      __threadfence();
+#pragma unroll 1
+      for (uint32_t sp = 0; sp < geo.splits; ++sp) {
+        const float *src = a.split_ws + ((size_t)(tile * geo.splits + sp) * MATS) * 1024u;
+#pragma unroll
+        for (int m = 0; m < MATS; ++m)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            acc[m][i] = __ldcg(src + m * 1024 + (warp * 16u + gid + (i >= 2 ? 8u : 0u)) * 8u + tig * 2u + (i & 1u));
+        if ((sp & 1u) == 0u) {
+          if (sp + 1u < geo.splits) tree_copy<MATS>(s0, acc);
+        } else {
+          tree_add<MATS>(acc, s0);
+          if ((sp & 2u) == 0u) {
+            if (sp + 1u < geo.splits) tree_copy<MATS>(s1, acc);
+          } else {
+            tree_add<MATS>(acc, s1);
+            if ((sp & 4u) == 0u) {
+              if (sp + 1u < geo.splits) tree_copy<MATS>(s2, acc);
+            } else {
+              tree_add<MATS>(acc, s2);
+            }
+          }
+        }
+      }
+      if (threadIdx.x == 0) a.split_cnt[tile] = 0u;  // ready for the next call
     }
 
     // epilogue: thread holds rows (gid, gid+8) x tokens (2 tig, 2 tig + 1)

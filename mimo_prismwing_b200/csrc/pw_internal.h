@@ -77,6 +77,9 @@ struct GemvArgs {
                                  //   ends, so the producer may stream them before waiting
   uint16_t *gate_bf16;           // tcgen05 kind 2: bf16(gate) and bf16(up) [*, rows], the
   uint16_t *up_bf16;             //   staged SwiGLU's inputs (k_swiglu_quant finishes it)
+  uint32_t splits;               // GEMV split-K over the 8-leaf K tree: 1, 2, 4 or 8
+  float *split_ws;               //   partial sums [tile][split][mats][128 rows][8 tokens]
+  uint32_t *split_cnt;           //   per-tile arrival counters (zero; reset by the last CTA)
 };
 
 // Wide-width grouped GEMM (tcgen05): the GEMV arguments plus TMA maps of the

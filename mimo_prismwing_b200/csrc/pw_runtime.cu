@@ -119,6 +119,8 @@ struct pw_runtime {
   pw_profile last_profile{};
   std::string err;
   EpState *ep = nullptr;
+  float *split_ws = nullptr;      // GEMV split-K partial sums (allocated on first use)
+  uint32_t *split_cnt = nullptr;  // and per-tile arrival counters
 };
 
 namespace {
@@ -360,6 +362,52 @@ int grid_for(const pw_runtime *rt, uint64_t units) {
   return g ? (int)g : 1;
 }
 
+// GEMV split-K: with fewer 128-row tiles than SMs (a lone expert), spread
+// each tile's K tree over 2, 4 or 8 CTAs.  Cost model per CTA: its units x
+// (1/S of a tile's streaming time + a fixed ~3 us per unit for staging the
+// activations and scales, publishing the partial sums and the last CTA's
+// reduction), a tile streaming at ~40 GB/s per SM.  Results do not depend on
+// the count (the GEMV adds K in a fixed 8-leaf tree).
+constexpr size_t kSplitWsBytes = (size_t)16 << 20;
+constexpr uint32_t kSplitCounters = 1024;
+
+uint32_t gemv_splits(const pw_runtime *rt, uint64_t tiles, uint32_t K, uint32_t layout, int mats) {
+  const uint32_t kbs = layout == PW_LAYOUT_PLAIN ? 2u : 4u;
+  const uint32_t kcs = (K / 128u + kbs - 1u) / kbs;
+  const uint64_t sms = (uint64_t)rt->num_sms;
+  if (kcs % 8u || tiles == 0 || tiles >= sms) return 1u;
+  const double tile_us = 128.0 * K * mats / 40e3;  // bytes / (40 GB/s) in us
+  const double ovh = 3.0 / tile_us;                 // per-unit overhead, in tiles
+  auto cost = [&](uint32_t S) { return (double)((tiles * S + sms - 1u) / sms) * (1.0 / S + ovh); };
+  uint32_t bs = 1u;
+  for (uint32_t S = 2u; S <= 8u; S *= 2u)
+    if (cost(S) < cost(bs)) bs = S;
+  return bs;
+}
+
+// Set up a GEMV launch over `tiles` (group, row-tile) pairs: split-K state
+// and the grid.
+int gemv_launch_setup(pw_runtime *rt, GemvArgs &a, uint64_t tiles, int mats, int &grid) {
+  const uint32_t S = gemv_splits(rt, tiles, a.K, a.layout, mats);
+  grid = grid_for(rt, tiles * S);
+  if (S == 1u) return PW_OK;
+  if ((size_t)tiles * S * mats * 4096u > kSplitWsBytes || tiles > kSplitCounters) {
+    grid = grid_for(rt, tiles);
+    return PW_OK;
+  }
+  if (!rt->split_ws) {
+    CK(cudaMalloc(&rt->split_ws, kSplitWsBytes));
+    CK(cudaMalloc(&rt->split_cnt, kSplitCounters * sizeof(uint32_t)));
+  }
+  // the last CTA of every tile resets its counter; clear them anyway in case
+  // an earlier call was cut short
+  CK(cudaMemsetAsync(rt->split_cnt, 0, tiles * sizeof(uint32_t), rt->stream));
+  a.splits = S;
+  a.split_ws = rt->split_ws;
+  a.split_cnt = rt->split_cnt;
+  return PW_OK;
+}
+
 }  // namespace
 
 // =================================================================== C ABI
@@ -414,6 +462,8 @@ void pw_runtime_destroy(pw_runtime *rt) {
     delete rt->ep;
   }
   if (rt->scratch) cudaFree(rt->scratch);
+  if (rt->split_ws) cudaFree(rt->split_ws);
+  if (rt->split_cnt) cudaFree(rt->split_cnt);
   if (rt->d_flags) cudaFree(rt->d_flags);
   if (rt->ev0) cudaEventDestroy(rt->ev0);
   if (rt->ev1) cudaEventDestroy(rt->ev1);
@@ -575,7 +625,9 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
     }
     {
       ProfScope ps(rt, P_PROJ, 1);
-      const int grid = grid_for(rt, (uint64_t)groups.size() * (N / (kind == 1 ? 64u : 128u)));
+      int grid = grid_for(rt, (uint64_t)groups.size() * (N / (kind == 1 ? 64u : 128u)));
+      if (!wide && kind != 1 && (s = gemv_launch_setup(rt, a, (uint64_t)groups.size() * (N / 128u), 1, grid)) != PW_OK)
+        return s;
       if (wide) {
         GemmArgs A{};
         A.g = a;
@@ -613,8 +665,8 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
                                 const uint32_t *tok_list, const uint8_t *xc, const float *xs, float *hidden,
                                 float *gate_tmp, float *up_tmp, uint8_t *hc, float *hs, float *down,
                                 uint32_t down_round, uint64_t units_hint) {
-  const int grid_gu = grid_for(rt, units_hint * (I / 128u));
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
+  int s = PW_OK, grid_gu = 0;
   {
   ProfScope ps(rt, P_GATEUP, fused ? 1 : 3);
   if (fused) {
@@ -628,6 +680,7 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
     a.out_stride = I;
     a.q_codes = hc;
     a.q_scales = hs;
+    if ((s = gemv_launch_setup(rt, a, units_hint * (I / 128u), 2, grid_gu)) != PW_OK) return s;
     CK(launch_gemv(2, a, grid_gu, rt->stream));
   } else {
     // gate and up as two block-scaled projections, then the staged SwiGLU
@@ -639,6 +692,8 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
     a.x_scales = xs;
     a.out_stride = I;
     a.out = gate_tmp;
+    // gate and up take the same split, so the pair is bit-identical to the fused kernel
+    if ((s = gemv_launch_setup(rt, a, units_hint * (I / 128u), 1, grid_gu)) != PW_OK) return s;
     CK(launch_gemv(0, a, grid_gu, rt->stream));
     // kind 3 is the same projection over each group's second matrix (up)
     GemvArgs b = a;
@@ -661,8 +716,10 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
   // groups and weights were final before gate/up ran; with PDL the down
   // kernel's producer streams weights during gate/up's last wave
   d.early_weights = (pdl_enabled() && fused) ? 1u : 0u;
+  int grid_dn = 0;
+  if ((s = gemv_launch_setup(rt, d, units_hint * (H / 128u), 1, grid_dn)) != PW_OK) return s;
   ProfScope ps(rt, P_DOWN, 1);
-  CK(launch_gemv(0, d, grid_for(rt, units_hint * (H / 128u)), rt->stream));
+  CK(launch_gemv(0, d, grid_dn, rt->stream));
   return PW_OK;
 }
 
