@@ -316,7 +316,8 @@ def run_ours(args, rank, world, local_rank):
     if ep:
         box = [WideMoeRuntime.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
-        rt.ep_init(rank, world, box[0], timeout_ms=120000)
+        rt.ep_init(rank, world, box[0], timeout_ms=120000, max_tokens=PREFILL_TOKENS // world, hidden=HIDDEN,
+                   local_experts=EXPERTS // world)
     layers = Layers(rt, rank, world, args.banks, dev)
     stream = torch.cuda.Stream(device=dev)
     rt.set_stream(stream)

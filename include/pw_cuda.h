@@ -251,8 +251,17 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
  * out of time, or sees an NCCL error, aborts the communicator and returns
  * PW_ERR_TIMEOUT / PW_ERR_NCCL, after which the runtime refuses further
  * expert-parallel calls. */
+/* max_tokens (0 = 2048, at most 2048) bounds the tokens any rank passes per
+ * layer; every rank must pass the same value.  The expert rows travel by
+ * peer-memory stores: each rank's receive window, sized for max_tokens,
+ * `hidden` and `local_experts` (experts per rank), is mapped into the other
+ * ranks through CUDA IPC here (hidden = 0 defers that to the first layer
+ * call, which is then collective too).  With PW_EP_NCCL_TRANSPORT in `flags`
+ * the rows travel by NCCL send/recv instead, planned on the host. */
+#define PW_EP_NCCL_TRANSPORT 1u
 int pw_ep_unique_id(void *id, uint32_t bytes);
-int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t bytes, uint32_t timeout_ms);
+int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t bytes, uint32_t timeout_ms,
+               uint32_t max_tokens, uint32_t hidden, uint32_t local_experts, uint32_t flags);
 int pw_ep_rank(const pw_runtime *rt, int *rank, int *world);
 
 /* Collective routed layer.  Every rank passes its own tokens (x [tokens, H],
@@ -260,10 +269,10 @@ int pw_ep_rank(const pw_runtime *rt, int *rank, int *world);
  * [g * n, (g + 1) * n) of the router's E = n * world.  Routing is local; token
  * codes and scales go to the expert owners and bf16 expert outputs come back;
  * the combine runs on the token's rank in ascending expert order, so y is
- * bit-identical to pw_moe_layer on one GPU.  The call waits (bounded) for the
- * all-gathered per-expert counts; with PW_MEM_DEVICE | PW_MEM_ASYNC it returns
- * once the rest is enqueued (the next expert-parallel call, pw_synchronize or
- * pw_read_error_flags observes it), otherwise when the layer is done.
+ * bit-identical to pw_moe_layer on one GPU.  With PW_MEM_DEVICE | PW_MEM_ASYNC
+ * it returns once its work is enqueued (the peer-memory transport needs no
+ * host round trip; the NCCL transport waits for the all-gathered per-expert
+ * counts first), otherwise when the layer is done.
  * stats->unique_experts / expert_rows count this rank's local work. */
 int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,
                     uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem,

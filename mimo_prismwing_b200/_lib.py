@@ -55,7 +55,7 @@ def _bind(L: ctypes.CDLL) -> None:
     L.pw_bank_destroy.restype = None
     L.pw_moe_layer.argtypes = [vp, vp, vp, vp, u32, vp, vp, vp, u32, vp]
     L.pw_ep_unique_id.argtypes = [vp, u32]
-    L.pw_ep_init.argtypes = [vp, i32, i32, vp, u32, u32]
+    L.pw_ep_init.argtypes = [vp, i32, i32, vp, u32, u32, u32, u32, u32, u32]
     L.pw_ep_rank.argtypes = [vp, _p(i32), _p(i32)]
     L.pw_ep_plan.argtypes = [vp, u32, u32, u32, vp, vp, vp, vp, vp]
     L.pw_ep_moe_layer.argtypes = [vp, vp, vp, vp, u32, vp, vp, vp, u32, vp]

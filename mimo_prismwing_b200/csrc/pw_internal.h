@@ -98,8 +98,9 @@ cudaError_t launch_gather_rows(const uint8_t *codes, const float *scales, const 
 
 // Kernel launchers (pw_kernels.cu).  All enqueue on `stream` and return the
 // launch status.
+// rows_dev (optional): the row count lives on the device; `rows` bounds it.
 cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_t *codes, float *scales,
-                            uint32_t *flags, cudaStream_t stream);
+                            uint32_t *flags, cudaStream_t stream, const uint32_t *rows_dev = nullptr);
 // kind: 0 = block-scaled (quantized x) over each group's w0/s0, 1 = readable
 // (f32 x), 2 = fused gate/up SwiGLU over w0/s0 and w1/s1, 3 = block-scaled
 // over w1/s1 (the unfused up projection)
@@ -158,11 +159,42 @@ cudaError_t launch_scatter_rows_bf16(const float *rows, const uint32_t *idx, uin
 // Staged SwiGLU of bf16 gate/up [rows, cols] followed by the hidden's dynamic
 // FP8 quantization (per 128 values); h (f32, optional) receives the SwiGLU.
 cudaError_t launch_swiglu_quant(const uint16_t *gate, const uint16_t *up, uint32_t rows, uint32_t cols, float *h,
-                                uint8_t *codes, float *scales, uint32_t *flags, cudaStream_t stream);
+                                uint8_t *codes, float *scales, uint32_t *flags, cudaStream_t stream,
+                                const uint32_t *rows_dev = nullptr);
+// n = rows * row_len elements; rows_dev (optional) caps the rows on the device
 cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t n, uint32_t *flags,
-                          cudaStream_t stream);
+                          cudaStream_t stream, const uint32_t *rows_dev = nullptr, uint32_t row_len = 1);
 cudaError_t launch_validate_fp8(const uint8_t *w, uint64_t n, const float *s, uint64_t ns,
                                 unsigned long long *first_bad, uint32_t *flags, cudaStream_t stream);
+
+// Expert-parallel window of one rank (byte offsets from its base): flags
+// written by peers, the mailbox (per-source per-local-expert counts and the
+// source's placement index of its first row for this owner), the receive
+// slots (source s: rows [s * slot_rows, (s + 1) * slot_rows)) and the
+// returned bf16 rows of this rank's own placements.
+struct EpWindow {
+  uint64_t flag_data, flag_ret, mail_cnt, mail_base, recv_codes, recv_scales, ret_rows, total;
+  uint32_t G, L, H, slot_rows;
+};
+
+struct EpArgs {
+  uint8_t *const *peers;  // device array: each rank's window base (this rank's too)
+  EpWindow w;
+  uint32_t rank, epoch;
+  uint32_t *flags;
+  uint64_t deadline_ns;
+};
+
+cudaError_t launch_ep_dispatch(const EpArgs &e, const uint32_t *offsets, const uint8_t *codes, const float *scales,
+                               uint32_t P, uint32_t *ctr, int grid, cudaStream_t stream);
+cudaError_t launch_ep_plan(const EpArgs &e, const BankTable &bank, uint32_t chunk, uint32_t cap, uint32_t *perm,
+                           uint32_t *src_rank, uint32_t *src_place, GemvGroup *gu, GemvGroup *dn, uint32_t *n_groups,
+                           uint32_t *p_recv, cudaStream_t stream);
+cudaError_t launch_ep_gather(const EpArgs &e, const uint32_t *perm, const uint32_t *p_recv, uint8_t *codes,
+                             float *scales, int grid, cudaStream_t stream);
+cudaError_t launch_ep_return(const EpArgs &e, const float *down, const uint32_t *src_rank, const uint32_t *src_place,
+                             const uint32_t *p_recv, uint32_t *ctr, int grid, cudaStream_t stream);
+cudaError_t launch_ep_wait_returns(const EpArgs &e, cudaStream_t stream);
 
 // NCCL, dlopen'ed on first use (pw_nccl.cu).  Every call that can wait takes
 // a deadline in seconds; ncclInProgress past it means "abort the comm".

@@ -19,9 +19,11 @@ void set_pdl(bool on) { t_pdl = on; }
 // code = RNE_e4m3(clamp(x/scale, +-448)).  IEEE divisions (__fdiv_rn) keep it
 // bit-exact with the reference; lane l holds values 4l..4l+3.
 __global__ void k_quantize(const float *__restrict__ x, uint64_t groups, uint8_t *__restrict__ codes,
-                           float *__restrict__ scales, uint32_t *flags) {
+                           float *__restrict__ scales, uint32_t *flags, const uint32_t *rows_dev,
+                           uint32_t groups_per_row) {
   pdl_wait();
   pdl_launch_dependents();
+  if (rows_dev) groups = min(groups, (uint64_t)*rows_dev * groups_per_row);
   const uint64_t warp_global = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32u;
   const uint32_t lane = threadIdx.x % 32u;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) / 32u;
@@ -42,14 +44,15 @@ __global__ void k_quantize(const float *__restrict__ x, uint64_t groups, uint8_t
 }
 
 cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_t *codes, float *scales,
-                            uint32_t *flags, cudaStream_t stream) {
+                            uint32_t *flags, cudaStream_t stream, const uint32_t *rows_dev) {
   if (cols % 128u) return cudaErrorInvalidValue;
   const uint64_t groups = (uint64_t)rows * (cols / 128u);
   if (groups == 0) return cudaSuccess;
   const int threads = 256;
   uint64_t blocks = (groups * 32u + threads - 1) / threads;
   if (blocks > 148u * 16u) blocks = 148u * 16u;
-  return launch_kernel(k_quantize, dim3((unsigned)blocks), dim3(threads), 0, stream, x, groups, codes, scales, flags);
+  return launch_kernel(k_quantize, dim3((unsigned)blocks), dim3(threads), 0, stream, x, groups, codes, scales, flags,
+                       rows_dev, cols / 128u);
 }
 
 // --------------------------------------------------------------- bf16 round
@@ -655,7 +658,8 @@ cudaError_t launch_validate_fp8(const uint8_t *w, uint64_t n, const float *s, ui
 // ----------------------------------------------------- unfused staged SwiGLU
 // kernels/block_fp8_gemv.metal:139 bf16_staged_swiglu (the non-fused runtime).
 __global__ void k_swiglu(const float *__restrict__ gate, const float *__restrict__ up, float *__restrict__ h,
-                         uint32_t n, uint32_t *flags) {
+                         uint32_t n, uint32_t *flags, const uint32_t *rows_dev, uint32_t row_len) {
+  if (rows_dev) n = min(n, *rows_dev * row_len);
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const float r = staged_swiglu(gate[i], up[i]);
     if (!finite(r)) raise_flag(flags, PW_FLAG_NONFINITE_SWIGLU);
@@ -664,11 +668,11 @@ __global__ void k_swiglu(const float *__restrict__ gate, const float *__restrict
 }
 
 cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t n, uint32_t *flags,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, const uint32_t *rows_dev, uint32_t row_len) {
   if (n == 0) return cudaSuccess;
   unsigned blocks = (n + 255u) / 256u;
   if (blocks > 148u * 8u) blocks = 148u * 8u;
-  k_swiglu<<<blocks, 256, 0, stream>>>(gate, up, h, n, flags);
+  k_swiglu<<<blocks, 256, 0, stream>>>(gate, up, h, n, flags, rows_dev, row_len);
   return cudaGetLastError();
 }
 
@@ -680,9 +684,10 @@ cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t
 // warp per 128-value group; lane l holds values 4l..4l+3.
 __global__ void k_swiglu_quant(const uint16_t *__restrict__ gate, const uint16_t *__restrict__ up, uint64_t groups,
                                float *__restrict__ h, uint8_t *__restrict__ codes, float *__restrict__ scales,
-                               uint32_t *flags) {
+                               uint32_t *flags, const uint32_t *rows_dev, uint32_t groups_per_row) {
   pdl_wait();
   pdl_launch_dependents();
+  if (rows_dev) groups = min(groups, (uint64_t)*rows_dev * groups_per_row);
   const uint64_t warp_global = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32u;
   const uint32_t lane = threadIdx.x % 32u;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) / 32u;
@@ -713,7 +718,8 @@ __global__ void k_swiglu_quant(const uint16_t *__restrict__ gate, const uint16_t
 }
 
 cudaError_t launch_swiglu_quant(const uint16_t *gate, const uint16_t *up, uint32_t rows, uint32_t cols, float *h,
-                                uint8_t *codes, float *scales, uint32_t *flags, cudaStream_t stream) {
+                                uint8_t *codes, float *scales, uint32_t *flags, cudaStream_t stream,
+                                const uint32_t *rows_dev) {
   if (cols % 128u) return cudaErrorInvalidValue;
   const uint64_t groups = (uint64_t)rows * (cols / 128u);
   if (groups == 0) return cudaSuccess;
@@ -721,7 +727,7 @@ cudaError_t launch_swiglu_quant(const uint16_t *gate, const uint16_t *up, uint32
   uint64_t blocks = (groups * 32u + threads - 1) / threads;
   if (blocks > 148u * 8u) blocks = 148u * 8u;
   return launch_kernel(k_swiglu_quant, dim3((unsigned)blocks), dim3(threads), 0, stream, gate, up, groups, h, codes,
-                       scales, flags);
+                       scales, flags, rows_dev, cols / 128u);
 }
 
 }  // namespace pw

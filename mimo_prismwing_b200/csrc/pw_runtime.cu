@@ -95,6 +95,15 @@ struct EpState {
   size_t h_off_cap = 0;
   void *h_plan = nullptr;            // pinned: row permutation + expert groups
   size_t h_plan_cap = 0;
+  // peer-memory transport (default)
+  bool p2p = true;
+  uint32_t max_tokens = 2048;        // per rank and call; sizes the receive slots
+  void *win = nullptr;               // this rank's window
+  EpWindow w{};
+  std::vector<void *> peer_win;      // IPC mappings of the other ranks' windows
+  uint8_t **d_peers = nullptr;       // device array of every rank's window base
+  uint32_t *d_ctr = nullptr;         // last-CTA counters of dispatch / return
+  uint32_t epoch = 0;
 };
 
 struct pw_runtime {
@@ -459,6 +468,11 @@ void pw_runtime_destroy(pw_runtime *rt) {
     if (rt->ep->scratch) cudaFree(rt->ep->scratch);
     if (rt->ep->h_off) cudaFreeHost(rt->ep->h_off);
     if (rt->ep->h_plan) cudaFreeHost(rt->ep->h_plan);
+    for (size_t g = 0; g < rt->ep->peer_win.size(); ++g)
+      if (rt->ep->peer_win[g] && rt->ep->peer_win[g] != rt->ep->win) cudaIpcCloseMemHandle(rt->ep->peer_win[g]);
+    if (rt->ep->win) cudaFree(rt->ep->win);
+    if (rt->ep->d_peers) cudaFree(rt->ep->d_peers);
+    if (rt->ep->d_ctr) cudaFree(rt->ep->d_ctr);
     delete rt->ep;
   }
   if (rt->scratch) cudaFree(rt->scratch);
@@ -664,7 +678,7 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
                                 const uint32_t *n_groups_dev, uint32_t slots, uint32_t H, uint32_t I,
                                 const uint32_t *tok_list, const uint8_t *xc, const float *xs, float *hidden,
                                 float *gate_tmp, float *up_tmp, uint8_t *hc, float *hs, float *down,
-                                uint32_t down_round, uint64_t units_hint) {
+                                uint32_t down_round, uint64_t units_hint, const uint32_t *slots_dev = nullptr) {
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   int s = PW_OK, grid_gu = 0;
   {
@@ -699,12 +713,12 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
     GemvArgs b = a;
     b.out = up_tmp;
     CK(launch_gemv(3, b, grid_gu, rt->stream));
-    CK(launch_swiglu(gate_tmp, up_tmp, hidden, slots * I, rt->d_flags, rt->stream));
+    CK(launch_swiglu(gate_tmp, up_tmp, hidden, slots * I, rt->d_flags, rt->stream, slots_dev, I));
   }
   }
   if (!fused) {
     ProfScope ps(rt, P_QUANT, 1);
-    CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream));
+    CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream, slots_dev));
   }
   GemvArgs d = gemv_args(rt, dn, n_groups, H, I, PW_LAYOUT_PLAIN);
   d.n_groups_dev = n_groups_dev;
@@ -730,7 +744,7 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
                                      const uint32_t *n_groups_dev, uint32_t slots, uint32_t H, uint32_t I,
                                      const uint8_t *xg, const float *xsg, float *hidden, float *gate_tmp,
                                      float *up_tmp, uint8_t *hc, float *hs, float *down, uint32_t down_round,
-                                     uint64_t units_hint) {
+                                     uint64_t units_hint, const uint32_t *slots_dev = nullptr) {
   const int grid_gu = grid_for(rt, units_hint * (I / 128u));
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   {
@@ -757,16 +771,16 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
       GemmArgs B = A;
       B.g.out = up_tmp;
       CK(launch_gemm_tc(3, B, grid_gu, rt->stream));
-      CK(launch_swiglu(gate_tmp, up_tmp, hidden, slots * I, rt->d_flags, rt->stream));
+      CK(launch_swiglu(gate_tmp, up_tmp, hidden, slots * I, rt->d_flags, rt->stream, slots_dev, I));
     }
   }
   {
     ProfScope ps(rt, P_QUANT, 1);
     if (fused)
       CK(launch_swiglu_quant(reinterpret_cast<const uint16_t *>(gate_tmp), reinterpret_cast<const uint16_t *>(up_tmp),
-                             slots, I, hidden, hc, hs, rt->d_flags, rt->stream));
+                             slots, I, hidden, hc, hs, rt->d_flags, rt->stream, slots_dev));
     else
-      CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream));
+      CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream, slots_dev));
   }
   GemmArgs D{};
   D.g = gemv_args(rt, dn, n_groups, H, I, PW_LAYOUT_PLAIN);
@@ -1351,6 +1365,194 @@ int ep_pinned(pw_runtime *rt, T *&buf, size_t &cap, size_t bytes) {
   return PW_OK;
 }
 
+// Builds this rank's window for L local experts of hidden H and maps every
+// other rank's (collective: IPC handles and geometry go through one
+// all-gather, and a second one orders every rank's zeroed, mapped window
+// before any peer stores into it).
+int ep_window_setup(pw_runtime *rt, uint32_t L, uint32_t H) {
+  EpState *ep = rt->ep;
+  const uint32_t G = (uint32_t)ep->world, r = (uint32_t)ep->rank;
+  CK(cudaStreamSynchronize(rt->stream));
+  for (size_t g = 0; g < ep->peer_win.size(); ++g)
+    if (ep->peer_win[g] && ep->peer_win[g] != ep->win) CK(cudaIpcCloseMemHandle(ep->peer_win[g]));
+  ep->peer_win.clear();
+  if (ep->win) CK(cudaFree(ep->win));
+  if (ep->d_peers) CK(cudaFree(ep->d_peers));
+  if (ep->d_ctr) CK(cudaFree(ep->d_ctr));
+  ep->win = nullptr;
+  ep->d_peers = nullptr;
+  ep->d_ctr = nullptr;
+  EpWindow w{};
+  w.G = G;
+  w.L = L;
+  w.H = H;
+  w.slot_rows = ep->max_tokens * 8u;
+  uint64_t off = 0;
+  auto take = [&](uint64_t bytes) {
+    const uint64_t o = off;
+    off += (bytes + 255u) & ~uint64_t(255);
+    return o;
+  };
+  w.flag_data = take(G * 4u);
+  w.flag_ret = take(G * 4u);
+  w.mail_cnt = take((uint64_t)G * L * 4u);
+  w.mail_base = take(G * 4u);
+  w.recv_codes = take((uint64_t)G * w.slot_rows * H);
+  w.recv_scales = take((uint64_t)G * w.slot_rows * (H / 128u) * 4u);
+  w.ret_rows = take((uint64_t)w.slot_rows * H * 2u);
+  w.total = off;
+  CK(cudaMalloc(&ep->win, w.total));
+  CK(cudaMemset(ep->win, 0, w.total));
+  struct Rec {
+    cudaIpcMemHandle_t h;
+    uint32_t L, H, slot_rows, pad;
+  };
+  Rec mine{};
+  if (G > 1) CK(cudaIpcGetMemHandle(&mine.h, ep->win));
+  mine.L = L;
+  mine.H = H;
+  mine.slot_rows = w.slot_rows;
+  std::vector<Rec> recs(G);
+  Rec *d_rec = nullptr;
+  CK(cudaMalloc(&d_rec, sizeof(Rec) * (G + 1)));
+  CK(cudaMemcpy(d_rec + G, &mine, sizeof(Rec), cudaMemcpyHostToDevice));
+  NK(pw::nccl::all_gather(d_rec + G, d_rec, sizeof(Rec), ncclUint8, ep->comm, rt->stream, ep->timeout_s),
+     "window handle exchange");
+  CK(cudaMemcpyAsync(recs.data(), d_rec, sizeof(Rec) * G, cudaMemcpyDeviceToHost, rt->stream));
+  int s = ep_wait(rt);
+  cudaFree(d_rec);
+  if (s != PW_OK) return s;
+  for (uint32_t g = 0; g < G; ++g)
+    if (recs[g].L != L || recs[g].H != H || recs[g].slot_rows != w.slot_rows)
+      return ep_dead(rt, PW_ERR_SHAPE, "ranks disagree on experts per rank, hidden size or max_tokens", ncclInvalidUsage);
+  ep->peer_win.assign(G, nullptr);
+  ep->peer_win[r] = ep->win;
+  for (uint32_t g = 0; g < G; ++g)
+    if (g != r) CK(cudaIpcOpenMemHandle(&ep->peer_win[g], recs[g].h, cudaIpcMemLazyEnablePeerAccess));
+  CK(cudaMalloc(&ep->d_peers, G * sizeof(uint8_t *)));
+  CK(cudaMemcpy(ep->d_peers, ep->peer_win.data(), G * sizeof(void *), cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&ep->d_ctr, 4 * sizeof(uint32_t)));
+  CK(cudaMemset(ep->d_ctr, 0, 4 * sizeof(uint32_t)));
+  ep->w = w;
+  ep->epoch = 0;
+  // barrier: no rank stores into a window before its owner has mapped all
+  uint32_t *d_b = nullptr;
+  CK(cudaMalloc(&d_b, (G + 1) * sizeof(uint32_t)));
+  CK(cudaMemset(d_b, 0, (G + 1) * sizeof(uint32_t)));
+  NK(pw::nccl::all_gather(d_b + G, d_b, 1, ncclUint32, ep->comm, rt->stream, ep->timeout_s), "window barrier");
+  s = ep_wait(rt);
+  cudaFree(d_b);
+  return s;
+}
+
+// Rest of a routed layer on the peer-memory transport: everything after the
+// local routing and the gathered send rows stays on the device.
+int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_t tokens,
+                 float *y, uint32_t *selected, float *weights, const ScheduleOut &so, float *dy, uint32_t *sel,
+                 float *wts, const uint8_t *xsend, const float *ssend) {
+  EpState *ep = rt->ep;
+  const EpWindow &w = ep->w;
+  const uint32_t G = w.G, L = w.L, H = bank->hidden, I = bank->inter, P = tokens * 8u;
+  const uint32_t cap = G * w.slot_rows;  // rows this rank can receive
+  // the tcgen05 GEMM when the layer is wide (judged from this rank's tokens:
+  // the owners' row counts are known only on the device)
+  const bool wide = (uint64_t)G * tokens >= kWideLayerTokens;
+  const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
+  const uint32_t max_groups = cap / chunk + L;
+  const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
+  int s;
+  Arena br;
+  uint32_t *perm = nullptr, *src_rank = nullptr, *src_place = nullptr, *n_groups = nullptr, *p_recv = nullptr;
+  GemvGroup *gu = nullptr, *dn = nullptr;
+  uint8_t *xg = nullptr, *hc = nullptr;
+  float *xsg = nullptr, *hid = nullptr, *gt = nullptr, *ut = nullptr, *hs = nullptr, *down = nullptr;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1 && br.off > ep->cap) {
+      CK(cudaStreamSynchronize(rt->stream));
+      if (ep->scratch) CK(cudaFree(ep->scratch));
+      ep->scratch = nullptr;
+      ep->cap = 0;
+      size_t c = (size_t)1 << 20;
+      while (c < br.off) c *= 2;
+      CK(cudaMalloc(&ep->scratch, c));
+      ep->cap = c;
+    }
+    if (pass == 1) br = Arena{static_cast<char *>(ep->scratch), 0};
+    perm = br.take<uint32_t>(cap);
+    src_rank = br.take<uint32_t>(cap);
+    src_place = br.take<uint32_t>(cap);
+    gu = br.take<GemvGroup>(max_groups);
+    dn = br.take<GemvGroup>(max_groups);
+    n_groups = br.take<uint32_t>(3);  // [n_groups, p_recv, experts used], read back together
+    p_recv = n_groups ? n_groups + 1 : nullptr;
+    xg = wide ? br.take<uint8_t>((size_t)cap * H) : nullptr;
+    xsg = wide ? br.take<float>((size_t)cap * (H / 128u)) : nullptr;
+    hid = fused ? nullptr : br.take<float>((size_t)cap * I);
+    gt = fused && !wide ? nullptr : br.take<float>((size_t)cap * I);
+    ut = fused && !wide ? nullptr : br.take<float>((size_t)cap * I);
+    hc = br.take<uint8_t>((size_t)cap * I);
+    hs = br.take<float>((size_t)cap * (I / 128u));
+    down = br.take<float>((size_t)cap * H);
+  }
+  const uint32_t epoch = ++ep->epoch;
+  const EpArgs ea{ep->d_peers, w, (uint32_t)ep->rank, epoch, rt->d_flags, (uint64_t)(ep->timeout_s * 1e9)};
+  uint8_t *mine = static_cast<uint8_t *>(ep->win);
+  {
+    ProfScope ps(rt, P_SCHED, 2);
+    CK(launch_ep_dispatch(ea, so.offsets, xsend, ssend, P, ep->d_ctr, grid_for(rt, P / 4u), rt->stream));
+    CK(launch_ep_plan(ea, bank->table, chunk, cap, perm, src_rank, src_place, gu, dn, n_groups, p_recv, rt->stream));
+  }
+  if (wide) {
+    {
+      ProfScope ps(rt, P_QUANT, 1);
+      CK(launch_ep_gather(ea, perm, p_recv, xg, xsg, rt->num_sms, rt->stream));
+    }
+    s = enqueue_expert_chain_wide(rt, gu, dn, max_groups, n_groups, cap, H, I, xg, xsg, hid, gt, ut, hc, hs, down, 1,
+                                  max_groups, p_recv);
+  } else {
+    s = enqueue_expert_chain(rt, gu, dn, max_groups, n_groups, cap, H, I, perm,
+                             reinterpret_cast<const uint8_t *>(mine + w.recv_codes),
+                             reinterpret_cast<const float *>(mine + w.recv_scales), hid, gt, ut, hc, hs, down, 1,
+                             max_groups, p_recv);
+  }
+  if (s != PW_OK) return s;
+  {
+    ProfScope ps(rt, P_COMBINE, 3);
+    CK(launch_ep_return(ea, down, src_rank, src_place, p_recv, ep->d_ctr + 1, rt->num_sms, rt->stream));
+    CK(launch_ep_wait_returns(ea, rt->stream));
+    if (tokens)
+      CK(launch_combine_bf16(reinterpret_cast<const uint16_t *>(mine + w.ret_rows), so.slot_place, so.placement_w,
+                             tokens, H, dy, rt->d_flags, rt->stream));
+  }
+  if (tokens) {
+    if (call.host()) {
+      if ((s = call.stage_out(y, dy, (size_t)tokens * H * 4)) != PW_OK) return s;
+      if (selected && (s = call.stage_out(selected, sel, (size_t)P * 4)) != PW_OK) return s;
+      if (weights && (s = call.stage_out(weights, wts, (size_t)P * 4)) != PW_OK) return s;
+    } else {
+      if (selected) CK(cudaMemcpyAsync(selected, sel, (size_t)P * 4, cudaMemcpyDeviceToDevice, rt->stream));
+      if (weights) CK(cudaMemcpyAsync(weights, wts, (size_t)P * 4, cudaMemcpyDeviceToDevice, rt->stream));
+    }
+  }
+  if (!call.async() && (s = ep_wait(rt)) != PW_OK) return s;
+  uint32_t got[3] = {0, 0, 0};
+  if (call.stats) {
+    CK(cudaMemcpyAsync(got, n_groups, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, rt->stream));
+    CK(cudaStreamSynchronize(rt->stream));
+  }
+  const pw_expert_weights &w0 = bank->host[0];
+  const uint64_t per_expert = 3ull * H * I + 4ull * (w0.gate.scale_rows * w0.gate.scale_cols * 2u +
+                                                     w0.down.scale_rows * w0.down.scale_cols);
+  s = call.finish(per_expert * got[2]);
+  if (call.stats) {
+    call.stats->expert_rows = got[1];
+    call.stats->unique_experts = got[2];
+  }
+  // a wait that ran out leaves the windows of this epoch unusable
+  if (s == PW_ERR_TIMEOUT) ep_dead(rt, PW_ERR_TIMEOUT, "expert-parallel exchange", ncclInProgress);
+  return s;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1365,7 +1567,8 @@ int pw_ep_unique_id(void *id, uint32_t bytes) {
   return PW_OK;
 }
 
-int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t bytes, uint32_t timeout_ms) {
+int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t bytes, uint32_t timeout_ms,
+               uint32_t max_tokens, uint32_t hidden, uint32_t local_experts, uint32_t flags) {
   if (!rt) return PW_ERR_ARGUMENT;
   if (!id || bytes < sizeof(ncclUniqueId)) return fail(rt, PW_ERR_ARGUMENT, "NCCL unique id must be %zu bytes",
                                                        sizeof(ncclUniqueId));
@@ -1379,6 +1582,12 @@ int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t byt
   ep->rank = rank;
   ep->world = world;
   ep->timeout_s = timeout_ms ? timeout_ms / 1e3 : 60.0;
+  if (max_tokens > 2048u) {
+    delete ep;
+    return fail(rt, PW_ERR_UNSUPPORTED, "at most 2048 tokens per rank and call");
+  }
+  ep->max_tokens = max_tokens ? max_tokens : 2048u;
+  ep->p2p = (flags & PW_EP_NCCL_TRANSPORT) == 0u;
   ncclUniqueId u;
   memcpy(&u, id, sizeof u);
   ncclComm_t comm = nullptr;
@@ -1412,6 +1621,12 @@ int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t byt
      "connection warm-up (send/recv)");
   s = ep_wait(rt);
   cudaFree(probe);
+  if (s != PW_OK) return s;
+  // the peer-memory windows are mapped now, while every rank is here
+  if (ep->p2p && hidden && local_experts) {
+    if (hidden % 512u || local_experts > 256u) return fail(rt, PW_ERR_SHAPE, "hidden must be a multiple of 512");
+    s = ep_window_setup(rt, local_experts, hidden);
+  }
   return s;
 }
 
@@ -1431,7 +1646,11 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
   if (tokens > 2048u) return fail(rt, PW_ERR_UNSUPPORTED, "at most 2048 tokens per rank and call");
   if ((mem & PW_MEM_ASYNC) && (mem & PW_MEM_HOST))
     return fail(rt, PW_ERR_ARGUMENT, "asynchronous expert-parallel calls need device I/O");
+  if (ep->p2p && tokens > ep->max_tokens)
+    return fail(rt, PW_ERR_UNSUPPORTED, "%u tokens exceed this rank's max_tokens %u", tokens, ep->max_tokens);
   CK(cudaSetDevice(rt->device));
+  if (ep->p2p && (!ep->win || ep->w.L != L || ep->w.H != H))
+    if ((s = ep_window_setup(rt, L, H)) != PW_OK) return s;
   const uint32_t P = tokens * 8u, Hs = H / 128u, Is = I / 128u;
   Call call{rt, mem, stats, 0};
   if ((s = call.begin()) != PW_OK) return s;
@@ -1489,6 +1708,7 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
       CK(launch_gather_rows(xc, xs, so.placement_tok, P, H, xsend, ssend, rt->stream));
     }
   }
+  if (ep->p2p) return ep_layer_p2p(rt, call, bank, tokens, y, selected, weights, so, dy, sel, wts, xsend, ssend);
   if ((s = ep_pinned(rt, ep->h_off, ep->h_off_cap, (size_t)G * (E + 1) * 4)) != PW_OK) return s;
   NK(pw::nccl::all_gather(so.offsets, alloff, E + 1, ncclUint32, ep->comm, rt->stream, ep->timeout_s),
      "ncclAllGather of expert offsets");

@@ -32,6 +32,7 @@ OUTPUT_F32 = 0x100
 MEM_DEVICE = 0
 MEM_HOST = 1
 MEM_ASYNC = 2
+EP_NCCL_TRANSPORT = 1
 RUNTIME_FUSED_GATE_UP = 1
 
 ERRORS = {
@@ -359,10 +360,15 @@ class WideMoeRuntime:
             raise PrismwingError(rc, "pw_ep_unique_id failed (is libnccl.so.2 loadable?)")
         return buf.raw
 
-    def ep_init(self, rank: int, world: int, uid: bytes, timeout_ms: int = 60000) -> None:
-        """Join the expert-parallel group (collective)."""
+    def ep_init(self, rank: int, world: int, uid: bytes, timeout_ms: int = 60000, max_tokens: int = 2048,
+                hidden: int = 0, local_experts: int = 0, nccl_transport: bool = False) -> None:
+        """Join the expert-parallel group (collective).  max_tokens bounds the
+        tokens per rank and layer (same on every rank); with hidden and
+        local_experts the peer-memory windows are mapped here; nccl_transport
+        moves the rows with NCCL send/recv instead of peer-memory stores."""
         buf = ctypes.create_string_buffer(bytes(uid), len(uid))
-        self._check(self._L.pw_ep_init(self._rt, rank, world, buf, len(uid), timeout_ms))
+        self._check(self._L.pw_ep_init(self._rt, rank, world, buf, len(uid), timeout_ms, max_tokens, hidden,
+                                       local_experts, EP_NCCL_TRANSPORT if nccl_transport else 0))
 
     def ep_moe_layer(self, x, router_weight_bf16: torch.Tensor, bias: torch.Tensor, bank,
                      want_routes: bool = False, stats: bool = True, asynchronous: bool = False,

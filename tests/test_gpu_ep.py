@@ -23,7 +23,7 @@ def _bank(dev, experts):
     return [synth.expert(HID, INTER, 900 + e, dev) for e in experts]
 
 
-def _worker(rank, world, uid_q, res_q, tokens_per_rank, mode):
+def _worker(rank, world, uid_q, res_q, tokens_per_rank, mode, nccl=False):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     try:
         torch.cuda.set_device(rank)
@@ -37,7 +37,8 @@ def _worker(rank, world, uid_q, res_q, tokens_per_rank, mode):
                 uid_q.put(uid)
         else:
             uid = uid_q.get(timeout=60)
-        rt.ep_init(rank, world, uid, timeout_ms=8000 if mode == "leave" else 20000)
+        rt.ep_init(rank, world, uid, timeout_ms=8000 if mode == "leave" else 20000, max_tokens=512,
+                   hidden=HID, local_experts=E // world, nccl_transport=nccl)
         L = E // world
         local = rt.create_bank(_bank(dev, range(rank * L, (rank + 1) * L)))
         w, bias = synth.router(E, HID, 77, dev)
@@ -95,10 +96,11 @@ def _worker(rank, world, uid_q, res_q, tokens_per_rank, mode):
         raise
 
 
-def _run(world, tokens_per_rank, mode, wait_s=300):
+def _run(world, tokens_per_rank, mode, wait_s=300, nccl=False):
     ctx = mp.get_context("spawn")
     uid_q, res_q = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, uid_q, res_q, tokens_per_rank, mode)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, uid_q, res_q, tokens_per_rank, mode, nccl))
+             for r in range(world)]
     for p in procs:
         p.start()
     out = {}
@@ -125,9 +127,10 @@ def test_ep_init_times_out_without_peer():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
 @pytest.mark.parametrize("tokens_per_rank", [(4, 4), (3, 0), (300, 200)])
-def test_ep_layer_two_gpus(tokens_per_rank):
-    out = _run(2, tokens_per_rank, "layer")
+def test_ep_layer_two_gpus(tokens_per_rank, transport):
+    out = _run(2, tokens_per_rank, "layer", nccl=transport == "nccl")
     assert out == {0: "ok", 1: "ok"}, out
 
 
