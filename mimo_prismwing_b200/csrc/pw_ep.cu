@@ -114,9 +114,8 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const EpArgs e, const uint3
 // ---------------------------------------------------------------------- plan
 // One CTA.  Outputs (expert order j): perm[j] = received row (slot s, row),
 // src_rank[j], src_place[j]; groups over each local expert's rows in chunks
-// of `chunk`; n_groups[0], p_recv[0] = p_recv - n_groups + 1 (the next
-// word), and the word after it = local experts with rows.  Rows beyond `cap`
-// are an error.
+// of `chunk`; *n_groups; *p_recv = rows received and p_recv[1] = local
+// experts with at least one row.  Rows beyond `cap` are an error.
 __global__ void __launch_bounds__(1024) k_ep_plan(const EpArgs e, BankTable bank, uint32_t chunk, uint32_t cap,
                                                   uint32_t *__restrict__ perm, uint32_t *__restrict__ src_rank,
                                                   uint32_t *__restrict__ src_place, GemvGroup *__restrict__ gu,
