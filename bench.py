@@ -318,7 +318,7 @@ def run_ours(args, rank, world, local_rank):
         box = [WideMoeRuntime.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         rt.ep_init(rank, world, box[0], timeout_ms=120000, max_tokens=PREFILL_TOKENS // world, hidden=HIDDEN,
-                   local_experts=EXPERTS // world)
+                   local_experts=EXPERTS // world, nccl_transport=args.ep_transport == "nccl")
     layers = Layers(rt, rank, world, args.banks, dev)
     stream = torch.cuda.Stream(device=dev)
     rt.set_stream(stream)
@@ -481,7 +481,9 @@ def run_ours(args, rank, world, local_rank):
                                    "(layer-major), 256 experts x [2048x4096 gate/up, 4096x2048 down] e4m3",
                        "hidden": HIDDEN, "intermediate": INTER, "experts": EXPERTS, "top_k": TOPK,
                        "tokens": PREFILL_TOKENS, "layers": STACK_LAYERS, "distinct_layer_banks": args.banks,
-                       "parallelism": f"expert-parallel x{world} (NCCL all-to-all)" if ep else "single GPU",
+                       "parallelism": (f"expert-parallel x{world} ("
+                                       + ("NCCL send/recv" if args.ep_transport == "nccl" else
+                                          "device-driven peer-memory dispatch/combine over NVLink") + ")") if ep else "single GPU",
                        "tokens_per_rank": T, "experts_per_rank": EXPERTS // world,
                        "l2": "no flush: every layer streams its experts' weights (>= 805 MB per GPU) from HBM"},
             "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "h2d_bytes_per_step": T * HIDDEN * 4 * STACK_LAYERS,
@@ -526,6 +528,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-configs", action="store_true", help="skip the configs[0]/[1]/[3] sub-benchmarks")
+    ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
+                    help="expert-parallel exchange: peer-memory stores (default) or NCCL send/recv")
     # smaller cases for ncu captures only; the metric is quoted at the defaults
     ap.add_argument("--experts", type=int, default=EXPERTS)
     ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS)

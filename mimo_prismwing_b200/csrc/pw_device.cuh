@@ -93,10 +93,13 @@ __device__ __forceinline__ float sigmoid_sleef(float logit) {
 
 // Staged bf16 SwiGLU (src/text_endpoint.rs:5336-5342,
 // kernels/block_fp8_gemv.metal:139): bf16 boundaries on g, u, silu and h.
-__device__ __forceinline__ float staged_swiglu(float gate, float up) {
+__device__ __forceinline__ float staged_silu(float gate) {
   const float g = round_bf16(gate);
+  return round_bf16(__fdiv_rn(g, __fadd_rn(1.0f, sleef_expf_u10(-g))));
+}
+__device__ __forceinline__ float staged_swiglu(float gate, float up) {
+  const float silu = staged_silu(gate);
   const float u = round_bf16(up);
-  const float silu = round_bf16(__fdiv_rn(g, __fadd_rn(1.0f, sleef_expf_u10(-g))));
   return round_bf16(__fmul_rn(silu, u));
 }
 

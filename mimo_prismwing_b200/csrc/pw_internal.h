@@ -108,11 +108,12 @@ cudaError_t launch_gemv(int kind, const GemvArgs &args, int grid, cudaStream_t s
 int gemv_max_ctas(int num_sms);
 cudaError_t launch_gemv_mma(int kind, const GemvArgs &args, int grid, cudaStream_t stream);
 cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_t stream);
-cudaError_t launch_router_logits(const float *x, uint32_t tokens, const uint16_t *w, uint32_t experts,
-                                 uint32_t hidden, float *logits, cudaStream_t stream);
-cudaError_t launch_router_topk(const float *logits, const float *bias, uint32_t tokens, uint32_t experts,
-                               uint32_t *selected, float *weights, uint32_t *tie_rows, uint32_t *flags,
-                               cudaStream_t stream);
+// Router logits (or, from 64 tokens, their partial trees) into `scratch`
+// (router_scratch_floats floats), then the sigmoid no-aux top-8.
+size_t router_scratch_floats(uint32_t tokens, uint32_t experts);
+cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, const float *bias, uint32_t experts,
+                          uint32_t hidden, float *scratch, uint32_t *selected, float *weights, uint32_t *tie_rows,
+                          uint32_t *flags, int num_sms, cudaStream_t stream);
 
 // Device-side schedule for a routed layer: from selected [tokens, 8] build
 // placements ordered by (expert asc, position asc) and the GEMV groups.
@@ -158,9 +159,11 @@ cudaError_t launch_scatter_rows_bf16(const float *rows, const uint32_t *idx, uin
                                      uint16_t *out, cudaStream_t stream);
 // Staged SwiGLU of bf16 gate/up [rows, cols] followed by the hidden's dynamic
 // FP8 quantization (per 128 values); h (f32, optional) receives the SwiGLU.
+// silu_lut: 65536 bf16 staged-silu values (build_silu_lut).
 cudaError_t launch_swiglu_quant(const uint16_t *gate, const uint16_t *up, uint32_t rows, uint32_t cols, float *h,
-                                uint8_t *codes, float *scales, uint32_t *flags, cudaStream_t stream,
-                                const uint32_t *rows_dev = nullptr);
+                                uint8_t *codes, float *scales, uint32_t *flags, const uint16_t *silu_lut,
+                                int num_sms, cudaStream_t stream, const uint32_t *rows_dev = nullptr);
+cudaError_t build_silu_lut(uint16_t *lut, cudaStream_t stream);
 // n = rows * row_len elements; rows_dev (optional) caps the rows on the device
 cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t n, uint32_t *flags,
                           cudaStream_t stream, const uint32_t *rows_dev = nullptr, uint32_t row_len = 1);

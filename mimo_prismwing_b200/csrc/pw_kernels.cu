@@ -137,123 +137,264 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
 }
 
 // Prefill-width router logits: the same per-(token, expert) order as
-// k_router_logits, for a tile of 8 tokens x 16 experts per CTA so that each
-// activation and weight value loaded feeds 16 (resp. 8) chains.  Thread
-// (warp w, lane l) runs the 128 lane chains of its columns four columns at a
-// time, two tokens per packed f32x2 FMA (each lane of the pair rounds like
-// fmaf).  The 32-lane xor tree is evaluated as a transpose-reduce (at each
-// level lane l adds its xor partner's value for the half of the pairs it
-// keeps): every pair gets the same tree of commutative additions as the
-// butterfly, in 124 exchanges instead of 640.  Lane l ends with pairs
-// 4l..4l+3; the 8 warp sums are then added in warp order.
-constexpr int kTileTok = 8, kTileExp = 16;
+// k_router_logits, computed as a register-tiled product.  The xor butterfly
+// (16, 8, 4, 2, 1) first adds lane l and lane l^16, then pairs of those at
+// distance 8, and so on; in bit-reversed lane order i (l = brev5(i)) that is
+// the plain pairwise tree over consecutive i (fadd is commutative).  So one
+// thread can form the tree for its outputs by walking the lane chains in
+// bit-reversed order with a stack of partial sums.
+//
+// Work unit: 64 tokens x 128 experts x (warp-slice w, half h) = the 16 lane
+// chains i = 16h .. 16h+15 of warp w, each an f32 FMA chain from +0 over the
+// lane's columns in the lane's order.  The unit stores its level-4 subtree
+// value V(w,h); k_router_topk forms the warp partial V(w,0) + V(w,1) and the
+// fold over warps in warp order.  Thread (tg, eg) owns tokens 4tg..4tg+3 and
+// experts 4eg..4eg+3, 64+4eg..64+4eg+3 of the tile: per column it reads two
+// float4 of duplicated activations and two float4 of widened weights from
+// shared memory for 16 packed FMAs.  A stage is one 16-column chain segment,
+// double-buffered in shared memory and fetched two stages ahead into
+// registers.  Persistent CTAs walk the units.
+namespace rp {
+constexpr int kTok = 64, kExp = 128, kCols = 16, kThreads = 256, kChains = 16;
+struct Smem {
+  float2 xs[2][kCols][kTok];       // activation, duplicated (v, v)
+  float ws[2][kCols][kExp];        // router weight widened to f32
+  float2 v3[kChains][kThreads];    // each thread's first level-3 values (16 float2 = its 32 outputs)
+};
+}  // namespace rp
 
-__global__ void __launch_bounds__(256) k_router_logits_tiled(const float *__restrict__ x, uint32_t tokens,
-                                                             const uint16_t *__restrict__ w, uint32_t experts,
-                                                             uint32_t hidden, float *__restrict__ logits) {
+struct RouterUnits {
+  uint32_t tokens, experts, hidden, slices, active_w, tiles_e, n_units;
+  __device__ __forceinline__ uint32_t nseg(uint32_t w) const { return (slices - w + 7u) / 8u; }
+};
+
+struct RouterCursor {
+  uint32_t u, st, stages, w, h, t0, e0, nseg;
+  __device__ __forceinline__ void decode(const RouterUnits &g) {
+    if (u >= g.n_units) return;
+    h = u & 1u;
+    const uint32_t rest = u >> 1;
+    w = rest % g.active_w;
+    const uint32_t tile = rest / g.active_w;
+    e0 = (tile % g.tiles_e) * rp::kExp;
+    t0 = (tile / g.tiles_e) * rp::kTok;
+    nseg = g.nseg(w);
+    stages = rp::kChains * nseg;
+  }
+  __device__ __forceinline__ bool valid(const RouterUnits &g) const { return u < g.n_units; }
+  __device__ __forceinline__ void next(const RouterUnits &g) {
+    if (++st == stages) {
+      st = 0;
+      u += gridDim.x;
+      decode(g);
+    }
+  }
+  // first column of this stage's chain segment (lane brev5(i) of warp w, slice w + 8m)
+  __device__ __forceinline__ uint32_t base() const {
+    const uint32_t ci = st / nseg, m = st % nseg;
+    const uint32_t l = __brev(rp::kChains * h + ci) >> 27;
+    return 512u * (w + 8u * m) + 8u * l;
+  }
+};
+
+__device__ __forceinline__ void router_gload(const float *__restrict__ x, const uint16_t *__restrict__ w,
+                                             const RouterUnits &g, const RouterCursor &c, float4 &xr, uint4 &wr) {
+  const uint32_t tid = threadIdx.x, base = c.base();
+  const uint32_t c4 = tid / 64u, r = tid % 64u;  // x: token r, 4 columns c4
+  const uint32_t t = c.t0 + r;
+  const uint32_t xc = base + (c4 < 2u ? 4u * c4 : 256u + 4u * (c4 - 2u));
+  xr = t < g.tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)t * g.hidden + xc))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+  const uint32_t hw = tid / 128u, e = c.e0 + tid % 128u;  // w: expert, 8 columns
+  wr = e < g.experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)e * g.hidden + base + 256u * hw))
+                     : make_uint4(0u, 0u, 0u, 0u);
+}
+
+__device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const float4 &xr, const uint4 &wr) {
+  const uint32_t tid = threadIdx.x;
+  const uint32_t c4 = tid / 64u, r = tid % 64u;
+  sm.xs[b][4 * c4 + 0][r] = make_float2(xr.x, xr.x);
+  sm.xs[b][4 * c4 + 1][r] = make_float2(xr.y, xr.y);
+  sm.xs[b][4 * c4 + 2][r] = make_float2(xr.z, xr.z);
+  sm.xs[b][4 * c4 + 3][r] = make_float2(xr.w, xr.w);
+  const uint32_t hw = tid / 128u, e = tid % 128u;
+  const uint32_t q[4] = {wr.x, wr.y, wr.z, wr.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sm.ws[b][8 * hw + 2 * j][e] = bf16lo(q[j]);
+    sm.ws[b][8 * hw + 2 * j + 1][e] = bf16hi(q[j]);
+  }
+}
+
+__global__ void __launch_bounds__(rp::kThreads, 1)
+    k_router_partials(const float *__restrict__ x, const uint16_t *__restrict__ w, RouterUnits g,
+                      float *__restrict__ part) {
   pdl_wait();
   pdl_launch_dependents();
-  constexpr int NP = kTileTok * kTileExp;  // pairs, index p = e * kTileTok + t
-  __shared__ float part[8][NP];
-  const uint32_t lane = threadIdx.x % 32u, warp = threadIdx.x / 32u;
-  const uint32_t e0 = blockIdx.x * kTileExp, t0 = blockIdx.y * kTileTok;
-  float2 acc[kTileExp][kTileTok / 2];  // acc[e][tp] = tokens 2tp, 2tp+1
+  extern __shared__ __align__(16) unsigned char router_smem[];
+  rp::Smem &sm = *reinterpret_cast<rp::Smem *>(router_smem);
+  const uint32_t tid = threadIdx.x, lane = tid % 32u, wp = tid / 32u;
+  const uint32_t eg = (wp % 2u) * 8u + lane % 8u, tg = (wp / 2u) * 4u + lane / 8u;
+  RouterCursor ld{blockIdx.x, 0, 0, 0, 0, 0, 0, 0};
+  ld.decode(g);
+  if (!ld.valid(g)) return;
+  RouterCursor cp = ld;
+  float4 xr1, xr2;
+  uint4 wr1, wr2;
+  router_gload(x, w, g, ld, xr1, wr1);
+  ld.next(g);
+  router_sstore(sm, 0, xr1, wr1);
+  bool v1 = ld.valid(g), v2 = false;
+  if (v1) {
+    router_gload(x, w, g, ld, xr1, wr1);
+    ld.next(g);
+  }
+  v2 = ld.valid(g);
+  if (v2) {
+    router_gload(x, w, g, ld, xr2, wr2);
+    ld.next(g);
+  }
+  __syncthreads();
+
+  float2 acc[4][4], s0[4][4], s1[4][4], s2[4][4];
 #pragma unroll
-  for (int e = 0; e < kTileExp; ++e)
+  for (int t = 0; t < 4; ++t)
 #pragma unroll
-    for (int tp = 0; tp < kTileTok / 2; ++tp) acc[e][tp] = make_float2(0.0f, 0.0f);
-  const uint32_t slices = hidden / 512u;
-  for (uint32_t sl = warp; sl < slices; sl += 8u) {
+    for (int p = 0; p < 4; ++p) acc[t][p] = make_float2(0.f, 0.f);
+  int b = 0;
+  while (cp.valid(g)) {
+#pragma unroll 4
+    for (int k = 0; k < rp::kCols; ++k) {
+      const float4 xa = *reinterpret_cast<const float4 *>(&sm.xs[b][k][4 * tg]);
+      const float4 xb = *reinterpret_cast<const float4 *>(&sm.xs[b][k][4 * tg + 2]);
+      const float4 wa = *reinterpret_cast<const float4 *>(&sm.ws[b][k][4 * eg]);
+      const float4 wb = *reinterpret_cast<const float4 *>(&sm.ws[b][k][64 + 4 * eg]);
+      const float2 xd[4] = {make_float2(xa.x, xa.y), make_float2(xa.z, xa.w), make_float2(xb.x, xb.y),
+                            make_float2(xb.z, xb.w)};
+      const float2 wv[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
+                            make_float2(wb.z, wb.w)};
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t c0 = 512u * sl + 8u * lane + 256u * (uint32_t)j;
+      for (int t = 0; t < 4; ++t)
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        float4 xq[kTileTok];
+        for (int p = 0; p < 4; ++p) acc[t][p] = __ffma2_rn(wv[p], xd[t], acc[t][p]);
+    }
+    const uint32_t ci = cp.st / cp.nseg;
+    if (cp.st % cp.nseg == cp.nseg - 1u) {  // chain ci complete: push it onto the tree
+      const uint32_t c = ci & 7u;
+      if ((c & 1u) == 0u) {
 #pragma unroll
-        for (int t = 0; t < kTileTok; ++t)
-          xq[t] = t0 + t < tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * hidden + c0) + hf)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t = 0; t < 4; ++t)
 #pragma unroll
-        for (int e = 0; e < kTileExp; ++e) {
-          const uint2 wq = e0 + e < experts
-                               ? __ldg(reinterpret_cast<const uint2 *>(w + (size_t)(e0 + e) * hidden + c0) + hf)
-                               : make_uint2(0u, 0u);
-          const float wf[4] = {bf16lo(wq.x), bf16hi(wq.x), bf16lo(wq.y), bf16hi(wq.y)};
+          for (int p = 0; p < 4; ++p) s0[t][p] = acc[t][p];
+      } else if (c == 1u || c == 5u) {
 #pragma unroll
-          for (int tp = 0; tp < kTileTok / 2; ++tp) {
-            const float4 a = xq[2 * tp], b = xq[2 * tp + 1];
-            acc[e][tp] = __ffma2_rn(make_float2(a.x, b.x), make_float2(wf[0], wf[0]), acc[e][tp]);
-            acc[e][tp] = __ffma2_rn(make_float2(a.y, b.y), make_float2(wf[1], wf[1]), acc[e][tp]);
-            acc[e][tp] = __ffma2_rn(make_float2(a.z, b.z), make_float2(wf[2], wf[2]), acc[e][tp]);
-            acc[e][tp] = __ffma2_rn(make_float2(a.w, b.w), make_float2(wf[3], wf[3]), acc[e][tp]);
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int p = 0; p < 4; ++p) s1[t][p] = __fadd2_rn(s0[t][p], acc[t][p]);
+      } else if (c == 3u) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int p = 0; p < 4; ++p) s2[t][p] = __fadd2_rn(s1[t][p], __fadd2_rn(s0[t][p], acc[t][p]));
+      } else {  // c == 7: a level-3 subtree is complete
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+            s0[t][p] = __fadd2_rn(s2[t][p], __fadd2_rn(s1[t][p], __fadd2_rn(s0[t][p], acc[t][p])));
+        if (ci == 7u) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+#pragma unroll
+            for (int p = 0; p < 4; ++p) sm.v3[t * 4 + p][tid] = s0[t][p];
+        } else {  // ci == 15: level 4 = first subtree + second; store the unit's values
+          const size_t plane = (size_t)g.tokens * g.experts;
+          float *dst = part + (size_t)(2u * cp.w + cp.h) * plane;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint32_t tok = cp.t0 + 4u * tg + (uint32_t)t;
+            float v[8];
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              const float2 r = __fadd2_rn(sm.v3[t * 4 + p][tid], s0[t][p]);
+              v[2 * p] = r.x;
+              v[2 * p + 1] = r.y;
+            }
+            if (tok < g.tokens) {
+#pragma unroll
+              for (int hlf = 0; hlf < 2; ++hlf) {
+                const uint32_t e = cp.e0 + 64u * hlf + 4u * eg;
+                float *row = dst + (size_t)tok * g.experts;
+                if ((g.experts & 3u) == 0u && e + 3u < g.experts) {
+                  *reinterpret_cast<float4 *>(row + e) =
+                      make_float4(v[4 * hlf], v[4 * hlf + 1], v[4 * hlf + 2], v[4 * hlf + 3]);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 4; ++j)
+                    if (e + j < g.experts) row[e + j] = v[4 * hlf + j];
+                }
+              }
+            }
           }
         }
       }
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) acc[t][p] = make_float2(0.f, 0.f);
     }
-  }
-  // flatten: v[e * 8 + t]
-  float v[NP];
-#pragma unroll
-  for (int e = 0; e < kTileExp; ++e)
-#pragma unroll
-    for (int tp = 0; tp < kTileTok / 2; ++tp) {
-      v[e * kTileTok + 2 * tp] = acc[e][tp].x;
-      v[e * kTileTok + 2 * tp + 1] = acc[e][tp].y;
+    if (v1) router_sstore(sm, b ^ 1, xr1, wr1);
+    xr1 = xr2;
+    wr1 = wr2;
+    v1 = v2;
+    v2 = ld.valid(g);
+    if (v2) {
+      router_gload(x, w, g, ld, xr2, wr2);
+      ld.next(g);
     }
-  // transpose-reduce over the 32 lanes: 128 pairs -> 4 per lane
-#pragma unroll
-  for (int o = 16, n = NP / 2; o >= 1; o >>= 1, n >>= 1) {
-    const bool upper = (lane & (uint32_t)o) != 0u;
-#pragma unroll
-    for (int i = 0; i < n; ++i) {
-      const float send = upper ? v[i] : v[i + n];
-      const float keep = upper ? v[i + n] : v[i];
-      v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < NP / 32; ++k) part[warp][(NP / 32) * lane + k] = v[k];
-  __syncthreads();
-  if (threadIdx.x < (unsigned)NP) {
-    const uint32_t p = threadIdx.x, e = p / kTileTok, t = p % kTileTok;
-    if (t0 + t < tokens && e0 + e < experts) {
-      float s = part[0][p];
-#pragma unroll
-      for (int k = 1; k < 8; ++k) s = __fadd_rn(s, part[k][p]);
-      logits[(size_t)(t0 + t) * experts + e0 + e] = s;
-    }
+    __syncthreads();
+    b ^= 1;
+    cp.next(g);
   }
 }
 
-cudaError_t launch_router_logits(const float *x, uint32_t tokens, const uint16_t *w, uint32_t experts,
-                                 uint32_t hidden, float *logits, cudaStream_t stream) {
-  if (hidden % 512u || tokens == 0) return cudaErrorInvalidValue;
-  if (tokens >= 64u) {
-    dim3 grid((experts + kTileExp - 1) / kTileExp, (tokens + kTileTok - 1) / kTileTok);
-    return launch_kernel(k_router_logits_tiled, grid, dim3(256), 0, stream, x, tokens, w, experts, hidden, logits);
-  }
-  dim3 grid(experts, (tokens + kRouterTok - 1) / kRouterTok);
-  return launch_kernel(k_router_logits, grid, dim3(256), 0, stream, x, tokens, w, experts, hidden, logits);
+static RouterUnits router_units(uint32_t tokens, uint32_t experts, uint32_t hidden) {
+  RouterUnits g{};
+  g.tokens = tokens;
+  g.experts = experts;
+  g.hidden = hidden;
+  g.slices = hidden / 512u;
+  g.active_w = g.slices < 8u ? g.slices : 8u;
+  g.tiles_e = (experts + rp::kExp - 1) / rp::kExp;
+  const uint32_t tiles_t = (tokens + rp::kTok - 1) / rp::kTok;
+  g.n_units = tiles_t * g.tiles_e * g.active_w * 2u;
+  return g;
+}
+
+constexpr uint32_t kRouterPartialMinTokens = 64;
+
+size_t router_scratch_floats(uint32_t tokens, uint32_t experts) {
+  return (size_t)tokens * experts * (tokens >= kRouterPartialMinTokens ? 16u : 1u);
 }
 
 // --------------------------------------------------------------- router top-k
-// One CTA per token (src/text_endpoint.rs:4394 pytorch_noaux_routes):
-// score = SLEEF sigmoid(logit); corrected = score + bias; 9 rounds of
-// block-wide argmax (ties -> lower index) give the 8 picks in canonical order
-// and the first rejected value (boundary margin / tie detection).
+// One warp per token (src/text_endpoint.rs:4394 pytorch_noaux_routes): the
+// logit (read, or folded from the partial trees: T_w = V(w,0) + V(w,1), then
+// T_0 + T_1 + ... + T_7 in warp order, T_w = +0 for idle warps); score =
+// SLEEF sigmoid(logit); corrected = score + bias; 9 rounds of warp argmax
+// (ties -> lower index) give the 8 picks in canonical order and the first
+// rejected value (boundary margin / tie detection).
 // weight_k = score_k / (pairwise sum of the 8 + 1e-20) (src/text_endpoint.rs:4382).
-constexpr int kTopkPer = 4;  // experts per thread: up to 1024 experts
-
 __device__ __forceinline__ bool better(float va, uint32_t ia, float vb, uint32_t ib) {
   return va > vb || (va == vb && ia < ib);
 }
 
-__device__ __forceinline__ void argmax_shfl(float &bv, uint32_t &bi, float &bs, int width) {
-  for (int o = width / 2; o >= 1; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o, width);
-    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o, width);
-    const float os = __shfl_xor_sync(0xffffffffu, bs, o, width);
+__device__ __forceinline__ void argmax_shfl(float &bv, uint32_t &bi, float &bs) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    const float os = __shfl_xor_sync(0xffffffffu, bs, o);
     if (better(ov, oi, bv, bi)) {
       bv = ov;
       bi = oi;
@@ -262,92 +403,117 @@ __device__ __forceinline__ void argmax_shfl(float &bv, uint32_t &bi, float &bs, 
   }
 }
 
-__global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ logits, const float *__restrict__ bias,
-                                                     uint32_t tokens, uint32_t experts, uint32_t *__restrict__ selected,
-                                                     float *__restrict__ weights, uint32_t *tie_rows, uint32_t *flags) {
+template <int NPL>
+__global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ src, uint32_t active_w,
+                                                     const float *__restrict__ bias, uint32_t tokens,
+                                                     uint32_t experts, uint32_t *__restrict__ selected,
+                                                     float *__restrict__ weights, uint32_t *tie_rows,
+                                                     uint32_t *flags) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float cv[8], cs[8];
-  __shared__ uint32_t ci[8];
-  __shared__ float pick_s[9], pick_v[9];
-  __shared__ uint32_t pick_i[9];
-  const uint32_t t = blockIdx.x;
-  const uint32_t tid = threadIdx.x, lane = tid % 32u, warp = tid / 32u;
-  float score[kTopkPer], corr[kTopkPer];
-  uint32_t taken = 0;
+  const uint32_t lane = threadIdx.x % 32u;
+  const uint32_t t = blockIdx.x * 8u + threadIdx.x / 32u;
+  if (t >= tokens) return;
+  const float ninf = -__int_as_float(0x7f800000);
+  float score[NPL], corr[NPL];
+  const size_t plane = (size_t)tokens * experts;
 #pragma unroll
-  for (int k = 0; k < kTopkPer; ++k) {
-    const uint32_t e = tid + 256u * k;
+  for (int k = 0; k < NPL; ++k) {
+    const uint32_t e = lane + 32u * k;
     score[k] = 0.0f;
-    corr[k] = -__int_as_float(0x7f800000);
+    corr[k] = ninf;
     if (e < experts) {
-      const float lg = logits[(size_t)t * experts + e];
+      const float *p = src + (size_t)t * experts + e;
+      float lg;
+      if (active_w == 0u) {
+        lg = *p;
+      } else {
+        lg = __fadd_rn(p[0], p[plane]);
+#pragma unroll
+        for (uint32_t w = 1; w < 8u; ++w) {
+          const float tw = w < active_w ? __fadd_rn(p[2u * w * plane], p[(2u * w + 1u) * plane]) : 0.0f;
+          lg = __fadd_rn(lg, tw);
+        }
+      }
       const float b = __ldg(bias + e);
       if (!finite(lg) || !finite(b)) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
       score[k] = sigmoid_sleef(lg);
       corr[k] = __fadd_rn(score[k], b);
     }
   }
+  uint32_t taken = 0;
+  float pv[9], ps[9];
+  uint32_t pi[9];
+#pragma unroll
   for (int round = 0; round < 9; ++round) {
-    float bv = -__int_as_float(0x7f800000), bs = 0.0f;
+    float bv = ninf, bs = 0.0f;
     uint32_t bi = 0xffffffffu;
 #pragma unroll
-    for (int k = 0; k < kTopkPer; ++k) {
-      const uint32_t e = tid + 256u * k;
-      if (e < experts && !(taken & (1u << k)) && better(corr[k], e, bv, bi)) {
+    for (int k = 0; k < NPL; ++k) {
+      const uint32_t e = lane + 32u * k;
+      if (e < experts && !((taken >> k) & 1u) && better(corr[k], e, bv, bi)) {
         bv = corr[k];
         bi = e;
         bs = score[k];
       }
     }
-    argmax_shfl(bv, bi, bs, 32);
-    if (lane == 0) {
-      cv[warp] = bv;
-      ci[warp] = bi;
-      cs[warp] = bs;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      bv = lane < 8u ? cv[lane] : -__int_as_float(0x7f800000);
-      bi = lane < 8u ? ci[lane] : 0xffffffffu;
-      bs = lane < 8u ? cs[lane] : 0.0f;
-      argmax_shfl(bv, bi, bs, 32);
-      if (lane == 0) {
-        pick_v[round] = bv;
-        pick_i[round] = bi;
-        pick_s[round] = bs;
-      }
-    }
-    __syncthreads();
-    const uint32_t w = pick_i[round];
-    if (round < 8 && w != 0xffffffffu && w % 256u == tid) taken |= 1u << (w / 256u);
+    argmax_shfl(bv, bi, bs);
+    pv[round] = bv;
+    pi[round] = bi;
+    ps[round] = bs;
+    if (round < 8 && bi != 0xffffffffu && bi % 32u == lane) taken |= 1u << (bi / 32u);
   }
-  if (tid == 0) {
-    const float l0 = __fadd_rn(pick_s[0], pick_s[4]);
-    const float l1 = __fadd_rn(pick_s[1], pick_s[5]);
-    const float l2 = __fadd_rn(pick_s[2], pick_s[6]);
-    const float l3 = __fadd_rn(pick_s[3], pick_s[7]);
+  if (lane == 0) {
+    const float l0 = __fadd_rn(ps[0], ps[4]);
+    const float l1 = __fadd_rn(ps[1], ps[5]);
+    const float l2 = __fadd_rn(ps[2], ps[6]);
+    const float l3 = __fadd_rn(ps[3], ps[7]);
     const float den = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, l0), l1), l2), l3), 1.0e-20f);
     float sum = 0.0f;
     bool ok = true;
+#pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const float wk = __fdiv_rn(pick_s[k], den);
-      ok = ok && finite(wk) && wk >= 0.0f && pick_i[k] < experts;
+      const float wk = __fdiv_rn(ps[k], den);
+      ok = ok && finite(wk) && wk >= 0.0f && pi[k] < experts;
       sum = __fadd_rn(sum, wk);
-      selected[(size_t)t * 8 + k] = pick_i[k];
+      selected[(size_t)t * 8 + k] = pi[k];
       weights[(size_t)t * 8 + k] = wk;
     }
     if (!ok || fabsf(__fsub_rn(sum, 1.0f)) > 1.0e-6f) raise_flag(flags, PW_FLAG_ROUTE_WEIGHTS);
-    if (pick_v[7] == pick_v[8] && tie_rows) atomicAdd(tie_rows, 1u);
+    if (pv[7] == pv[8] && tie_rows) atomicAdd(tie_rows, 1u);
   }
 }
 
-cudaError_t launch_router_topk(const float *logits, const float *bias, uint32_t tokens, uint32_t experts,
-                               uint32_t *selected, float *weights, uint32_t *tie_rows, uint32_t *flags,
-                               cudaStream_t stream) {
-  if (experts <= 8 || experts > 256u * kTopkPer || tokens == 0) return cudaErrorInvalidValue;
-  return launch_kernel(k_router_topk, dim3(tokens), dim3(256), 0, stream, logits, bias, tokens, experts, selected,
-                       weights, tie_rows, flags);
+cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, const float *bias, uint32_t experts,
+                          uint32_t hidden, float *scratch, uint32_t *selected, float *weights, uint32_t *tie_rows,
+                          uint32_t *flags, int num_sms, cudaStream_t stream) {
+  if (hidden % 512u || tokens == 0 || experts <= 8 || experts > 1024u) return cudaErrorInvalidValue;
+  uint32_t active_w = 0;
+  cudaError_t st;
+  if (tokens >= kRouterPartialMinTokens) {
+    const RouterUnits g = router_units(tokens, experts, hidden);
+    static bool configured = false;
+    if (!configured) {
+      st = cudaFuncSetAttribute(k_router_partials, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(rp::Smem));
+      if (st != cudaSuccess) return st;
+      configured = true;
+    }
+    const uint32_t grid = g.n_units < (uint32_t)num_sms ? g.n_units : (uint32_t)num_sms;
+    st = launch_kernel(k_router_partials, dim3(grid), dim3(rp::kThreads), sizeof(rp::Smem), stream, x, w, g,
+                       scratch);
+    active_w = g.active_w;
+  } else {
+    st = launch_kernel(k_router_logits, dim3(experts, (tokens + kRouterTok - 1) / kRouterTok), dim3(256), 0,
+                       stream, x, tokens, w, experts, hidden, scratch);
+  }
+  if (st != cudaSuccess) return st;
+  const dim3 grid((tokens + 7u) / 8u);
+  if (experts <= 256u)
+    return launch_kernel(k_router_topk<8>, grid, dim3(256), 0, stream, (const float *)scratch, active_w, bias,
+                         tokens, experts, selected, weights, tie_rows, flags);
+  return launch_kernel(k_router_topk<32>, grid, dim3(256), 0, stream, (const float *)scratch, active_w, bias,
+                       tokens, experts, selected, weights, tie_rows, flags);
 }
 
 // ----------------------------------------------------------------- schedule
@@ -355,29 +521,52 @@ cudaError_t launch_router_topk(const float *logits, const float *bias, uint32_t 
 // ascending) -- the reference's BTreeMap<expert, [(position, weight)]>
 // (src/text_endpoint.rs:4768-4776, src/text_endpoint.rs:5302-5310).  The rank
 // of a token among an expert's placements comes from per-expert token
-// bitmasks, so the order is deterministic without sorting.
+// bitmasks, so the order is deterministic without sorting:
+//   1. bitmask[e][t / 32] |= bit(t) for every (t, slot);
+//   2. four threads per expert popcount a quarter of its words each and
+//      exclusive-scan them (word prefixes and the expert's count);
+//   3. a block scan over experts gives placement and group offsets;
+//   4. one thread per token computes its 8 placement indices, writes the
+//      placement lists and, through a sorting network, its placements in
+//      ascending expert order (the combine order);
+//   5. one thread per expert writes its GEMV/GEMM groups.
 constexpr uint32_t kSchedMaxTokens = 2048;
 constexpr uint32_t kSchedMaxExperts = 256;
 constexpr uint32_t kSchedWords = kSchedMaxTokens / 32u;
+constexpr uint32_t kSchedThreads = 1024;
 
-__global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ selected,
-                                                   const float *__restrict__ weights, uint32_t tokens,
-                                                   uint32_t experts, BankTable bank, ScheduleOut out,
-                                                   uint32_t *flags, uint32_t chunk) {
+__device__ __forceinline__ void cswap(uint32_t &ea, uint32_t &pa, uint32_t &eb, uint32_t &pb) {
+  const bool sw = ea > eb;
+  const uint32_t e0 = sw ? eb : ea, e1 = sw ? ea : eb, p0 = sw ? pb : pa, p1 = sw ? pa : pb;
+  ea = e0;
+  eb = e1;
+  pa = p0;
+  pb = p1;
+}
+
+__global__ void __launch_bounds__(kSchedThreads) k_schedule(const uint32_t *__restrict__ selected,
+                                                            const float *__restrict__ weights, uint32_t tokens,
+                                                            uint32_t experts, BankTable bank, ScheduleOut out,
+                                                            uint32_t *flags, uint32_t chunk) {
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ uint32_t sm[];
-  uint32_t *mask = sm;                                      // [experts][words]
-  uint16_t *prefix = reinterpret_cast<uint16_t *>(mask + experts * kSchedWords);  // [experts][words]
-  uint32_t *cnt = reinterpret_cast<uint32_t *>(prefix + experts * kSchedWords);   // [experts + 1]
-  uint32_t *grp_off = cnt + experts + 1;                    // [experts + 1]
-  __shared__ uint32_t bad;
+  uint32_t *mask = sm;                                                            // [experts][kSchedWords]
+  uint16_t *prefix = reinterpret_cast<uint16_t *>(mask + experts * kSchedWords);  // [experts][kSchedWords]
+  uint32_t *off = reinterpret_cast<uint32_t *>(prefix + experts * kSchedWords);   // [experts + 1]
+  uint32_t *grp_off = off + experts + 1;                                          // [experts + 1]
+  __shared__ uint32_t bad, uniq, maxc, wsum_c[kSchedThreads / 32], wsum_g[kSchedThreads / 32];
   const uint32_t words = (tokens + 31u) / 32u;
-  const uint32_t tid = threadIdx.x, nt = blockDim.x;
-  if (tid == 0) bad = 0;
-  for (uint32_t i = tid; i < experts * words; i += nt) mask[(i / words) * kSchedWords + i % words] = 0;
+  const uint32_t tid = threadIdx.x, lane = tid % 32u, warp = tid / 32u;
+  if (tid == 0) {
+    bad = 0;
+    uniq = 0;
+    maxc = 0;
+  }
+  for (uint32_t i = tid; i < experts * words; i += kSchedThreads) mask[(i / words) * kSchedWords + i % words] = 0;
   __syncthreads();
-  for (uint32_t i = tid; i < tokens * 8u; i += nt) {
+  // 1. bitmasks
+  for (uint32_t i = tid; i < tokens * 8u; i += kSchedThreads) {
     const uint32_t e = selected[i];
     const uint32_t t = i / 8u;
     if (e >= experts) {
@@ -393,75 +582,120 @@ __global__ void __launch_bounds__(1024) k_schedule(const uint32_t *__restrict__ 
     if (tid == 0 && out.n_groups) *out.n_groups = 0;
     return;
   }
-  // per-expert counts and word prefixes (thread per expert)
-  for (uint32_t e = tid; e < experts; e += nt) {
-    uint32_t run = 0;
-    for (uint32_t wi = 0; wi < words; ++wi) {
-      prefix[e * kSchedWords + wi] = (uint16_t)run;
-      run += __popc(mask[e * kSchedWords + wi]);
+  // 2. word prefixes, four threads per expert (experts <= 256)
+  uint32_t cnt = 0;
+  {
+    const uint32_t e = tid / 4u, q = tid % 4u;
+    const uint32_t per = (words + 3u) / 4u, w0 = min(words, q * per), w1 = min(words, w0 + per);
+    uint32_t local = 0;
+    if (e < experts)
+      for (uint32_t wi = w0; wi < w1; ++wi) local += __popc(mask[e * kSchedWords + wi]);
+    // exclusive scan over the 4 lanes of this expert (lanes 4k..4k+3 of a warp)
+    uint32_t incl = local;
+#pragma unroll
+    for (uint32_t o = 1; o < 4u; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o, 4);
+      if (q >= o) incl += v;
     }
-    cnt[e] = run;
+    uint32_t run = incl - local;
+    if (e < experts)
+      for (uint32_t wi = w0; wi < w1; ++wi) {
+        prefix[e * kSchedWords + wi] = (uint16_t)run;
+        run += __popc(mask[e * kSchedWords + wi]);
+      }
+    cnt = __shfl_sync(0xffffffffu, incl, 3, 4);  // the expert's total
+  }
+  __syncthreads();
+  // 3. offsets: thread e (< experts) holds count c and group count g
+  {
+    const uint32_t e = tid;
+    uint32_t c = 0;
+    // counts live in lanes 4e..4e+3 of step 2; gather them through shared memory
+    if (tid % 4u == 0u && tid / 4u < experts) off[tid / 4u] = cnt;
+    __syncthreads();
+    if (e < experts) c = off[e];
+    const uint32_t g = (c + chunk - 1u) / chunk;
+    uint32_t ic = c, ig = g;
+#pragma unroll
+    for (uint32_t o = 1; o < 32u; o <<= 1) {
+      const uint32_t vc = __shfl_up_sync(0xffffffffu, ic, o), vg = __shfl_up_sync(0xffffffffu, ig, o);
+      if (lane >= o) {
+        ic += vc;
+        ig += vg;
+      }
+    }
+    if (lane == 31u) {
+      wsum_c[warp] = ic;
+      wsum_g[warp] = ig;
+    }
+    if (e < experts && c) {
+      atomicAdd(&uniq, 1u);
+      atomicMax(&maxc, c);
+    }
+    __syncthreads();  // everyone has read off[] (counts) before it is overwritten
+    uint32_t bc = 0, bg = 0;
+    for (uint32_t k = 0; k < warp; ++k) {
+      bc += wsum_c[k];
+      bg += wsum_g[k];
+    }
+    if (e < experts) {
+      off[e] = bc + ic - c;
+      grp_off[e] = bg + ig - g;
+      out.offsets[e] = bc + ic - c;
+      if (e == experts - 1u) {
+        const uint32_t total = bc + ic, gtotal = bg + ig;
+        off[experts] = total;
+        grp_off[experts] = gtotal;
+        out.offsets[experts] = total;
+        if (out.n_groups) *out.n_groups = gtotal;
+        out.counters[1] = total;
+      }
+    }
   }
   __syncthreads();
   if (tid == 0) {
-    uint32_t off = 0, goff = 0, uniq = 0, maxc = 0;
-    for (uint32_t e = 0; e < experts; ++e) {
-      const uint32_t c = cnt[e];
-      out.offsets[e] = off;
-      grp_off[e] = goff;
-      off += c;
-      goff += (c + chunk - 1u) / chunk;
-      uniq += c ? 1u : 0u;
-      maxc = c > maxc ? c : maxc;
-    }
-    out.offsets[experts] = off;
-    grp_off[experts] = goff;
-    if (out.n_groups) *out.n_groups = goff;
     out.counters[0] = uniq;
-    out.counters[1] = off;
     out.counters[2] = maxc;
   }
-  __syncthreads();
-  // placement index of every (token, slot)
-  for (uint32_t i = tid; i < tokens * 8u; i += nt) {
-    const uint32_t e = selected[i];
-    const uint32_t t = i / 8u;
-    const uint32_t wi = t / 32u;
-    const uint32_t below = mask[e * kSchedWords + wi] & ((1u << (t % 32u)) - 1u);
-    const uint32_t p = out.offsets[e] + prefix[e * kSchedWords + wi] + __popc(below);
-    out.placement_tok[p] = t;
-    out.placement_w[p] = weights[i];
-  }
-  // per token: its 8 placements in ascending expert order (combine order)
-  for (uint32_t t = tid; t < tokens; t += nt) {
-    uint32_t ex[8], pl[8];
+  // 4. per token: placements, placement lists and the combine order
+  for (uint32_t t = tid; t < tokens; t += kSchedThreads) {
+    const uint4 sa = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u);
+    const uint4 sb = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u + 4u);
+    const float4 wa = *reinterpret_cast<const float4 *>(weights + (size_t)t * 8u);
+    const float4 wb = *reinterpret_cast<const float4 *>(weights + (size_t)t * 8u + 4u);
+    uint32_t ex[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+    const float wt[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    const uint32_t wi = t / 32u, below_mask = (1u << (t % 32u)) - 1u;
+    uint32_t pl[8];
+#pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const uint32_t e = selected[t * 8u + k];
-      const uint32_t wi = t / 32u;
-      const uint32_t below = mask[e * kSchedWords + wi] & ((1u << (t % 32u)) - 1u);
-      ex[k] = e;
-      pl[k] = out.offsets[e] + prefix[e * kSchedWords + wi] + __popc(below);
+      const uint32_t e = ex[k];
+      pl[k] = off[e] + prefix[e * kSchedWords + wi] + __popc(mask[e * kSchedWords + wi] & below_mask);
+      out.placement_tok[pl[k]] = t;
+      out.placement_w[pl[k]] = wt[k];
     }
-    for (int a = 1; a < 8; ++a) {
-      const uint32_t ke = ex[a], kp = pl[a];
-      int b = a - 1;
-      while (b >= 0 && ex[b] > ke) {
-        ex[b + 1] = ex[b];
-        pl[b + 1] = pl[b];
-        --b;
-      }
-      ex[b + 1] = ke;
-      pl[b + 1] = kp;
-    }
-    for (int k = 0; k < 8; ++k) out.slot_place[t * 8u + k] = pl[k];
+    // Batcher odd-even merge sort of 8 (experts of a row are distinct)
+    cswap(ex[0], pl[0], ex[1], pl[1]); cswap(ex[2], pl[2], ex[3], pl[3]);
+    cswap(ex[4], pl[4], ex[5], pl[5]); cswap(ex[6], pl[6], ex[7], pl[7]);
+    cswap(ex[0], pl[0], ex[2], pl[2]); cswap(ex[1], pl[1], ex[3], pl[3]);
+    cswap(ex[4], pl[4], ex[6], pl[6]); cswap(ex[5], pl[5], ex[7], pl[7]);
+    cswap(ex[1], pl[1], ex[2], pl[2]); cswap(ex[5], pl[5], ex[6], pl[6]);
+    cswap(ex[0], pl[0], ex[4], pl[4]); cswap(ex[1], pl[1], ex[5], pl[5]);
+    cswap(ex[2], pl[2], ex[6], pl[6]); cswap(ex[3], pl[3], ex[7], pl[7]);
+    cswap(ex[2], pl[2], ex[4], pl[4]); cswap(ex[3], pl[3], ex[5], pl[5]);
+    cswap(ex[1], pl[1], ex[2], pl[2]); cswap(ex[3], pl[3], ex[4], pl[4]);
+    cswap(ex[5], pl[5], ex[6], pl[6]);
+    uint4 *sp = reinterpret_cast<uint4 *>(out.slot_place + (size_t)t * 8u);
+    sp[0] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    sp[1] = make_uint4(pl[4], pl[5], pl[6], pl[7]);
   }
-  // GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
+  // 5. GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
   // (skipped when the caller runs the experts elsewhere: no group arrays)
-  for (uint32_t e = tid; e < experts && out.gu_groups; e += nt) {
-    const uint32_t c = cnt[e];
+  for (uint32_t e = tid; e < experts && out.gu_groups; e += kSchedThreads) {
+    const uint32_t c = off[e + 1] - off[e];
     for (uint32_t j = 0; j * chunk < c; ++j) {
       GemvGroup g;
-      g.tok_begin = out.offsets[e] + chunk * j;
+      g.tok_begin = off[e] + chunk * j;
       g.count = min(chunk, c - chunk * j);
       g.expert = e;
       g.pad = 0;
@@ -499,8 +733,8 @@ cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  return launch_kernel(k_schedule, dim3(1), dim3(1024), smem, stream, selected, weights, tokens, experts, bank, out,
-                       flags, chunk);
+  return launch_kernel(k_schedule, dim3(1), dim3(kSchedThreads), smem, stream, selected, weights, tokens, experts,
+                       bank, out, flags, chunk);
 }
 
 // ------------------------------------------------------------------ combine
@@ -678,56 +912,133 @@ cudaError_t launch_swiglu(const float *gate, const float *up, float *h, uint32_t
 
 // ------------------------------------- staged SwiGLU + hidden quantization
 // The wide (tcgen05) gate/up kernel stores bf16(gate) and bf16(up), the first
-// two roundings of the staged SwiGLU; this pass finishes it at full occupancy:
+// two roundings of the staged SwiGLU; this pass finishes it:
 // h = bf16(bf16(g / (1 + exp(-g))) * u) (kernels/block_fp8_gemv.metal:139),
-// then the down input's dynamic FP8 quantization exactly as k_quantize.  One
-// warp per 128-value group; lane l holds values 4l..4l+3.
-__global__ void k_swiglu_quant(const uint16_t *__restrict__ gate, const uint16_t *__restrict__ up, uint64_t groups,
-                               float *__restrict__ h, uint8_t *__restrict__ codes, float *__restrict__ scales,
-                               uint32_t *flags, const uint32_t *rows_dev, uint32_t groups_per_row) {
+// then the down input's dynamic FP8 quantization exactly as k_quantize.
+// g is a bf16, so silu(g) is a function of 16 bits: a 64 Ki-entry table of
+// staged_silu over every bf16 pattern (built once on the device by the same
+// code) replaces the exponential and the division.  The table sits in
+// shared memory (loaded before the programmatic-launch wait, so it overlaps
+// the GEMM's tail); each thread owns 8 consecutive values, a half-warp one
+// 128-value group, a warp two groups per step, two steps in flight.
+constexpr uint32_t kSiluLutEntries = 65536;
+
+__global__ void k_build_silu_lut(uint16_t *lut) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < kSiluLutEntries) lut[i] = (uint16_t)(__float_as_uint(staged_silu(__uint_as_float(i << 16))) >> 16);
+}
+
+cudaError_t build_silu_lut(uint16_t *lut, cudaStream_t stream) {
+  k_build_silu_lut<<<kSiluLutEntries / 256u, 256, 0, stream>>>(lut);
+  return cudaGetLastError();
+}
+
+namespace {
+struct SwigluChunk {
+  uint4 g, u;
+};
+
+__device__ __forceinline__ void swiglu_chunk_load(const uint16_t *__restrict__ gate, const uint16_t *__restrict__ up,
+                                                  uint64_t chunk, bool ok, SwigluChunk &c) {
+  if (ok) {
+    c.g = __ldcs(reinterpret_cast<const uint4 *>(gate) + chunk);
+    c.u = __ldcs(reinterpret_cast<const uint4 *>(up) + chunk);
+  } else {
+    c.g = make_uint4(0u, 0u, 0u, 0u);
+    c.u = c.g;
+  }
+}
+
+__device__ __forceinline__ void swiglu_chunk_finish(const SwigluChunk &c, const uint16_t *slut, uint64_t chunk,
+                                                    bool ok, float *__restrict__ h, uint8_t *__restrict__ codes,
+                                                    float *__restrict__ scales, uint32_t *flags) {
+  const uint32_t gw[4] = {c.g.x, c.g.y, c.g.z, c.g.w}, uw[4] = {c.u.x, c.u.y, c.u.z, c.u.w};
+  float v[8];
+  bool fin = true;
+  float m = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t gb = (k & 1) ? (gw[k / 2] >> 16) : (gw[k / 2] & 0xffffu);
+    const float silu = __uint_as_float((uint32_t)slut[gb] << 16);
+    const float u = __uint_as_float((k & 1) ? (uw[k / 2] & 0xffff0000u) : (uw[k / 2] << 16));
+    v[k] = round_bf16(__fmul_rn(silu, round_bf16(u)));
+    fin = fin && finite(v[k]);
+    m = fmaxf(m, fabsf(v[k]));
+  }
+  if (ok && !fin) raise_flag(flags, PW_FLAG_NONFINITE_FUSED);
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (!ok) return;
+  if (h) {
+    float4 *hp = reinterpret_cast<float4 *>(h) + 2u * chunk;
+    hp[0] = make_float4(v[0], v[1], v[2], v[3]);
+    hp[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  const float scale = __fdiv_rn(fmaxf(m, 1.0e-10f), 448.0f);
+  auto q = [&](float val) { return fminf(fmaxf(__fdiv_rn(val, scale), -448.0f), 448.0f); };
+  const uint32_t w0 = encode2(q(v[0]), q(v[1])) | (encode2(q(v[2]), q(v[3])) << 16);
+  const uint32_t w1 = encode2(q(v[4]), q(v[5])) | (encode2(q(v[6]), q(v[7])) << 16);
+  reinterpret_cast<uint2 *>(codes)[chunk] = make_uint2(w0, w1);
+  if ((threadIdx.x & 15u) == 0u) scales[chunk / 16u] = scale;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(1024, 1)
+    k_swiglu_quant(const uint16_t *__restrict__ gate, const uint16_t *__restrict__ up, uint64_t groups,
+                   float *__restrict__ h, uint8_t *__restrict__ codes, float *__restrict__ scales, uint32_t *flags,
+                   const uint32_t *rows_dev, uint32_t groups_per_row, const uint16_t *__restrict__ lut) {
+  extern __shared__ __align__(16) uint16_t slut[];
+  for (uint32_t i = threadIdx.x; i < kSiluLutEntries / 8u; i += blockDim.x)
+    reinterpret_cast<uint4 *>(slut)[i] = __ldg(reinterpret_cast<const uint4 *>(lut) + i);
+  __syncthreads();
   pdl_wait();
   pdl_launch_dependents();
   if (rows_dev) groups = min(groups, (uint64_t)*rows_dev * groups_per_row);
+  const uint64_t chunks = groups * 16u;  // 8 values per chunk
   const uint64_t warp_global = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32u;
-  const uint32_t lane = threadIdx.x % 32u;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) / 32u;
-  for (uint64_t grp = warp_global; grp < groups; grp += nwarps) {
-    const uint2 gq = __ldg(reinterpret_cast<const uint2 *>(gate + grp * 128u) + lane);
-    const uint2 uq = __ldg(reinterpret_cast<const uint2 *>(up + grp * 128u) + lane);
-    const uint32_t gw[2] = {gq.x, gq.y}, uw[2] = {uq.x, uq.y};
-    float v[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float g = __uint_as_float((k & 1) ? (gw[k / 2] & 0xffff0000u) : (gw[k / 2] << 16));
-      const float u = __uint_as_float((k & 1) ? (uw[k / 2] & 0xffff0000u) : (uw[k / 2] << 16));
-      v[k] = staged_swiglu(g, u);
+  const uint32_t lane = threadIdx.x % 32u;
+  // warp step s covers chunks [64 s, 64 s + 64): lane l takes chunk 64 s + l
+  // and 64 s + 32 + l (two groups per 32 lanes)
+  for (uint64_t s = warp_global; 64u * s < chunks; s += 2u * nwarps) {
+    const uint64_t s2 = s + nwarps;
+    const uint64_t c0 = 64u * s + lane, c1 = c0 + 32u, c2 = 64u * s2 + lane, c3 = c2 + 32u;
+    const bool second = 64u * s2 < chunks;  // uniform across the warp
+    SwigluChunk a, b, c, d;
+    swiglu_chunk_load(gate, up, c0, c0 < chunks, a);
+    swiglu_chunk_load(gate, up, c1, c1 < chunks, b);
+    if (second) {
+      swiglu_chunk_load(gate, up, c2, c2 < chunks, c);
+      swiglu_chunk_load(gate, up, c3, c3 < chunks, d);
     }
-    const bool ok = finite(v[0]) && finite(v[1]) && finite(v[2]) && finite(v[3]);
-    if (!ok) raise_flag(flags, PW_FLAG_NONFINITE_FUSED);
-    if (h) reinterpret_cast<float4 *>(h + grp * 128u)[lane] = make_float4(v[0], v[1], v[2], v[3]);
-    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float scale = __fdiv_rn(fmaxf(m, 1.0e-10f), 448.0f);
-    auto q = [&](float val) { return fminf(fmaxf(__fdiv_rn(val, scale), -448.0f), 448.0f); };
-    const uint32_t lo = encode2(q(v[0]), q(v[1]));
-    const uint32_t hi = encode2(q(v[2]), q(v[3]));
-    reinterpret_cast<uint32_t *>(codes + grp * 128u)[lane] = lo | (hi << 16);
-    if (lane == 0) scales[grp] = scale;
+    swiglu_chunk_finish(a, slut, c0, c0 < chunks, h, codes, scales, flags);
+    swiglu_chunk_finish(b, slut, c1, c1 < chunks, h, codes, scales, flags);
+    if (second) {
+      swiglu_chunk_finish(c, slut, c2, c2 < chunks, h, codes, scales, flags);
+      swiglu_chunk_finish(d, slut, c3, c3 < chunks, h, codes, scales, flags);
+    }
   }
 }
 
 cudaError_t launch_swiglu_quant(const uint16_t *gate, const uint16_t *up, uint32_t rows, uint32_t cols, float *h,
-                                uint8_t *codes, float *scales, uint32_t *flags, cudaStream_t stream,
-                                const uint32_t *rows_dev) {
-  if (cols % 128u) return cudaErrorInvalidValue;
+                                uint8_t *codes, float *scales, uint32_t *flags, const uint16_t *silu_lut,
+                                int num_sms, cudaStream_t stream, const uint32_t *rows_dev) {
+  if (cols % 128u || !silu_lut) return cudaErrorInvalidValue;
   const uint64_t groups = (uint64_t)rows * (cols / 128u);
   if (groups == 0) return cudaSuccess;
-  const int threads = 256;
-  uint64_t blocks = (groups * 32u + threads - 1) / threads;
-  if (blocks > 148u * 8u) blocks = 148u * 8u;
-  return launch_kernel(k_swiglu_quant, dim3((unsigned)blocks), dim3(threads), 0, stream, gate, up, groups, h, codes,
-                       scales, flags, rows_dev, cols / 128u);
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(k_swiglu_quant, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(kSiluLutEntries * 2u));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  // one 1024-thread CTA per SM; fewer when there is little work
+  const uint64_t steps = (groups * 16u + 63u) / 64u;  // warp steps
+  uint64_t blocks = (steps + 31u) / 32u;
+  if (blocks > (uint64_t)num_sms) blocks = (uint64_t)num_sms;
+  return launch_kernel(k_swiglu_quant, dim3((unsigned)blocks), dim3(1024), (size_t)kSiluLutEntries * 2u, stream,
+                       gate, up, groups, h, codes, scales, flags, rows_dev, cols / 128u, silu_lut);
 }
 
 }  // namespace pw

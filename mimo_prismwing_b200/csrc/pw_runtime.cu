@@ -130,6 +130,7 @@ struct pw_runtime {
   EpState *ep = nullptr;
   float *split_ws = nullptr;      // GEMV split-K partial sums (allocated on first use)
   uint32_t *split_cnt = nullptr;  // and per-tile arrival counters
+  uint16_t *silu_lut = nullptr;   // staged silu of every bf16 pattern (built on first use)
 };
 
 namespace {
@@ -478,6 +479,7 @@ void pw_runtime_destroy(pw_runtime *rt) {
   if (rt->scratch) cudaFree(rt->scratch);
   if (rt->split_ws) cudaFree(rt->split_ws);
   if (rt->split_cnt) cudaFree(rt->split_cnt);
+  if (rt->silu_lut) cudaFree(rt->silu_lut);
   if (rt->d_flags) cudaFree(rt->d_flags);
   if (rt->ev0) cudaEventDestroy(rt->ev0);
   if (rt->ev1) cudaEventDestroy(rt->ev1);
@@ -747,6 +749,10 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
                                      uint64_t units_hint, const uint32_t *slots_dev = nullptr) {
   const int grid_gu = grid_for(rt, units_hint * (I / 128u));
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
+  if (fused && !rt->silu_lut) {
+    CK(cudaMalloc(&rt->silu_lut, 65536u * sizeof(uint16_t)));
+    CK(build_silu_lut(rt->silu_lut, rt->stream));
+  }
   {
     ProfScope ps(rt, P_GATEUP, fused ? 1 : 3);
     GemmArgs A{};
@@ -778,7 +784,8 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
     ProfScope ps(rt, P_QUANT, 1);
     if (fused)
       CK(launch_swiglu_quant(reinterpret_cast<const uint16_t *>(gate_tmp), reinterpret_cast<const uint16_t *>(up_tmp),
-                             slots, I, hidden, hc, hs, rt->d_flags, rt->stream, slots_dev));
+                             slots, I, hidden, hc, hs, rt->d_flags, rt->silu_lut, rt->num_sms, rt->stream,
+                             slots_dev));
     else
       CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream, slots_dev));
   }
@@ -891,14 +898,14 @@ int pw_route(pw_runtime *rt, const pw_router *router, const float *x, uint32_t t
     float *dx = call.host() ? ar.take<float>((size_t)tokens * H) : const_cast<float *>(x);
     uint32_t *dsel = call.host() ? ar.take<uint32_t>((size_t)tokens * 8) : selected;
     float *dw = call.host() ? ar.take<float>((size_t)tokens * 8) : weights;
-    float *logits = ar.take<float>((size_t)tokens * E);
+    float *logits = ar.take<float>(router_scratch_floats(tokens, E));
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)tokens * H * 4)) != PW_OK) return s;
     CK(cudaMemsetAsync(rt->d_ties, 0, 4, rt->stream));
     {
       ProfScope ps(rt, P_ROUTER, 2);
-      CK(launch_router_logits(dx, tokens, router->weight_bf16, E, H, logits, rt->stream));
-      CK(launch_router_topk(logits, router->bias, tokens, E, dsel, dw, rt->d_ties, rt->d_flags, rt->stream));
+      CK(launch_router(dx, tokens, router->weight_bf16, router->bias, E, H, logits, dsel, dw, rt->d_ties,
+                       rt->d_flags, rt->num_sms, rt->stream));
     }
     if (call.host()) {
       if ((s = call.stage_out(selected, dsel, (size_t)tokens * 32)) != PW_OK) return s;
@@ -1183,7 +1190,7 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     float *dy = call.host() ? ar.take<float>((size_t)tokens * H) : y;
     uint8_t *xc = ar.take<uint8_t>((size_t)tokens * H);
     float *xs = ar.take<float>((size_t)tokens * H / 128u);
-    float *logits = ar.take<float>((size_t)tokens * E);
+    float *logits = ar.take<float>(router_scratch_floats(tokens, E));
     uint32_t *sel = ar.take<uint32_t>(P);
     float *wts = ar.take<float>(P);
     ScheduleOut so{};
@@ -1215,8 +1222,8 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     }
     {
       ProfScope ps(rt, P_ROUTER, 2);
-      CK(launch_router_logits(dx, tokens, router->weight_bf16, E, H, logits, rt->stream));
-      CK(launch_router_topk(logits, router->bias, tokens, E, sel, wts, rt->d_ties, rt->d_flags, rt->stream));
+      CK(launch_router(dx, tokens, router->weight_bf16, router->bias, E, H, logits, sel, wts, rt->d_ties,
+                       rt->d_flags, rt->num_sms, rt->stream));
     }
     {
       ProfScope ps(rt, P_SCHED, 1);
@@ -1673,7 +1680,7 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
     dy = call.host() ? ar.take<float>((size_t)tokens * H) : y;
     uint8_t *xc = ar.take<uint8_t>((size_t)tokens * H);
     float *xs = ar.take<float>((size_t)tokens * Hs);
-    float *logits = ar.take<float>((size_t)tokens * E);
+    float *logits = ar.take<float>(router_scratch_floats(tokens, E));
     sel = ar.take<uint32_t>(P);
     wts = ar.take<float>(P);
     so = ScheduleOut{};
@@ -1699,8 +1706,8 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
     }
     {
       ProfScope ps(rt, P_ROUTER, 2);
-      CK(launch_router_logits(dx, tokens, router->weight_bf16, E, H, logits, rt->stream));
-      CK(launch_router_topk(logits, router->bias, tokens, E, sel, wts, rt->d_ties, rt->d_flags, rt->stream));
+      CK(launch_router(dx, tokens, router->weight_bf16, router->bias, E, H, logits, sel, wts, rt->d_ties,
+                       rt->d_flags, rt->num_sms, rt->stream));
     }
     {
       ProfScope ps(rt, P_SCHED, 2);
