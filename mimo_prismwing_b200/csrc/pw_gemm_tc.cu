@@ -4,17 +4,24 @@
 // same equation as the GEMV (src/wide_metal_moe.rs:404-423)
 //   y[t, r] = sum_kb ( sum_{c in kb} dec(W[r, c]) * dec(code[t, c]) ) * S[r/128, kb] * xs[t, kb]
 // runs on the 5th-generation tensor cores:
-//  * A = 128 weight rows x 32 columns, B = N token rows x 32 columns, both
-//    K-major e4m3 in shared memory (128B swizzle, written by TMA);
+//  * A = 128 token rows x 32 columns, B = 128 weight rows x 32 columns, both
+//    K-major e4m3 in shared memory (128B swizzle, written by TMA); D[t, r]
+//    puts tokens on TMEM lanes and weight rows on columns.  Only the group's
+//    tokens rounded up to 32 are loaded; the lanes past them hold whatever
+//    the slot held before and are never read back;
 //  * one elected thread issues tcgen05.mma.kind::f8f6f4 into a TMEM
 //    accumulator; every 128-column block gets a fresh accumulator (the
 //    checkpoint's f32 block scales are not power-of-two UE8M0 scales, so the
-//    hardware block-scaled MMA cannot apply them).  N is the group's token
-//    count rounded up to 32, so a 40-token expert costs 64 columns, not 128;
-//  * eight epilogue warps (two per TMEM lane quarter, each owning half of the
-//    32-token chunks) tcgen05.ld each block's result and promote it into f32
-//    registers, acc += v * (S * xs) with packed f32x2 multiply/FMA, while the
-//    MMA fills the next of the rotating 128-column TMEM accumulator slots;
+//    hardware block-scaled MMA cannot apply them);
+//  * eight epilogue warps (two per TMEM lane quarter, each owning 64 of the
+//    128 weight rows) tcgen05.ld each block's result and promote it into f32
+//    registers, acc += v * (S * xs) with packed f32x2 FMAs.  A thread holds
+//    one token, so its scale S * xs is one value per block (with weight rows
+//    on the lanes every thread needed all 32 token scales of its chunk per
+//    block, broadcast reads that took half of the shared-memory bandwidth),
+//    and its outputs are one contiguous run of the output row, written with
+//    16-byte stores.  Meanwhile the MMA fills the next of the rotating
+//    128-column TMEM accumulator slots;
 //  * a producer warp streams stages of {128 rows x 2 blocks} weights (one
 //    32 KB 3-D TMA box) and {n tokens x 2 blocks} activation codes, n the
 //    group's tokens rounded up to 32.  The fused kind runs all gate stages of
@@ -43,7 +50,6 @@ constexpr int kProducerWarp = 0;
 constexpr int kMmaWarp = 1;
 constexpr int kEpiWarp0 = 2;
 constexpr int kEpiWarps = 8;
-constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr int kTileRows = 128;
 constexpr int kTN = 128;           // tokens per group
@@ -51,8 +57,6 @@ constexpr int kWBox = 32 * 1024;   // weights: 128 rows x 2 k-blocks x 128 B
 constexpr int kXBox = kTN * 256;   // activations: 128 tokens x 2 k-blocks x 128 B
 constexpr int kStage = kWBox + kXBox;
 constexpr int kNst = 3;
-constexpr int kChunks = kTN / 32;              // 32-token chunks per group
-constexpr int kThreadChunks = kChunks / 2;     // chunks per epilogue thread
 constexpr int kTmemCols = 512;                 // four 128-column slots
 
 template <int KIND>
@@ -60,9 +64,8 @@ struct Cfg {
   static constexpr bool FUSED = KIND == 2;
   static constexpr int MATS = FUSED ? 2 : 1;
   static constexpr int RING = kNst * kStage;
-  static constexpr int XS = RING;                     // token scales [32 kb][kTN] f32
-  static constexpr int WS = XS + 32 * kTN * 4;        // weight scales [2 mats][32] f32
-  static constexpr int BARS = WS + 2 * 32 * 4;        // mbarriers
+  static constexpr int XS = RING;                     // token scales [2 bufs][4 quarters][32 kb][32 t] f32
+  static constexpr int BARS = XS + 2 * 4 * 32 * 32 * 4;  // mbarriers
   static constexpr int NACC = FUSED ? 3 : 4;          // rotating accumulator slots (fused: + gate stash)
   static constexpr int NBARS = 2 * kNst + 2 * NACC;   // full, empty, tfull[NACC], tempty[NACC]
   static constexpr int MISC = BARS + NBARS * 8;       // tmem base, abort
@@ -84,6 +87,13 @@ __device__ __forceinline__ void tensormap_acquire(const CUtensorMap *map) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
 }
 
+// 4-byte asynchronous copy global -> shared (completion: cp.async.wait_group).
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -100,6 +110,7 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
 }
 
 // kind::f8f6f4 instruction descriptor: D f32, A/B e4m3, both K-major, M=128, N=n.
+// (A: token rows, B: weight rows.)
 __device__ __forceinline__ uint32_t instr_desc(uint32_t n) {
   return (1u << 4)                   // c_format F32
          | (0u << 7) | (0u << 10)    // a, b: E4M3
@@ -138,19 +149,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// 32 lanes x 16 consecutive f32 columns.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // 32 lanes x 32 consecutive f32 columns from registers into TMEM.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float2 (&v)[16]) {
   asm volatile(
@@ -165,27 +163,9 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float2 (&v)[16])
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// acc[t] += v[t] * (ws * xs[t]) for N tokens, two at a time (packed f32x2);
-// each product and sum rounds exactly like the scalar fmaf(v, ws * xs, acc).
-template <int N>
-__device__ __forceinline__ void promote(float2 *acc, const float (&v)[N], float ws, const float *xs) {
-  const float2 w2 = make_float2(ws, ws);
-#pragma unroll
-  for (int i = 0; i < N / 2; i += 2) {
-    const float4 x4 = *reinterpret_cast<const float4 *>(xs + 2 * i);
-    const float2 c0 = __fmul2_rn(w2, make_float2(x4.x, x4.y));
-    const float2 c1 = __fmul2_rn(w2, make_float2(x4.z, x4.w));
-    acc[i] = __ffma2_rn(make_float2(v[2 * i], v[2 * i + 1]), c0, acc[i]);
-    acc[i + 1] = __ffma2_rn(make_float2(v[2 * i + 2], v[2 * i + 3]), c1, acc[i + 1]);
-  }
-}
-
-__device__ __forceinline__ float &el(float2 (&v)[16], int i) { return (i & 1) ? v[i / 2].y : v[i / 2].x; }
-
 struct Shared {
   uint8_t *ring;
   float *xs;
-  float *ws;
   uint64_t *full, *empty, *tfull, *tempty;
   uint32_t *tmem_base;
   volatile int *abort;
@@ -216,7 +196,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   Shared sh;
   sh.ring = smem;
   sh.xs = reinterpret_cast<float *>(smem + C::XS);
-  sh.ws = reinterpret_cast<float *>(smem + C::WS);
   sh.full = reinterpret_cast<uint64_t *>(smem + C::BARS);
   sh.empty = sh.full + kNst;
   sh.tfull = sh.empty + kNst;
@@ -254,8 +233,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   const uint32_t n_groups = a.n_groups_dev ? min(*a.n_groups_dev, a.n_groups) : a.n_groups;
   const uint32_t tpg = a.rows / kTileRows;
   const uint64_t total = (uint64_t)n_groups * tpg;
-  const uint32_t u_begin = (uint32_t)(total * blockIdx.x / gridDim.x);
-  const uint32_t u_end = (uint32_t)(total * (blockIdx.x + 1) / gridDim.x);
+  // tiles are dealt round-robin: at any moment the CTAs work on neighbouring
+  // tiles, i.e. a few groups, whose activation rows stay in L2 across the
+  // group's row tiles (contiguous ranges per CTA spread the working set over
+  // ~150 groups and the weight stream evicted it: ~30% more HBM traffic)
+  const uint32_t u_begin = blockIdx.x;
+  const uint32_t u_end = (uint32_t)total;
+  const uint32_t u_step = gridDim.x;
   const uint32_t kblocks = a.K / 128u;
   const uint32_t kcs = (kblocks + 1u) / 2u;          // stages per matrix per tile
   const uint32_t per_tile = kcs * (uint32_t)MATS;   // stages per tile; fused: all gate, then all up
@@ -264,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   if (warp == kProducerWarp) {
     if (lane == 0) {
       uint32_t slot = 0, phase = 0, issued = 0, parity = 0;
-      for (uint32_t u = u_begin; u < u_end; ++u) {
+      for (uint32_t u = u_begin; u < u_end; u += u_step) {
         const GemvGroup &g = a.groups[u / tpg];
         const CUtensorMap *m0 = KIND == 3 ? g.tm1 : g.tm0;
         tensormap_acquire(m0);
@@ -314,9 +298,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       const uint32_t ring = smem_addr(sh.ring);
       uint32_t slot = 0, phase = 0, acc = 0, aphase = 0;
       uint32_t pending = 0, pend_parity = 0;  // accumulator slots with a commit in flight
-      for (uint32_t u = u_begin; u < u_end; ++u) {
-        const uint32_t n = mma_cols(a.groups[u / tpg].count);
-        const uint32_t idesc = instr_desc(n);
+      uint32_t n_next = u_begin < u_end ? mma_cols(a.groups[u_begin / tpg].count) : 32u;
+      for (uint32_t u = u_begin; u < u_end; u += u_step) {
+        const uint32_t n = n_next;  // token rows loaded
+        if (u + u_step < u_end) n_next = mma_cols(a.groups[(u + u_step) / tpg].count);
+        const uint32_t idesc = instr_desc((uint32_t)kTileRows);
         for (uint32_t st = 0; st < per_tile; ++st) {
           const uint32_t kc = st % kcs;
           const bool ok_full = bwait(sh, &sh.full[slot], phase, a.flags);
@@ -332,8 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
               const uint32_t d = tmem + acc * (uint32_t)kTN;
 #pragma unroll
               for (uint32_t s = 0; s < 4; ++s) {
-                const uint64_t ad = smem_desc_sw128(wbase + j * (kTileRows * 128u) + s * 32u);
-                const uint64_t bd = smem_desc_sw128(xbase + j * (n * 128u) + s * 32u);
+                const uint64_t ad = smem_desc_sw128(xbase + j * (n * 128u) + s * 32u);
+                const uint64_t bd = smem_desc_sw128(wbase + j * (kTileRows * 128u) + s * 32u);
                 mma_f8(d, ad, bd, idesc, s > 0 ? 1u : 0u);
               }
             }
@@ -361,76 +347,97 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     // ---------------------------------------------------------- epilogue
     const uint32_t ew = warp - kEpiWarp0;          // 0..7
     const uint32_t quarter = warp % 4u;            // TMEM lane quarter this warp may access
-    const uint32_t half = ew / 4u;                 // owns chunks half, half + 2
-    const uint32_t r_local = quarter * 32u + lane;  // tile row owned by this thread
-    const uint32_t etid = ew * 32u + lane;
+    const uint32_t half = ew / 4u;                 // owns weight rows 64 * half .. + 63 of the tile
+    const uint32_t t_local = quarter * 32u + lane;  // token of the group owned by this thread
     const uint32_t lane_base = (quarter * 32u) << 16;
-    const uint32_t stash = tmem + lane_base + NACC * (uint32_t)kTN;  // fused: gate sums
+    const uint32_t col0 = half * 64u;
+    const uint32_t stash = tmem + lane_base + NACC * (uint32_t)kTN + col0;  // fused: gate sums
     uint32_t acc_slot = 0, aphase = 0;
-    uint32_t cur_group = 0xffffffffu;
-    for (uint32_t u = u_begin; u < u_end; ++u) {
+    // Token scales: the two warps of a lane quarter copy their 32 tokens'
+    // scales ([kb][t], conflict-free reads by lane) for the NEXT tile with
+    // cp.async while this tile runs, double-buffered; a 64-thread barrier
+    // per quarter at the tile start is the only synchronisation.
+    auto xs_fetch = [&](uint32_t uu, uint32_t buf) {
+      const GemvGroup &gg = a.groups[uu / tpg];
+      const uint32_t c = min(gg.count, (uint32_t)kTN);
+      float *dst = sh.xs + (buf * 4u + quarter) * 1024u;
+      for (uint32_t e = half * 32u + lane; e < 32u * kblocks; e += 64u) {
+        const uint32_t kb = e / 32u, t = e % 32u, tok = quarter * 32u + t;
+        if (tok < c) cp_async4(dst + kb * 32u + t, a.x_scales + (size_t)(gg.tok_begin + tok) * kblocks + kb);
+      }
+      cp_async_commit();
+    };
+    // Weight scales live in registers: lane l of every epilogue warp holds
+    // the tile's two scale rows at k-block l (row 0: the first matrix, or
+    // QKV rows 0-63; row 1: the up matrix, or QKV rows 64-127) and each
+    // k-block's value is a shuffle.  The next tile's are fetched while this
+    // one runs, so a tile boundary needs neither a load round trip nor a
+    // barrier; only a group change (new token scales in shared memory) does.
+    auto ws_load = [&](uint32_t uu, float &w0, float &w1) {
+      const GemvGroup &gg = a.groups[uu / tpg];
+      const uint32_t trow0 = (uu % tpg) * kTileRows;
+      uint32_t srow = trow0 / 128u, srow1 = srow;
+      if (qkv) {
+        uint32_t src_unused = 0;
+        map_row(a.layout, trow0, src_unused, srow);
+        map_row(a.layout, trow0 + 64u, src_unused, srow1);
+      }
+      w0 = 0.0f;
+      w1 = 0.0f;
+      if (lane < kblocks) {
+        w0 = __ldg((KIND == 3 ? gg.s1 : gg.s0) + (size_t)srow * a.scale_cols + lane);
+        if (MATS == 2) w1 = __ldg(gg.s1 + (size_t)srow * a.scale_cols + lane);
+        if (qkv) w1 = __ldg(gg.s0 + (size_t)srow1 * a.scale_cols + lane);
+      }
+    };
+    float wn0 = 0.0f, wn1 = 0.0f;
+    if (u_begin < u_end) {
+      ws_load(u_begin, wn0, wn1);
+      xs_fetch(u_begin, 0u);
+    }
+    uint32_t ti = 0;  // tile ordinal: token-scale buffer ti & 1
+    for (uint32_t u = u_begin; u < u_end; u += u_step, ++ti) {
       const uint32_t gi = u / tpg;
       const GemvGroup grp = a.groups[gi];
       const uint32_t row0 = (u % tpg) * kTileRows;
       const uint32_t cnt = min(grp.count, (uint32_t)kTN);
-      const uint32_t nch = (cnt + 31u) / 32u;
-      // token scales ([kb][t], reloaded when the group changes) and this
-      // tile's weight-scale rows
-      named_bar_sync(1, kEpiThreads);
-      if (gi != cur_group) {
-        for (uint32_t i = etid; i < (uint32_t)kTN * kblocks; i += kEpiThreads) {
-          const uint32_t t = i / kblocks, kb = i % kblocks;
-          sh.xs[kb * kTN + t] = t < cnt ? __ldg(a.x_scales + (size_t)(grp.tok_begin + t) * kblocks + kb) : 0.0f;
-        }
-        cur_group = gi;
-      }
-      {
-        uint32_t srow = row0 / 128u, srow1 = srow;
-        if (qkv) {
-          uint32_t src_unused = 0;
-          map_row(a.layout, row0, src_unused, srow);
-          map_row(a.layout, row0 + 64u, src_unused, srow1);
-        }
-        const float *s0 = (KIND == 3 ? grp.s1 : grp.s0) + (size_t)srow * a.scale_cols;
-        for (uint32_t i = etid; i < kblocks; i += kEpiThreads) {
-          sh.ws[i] = __ldg(s0 + i);
-          if (MATS == 2) sh.ws[32u + i] = __ldg(grp.s1 + (size_t)srow * a.scale_cols + i);
-          if (qkv) sh.ws[32u + i] = __ldg(grp.s0 + (size_t)srow1 * a.scale_cols + i);  // rows 64..127
-        }
-      }
-      named_bar_sync(1, kEpiThreads);
+      const bool active = quarter * 32u < cnt;  // this warp's lane quarter holds tokens
+      // this tile's token scales have landed (both warps), the other buffer is free
+      cp_async_wait_all();
+      named_bar_sync(2u + quarter, 64u);
+      const float *xsb = sh.xs + ((ti & 1u) * 4u + quarter) * 1024u;
+      if (u + u_step < u_end) xs_fetch(u + u_step, (ti & 1u) ^ 1u);
+      const float wc0 = wn0, wc1 = wn1;
+      if (u + u_step < u_end) ws_load(u + u_step, wn0, wn1);
 
-      float2 acc[kThreadChunks][16];
+      float2 acc[32];  // weight rows col0 + 2i, col0 + 2i + 1
 #pragma unroll
       for (int m = 0; m < MATS; ++m) {
-        if (m == 1) {
+        if (m == 1 && active) {
           // gate finished: park its sums in the stash slot, start the up sums
-#pragma unroll
-          for (int q = 0; q < kThreadChunks; ++q) {
-            const uint32_t ch = half + 2u * (uint32_t)q;
-            if (ch < nch) tmem_st32(stash + ch * 32u, acc[q]);
-          }
+          tmem_st32(stash, *reinterpret_cast<const float2(*)[16]>(&acc[0]));
+          tmem_st32(stash + 32u, *reinterpret_cast<const float2(*)[16]>(&acc[16]));
           tmem_wait_st();
         }
 #pragma unroll
-        for (int q = 0; q < kThreadChunks; ++q)
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[q][i] = make_float2(0.0f, 0.0f);
+        for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
+        const uint32_t sel = qkv ? half : (uint32_t)m;
         for (uint32_t kb = 0; kb < kblocks; ++kb) {
+          const float ws = __shfl_sync(0xffffffffu, sel == 0u ? wc0 : wc1, kb);
           const bool ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
           tc_fence_after();
-          if (ok) {
-            const float ws = sh.ws[(qkv ? quarter / 2u : (uint32_t)m) * 32u + kb];
-            const float *xrow = sh.xs + kb * kTN;
+          if (ok && active) {
+            const float c = __fmul_rn(ws, xsb[kb * 32u + lane]);
+            const float2 c2 = make_float2(c, c);
+            const uint32_t src = tmem + lane_base + acc_slot * (uint32_t)kTN + col0;
+            float v0[32], v1[32];
+            tmem_ld32(src, v0);
+            tmem_ld32(src + 32u, v1);
+            tmem_wait_ld();
 #pragma unroll
-            for (int q = 0; q < kThreadChunks; ++q) {
-              const uint32_t ch = half + 2u * (uint32_t)q;
-              if (ch < nch) {
-                float v[32];
-                tmem_ld32(tmem + lane_base + acc_slot * (uint32_t)kTN + ch * 32u, v);
-                tmem_wait_ld();
-                promote<32>(acc[q], v, ws, xrow + ch * 32u);
-              }
+            for (int i = 0; i < 16; ++i) {
+              acc[i] = __ffma2_rn(make_float2(v0[2 * i], v0[2 * i + 1]), c2, acc[i]);
+              acc[16 + i] = __ffma2_rn(make_float2(v1[2 * i], v1[2 * i + 1]), c2, acc[16 + i]);
             }
           }
           tc_fence_before();
@@ -443,63 +450,51 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
         }
       }
 
-      // outputs: thread owns row row0 + r_local and token chunks half, half + 2
-      const uint32_t r = row0 + r_local;
-      // (branch-free bodies: a guard per element would split the unrolled
-      // stores into serial basic blocks, ~3x slower)
+      // outputs: this thread's token, weight rows row0 + col0 .. + 63 (one
+      // contiguous run of the output row)
       if (KIND != 2) {
-        const bool rb = a.round_bf16 != 0u;
-        bool bad = false;
+        if (t_local < cnt) {
+          const bool rb = a.round_bf16 != 0u;
+          float o[64];
+          bool bad = false;
 #pragma unroll
-        for (int q = 0; q < kThreadChunks; ++q) {
-          const uint32_t ch = half + 2u * (uint32_t)q;
-          if (ch < nch) {
-            float *dst = a.out + (size_t)(grp.tok_begin + ch * 32u) * a.out_stride + r;
-            if (ch * 32u + 32u <= cnt) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const float v = el(acc[q], i);
-                const float out = rb ? round_bf16(v) : v;
-                bad |= !finite(out);
-                dst[(size_t)i * a.out_stride] = out;
-              }
-            } else {
-              const uint32_t tend = cnt - ch * 32u;
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const float v = el(acc[q], i);
-                const float out = rb ? round_bf16(v) : v;
-                const bool live = (uint32_t)i < tend;
-                bad |= live && !finite(out);
-                if (live) dst[(size_t)i * a.out_stride] = out;
-              }
-            }
+          for (int i = 0; i < 32; ++i) {
+            o[2 * i] = rb ? round_bf16(acc[i].x) : acc[i].x;
+            o[2 * i + 1] = rb ? round_bf16(acc[i].y) : acc[i].y;
+            bad |= !finite(o[2 * i]) || !finite(o[2 * i + 1]);
           }
+          float *dst = a.out + (size_t)(grp.tok_begin + t_local) * a.out_stride + row0 + col0;
+          if ((a.out_stride & 3u) == 0u && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0u) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              reinterpret_cast<float4 *>(dst)[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) dst[i] = o[i];
+          }
+          if (bad) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
         }
-        if (bad) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
-      } else {
+      } else if (active) {
         // bf16(gate) (from the stash) and bf16(up) (registers): the staged
         // SwiGLU's first roundings; k_swiglu_quant finishes the hidden
-        const uint32_t I = a.rows;
+        float g0[32], g1[32];
+        tmem_ld32(stash, g0);
+        tmem_ld32(stash + 32u, g1);
+        tmem_wait_ld();
+        if (t_local < cnt) {
+          const uint32_t I = a.rows;
+          uint4 *gd = reinterpret_cast<uint4 *>(a.gate_bf16 + (size_t)(grp.tok_begin + t_local) * I + row0 + col0);
+          uint4 *ud = reinterpret_cast<uint4 *>(a.up_bf16 + (size_t)(grp.tok_begin + t_local) * I + row0 + col0);
+          auto pack = [](float lo, float hi) {
+            return (__float_as_uint(round_bf16(lo)) >> 16) | (__float_as_uint(round_bf16(hi)) & 0xffff0000u);
+          };
 #pragma unroll
-        for (int q = 0; q < kThreadChunks; ++q) {
-          const uint32_t ch = half + 2u * (uint32_t)q;
-          if (ch < nch) {
-            float g[32];
-            tmem_ld32(stash + ch * 32u, g);
-            tmem_wait_ld();
-            uint16_t *gd = a.gate_bf16 + (size_t)(grp.tok_begin + ch * 32u) * I + r;
-            uint16_t *ud = a.up_bf16 + (size_t)(grp.tok_begin + ch * 32u) * I + r;
-            const uint32_t tend = min(32u, cnt - ch * 32u);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const uint16_t gb = (uint16_t)(__float_as_uint(round_bf16(g[i])) >> 16);
-              const uint16_t ub = (uint16_t)(__float_as_uint(round_bf16(el(acc[q], i))) >> 16);
-              if ((uint32_t)i < tend) {
-                gd[(size_t)i * I] = gb;
-                ud[(size_t)i * I] = ub;
-              }
-            }
+          for (int i = 0; i < 8; ++i) {
+            const float *gs = i < 4 ? g0 + 8 * i : g1 + 8 * (i - 4);
+            gd[i] = make_uint4(pack(gs[0], gs[1]), pack(gs[2], gs[3]), pack(gs[4], gs[5]), pack(gs[6], gs[7]));
+            const float2 *us = acc + 4 * i;
+            ud[i] = make_uint4(pack(us[0].x, us[0].y), pack(us[1].x, us[1].y), pack(us[2].x, us[2].y),
+                               pack(us[3].x, us[3].y));
           }
         }
       }
