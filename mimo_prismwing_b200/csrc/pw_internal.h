@@ -126,7 +126,9 @@ struct ScheduleOut {
   GemvGroup *dn_groups;     // down groups
   uint32_t *n_groups;       // [1] number of groups
   uint32_t *counters;       // [4] unique experts, placements, max count, tie rows (stats)
+  uint32_t *work;           // [schedule_work_words(experts)] scratch
 };
+size_t schedule_work_words(uint32_t experts);
 struct BankTable {
   const uint8_t *const *gate_w;
   const float *const *gate_s;

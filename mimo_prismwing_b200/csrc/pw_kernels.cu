@@ -517,23 +517,28 @@ cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, co
 }
 
 // ----------------------------------------------------------------- schedule
-// Single CTA.  Placements are ordered by (expert ascending, position
-// ascending) -- the reference's BTreeMap<expert, [(position, weight)]>
+// Placements are ordered by (expert ascending, position ascending) -- the
+// reference's BTreeMap<expert, [(position, weight)]>
 // (src/text_endpoint.rs:4768-4776, src/text_endpoint.rs:5302-5310).  The rank
 // of a token among an expert's placements comes from per-expert token
-// bitmasks, so the order is deterministic without sorting:
-//   1. bitmask[e][t / 32] |= bit(t) for every (t, slot);
-//   2. four threads per expert popcount a quarter of its words each and
-//      exclusive-scan them (word prefixes and the expert's count);
-//   3. a block scan over experts gives placement and group offsets;
-//   4. one thread per token computes its 8 placement indices, writes the
-//      placement lists and, through a sorting network, its placements in
-//      ascending expert order (the combine order);
-//   5. one thread per expert writes its GEMV/GEMM groups.
+// bitmasks, so the order is deterministic without sorting.  Three launches:
+//   k_sched_mask  (one CTA per 32 tokens): warp b ballots, for experts
+//                 32b .. 32b+31, which of the 32 tokens chose them -> the mask
+//                 word [expert][word]; rows are validated here;
+//   k_sched_scan  (one CTA): per-expert prefix counts over the words, the
+//                 scan over experts (placement and group offsets), the groups;
+//   k_sched_place (one CTA per 32 tokens): each token's 8 placement indices,
+//                 the placement lists and, through a sorting network, its
+//                 placements in ascending expert order (the combine order).
+// Scratch (ScheduleOut::work): mask [experts][64], base [experts][64]
+// (placement index of each word's first token), 64 per-word error words and
+// one summary word.
 constexpr uint32_t kSchedMaxTokens = 2048;
 constexpr uint32_t kSchedMaxExperts = 256;
 constexpr uint32_t kSchedWords = kSchedMaxTokens / 32u;
 constexpr uint32_t kSchedThreads = 1024;
+
+size_t schedule_work_words(uint32_t experts) { return 2u * (size_t)experts * kSchedWords + kSchedWords + 1u; }
 
 __device__ __forceinline__ void cswap(uint32_t &ea, uint32_t &pa, uint32_t &eb, uint32_t &pb) {
   const bool sw = ea > eb;
@@ -544,76 +549,95 @@ __device__ __forceinline__ void cswap(uint32_t &ea, uint32_t &pa, uint32_t &eb, 
   pb = p1;
 }
 
-__global__ void __launch_bounds__(kSchedThreads) k_schedule(const uint32_t *__restrict__ selected,
-                                                            const float *__restrict__ weights, uint32_t tokens,
-                                                            uint32_t experts, BankTable bank, ScheduleOut out,
-                                                            uint32_t *flags, uint32_t chunk) {
+__global__ void __launch_bounds__(256) k_sched_mask(const uint32_t *__restrict__ selected, uint32_t tokens,
+                                                    uint32_t experts, uint32_t *__restrict__ work) {
   pdl_wait();
   pdl_launch_dependents();
-  extern __shared__ uint32_t sm[];
-  uint32_t *mask = sm;                                                            // [experts][kSchedWords]
-  uint16_t *prefix = reinterpret_cast<uint16_t *>(mask + experts * kSchedWords);  // [experts][kSchedWords]
-  uint32_t *off = reinterpret_cast<uint32_t *>(prefix + experts * kSchedWords);   // [experts + 1]
-  uint32_t *grp_off = off + experts + 1;                                          // [experts + 1]
-  __shared__ uint32_t bad, uniq, maxc, wsum_c[kSchedThreads / 32], wsum_g[kSchedThreads / 32];
+  uint32_t *mask = work, *badw = work + 2u * experts * kSchedWords;
+  const uint32_t w = blockIdx.x, lane = threadIdx.x % 32u, eb = threadIdx.x / 32u;
+  const uint32_t t = 32u * w + lane;
+  uint32_t sel[8];
+  if (t < tokens) {
+    const uint4 a = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u);
+    const uint4 b = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u + 4u);
+    sel[0] = a.x; sel[1] = a.y; sel[2] = a.z; sel[3] = a.w;
+    sel[4] = b.x; sel[5] = b.y; sel[6] = b.z; sel[7] = b.w;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sel[k] = 0xffffffffu;
+  }
+  if (eb == 0u) {  // validation: experts in range, no expert twice in a row
+    bool bad = false;
+    if (t < tokens) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        bad |= sel[k] >= experts;
+#pragma unroll
+        for (int j = k + 1; j < 8; ++j) bad |= sel[k] == sel[j];
+      }
+    }
+    const uint32_t any = __ballot_sync(0xffffffffu, bad);
+    if (lane == 0) badw[w] = any ? 1u : 0u;
+  }
+  if (32u * eb >= experts) return;
+  uint32_t bits = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    if (sel[k] < experts && sel[k] / 32u == eb) bits |= 1u << (sel[k] % 32u);
+  uint32_t mine = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < 32u; ++j) {
+    const uint32_t b = __ballot_sync(0xffffffffu, (bits >> j) & 1u);
+    mine = lane == j ? b : mine;
+  }
+  const uint32_t e = 32u * eb + lane;
+  if (e < experts) mask[e * kSchedWords + w] = mine;
+}
+
+__global__ void __launch_bounds__(kSchedThreads) k_sched_scan(uint32_t tokens, uint32_t experts, BankTable bank,
+                                                              ScheduleOut out, uint32_t *flags, uint32_t chunk) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t *mask = out.work;
+  uint32_t *base = out.work + experts * kSchedWords, *badw = base + experts * kSchedWords;
+  uint32_t *summary = badw + kSchedWords;
+  __shared__ uint32_t off[kSchedMaxExperts + 1], grp_off[kSchedMaxExperts + 1];
+  __shared__ uint32_t uniq, maxc, wsum_c[kSchedThreads / 32], wsum_g[kSchedThreads / 32];
   const uint32_t words = (tokens + 31u) / 32u;
   const uint32_t tid = threadIdx.x, lane = tid % 32u, warp = tid / 32u;
   if (tid == 0) {
-    bad = 0;
     uniq = 0;
     maxc = 0;
   }
-  for (uint32_t i = tid; i < experts * words; i += kSchedThreads) mask[(i / words) * kSchedWords + i % words] = 0;
-  __syncthreads();
-  // 1. bitmasks
-  for (uint32_t i = tid; i < tokens * 8u; i += kSchedThreads) {
-    const uint32_t e = selected[i];
-    const uint32_t t = i / 8u;
-    if (e >= experts) {
-      bad = 1;
-      continue;
-    }
-    const uint32_t prev = atomicOr(&mask[e * kSchedWords + t / 32u], 1u << (t % 32u));
-    if (prev & (1u << (t % 32u))) bad = 1;  // duplicate expert in one row
-  }
-  __syncthreads();
+  const int bad = __syncthreads_or(tid < words && badw[tid] != 0u);
   if (bad) {
-    if (tid == 0) raise_flag(flags, PW_FLAG_BAD_EXPERT_COUNT);
-    if (tid == 0 && out.n_groups) *out.n_groups = 0;
+    if (tid == 0) {
+      raise_flag(flags, PW_FLAG_BAD_EXPERT_COUNT);
+      if (out.n_groups) *out.n_groups = 0;
+      *summary = 1u;
+    }
     return;
   }
-  // 2. word prefixes, four threads per expert (experts <= 256)
-  uint32_t cnt = 0;
-  {
-    const uint32_t e = tid / 4u, q = tid % 4u;
-    const uint32_t per = (words + 3u) / 4u, w0 = min(words, q * per), w1 = min(words, w0 + per);
-    uint32_t local = 0;
-    if (e < experts)
-      for (uint32_t wi = w0; wi < w1; ++wi) local += __popc(mask[e * kSchedWords + wi]);
-    // exclusive scan over the 4 lanes of this expert (lanes 4k..4k+3 of a warp)
-    uint32_t incl = local;
+  if (tid == 0) *summary = 0u;
+  // per-expert counts, four threads per expert (experts <= 256)
+  const uint32_t ex = tid / 4u, q = tid % 4u;
+  const uint32_t per = (words + 3u) / 4u, w0 = min(words, q * per), w1 = min(words, w0 + per);
+  uint32_t local = 0;
+  if (ex < experts)
+    for (uint32_t wi = w0; wi < w1; ++wi) local += __popc(mask[ex * kSchedWords + wi]);
+  uint32_t incl = local;
 #pragma unroll
-    for (uint32_t o = 1; o < 4u; o <<= 1) {
-      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o, 4);
-      if (q >= o) incl += v;
-    }
-    uint32_t run = incl - local;
-    if (e < experts)
-      for (uint32_t wi = w0; wi < w1; ++wi) {
-        prefix[e * kSchedWords + wi] = (uint16_t)run;
-        run += __popc(mask[e * kSchedWords + wi]);
-      }
-    cnt = __shfl_sync(0xffffffffu, incl, 3, 4);  // the expert's total
+  for (uint32_t o = 1; o < 4u; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o, 4);
+    if (q >= o) incl += v;
   }
+  const uint32_t cnt_e = __shfl_sync(0xffffffffu, incl, 3, 4);
+  if (q == 0u && ex < experts) off[ex] = cnt_e;
   __syncthreads();
-  // 3. offsets: thread e (< experts) holds count c and group count g
+  // scan over experts: thread e holds count c and group count g
   {
     const uint32_t e = tid;
-    uint32_t c = 0;
-    // counts live in lanes 4e..4e+3 of step 2; gather them through shared memory
-    if (tid % 4u == 0u && tid / 4u < experts) off[tid / 4u] = cnt;
-    __syncthreads();
-    if (e < experts) c = off[e];
+    const uint32_t c = e < experts ? off[e] : 0u;
     const uint32_t g = (c + chunk - 1u) / chunk;
     uint32_t ic = c, ig = g;
 #pragma unroll
@@ -632,7 +656,7 @@ __global__ void __launch_bounds__(kSchedThreads) k_schedule(const uint32_t *__re
       atomicAdd(&uniq, 1u);
       atomicMax(&maxc, c);
     }
-    __syncthreads();  // everyone has read off[] (counts) before it is overwritten
+    __syncthreads();  // every count read before off[] is overwritten
     uint32_t bc = 0, bg = 0;
     for (uint32_t k = 0; k < warp; ++k) {
       bc += wsum_c[k];
@@ -643,12 +667,11 @@ __global__ void __launch_bounds__(kSchedThreads) k_schedule(const uint32_t *__re
       grp_off[e] = bg + ig - g;
       out.offsets[e] = bc + ic - c;
       if (e == experts - 1u) {
-        const uint32_t total = bc + ic, gtotal = bg + ig;
-        off[experts] = total;
-        grp_off[experts] = gtotal;
-        out.offsets[experts] = total;
-        if (out.n_groups) *out.n_groups = gtotal;
-        out.counters[1] = total;
+        off[experts] = bc + ic;
+        grp_off[experts] = bg + ig;
+        out.offsets[experts] = bc + ic;
+        if (out.n_groups) *out.n_groups = bg + ig;
+        out.counters[1] = bc + ic;
       }
     }
   }
@@ -657,39 +680,15 @@ __global__ void __launch_bounds__(kSchedThreads) k_schedule(const uint32_t *__re
     out.counters[0] = uniq;
     out.counters[2] = maxc;
   }
-  // 4. per token: placements, placement lists and the combine order
-  for (uint32_t t = tid; t < tokens; t += kSchedThreads) {
-    const uint4 sa = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u);
-    const uint4 sb = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u + 4u);
-    const float4 wa = *reinterpret_cast<const float4 *>(weights + (size_t)t * 8u);
-    const float4 wb = *reinterpret_cast<const float4 *>(weights + (size_t)t * 8u + 4u);
-    uint32_t ex[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
-    const float wt[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-    const uint32_t wi = t / 32u, below_mask = (1u << (t % 32u)) - 1u;
-    uint32_t pl[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t e = ex[k];
-      pl[k] = off[e] + prefix[e * kSchedWords + wi] + __popc(mask[e * kSchedWords + wi] & below_mask);
-      out.placement_tok[pl[k]] = t;
-      out.placement_w[pl[k]] = wt[k];
+  // placement index of the first token of every (expert, word)
+  if (ex < experts) {
+    uint32_t run = off[ex] + incl - local;
+    for (uint32_t wi = w0; wi < w1; ++wi) {
+      base[ex * kSchedWords + wi] = run;
+      run += __popc(mask[ex * kSchedWords + wi]);
     }
-    // Batcher odd-even merge sort of 8 (experts of a row are distinct)
-    cswap(ex[0], pl[0], ex[1], pl[1]); cswap(ex[2], pl[2], ex[3], pl[3]);
-    cswap(ex[4], pl[4], ex[5], pl[5]); cswap(ex[6], pl[6], ex[7], pl[7]);
-    cswap(ex[0], pl[0], ex[2], pl[2]); cswap(ex[1], pl[1], ex[3], pl[3]);
-    cswap(ex[4], pl[4], ex[6], pl[6]); cswap(ex[5], pl[5], ex[7], pl[7]);
-    cswap(ex[1], pl[1], ex[2], pl[2]); cswap(ex[5], pl[5], ex[6], pl[6]);
-    cswap(ex[0], pl[0], ex[4], pl[4]); cswap(ex[1], pl[1], ex[5], pl[5]);
-    cswap(ex[2], pl[2], ex[6], pl[6]); cswap(ex[3], pl[3], ex[7], pl[7]);
-    cswap(ex[2], pl[2], ex[4], pl[4]); cswap(ex[3], pl[3], ex[5], pl[5]);
-    cswap(ex[1], pl[1], ex[2], pl[2]); cswap(ex[3], pl[3], ex[4], pl[4]);
-    cswap(ex[5], pl[5], ex[6], pl[6]);
-    uint4 *sp = reinterpret_cast<uint4 *>(out.slot_place + (size_t)t * 8u);
-    sp[0] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-    sp[1] = make_uint4(pl[4], pl[5], pl[6], pl[7]);
   }
-  // 5. GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
+  // GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
   // (skipped when the caller runs the experts elsewhere: no group arrays)
   for (uint32_t e = tid; e < experts && out.gu_groups; e += kSchedThreads) {
     const uint32_t c = off[e + 1] - off[e];
@@ -718,23 +717,58 @@ __global__ void __launch_bounds__(kSchedThreads) k_schedule(const uint32_t *__re
   }
 }
 
+__global__ void __launch_bounds__(32) k_sched_place(const uint32_t *__restrict__ selected,
+                                                    const float *__restrict__ weights, uint32_t tokens,
+                                                    uint32_t experts, ScheduleOut out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t *mask = out.work, *base = out.work + experts * kSchedWords;
+  if (base[experts * kSchedWords + kSchedWords] != 0u) return;  // invalid rows: k_sched_scan flagged them
+  const uint32_t w = blockIdx.x, t = 32u * w + threadIdx.x;
+  if (t >= tokens) return;
+  const uint4 sa = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u);
+  const uint4 sb = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u + 4u);
+  const float4 wa = *reinterpret_cast<const float4 *>(weights + (size_t)t * 8u);
+  const float4 wb = *reinterpret_cast<const float4 *>(weights + (size_t)t * 8u + 4u);
+  uint32_t ex[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+  const float wt[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+  const uint32_t below = (1u << (t % 32u)) - 1u;
+  uint32_t pl[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t i = ex[k] * kSchedWords + w;
+    pl[k] = base[i] + __popc(mask[i] & below);
+    out.placement_tok[pl[k]] = t;
+    out.placement_w[pl[k]] = wt[k];
+  }
+  // Batcher odd-even merge sort of 8 (experts of a row are distinct)
+  cswap(ex[0], pl[0], ex[1], pl[1]); cswap(ex[2], pl[2], ex[3], pl[3]);
+  cswap(ex[4], pl[4], ex[5], pl[5]); cswap(ex[6], pl[6], ex[7], pl[7]);
+  cswap(ex[0], pl[0], ex[2], pl[2]); cswap(ex[1], pl[1], ex[3], pl[3]);
+  cswap(ex[4], pl[4], ex[6], pl[6]); cswap(ex[5], pl[5], ex[7], pl[7]);
+  cswap(ex[1], pl[1], ex[2], pl[2]); cswap(ex[5], pl[5], ex[6], pl[6]);
+  cswap(ex[0], pl[0], ex[4], pl[4]); cswap(ex[1], pl[1], ex[5], pl[5]);
+  cswap(ex[2], pl[2], ex[6], pl[6]); cswap(ex[3], pl[3], ex[7], pl[7]);
+  cswap(ex[2], pl[2], ex[4], pl[4]); cswap(ex[3], pl[3], ex[5], pl[5]);
+  cswap(ex[1], pl[1], ex[2], pl[2]); cswap(ex[3], pl[3], ex[4], pl[4]);
+  cswap(ex[5], pl[5], ex[6], pl[6]);
+  uint4 *sp = reinterpret_cast<uint4 *>(out.slot_place + (size_t)t * 8u);
+  sp[0] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+  sp[1] = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+}
+
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
                             const BankTable &bank, const ScheduleOut &out, uint32_t *flags, uint32_t chunk,
                             cudaStream_t stream) {
-  if (tokens == 0 || tokens > kSchedMaxTokens || experts > kSchedMaxExperts || experts < 8 || chunk == 0)
+  if (tokens == 0 || tokens > kSchedMaxTokens || experts > kSchedMaxExperts || experts < 8 || chunk == 0 ||
+      !out.work)
     return cudaErrorInvalidValue;
-  const size_t smem = (size_t)experts * kSchedWords * 4 + (size_t)experts * kSchedWords * 2 +
-                      (size_t)(experts + 1) * 8;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(k_schedule, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)((size_t)kSchedMaxExperts * kSchedWords * 6 +
-                                               (size_t)(kSchedMaxExperts + 1) * 8));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  return launch_kernel(k_schedule, dim3(1), dim3(kSchedThreads), smem, stream, selected, weights, tokens, experts,
-                       bank, out, flags, chunk);
+  const uint32_t words = (tokens + 31u) / 32u;
+  cudaError_t e = launch_kernel(k_sched_mask, dim3(words), dim3(256), 0, stream, selected, tokens, experts, out.work);
+  if (e != cudaSuccess) return e;
+  e = launch_kernel(k_sched_scan, dim3(1), dim3(kSchedThreads), 0, stream, tokens, experts, bank, out, flags, chunk);
+  if (e != cudaSuccess) return e;
+  return launch_kernel(k_sched_place, dim3(words), dim3(32), 0, stream, selected, weights, tokens, experts, out);
 }
 
 // ------------------------------------------------------------------ combine

@@ -1202,6 +1202,7 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     so.dn_groups = ar.take<GemvGroup>(max_groups);
     so.n_groups = ar.take<uint32_t>(1);
     so.counters = ar.take<uint32_t>(4);
+    so.work = ar.take<uint32_t>(schedule_work_words(E));
     float *hid = fused ? nullptr : ar.take<float>((size_t)P * I);
     float *gt = fused && !wide ? nullptr : ar.take<float>((size_t)P * I);
     float *ut = fused && !wide ? nullptr : ar.take<float>((size_t)P * I);
@@ -1226,7 +1227,7 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
                        rt->d_flags, rt->num_sms, rt->stream));
     }
     {
-      ProfScope ps(rt, P_SCHED, 1);
+      ProfScope ps(rt, P_SCHED, 3);
       CK(launch_schedule(sel, wts, tokens, E, bank->table, so, rt->d_flags, chunk, rt->stream));
     }
     // the grid covers the worst case; CTAs read the real group count
@@ -1689,6 +1690,7 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
     so.placement_w = ar.take<float>(P);
     so.slot_place = ar.take<uint32_t>(P);
     so.counters = ar.take<uint32_t>(4);
+    so.work = ar.take<uint32_t>(schedule_work_words(E));
     xsend = ar.take<uint8_t>((size_t)P * H);
     ssend = ar.take<float>((size_t)P * Hs);
     ret = ar.take<uint16_t>((size_t)P * H);
@@ -1710,7 +1712,7 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
                        rt->d_flags, rt->num_sms, rt->stream));
     }
     {
-      ProfScope ps(rt, P_SCHED, 2);
+      ProfScope ps(rt, P_SCHED, 4);
       CK(launch_schedule(sel, wts, tokens, E, BankTable{}, so, rt->d_flags, 1u, rt->stream));
       CK(launch_gather_rows(xc, xs, so.placement_tok, P, H, xsend, ssend, rt->stream));
     }
