@@ -108,9 +108,9 @@ cudaError_t launch_gemv(int kind, const GemvArgs &args, int grid, cudaStream_t s
 int gemv_max_ctas(int num_sms);
 cudaError_t launch_gemv_mma(int kind, const GemvArgs &args, int grid, cudaStream_t stream);
 cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_t stream);
-// Router logits (or, from 64 tokens, their partial trees) into `scratch`
+// Router logits (or, from 64 tokens, their per-slice sums) into `scratch`
 // (router_scratch_floats floats), then the sigmoid no-aux top-8.
-size_t router_scratch_floats(uint32_t tokens, uint32_t experts);
+size_t router_scratch_floats(uint32_t tokens, uint32_t experts, uint32_t hidden);
 cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, const float *bias, uint32_t experts,
                           uint32_t hidden, float *scratch, uint32_t *selected, float *weights, uint32_t *tie_rows,
                           uint32_t *flags, int num_sms, cudaStream_t stream);

@@ -74,282 +74,216 @@ cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_
 
 // ------------------------------------------------------------ router logits
 // logit[t,e] = sum_c x[t,c] * w[e,c] in f32 in a fixed order (the oracle's
-// pwo_router_logits restates it; the reference's own logits are f32 too):
-//   the K axis is cut into 512-column slices; warp w (of 8) owns slices
-//   s = w, w+8, ...; lane l accumulates, for each owned slice in ascending
-//   order, the 8-column chunks at 512s + 8l and 512s + 8l + 256, column by
-//   column, with fused multiply-adds; an xor butterfly (16, 8, 4, 2, 1) adds
-//   the lanes; the CTA then adds the 8 warp partials in warp order starting
-//   from warp 0's.  bf16 weights widen to f32 exactly (a shift).
-// Decode widths: one CTA per (expert, 8 tokens).
-constexpr int kRouterTok = 8;
+// pwo_router_logits restates it; the reference's own logits are f32 too,
+// from an SGEMM of unspecified order): the K axis is cut into 256-column
+// slices; slice s's sum is a chain of fused multiply-adds from +0 over its
+// columns in ascending order; the logit adds the slice sums in slice order
+// starting from slice 0's.  bf16 weights widen to f32 exactly (a shift).
+constexpr uint32_t kRouterSlice = 256;
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Decode widths: one CTA per (expert, 8 tokens); a thread runs whole slice
+// chains, the first 8 threads add each token's slice sums.
+constexpr int kRouterTok = 8;
+constexpr uint32_t kRouterMaxSlices = 64;  // hidden <= 16384
 
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, uint32_t tokens,
                                                        const uint16_t *__restrict__ w, uint32_t experts,
                                                        uint32_t hidden, float *__restrict__ logits) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float part[8][kRouterTok];
-  const uint32_t lane = threadIdx.x % 32u, warp = threadIdx.x / 32u;
-  const uint32_t e = blockIdx.x;
-  const uint32_t t0 = blockIdx.y * kRouterTok;
-  float acc[kRouterTok];
-#pragma unroll
-  for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0f;
+  __shared__ float part[kRouterTok][kRouterMaxSlices];
+  const uint32_t e = blockIdx.x, t0 = blockIdx.y * kRouterTok;
+  const uint32_t S = hidden / kRouterSlice;
   const uint16_t *wrow = w + (size_t)e * hidden;
-  const uint32_t slices = hidden / 512u;
-  for (uint32_t sl = warp; sl < slices; sl += 8u) {
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t c0 = 512u * sl + 8u * lane + 256u * j;
-      const uint4 wq = __ldg(reinterpret_cast<const uint4 *>(wrow + c0));
-      const float wf[8] = {bf16lo(wq.x), bf16hi(wq.x), bf16lo(wq.y), bf16hi(wq.y),
-                           bf16lo(wq.z), bf16hi(wq.z), bf16lo(wq.w), bf16hi(wq.w)};
-#pragma unroll
-      for (int t = 0; t < kRouterTok; ++t) {
-        if (t0 + t < tokens) {
-          const float4 *xp = reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * hidden + c0);
-          const float4 a = __ldg(xp), b = __ldg(xp + 1);
-          const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[t] = __fmaf_rn(xv[i], wf[i], acc[t]);
-        }
+  for (uint32_t c = threadIdx.x; c < (uint32_t)kRouterTok * S; c += blockDim.x) {
+    const uint32_t j = c / S, s = c % S;
+    float acc = 0.0f;
+    if (t0 + j < tokens) {
+      const float4 *xp = reinterpret_cast<const float4 *>(x + (size_t)(t0 + j) * hidden + kRouterSlice * s);
+      const uint4 *wp = reinterpret_cast<const uint4 *>(wrow + kRouterSlice * s);
+#pragma unroll 4
+      for (uint32_t i = 0; i < kRouterSlice / 8u; ++i) {
+        const float4 a = __ldg(xp + 2 * i), b = __ldg(xp + 2 * i + 1);
+        const uint4 q = __ldg(wp + i);
+        acc = __fmaf_rn(a.x, bf16lo(q.x), acc);
+        acc = __fmaf_rn(a.y, bf16hi(q.x), acc);
+        acc = __fmaf_rn(a.z, bf16lo(q.y), acc);
+        acc = __fmaf_rn(a.w, bf16hi(q.y), acc);
+        acc = __fmaf_rn(b.x, bf16lo(q.z), acc);
+        acc = __fmaf_rn(b.y, bf16hi(q.z), acc);
+        acc = __fmaf_rn(b.z, bf16lo(q.w), acc);
+        acc = __fmaf_rn(b.w, bf16hi(q.w), acc);
       }
     }
-  }
-#pragma unroll
-  for (int t = 0; t < kRouterTok; ++t) {
-    float v = acc[t];
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) part[warp][t] = v;
+    part[j][s] = acc;
   }
   __syncthreads();
-  if (threadIdx.x < kRouterTok && t0 + threadIdx.x < tokens) {
-    float s = part[0][threadIdx.x];
-#pragma unroll
-    for (int k = 1; k < 8; ++k) s = __fadd_rn(s, part[k][threadIdx.x]);
-    logits[(size_t)(t0 + threadIdx.x) * experts + e] = s;
+  if (threadIdx.x < (unsigned)kRouterTok && t0 + threadIdx.x < tokens) {
+    float lg = part[threadIdx.x][0];
+    for (uint32_t s = 1; s < S; ++s) lg = __fadd_rn(lg, part[threadIdx.x][s]);
+    logits[(size_t)(t0 + threadIdx.x) * experts + e] = lg;
   }
 }
 
-// Prefill-width router logits: the same per-(token, expert) order as
-// k_router_logits, computed as a register-tiled product.  The xor butterfly
-// (16, 8, 4, 2, 1) first adds lane l and lane l^16, then pairs of those at
-// distance 8, and so on; in bit-reversed lane order i (l = brev5(i)) that is
-// the plain pairwise tree over consecutive i (fadd is commutative).  So one
-// thread can form the tree for its outputs by walking the lane chains in
-// bit-reversed order with a stack of partial sums.
-//
-// Work unit: 64 tokens x 128 experts x (warp-slice w, half h) = the 16 lane
-// chains i = 16h .. 16h+15 of warp w, each an f32 FMA chain from +0 over the
-// lane's columns in the lane's order.  The unit stores its level-4 subtree
-// value V(w,h); k_router_topk forms the warp partial V(w,0) + V(w,1) and the
-// fold over warps in warp order.  Thread (tg, eg) owns tokens 4tg..4tg+3 and
-// experts 4eg..4eg+3, 64+4eg..64+4eg+3 of the tile: per column it reads two
-// float4 of duplicated activations and two float4 of widened weights from
-// shared memory for 16 packed FMAs.  A stage is one 16-column chain segment,
-// double-buffered in shared memory and fetched two stages ahead into
-// registers.  Persistent CTAs walk the units.
+// Prefill widths: the slice chains as a register-tiled product.  Work unit:
+// 64 tokens x 128 experts x one slice (256 columns, 8 stages of 32); thread
+// (tg, eg) owns tokens 8tg..8tg+7 and experts 4eg..4eg+3, 64+4eg..64+4eg+3,
+// one f32 chain each (packed f32x2 FMAs over expert pairs; each lane of a
+// pair rounds like fmaf).  Stages are double-buffered in shared memory and
+// fetched one stage ahead into registers; persistent CTAs walk the units and
+// store each unit's slice sums to partials [slice][token][expert], which
+// k_router_topk adds in slice order.
 namespace rp {
-constexpr int kTok = 64, kExp = 128, kCols = 16, kThreads = 256, kChains = 16;
+constexpr int kTok = 64, kExp = 128, kCols = 32, kThreads = 128;
+constexpr uint32_t kStages = kRouterSlice / kCols;
 struct Smem {
-  float2 xs[2][kCols][kTok];       // activation, duplicated (v, v)
-  float ws[2][kCols][kExp];        // router weight widened to f32
-  float2 v3[kChains][kThreads];    // each thread's first level-3 values (16 float2 = its 32 outputs)
+  float xs[2][kCols][kTok];  // activation [column][token]
+  float ws[2][kCols][kExp];  // router weight widened to f32 [column][expert]
 };
 }  // namespace rp
 
 struct RouterUnits {
-  uint32_t tokens, experts, hidden, slices, active_w, tiles_e, n_units;
-  __device__ __forceinline__ uint32_t nseg(uint32_t w) const { return (slices - w + 7u) / 8u; }
+  uint32_t tokens, experts, hidden, slices, tiles_e, n_units;
 };
 
 struct RouterCursor {
-  uint32_t u, st, stages, w, h, t0, e0, nseg;
+  uint32_t u, st, s, t0, e0;
   __device__ __forceinline__ void decode(const RouterUnits &g) {
     if (u >= g.n_units) return;
-    h = u & 1u;
-    const uint32_t rest = u >> 1;
-    w = rest % g.active_w;
-    const uint32_t tile = rest / g.active_w;
+    s = u % g.slices;
+    const uint32_t tile = u / g.slices;
     e0 = (tile % g.tiles_e) * rp::kExp;
     t0 = (tile / g.tiles_e) * rp::kTok;
-    nseg = g.nseg(w);
-    stages = rp::kChains * nseg;
   }
   __device__ __forceinline__ bool valid(const RouterUnits &g) const { return u < g.n_units; }
   __device__ __forceinline__ void next(const RouterUnits &g) {
-    if (++st == stages) {
+    if (++st == rp::kStages) {
       st = 0;
       u += gridDim.x;
       decode(g);
     }
   }
-  // first column of this stage's chain segment (lane brev5(i) of warp w, slice w + 8m)
-  __device__ __forceinline__ uint32_t base() const {
-    const uint32_t ci = st / nseg, m = st % nseg;
-    const uint32_t l = __brev(rp::kChains * h + ci) >> 27;
-    return 512u * (w + 8u * m) + 8u * l;
-  }
+  __device__ __forceinline__ uint32_t base() const { return kRouterSlice * s + rp::kCols * st; }
+};
+
+struct RouterStage {
+  float4 x[4];
+  uint4 w[4];
 };
 
 __device__ __forceinline__ void router_gload(const float *__restrict__ x, const uint16_t *__restrict__ w,
-                                             const RouterUnits &g, const RouterCursor &c, float4 &xr, uint4 &wr) {
-  const uint32_t tid = threadIdx.x, base = c.base();
-  const uint32_t c4 = tid / 64u, r = tid % 64u;  // x: token r, 4 columns c4
-  const uint32_t t = c.t0 + r;
-  const uint32_t xc = base + (c4 < 2u ? 4u * c4 : 256u + 4u * (c4 - 2u));
-  xr = t < g.tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)t * g.hidden + xc))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-  const uint32_t hw = tid / 128u, e = c.e0 + tid % 128u;  // w: expert, 8 columns
-  wr = e < g.experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)e * g.hidden + base + 256u * hw))
-                     : make_uint4(0u, 0u, 0u, 0u);
-}
-
-__device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const float4 &xr, const uint4 &wr) {
-  const uint32_t tid = threadIdx.x;
-  const uint32_t c4 = tid / 64u, r = tid % 64u;
-  sm.xs[b][4 * c4 + 0][r] = make_float2(xr.x, xr.x);
-  sm.xs[b][4 * c4 + 1][r] = make_float2(xr.y, xr.y);
-  sm.xs[b][4 * c4 + 2][r] = make_float2(xr.z, xr.z);
-  sm.xs[b][4 * c4 + 3][r] = make_float2(xr.w, xr.w);
-  const uint32_t hw = tid / 128u, e = tid % 128u;
-  const uint32_t q[4] = {wr.x, wr.y, wr.z, wr.w};
+                                             const RouterUnits &g, const RouterCursor &c, RouterStage &r) {
+  const uint32_t base = c.base();
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    sm.ws[b][8 * hw + 2 * j][e] = bf16lo(q[j]);
-    sm.ws[b][8 * hw + 2 * j + 1][e] = bf16hi(q[j]);
+  for (int m = 0; m < 4; ++m) {
+    const uint32_t i = threadIdx.x + rp::kThreads * m;
+    const uint32_t tok = c.t0 + i % 64u, c4 = i / 64u;  // x: token, 4 columns
+    r.x[m] = tok < g.tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)tok * g.hidden + base + 4u * c4))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint32_t e = c.e0 + i % 128u, c8 = i / 128u;  // w: expert, 8 columns
+    r.w[m] = e < g.experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)e * g.hidden + base + 8u * c8))
+                           : make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
-__global__ void __launch_bounds__(rp::kThreads, 1)
+__device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterStage &r) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const uint32_t i = threadIdx.x + rp::kThreads * m;
+    const uint32_t tok = i % 64u, c4 = i / 64u;
+    sm.xs[b][4 * c4 + 0][tok] = r.x[m].x;
+    sm.xs[b][4 * c4 + 1][tok] = r.x[m].y;
+    sm.xs[b][4 * c4 + 2][tok] = r.x[m].z;
+    sm.xs[b][4 * c4 + 3][tok] = r.x[m].w;
+    const uint32_t e = i % 128u, c8 = i / 128u;
+    const uint32_t q[4] = {r.w[m].x, r.w[m].y, r.w[m].z, r.w[m].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      sm.ws[b][8 * c8 + 2 * j][e] = bf16lo(q[j]);
+      sm.ws[b][8 * c8 + 2 * j + 1][e] = bf16hi(q[j]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(rp::kThreads, 2)
     k_router_partials(const float *__restrict__ x, const uint16_t *__restrict__ w, RouterUnits g,
                       float *__restrict__ part) {
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char router_smem[];
   rp::Smem &sm = *reinterpret_cast<rp::Smem *>(router_smem);
-  const uint32_t tid = threadIdx.x, lane = tid % 32u, wp = tid / 32u;
-  const uint32_t eg = (wp % 2u) * 8u + lane % 8u, tg = (wp / 2u) * 4u + lane / 8u;
-  RouterCursor ld{blockIdx.x, 0, 0, 0, 0, 0, 0, 0};
+  const uint32_t lane = threadIdx.x % 32u, wp = threadIdx.x / 32u;
+  const uint32_t eg = lane % 16u, tg = 2u * wp + lane / 16u;
+  RouterCursor ld{blockIdx.x, 0, 0, 0, 0};
   ld.decode(g);
   if (!ld.valid(g)) return;
   RouterCursor cp = ld;
-  float4 xr1, xr2;
-  uint4 wr1, wr2;
-  router_gload(x, w, g, ld, xr1, wr1);
+  RouterStage r;
+  router_gload(x, w, g, ld, r);
   ld.next(g);
-  router_sstore(sm, 0, xr1, wr1);
-  bool v1 = ld.valid(g), v2 = false;
-  if (v1) {
-    router_gload(x, w, g, ld, xr1, wr1);
-    ld.next(g);
-  }
-  v2 = ld.valid(g);
-  if (v2) {
-    router_gload(x, w, g, ld, xr2, wr2);
+  router_sstore(sm, 0, r);
+  bool have = ld.valid(g);
+  if (have) {
+    router_gload(x, w, g, ld, r);
     ld.next(g);
   }
   __syncthreads();
 
-  float2 acc[4][4], s0[4][4], s1[4][4], s2[4][4];
+  float2 acc[8][4];
 #pragma unroll
-  for (int t = 0; t < 4; ++t)
+  for (int t = 0; t < 8; ++t)
 #pragma unroll
     for (int p = 0; p < 4; ++p) acc[t][p] = make_float2(0.f, 0.f);
   int b = 0;
   while (cp.valid(g)) {
 #pragma unroll 4
     for (int k = 0; k < rp::kCols; ++k) {
-      const float4 xa = *reinterpret_cast<const float4 *>(&sm.xs[b][k][4 * tg]);
-      const float4 xb = *reinterpret_cast<const float4 *>(&sm.xs[b][k][4 * tg + 2]);
+      const float4 xa = *reinterpret_cast<const float4 *>(&sm.xs[b][k][8 * tg]);
+      const float4 xb = *reinterpret_cast<const float4 *>(&sm.xs[b][k][8 * tg + 4]);
       const float4 wa = *reinterpret_cast<const float4 *>(&sm.ws[b][k][4 * eg]);
       const float4 wb = *reinterpret_cast<const float4 *>(&sm.ws[b][k][64 + 4 * eg]);
-      const float2 xd[4] = {make_float2(xa.x, xa.y), make_float2(xa.z, xa.w), make_float2(xb.x, xb.y),
-                            make_float2(xb.z, xb.w)};
+      const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
       const float2 wv[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
                             make_float2(wb.z, wb.w)};
 #pragma unroll
-      for (int t = 0; t < 4; ++t)
+      for (int t = 0; t < 8; ++t) {
+        const float2 xd = make_float2(xv[t], xv[t]);
 #pragma unroll
-        for (int p = 0; p < 4; ++p) acc[t][p] = __ffma2_rn(wv[p], xd[t], acc[t][p]);
+        for (int p = 0; p < 4; ++p) acc[t][p] = __ffma2_rn(wv[p], xd, acc[t][p]);
+      }
     }
-    const uint32_t ci = cp.st / cp.nseg;
-    if (cp.st % cp.nseg == cp.nseg - 1u) {  // chain ci complete: push it onto the tree
-      const uint32_t c = ci & 7u;
-      if ((c & 1u) == 0u) {
+    if (cp.st == rp::kStages - 1u) {  // the unit's slice chains are complete
+      float *dst = part + (size_t)cp.s * g.tokens * g.experts;
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
+      for (int t = 0; t < 8; ++t) {
+        const uint32_t tok = cp.t0 + 8u * tg + (uint32_t)t;
+        if (tok < g.tokens) {
+          float *row = dst + (size_t)tok * g.experts;
 #pragma unroll
-          for (int p = 0; p < 4; ++p) s0[t][p] = acc[t][p];
-      } else if (c == 1u || c == 5u) {
+          for (int hlf = 0; hlf < 2; ++hlf) {
+            const uint32_t e = cp.e0 + 64u * hlf + 4u * eg;
+            const float v[4] = {acc[t][2 * hlf].x, acc[t][2 * hlf].y, acc[t][2 * hlf + 1].x, acc[t][2 * hlf + 1].y};
+            if ((g.experts & 3u) == 0u && e + 3u < g.experts) {
+              *reinterpret_cast<float4 *>(row + e) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int p = 0; p < 4; ++p) s1[t][p] = __fadd2_rn(s0[t][p], acc[t][p]);
-      } else if (c == 3u) {
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int p = 0; p < 4; ++p) s2[t][p] = __fadd2_rn(s1[t][p], __fadd2_rn(s0[t][p], acc[t][p]));
-      } else {  // c == 7: a level-3 subtree is complete
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int p = 0; p < 4; ++p)
-            s0[t][p] = __fadd2_rn(s2[t][p], __fadd2_rn(s1[t][p], __fadd2_rn(s0[t][p], acc[t][p])));
-        if (ci == 7u) {
-#pragma unroll
-          for (int t = 0; t < 4; ++t)
-#pragma unroll
-            for (int p = 0; p < 4; ++p) sm.v3[t * 4 + p][tid] = s0[t][p];
-        } else {  // ci == 15: level 4 = first subtree + second; store the unit's values
-          const size_t plane = (size_t)g.tokens * g.experts;
-          float *dst = part + (size_t)(2u * cp.w + cp.h) * plane;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const uint32_t tok = cp.t0 + 4u * tg + (uint32_t)t;
-            float v[8];
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-              const float2 r = __fadd2_rn(sm.v3[t * 4 + p][tid], s0[t][p]);
-              v[2 * p] = r.x;
-              v[2 * p + 1] = r.y;
-            }
-            if (tok < g.tokens) {
-#pragma unroll
-              for (int hlf = 0; hlf < 2; ++hlf) {
-                const uint32_t e = cp.e0 + 64u * hlf + 4u * eg;
-                float *row = dst + (size_t)tok * g.experts;
-                if ((g.experts & 3u) == 0u && e + 3u < g.experts) {
-                  *reinterpret_cast<float4 *>(row + e) =
-                      make_float4(v[4 * hlf], v[4 * hlf + 1], v[4 * hlf + 2], v[4 * hlf + 3]);
-                } else {
-#pragma unroll
-                  for (int j = 0; j < 4; ++j)
-                    if (e + j < g.experts) row[e + j] = v[4 * hlf + j];
-                }
-              }
+              for (int j = 0; j < 4; ++j)
+                if (e + j < g.experts) row[e + j] = v[j];
             }
           }
         }
-      }
-#pragma unroll
-      for (int t = 0; t < 4; ++t)
 #pragma unroll
         for (int p = 0; p < 4; ++p) acc[t][p] = make_float2(0.f, 0.f);
+      }
     }
-    if (v1) router_sstore(sm, b ^ 1, xr1, wr1);
-    xr1 = xr2;
-    wr1 = wr2;
-    v1 = v2;
-    v2 = ld.valid(g);
-    if (v2) {
-      router_gload(x, w, g, ld, xr2, wr2);
+    const bool next_ok = have;
+    if (next_ok) router_sstore(sm, b ^ 1, r);
+    have = ld.valid(g);
+    if (have) {
+      router_gload(x, w, g, ld, r);
       ld.next(g);
     }
     __syncthreads();
@@ -363,24 +297,22 @@ static RouterUnits router_units(uint32_t tokens, uint32_t experts, uint32_t hidd
   g.tokens = tokens;
   g.experts = experts;
   g.hidden = hidden;
-  g.slices = hidden / 512u;
-  g.active_w = g.slices < 8u ? g.slices : 8u;
+  g.slices = hidden / kRouterSlice;
   g.tiles_e = (experts + rp::kExp - 1) / rp::kExp;
   const uint32_t tiles_t = (tokens + rp::kTok - 1) / rp::kTok;
-  g.n_units = tiles_t * g.tiles_e * g.active_w * 2u;
+  g.n_units = tiles_t * g.tiles_e * g.slices;
   return g;
 }
 
 constexpr uint32_t kRouterPartialMinTokens = 64;
 
-size_t router_scratch_floats(uint32_t tokens, uint32_t experts) {
-  return (size_t)tokens * experts * (tokens >= kRouterPartialMinTokens ? 16u : 1u);
+size_t router_scratch_floats(uint32_t tokens, uint32_t experts, uint32_t hidden) {
+  return (size_t)tokens * experts * (tokens >= kRouterPartialMinTokens ? hidden / kRouterSlice : 1u);
 }
 
 // --------------------------------------------------------------- router top-k
 // One warp per token (src/text_endpoint.rs:4394 pytorch_noaux_routes): the
-// logit (read, or folded from the partial trees: T_w = V(w,0) + V(w,1), then
-// T_0 + T_1 + ... + T_7 in warp order, T_w = +0 for idle warps); score =
+// logit (read, or the slice sums added in slice order); score =
 // SLEEF sigmoid(logit); corrected = score + bias; 9 rounds of warp argmax
 // (ties -> lower index) give the 8 picks in canonical order and the first
 // rejected value (boundary margin / tie detection).
@@ -404,7 +336,7 @@ __device__ __forceinline__ void argmax_shfl(float &bv, uint32_t &bi, float &bs) 
 }
 
 template <int NPL>
-__global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ src, uint32_t active_w,
+__global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ src, uint32_t slices,
                                                      const float *__restrict__ bias, uint32_t tokens,
                                                      uint32_t experts, uint32_t *__restrict__ selected,
                                                      float *__restrict__ weights, uint32_t *tie_rows,
@@ -425,15 +357,17 @@ __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ s
     if (e < experts) {
       const float *p = src + (size_t)t * experts + e;
       float lg;
-      if (active_w == 0u) {
-        lg = *p;
-      } else {
-        lg = __fadd_rn(p[0], p[plane]);
+      if (slices <= 16u) {  // independent loads first, then the ordered sum
+        float v[16];
 #pragma unroll
-        for (uint32_t w = 1; w < 8u; ++w) {
-          const float tw = w < active_w ? __fadd_rn(p[2u * w * plane], p[(2u * w + 1u) * plane]) : 0.0f;
-          lg = __fadd_rn(lg, tw);
-        }
+        for (uint32_t s = 0; s < 16u; ++s) v[s] = s < slices ? p[s * plane] : 0.0f;
+        lg = v[0];
+#pragma unroll
+        for (uint32_t s = 1; s < 16u; ++s)
+          if (s < slices) lg = __fadd_rn(lg, v[s]);
+      } else {
+        lg = p[0];
+        for (uint32_t s = 1; s < slices; ++s) lg = __fadd_rn(lg, p[s * plane]);
       }
       const float b = __ldg(bias + e);
       if (!finite(lg) || !finite(b)) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
@@ -487,8 +421,9 @@ __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ s
 cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, const float *bias, uint32_t experts,
                           uint32_t hidden, float *scratch, uint32_t *selected, float *weights, uint32_t *tie_rows,
                           uint32_t *flags, int num_sms, cudaStream_t stream) {
-  if (hidden % 512u || tokens == 0 || experts <= 8 || experts > 1024u) return cudaErrorInvalidValue;
-  uint32_t active_w = 0;
+  if (hidden % 512u || hidden > kRouterSlice * kRouterMaxSlices || tokens == 0 || experts <= 8 || experts > 1024u)
+    return cudaErrorInvalidValue;
+  uint32_t slices = 1;  // partial planes k_router_topk adds
   cudaError_t st;
   if (tokens >= kRouterPartialMinTokens) {
     const RouterUnits g = router_units(tokens, experts, hidden);
@@ -499,20 +434,24 @@ cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, co
       if (st != cudaSuccess) return st;
       configured = true;
     }
-    const uint32_t grid = g.n_units < (uint32_t)num_sms ? g.n_units : (uint32_t)num_sms;
+    // two 4-warp CTAs per SM: one warp per scheduler left the FMA pipe idle
+    // on every short dependency (measured ~50% FMA-pipe activity)
+    const uint32_t grid = g.n_units < 2u * (uint32_t)num_sms ? g.n_units : 2u * (uint32_t)num_sms;
     st = launch_kernel(k_router_partials, dim3(grid), dim3(rp::kThreads), sizeof(rp::Smem), stream, x, w, g,
                        scratch);
-    active_w = g.active_w;
+    slices = g.slices;
   } else {
-    st = launch_kernel(k_router_logits, dim3(experts, (tokens + kRouterTok - 1) / kRouterTok), dim3(256), 0,
+    const uint32_t chains = (uint32_t)kRouterTok * (hidden / kRouterSlice);  // one thread per slice chain
+    st = launch_kernel(k_router_logits, dim3(experts, (tokens + kRouterTok - 1) / kRouterTok),
+                       dim3(chains < 256u ? chains : 256u), 0,
                        stream, x, tokens, w, experts, hidden, scratch);
   }
   if (st != cudaSuccess) return st;
   const dim3 grid((tokens + 7u) / 8u);
   if (experts <= 256u)
-    return launch_kernel(k_router_topk<8>, grid, dim3(256), 0, stream, (const float *)scratch, active_w, bias,
+    return launch_kernel(k_router_topk<8>, grid, dim3(256), 0, stream, (const float *)scratch, slices, bias,
                          tokens, experts, selected, weights, tie_rows, flags);
-  return launch_kernel(k_router_topk<32>, grid, dim3(256), 0, stream, (const float *)scratch, active_w, bias,
+  return launch_kernel(k_router_topk<32>, grid, dim3(256), 0, stream, (const float *)scratch, slices, bias,
                        tokens, experts, selected, weights, tie_rows, flags);
 }
 

@@ -873,8 +873,8 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
 static int check_router(pw_runtime *rt, const pw_router *r) {
   if (!r || !r->weight_bf16 || !r->bias) return fail(rt, PW_ERR_ARGUMENT, "router descriptor is null");
   if (r->top_k != 8) return fail(rt, PW_ERR_UNSUPPORTED, "top_k must be 8");
-  if (r->experts <= 8 || r->experts > 256 || r->hidden == 0 || r->hidden % 512u)
-    return fail(rt, PW_ERR_SHAPE, "router shape mismatch (experts 9..256, hidden a multiple of 512)");
+  if (r->experts <= 8 || r->experts > 256 || r->hidden == 0 || r->hidden % 512u || r->hidden > 16384u)
+    return fail(rt, PW_ERR_SHAPE, "router shape mismatch (experts 9..256, hidden a multiple of 512 up to 16384)");
   return PW_OK;
 }
 
@@ -898,7 +898,7 @@ int pw_route(pw_runtime *rt, const pw_router *router, const float *x, uint32_t t
     float *dx = call.host() ? ar.take<float>((size_t)tokens * H) : const_cast<float *>(x);
     uint32_t *dsel = call.host() ? ar.take<uint32_t>((size_t)tokens * 8) : selected;
     float *dw = call.host() ? ar.take<float>((size_t)tokens * 8) : weights;
-    float *logits = ar.take<float>(router_scratch_floats(tokens, E));
+    float *logits = ar.take<float>(router_scratch_floats(tokens, E, H));
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)tokens * H * 4)) != PW_OK) return s;
     CK(cudaMemsetAsync(rt->d_ties, 0, 4, rt->stream));
@@ -1190,7 +1190,7 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     float *dy = call.host() ? ar.take<float>((size_t)tokens * H) : y;
     uint8_t *xc = ar.take<uint8_t>((size_t)tokens * H);
     float *xs = ar.take<float>((size_t)tokens * H / 128u);
-    float *logits = ar.take<float>(router_scratch_floats(tokens, E));
+    float *logits = ar.take<float>(router_scratch_floats(tokens, E, H));
     uint32_t *sel = ar.take<uint32_t>(P);
     float *wts = ar.take<float>(P);
     ScheduleOut so{};
@@ -1681,7 +1681,7 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
     dy = call.host() ? ar.take<float>((size_t)tokens * H) : y;
     uint8_t *xc = ar.take<uint8_t>((size_t)tokens * H);
     float *xs = ar.take<float>((size_t)tokens * Hs);
-    float *logits = ar.take<float>(router_scratch_floats(tokens, E));
+    float *logits = ar.take<float>(router_scratch_floats(tokens, E, H));
     sel = ar.take<uint32_t>(P);
     wts = ar.take<float>(P);
     so = ScheduleOut{};

@@ -263,7 +263,8 @@ def swa_qkv_source_row(r: int) -> int:
 
 
 def router_logits(x: np.ndarray, weight_bf16_bits: np.ndarray) -> np.ndarray:
-    """Router logits, f32 fused multiply-adds in the pinned lane order (see pw_oracle.c)."""
+    """Router logits, f32 fused-multiply-add chains over 256-column slices, added in slice order
+    (the pinned order; see pw_oracle.c)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     w = np.ascontiguousarray(weight_bf16_bits, dtype=np.uint16)
     tokens, hidden = x.shape

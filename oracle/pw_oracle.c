@@ -441,47 +441,30 @@ float pwo_staged_swiglu(float gate, float up, int exp_kind) {
 /* computes f32 logits with an SGEMM (src/text_endpoint.rs:4350 via    */
 /* f32_linear :3458) whose order is unspecified; this build pins the   */
 /* order so that CPU and GPU agree bit for bit:                         */
-/*   the K axis is cut into 512-column slices; "warp" w in 0..7 owns    */
-/*   slices s = w, w+8, ...; "lane" l in 0..31 accumulates, per owned   */
-/*   slice in ascending order, the 8-column chunks at 512s+8l and       */
-/*   512s+8l+256, column by column, with a fused multiply-add in f32    */
-/*   (fmaf: one rounding per step); the 32 lane sums combine by the xor */
-/*   butterfly 16,8,4,2,1 (f32 adds); the 8 warp sums are added in warp */
-/*   order starting from warp 0's.  The weight is bf16 bits (exact in   */
-/*   f32).                                                              */
+/*   the K axis is cut into 256-column slices; slice s's sum is a chain */
+/*   of fused multiply-adds in f32 (fmaf: one rounding per step) from   */
+/*   +0 over its columns in ascending order; the logit is the slice    */
+/*   sums added in slice order starting from slice 0's.  The weight is  */
+/*   bf16 bits (exact in f32).                                          */
 /* ------------------------------------------------------------------ */
 static inline float bf16_bits_to_f32(uint16_t b) { return u2f((uint32_t)b << 16); }
 
 int pwo_router_logits(const float *x, size_t tokens, const uint16_t *weight_bf16, size_t experts,
                       size_t hidden, float *logits) {
   if (hidden % 512 != 0) return -1;
-  const size_t slices = hidden / 512;
+  const size_t slices = hidden / 256;
 #pragma omp parallel for schedule(static)
   for (size_t te = 0; te < tokens * experts; ++te) {
     const size_t t = te / experts, e = te % experts;
-    float part[8];
-    for (int w = 0; w < 8; ++w) {
-      float lane[32];
-      for (int l = 0; l < 32; ++l) {
-        float s = 0.0f;
-        for (size_t sl = (size_t)w; sl < slices; sl += 8)
-          for (size_t j = 0; j < 2; ++j) {
-            const size_t c0 = 512 * sl + 8 * (size_t)l + 256 * j;
-            for (size_t i = 0; i < 8; ++i)
-              s = fmaf(x[t * hidden + c0 + i], bf16_bits_to_f32(weight_bf16[e * hidden + c0 + i]), s);
-          }
-        lane[l] = s;
-      }
-      for (int o = 16; o >= 1; o >>= 1) {
-        float next[32];
-        for (int l = 0; l < 32; ++l) next[l] = lane[l] + lane[l ^ o];
-        memcpy(lane, next, sizeof lane);
-      }
-      part[w] = lane[0];
+    const float *xr = x + t * hidden;
+    const uint16_t *wr = weight_bf16 + e * hidden;
+    float logit = 0.0f;
+    for (size_t s = 0; s < slices; ++s) {
+      float c = 0.0f;
+      for (size_t i = 256 * s; i < 256 * (s + 1); ++i) c = fmaf(xr[i], bf16_bits_to_f32(wr[i]), c);
+      logit = s == 0 ? c : logit + c;
     }
-    float s = part[0];
-    for (int w = 1; w < 8; ++w) s += part[w];
-    logits[t * experts + e] = s;
+    logits[t * experts + e] = logit;
   }
   return 0;
 }
