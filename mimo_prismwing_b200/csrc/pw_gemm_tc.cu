@@ -463,14 +463,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
             o[2 * i + 1] = rb ? round_bf16(acc[i].y) : acc[i].y;
             bad |= !finite(o[2 * i]) || !finite(o[2 * i + 1]);
           }
-          float *dst = a.out + (size_t)(grp.tok_begin + t_local) * a.out_stride + row0 + col0;
-          if ((a.out_stride & 3u) == 0u && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0u) {
+          if (a.out_bf16) {  // exact: the values are bf16-rounded
+            uint4 *d16 = reinterpret_cast<uint4 *>(a.out_bf16 + (size_t)(grp.tok_begin + t_local) * a.out_stride +
+                                                   row0 + col0);
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              reinterpret_cast<float4 *>(dst)[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            for (int i = 0; i < 8; ++i) {
+              const float *oo = o + 8 * i;
+              d16[i] = make_uint4((__float_as_uint(oo[0]) >> 16) | (__float_as_uint(oo[1]) & 0xffff0000u),
+                                  (__float_as_uint(oo[2]) >> 16) | (__float_as_uint(oo[3]) & 0xffff0000u),
+                                  (__float_as_uint(oo[4]) >> 16) | (__float_as_uint(oo[5]) & 0xffff0000u),
+                                  (__float_as_uint(oo[6]) >> 16) | (__float_as_uint(oo[7]) & 0xffff0000u));
+            }
           } else {
+            float *dst = a.out + (size_t)(grp.tok_begin + t_local) * a.out_stride + row0 + col0;
+            if ((a.out_stride & 3u) == 0u && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0u) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) dst[i] = o[i];
+              for (int i = 0; i < 16; ++i)
+                reinterpret_cast<float4 *>(dst)[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 64; ++i) dst[i] = o[i];
+            }
           }
           if (bad) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
         }

@@ -77,6 +77,8 @@ struct GemvArgs {
                                  //   ends, so the producer may stream them before waiting
   uint16_t *gate_bf16;           // tcgen05 kind 2: bf16(gate) and bf16(up) [*, rows], the
   uint16_t *up_bf16;             //   staged SwiGLU's inputs (k_swiglu_quant finishes it)
+  uint16_t *out_bf16;            // tcgen05 kind 0 with round_bf16: the rounded result as bf16 bits
+                                 //   [*, out_stride] instead of f32 in out
   uint32_t splits;               // GEMV split-K over the 8-leaf K tree: 1, 2, 4 or 8
   float *split_ws;               //   partial sums [tile][split][mats][128 rows][8 tokens]
   uint32_t *split_cnt;           //   per-tile arrival counters (zero; reset by the last CTA)

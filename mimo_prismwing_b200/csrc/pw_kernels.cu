@@ -84,48 +84,47 @@ constexpr uint32_t kRouterSlice = 256;
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// Decode widths: one CTA per (expert, 8 tokens); a thread runs whole slice
-// chains, the first 8 threads add each token's slice sums.
+// Decode widths: one CTA per (slice, 32 experts, 8 tokens) stages the
+// slice's activation columns and weight rows in shared memory with coalesced
+// loads; thread (token, expert) then runs its chain from shared memory (the
+// warp shares a token: broadcast reads of x, consecutive experts' weights).
+// The slice sums go to the same partials as the prefill kernel.
 constexpr int kRouterTok = 8;
 constexpr uint32_t kRouterMaxSlices = 64;  // hidden <= 16384
 
-__global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, uint32_t tokens,
-                                                       const uint16_t *__restrict__ w, uint32_t experts,
-                                                       uint32_t hidden, float *__restrict__ logits) {
+__global__ void __launch_bounds__(256) k_router_slices_small(const float *__restrict__ x, uint32_t tokens,
+                                                             const uint16_t *__restrict__ w, uint32_t experts,
+                                                             uint32_t hidden, float *__restrict__ part) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float part[kRouterTok][kRouterMaxSlices];
-  const uint32_t e = blockIdx.x, t0 = blockIdx.y * kRouterTok;
-  const uint32_t S = hidden / kRouterSlice;
-  const uint16_t *wrow = w + (size_t)e * hidden;
-  for (uint32_t c = threadIdx.x; c < (uint32_t)kRouterTok * S; c += blockDim.x) {
-    const uint32_t j = c / S, s = c % S;
-    float acc = 0.0f;
-    if (t0 + j < tokens) {
-      const float4 *xp = reinterpret_cast<const float4 *>(x + (size_t)(t0 + j) * hidden + kRouterSlice * s);
-      const uint4 *wp = reinterpret_cast<const uint4 *>(wrow + kRouterSlice * s);
-#pragma unroll 4
-      for (uint32_t i = 0; i < kRouterSlice / 8u; ++i) {
-        const float4 a = __ldg(xp + 2 * i), b = __ldg(xp + 2 * i + 1);
-        const uint4 q = __ldg(wp + i);
-        acc = __fmaf_rn(a.x, bf16lo(q.x), acc);
-        acc = __fmaf_rn(a.y, bf16hi(q.x), acc);
-        acc = __fmaf_rn(a.z, bf16lo(q.y), acc);
-        acc = __fmaf_rn(a.w, bf16hi(q.y), acc);
-        acc = __fmaf_rn(b.x, bf16lo(q.z), acc);
-        acc = __fmaf_rn(b.y, bf16hi(q.z), acc);
-        acc = __fmaf_rn(b.z, bf16lo(q.w), acc);
-        acc = __fmaf_rn(b.w, bf16hi(q.w), acc);
-      }
+  __shared__ __align__(16) float xs[kRouterTok][kRouterSlice];
+  __shared__ __align__(16) uint16_t ws[kRouterSlice][32];
+  const uint32_t s = blockIdx.x, e0 = blockIdx.y * 32u, t0 = blockIdx.z * kRouterTok;
+  const uint32_t tid = threadIdx.x, col0 = kRouterSlice * s;
+  for (uint32_t i = tid; i < (uint32_t)kRouterTok * kRouterSlice / 4u; i += 256u) {
+    const uint32_t j = i / (kRouterSlice / 4u), c4 = i % (kRouterSlice / 4u);
+    reinterpret_cast<float4 *>(&xs[j][0])[c4] =
+        t0 + j < tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + j) * hidden + col0) + c4)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (uint32_t i = tid; i < 32u * kRouterSlice / 8u; i += 256u) {
+    const uint32_t el = i % 32u, c8 = i / 32u;  // lanes: consecutive experts (conflict-free stores)
+    const uint4 q = e0 + el < experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)(e0 + el) * hidden + col0) + c8)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      ws[8u * c8 + 2u * k][el] = (uint16_t)(qq[k] & 0xffffu);
+      ws[8u * c8 + 2u * k + 1u][el] = (uint16_t)(qq[k] >> 16);
     }
-    part[j][s] = acc;
   }
   __syncthreads();
-  if (threadIdx.x < (unsigned)kRouterTok && t0 + threadIdx.x < tokens) {
-    float lg = part[threadIdx.x][0];
-    for (uint32_t s = 1; s < S; ++s) lg = __fadd_rn(lg, part[threadIdx.x][s]);
-    logits[(size_t)(t0 + threadIdx.x) * experts + e] = lg;
-  }
+  const uint32_t el = tid % 32u, j = tid / 32u;
+  float acc = 0.0f;
+#pragma unroll 16
+  for (uint32_t i = 0; i < kRouterSlice; ++i)
+    acc = __fmaf_rn(xs[j][i], __uint_as_float((uint32_t)ws[i][el] << 16), acc);
+  if (t0 + j < tokens && e0 + el < experts) part[((size_t)s * tokens + t0 + j) * experts + e0 + el] = acc;
 }
 
 // Prefill widths: the slice chains as a register-tiled product.  Work unit:
@@ -304,10 +303,10 @@ static RouterUnits router_units(uint32_t tokens, uint32_t experts, uint32_t hidd
   return g;
 }
 
-constexpr uint32_t kRouterPartialMinTokens = 64;
+constexpr uint32_t kRouterPartialMinTokens = 64;  // below: k_router_slices_small
 
 size_t router_scratch_floats(uint32_t tokens, uint32_t experts, uint32_t hidden) {
-  return (size_t)tokens * experts * (tokens >= kRouterPartialMinTokens ? hidden / kRouterSlice : 1u);
+  return (size_t)tokens * experts * (hidden / kRouterSlice);
 }
 
 // --------------------------------------------------------------- router top-k
@@ -423,10 +422,9 @@ cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, co
                           uint32_t *flags, int num_sms, cudaStream_t stream) {
   if (hidden % 512u || hidden > kRouterSlice * kRouterMaxSlices || tokens == 0 || experts <= 8 || experts > 1024u)
     return cudaErrorInvalidValue;
-  uint32_t slices = 1;  // partial planes k_router_topk adds
+  const RouterUnits g = router_units(tokens, experts, hidden);
   cudaError_t st;
   if (tokens >= kRouterPartialMinTokens) {
-    const RouterUnits g = router_units(tokens, experts, hidden);
     static bool configured = false;
     if (!configured) {
       st = cudaFuncSetAttribute(k_router_partials, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -439,19 +437,17 @@ cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, co
     const uint32_t grid = g.n_units < 2u * (uint32_t)num_sms ? g.n_units : 2u * (uint32_t)num_sms;
     st = launch_kernel(k_router_partials, dim3(grid), dim3(rp::kThreads), sizeof(rp::Smem), stream, x, w, g,
                        scratch);
-    slices = g.slices;
   } else {
-    const uint32_t chains = (uint32_t)kRouterTok * (hidden / kRouterSlice);  // one thread per slice chain
-    st = launch_kernel(k_router_logits, dim3(experts, (tokens + kRouterTok - 1) / kRouterTok),
-                       dim3(chains < 256u ? chains : 256u), 0,
+    st = launch_kernel(k_router_slices_small,
+                       dim3(g.slices, (experts + 31u) / 32u, (tokens + kRouterTok - 1) / kRouterTok), dim3(256), 0,
                        stream, x, tokens, w, experts, hidden, scratch);
   }
   if (st != cudaSuccess) return st;
   const dim3 grid((tokens + 7u) / 8u);
   if (experts <= 256u)
-    return launch_kernel(k_router_topk<8>, grid, dim3(256), 0, stream, (const float *)scratch, slices, bias,
+    return launch_kernel(k_router_topk<8>, grid, dim3(256), 0, stream, (const float *)scratch, g.slices, bias,
                          tokens, experts, selected, weights, tie_rows, flags);
-  return launch_kernel(k_router_topk<32>, grid, dim3(256), 0, stream, (const float *)scratch, slices, bias,
+  return launch_kernel(k_router_topk<32>, grid, dim3(256), 0, stream, (const float *)scratch, g.slices, bias,
                        tokens, experts, selected, weights, tie_rows, flags);
 }
 
@@ -696,12 +692,196 @@ __global__ void __launch_bounds__(32) k_sched_place(const uint32_t *__restrict__
   sp[1] = make_uint4(pl[4], pl[5], pl[6], pl[7]);
 }
 
+// Decode widths (<= 256 tokens): everything in one CTA, the bitmasks built
+// with shared-memory atomics; the same placements as the three-launch path.
+constexpr uint32_t kSchedSmallTokens = 256;
+constexpr uint32_t kSchedSmallWords = kSchedSmallTokens / 32u;
+
+__global__ void __launch_bounds__(kSchedThreads) k_schedule_small(const uint32_t *__restrict__ selected,
+                                                            const float *__restrict__ weights, uint32_t tokens,
+                                                            uint32_t experts, BankTable bank, ScheduleOut out,
+                                                            uint32_t *flags, uint32_t chunk) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ uint32_t sm[];
+  uint32_t *mask = sm;                                                            // [experts][kSchedSmallWords]
+  uint16_t *prefix = reinterpret_cast<uint16_t *>(mask + experts * kSchedSmallWords);  // [experts][kSchedSmallWords]
+  uint32_t *off = reinterpret_cast<uint32_t *>(prefix + experts * kSchedSmallWords);   // [experts + 1]
+  uint32_t *grp_off = off + experts + 1;                                          // [experts + 1]
+  __shared__ uint32_t bad, uniq, maxc, wsum_c[kSchedThreads / 32], wsum_g[kSchedThreads / 32];
+  const uint32_t words = (tokens + 31u) / 32u;
+  const uint32_t tid = threadIdx.x, lane = tid % 32u, warp = tid / 32u;
+  if (tid == 0) {
+    bad = 0;
+    uniq = 0;
+    maxc = 0;
+  }
+  for (uint32_t i = tid; i < experts * words; i += kSchedThreads) mask[(i / words) * kSchedSmallWords + i % words] = 0;
+  __syncthreads();
+  // 1. bitmasks
+  for (uint32_t i = tid; i < tokens * 8u; i += kSchedThreads) {
+    const uint32_t e = selected[i];
+    const uint32_t t = i / 8u;
+    if (e >= experts) {
+      bad = 1;
+      continue;
+    }
+    const uint32_t prev = atomicOr(&mask[e * kSchedSmallWords + t / 32u], 1u << (t % 32u));
+    if (prev & (1u << (t % 32u))) bad = 1;  // duplicate expert in one row
+  }
+  __syncthreads();
+  if (bad) {
+    if (tid == 0) raise_flag(flags, PW_FLAG_BAD_EXPERT_COUNT);
+    if (tid == 0 && out.n_groups) *out.n_groups = 0;
+    return;
+  }
+  // 2. word prefixes, four threads per expert (experts <= 256)
+  uint32_t cnt = 0;
+  {
+    const uint32_t e = tid / 4u, q = tid % 4u;
+    const uint32_t per = (words + 3u) / 4u, w0 = min(words, q * per), w1 = min(words, w0 + per);
+    uint32_t local = 0;
+    if (e < experts)
+      for (uint32_t wi = w0; wi < w1; ++wi) local += __popc(mask[e * kSchedSmallWords + wi]);
+    // exclusive scan over the 4 lanes of this expert (lanes 4k..4k+3 of a warp)
+    uint32_t incl = local;
+#pragma unroll
+    for (uint32_t o = 1; o < 4u; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o, 4);
+      if (q >= o) incl += v;
+    }
+    uint32_t run = incl - local;
+    if (e < experts)
+      for (uint32_t wi = w0; wi < w1; ++wi) {
+        prefix[e * kSchedSmallWords + wi] = (uint16_t)run;
+        run += __popc(mask[e * kSchedSmallWords + wi]);
+      }
+    cnt = __shfl_sync(0xffffffffu, incl, 3, 4);  // the expert's total
+  }
+  __syncthreads();
+  // 3. offsets: thread e (< experts) holds count c and group count g
+  {
+    const uint32_t e = tid;
+    uint32_t c = 0;
+    // counts live in lanes 4e..4e+3 of step 2; gather them through shared memory
+    if (tid % 4u == 0u && tid / 4u < experts) off[tid / 4u] = cnt;
+    __syncthreads();
+    if (e < experts) c = off[e];
+    const uint32_t g = (c + chunk - 1u) / chunk;
+    uint32_t ic = c, ig = g;
+#pragma unroll
+    for (uint32_t o = 1; o < 32u; o <<= 1) {
+      const uint32_t vc = __shfl_up_sync(0xffffffffu, ic, o), vg = __shfl_up_sync(0xffffffffu, ig, o);
+      if (lane >= o) {
+        ic += vc;
+        ig += vg;
+      }
+    }
+    if (lane == 31u) {
+      wsum_c[warp] = ic;
+      wsum_g[warp] = ig;
+    }
+    if (e < experts && c) {
+      atomicAdd(&uniq, 1u);
+      atomicMax(&maxc, c);
+    }
+    __syncthreads();  // everyone has read off[] (counts) before it is overwritten
+    uint32_t bc = 0, bg = 0;
+    for (uint32_t k = 0; k < warp; ++k) {
+      bc += wsum_c[k];
+      bg += wsum_g[k];
+    }
+    if (e < experts) {
+      off[e] = bc + ic - c;
+      grp_off[e] = bg + ig - g;
+      out.offsets[e] = bc + ic - c;
+      if (e == experts - 1u) {
+        const uint32_t total = bc + ic, gtotal = bg + ig;
+        off[experts] = total;
+        grp_off[experts] = gtotal;
+        out.offsets[experts] = total;
+        if (out.n_groups) *out.n_groups = gtotal;
+        out.counters[1] = total;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    out.counters[0] = uniq;
+    out.counters[2] = maxc;
+  }
+  // 4. per token: placements, placement lists and the combine order
+  for (uint32_t t = tid; t < tokens; t += kSchedThreads) {
+    const uint4 sa = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u);
+    const uint4 sb = *reinterpret_cast<const uint4 *>(selected + (size_t)t * 8u + 4u);
+    const float4 wa = *reinterpret_cast<const float4 *>(weights + (size_t)t * 8u);
+    const float4 wb = *reinterpret_cast<const float4 *>(weights + (size_t)t * 8u + 4u);
+    uint32_t ex[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+    const float wt[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    const uint32_t wi = t / 32u, below_mask = (1u << (t % 32u)) - 1u;
+    uint32_t pl[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t e = ex[k];
+      pl[k] = off[e] + prefix[e * kSchedSmallWords + wi] + __popc(mask[e * kSchedSmallWords + wi] & below_mask);
+      out.placement_tok[pl[k]] = t;
+      out.placement_w[pl[k]] = wt[k];
+    }
+    // Batcher odd-even merge sort of 8 (experts of a row are distinct)
+    cswap(ex[0], pl[0], ex[1], pl[1]); cswap(ex[2], pl[2], ex[3], pl[3]);
+    cswap(ex[4], pl[4], ex[5], pl[5]); cswap(ex[6], pl[6], ex[7], pl[7]);
+    cswap(ex[0], pl[0], ex[2], pl[2]); cswap(ex[1], pl[1], ex[3], pl[3]);
+    cswap(ex[4], pl[4], ex[6], pl[6]); cswap(ex[5], pl[5], ex[7], pl[7]);
+    cswap(ex[1], pl[1], ex[2], pl[2]); cswap(ex[5], pl[5], ex[6], pl[6]);
+    cswap(ex[0], pl[0], ex[4], pl[4]); cswap(ex[1], pl[1], ex[5], pl[5]);
+    cswap(ex[2], pl[2], ex[6], pl[6]); cswap(ex[3], pl[3], ex[7], pl[7]);
+    cswap(ex[2], pl[2], ex[4], pl[4]); cswap(ex[3], pl[3], ex[5], pl[5]);
+    cswap(ex[1], pl[1], ex[2], pl[2]); cswap(ex[3], pl[3], ex[4], pl[4]);
+    cswap(ex[5], pl[5], ex[6], pl[6]);
+    uint4 *sp = reinterpret_cast<uint4 *>(out.slot_place + (size_t)t * 8u);
+    sp[0] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    sp[1] = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+  }
+  // 5. GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
+  // (skipped when the caller runs the experts elsewhere: no group arrays)
+  for (uint32_t e = tid; e < experts && out.gu_groups; e += kSchedThreads) {
+    const uint32_t c = off[e + 1] - off[e];
+    for (uint32_t j = 0; j * chunk < c; ++j) {
+      GemvGroup g;
+      g.tok_begin = off[e] + chunk * j;
+      g.count = min(chunk, c - chunk * j);
+      g.expert = e;
+      g.pad = 0;
+      g.w0 = bank.gate_w[e];
+      g.s0 = bank.gate_s[e];
+      g.w1 = bank.up_w[e];
+      g.s1 = bank.up_s[e];
+      g.tm0 = bank.gate_tm + e;
+      g.tm1 = bank.up_tm + e;
+      out.gu_groups[grp_off[e] + j] = g;
+      GemvGroup d = g;
+      d.w0 = bank.down_w[e];
+      d.s0 = bank.down_s[e];
+      d.w1 = nullptr;
+      d.s1 = nullptr;
+      d.tm0 = bank.down_tm + e;
+      d.tm1 = nullptr;
+      out.dn_groups[grp_off[e] + j] = d;
+    }
+  }
+}
+
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
                             const BankTable &bank, const ScheduleOut &out, uint32_t *flags, uint32_t chunk,
                             cudaStream_t stream) {
   if (tokens == 0 || tokens > kSchedMaxTokens || experts > kSchedMaxExperts || experts < 8 || chunk == 0 ||
       !out.work)
     return cudaErrorInvalidValue;
+  if (tokens <= kSchedSmallTokens) {
+    const size_t smem = (size_t)experts * kSchedSmallWords * 6 + (size_t)(experts + 1) * 8;
+    return launch_kernel(k_schedule_small, dim3(1), dim3(kSchedThreads), smem, stream, selected, weights, tokens,
+                         experts, bank, out, flags, chunk);
+  }
   const uint32_t words = (tokens + 31u) / 32u;
   cudaError_t e = launch_kernel(k_sched_mask, dim3(words), dim3(256), 0, stream, selected, tokens, experts, out.work);
   if (e != cudaSuccess) return e;

@@ -746,7 +746,8 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
                                      const uint32_t *n_groups_dev, uint32_t slots, uint32_t H, uint32_t I,
                                      const uint8_t *xg, const float *xsg, float *hidden, float *gate_tmp,
                                      float *up_tmp, uint8_t *hc, float *hs, float *down, uint32_t down_round,
-                                     uint64_t units_hint, const uint32_t *slots_dev = nullptr) {
+                                     uint64_t units_hint, const uint32_t *slots_dev = nullptr,
+                                     uint16_t *down16 = nullptr) {
   const int grid_gu = grid_for(rt, units_hint * (I / 128u));
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   if (fused && !rt->silu_lut) {
@@ -797,6 +798,7 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
   D.g.out = down;
   D.g.out_stride = H;
   D.g.round_bf16 = down_round;
+  if (down16 && down_round) D.g.out_bf16 = down16;  // bf16 rows: half the bytes for the combine
   if (!encode_act_maps(D.xmap, hc, slots, I))
     return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the hidden codes");
   ProfScope ps(rt, P_DOWN, 1);
@@ -1046,7 +1048,7 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
         CK(launch_gather_rows(xc, xs, dtok, P, H, xg, xsg, rt->stream));
       }
       s = enqueue_expert_chain_wide(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, P, H, I, xg, xsg, hid, gt, ut, hc, hs,
-                                    down, 1, gu.size());
+                                    down, 1, gu.size(), nullptr, reinterpret_cast<uint16_t *>(down));
     } else {
       s = enqueue_expert_chain(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, P, H, I, dtok, xc, xs, hid, gt, ut, hc, hs,
                                down, 1, gu.size());
@@ -1054,7 +1056,11 @@ int pw_moe_execute(pw_runtime *rt, const float *x, uint32_t rows, const pw_exper
     if (s != PW_OK) return s;
     {
       ProfScope ps(rt, P_COMBINE, 1);
-      CK(launch_combine(down, dslot, dpw, rows, H, dy, rt->d_flags, rt->stream));
+      if (wide)
+        CK(launch_combine_bf16(reinterpret_cast<const uint16_t *>(down), dslot, dpw, rows, H, dy, rt->d_flags,
+                               rt->stream));
+      else
+        CK(launch_combine(down, dslot, dpw, rows, H, dy, rt->d_flags, rt->stream));
     }
     if (call.host() && (s = call.stage_out(y, dy, (size_t)rows * H * 4)) != PW_OK) return s;
   }
@@ -1237,7 +1243,7 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
         CK(launch_gather_rows(xc, xs, so.placement_tok, P, H, xg, xsg, rt->stream));
       }
       s = enqueue_expert_chain_wide(rt, so.gu_groups, so.dn_groups, max_groups, so.n_groups, P, H, I, xg, xsg, hid,
-                                    gt, ut, hc, hs, down, 1, max_groups);
+                                    gt, ut, hc, hs, down, 1, max_groups, nullptr, reinterpret_cast<uint16_t *>(down));
     } else {
       s = enqueue_expert_chain(rt, so.gu_groups, so.dn_groups, max_groups, so.n_groups, P, H, I, so.placement_tok, xc,
                                xs, hid, gt, ut, hc, hs, down, 1, max_groups);
@@ -1245,7 +1251,11 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     if (s != PW_OK) return s;
     {
       ProfScope ps(rt, P_COMBINE, 1);
-      CK(launch_combine(down, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream));
+      if (wide)
+        CK(launch_combine_bf16(reinterpret_cast<const uint16_t *>(down), so.slot_place, so.placement_w, tokens, H, dy,
+                               rt->d_flags, rt->stream));
+      else
+        CK(launch_combine(down, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream));
     }
     if (call.host()) {
       if ((s = call.stage_out(y, dy, (size_t)tokens * H * 4)) != PW_OK) return s;
