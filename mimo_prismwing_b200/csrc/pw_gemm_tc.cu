@@ -118,19 +118,26 @@ __device__ __forceinline__ uint32_t instr_desc(uint32_t n) {
          | ((n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+// One MMA (M=128, N, K=32) issued by one lane elected from the (converged)
+// calling warp; accum = 0 starts a fresh accumulator.
+__device__ __forceinline__ void mma_f8_elect(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(accum), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
 
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
+__device__ __forceinline__ void mma_commit_elect(uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_addr(bar))
+      : "memory");
 }
+
 
 // 32 lanes x 32 consecutive f32 columns (one per register) of the warp's lane quarter.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -294,8 +301,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
           if (!mbar_wait(&sh.full[i], (parity >> i) & 1u)) raise_flag(a.flags, PW_FLAG_WAIT_TIMEOUT);
     }
   } else if (warp == kMmaWarp) {
-    if (lane == 0) {
+    // The whole warp walks the pipeline (every lane waits); one elected lane
+    // issues each MMA and commit.  Descriptors are the ring's base descriptor
+    // plus constant offsets (the start-address field counts 16-byte units).
+    {
       const uint32_t ring = smem_addr(sh.ring);
+      const uint64_t ring_desc = smem_desc_sw128(ring);
       uint32_t slot = 0, phase = 0, acc = 0, aphase = 0;
       uint32_t pending = 0, pend_parity = 0;  // accumulator slots with a commit in flight
       uint32_t n_next = u_begin < u_end ? mma_cols(a.groups[u_begin / tpg].count) : 32u;
@@ -307,8 +318,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
           const uint32_t kc = st % kcs;
           const bool ok_full = bwait(sh, &sh.full[slot], phase, a.flags);
           tc_fence_after();
-          const uint32_t wbase = ring + slot * kStage;
-          const uint32_t xbase = wbase + kWBox;
 #pragma unroll
           for (uint32_t j = 0; j < 2; ++j) {
             if (kc * 2u + j >= kblocks) break;
@@ -316,14 +325,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
             tc_fence_after();
             if (ok_full && ok_acc) {
               const uint32_t d = tmem + acc * (uint32_t)kTN;
+              const uint64_t ad = ring_desc + ((slot * (uint32_t)kStage + (uint32_t)kWBox + j * (n * 128u)) >> 4);
+              const uint64_t bd = ring_desc + ((slot * (uint32_t)kStage + j * (kTileRows * 128u)) >> 4);
 #pragma unroll
-              for (uint32_t s = 0; s < 4; ++s) {
-                const uint64_t ad = smem_desc_sw128(xbase + j * (n * 128u) + s * 32u);
-                const uint64_t bd = smem_desc_sw128(wbase + j * (kTileRows * 128u) + s * 32u);
-                mma_f8(d, ad, bd, idesc, s > 0 ? 1u : 0u);
-              }
+              for (uint32_t s = 0; s < 4; ++s) mma_f8_elect(d, ad + 2u * s, bd + 2u * s, idesc, s > 0 ? 1u : 0u);
             }
-            mma_commit(&sh.tfull[acc]);  // this k-block's sums ready for the epilogue
+            mma_commit_elect(&sh.tfull[acc]);  // this k-block's sums ready for the epilogue
             pending |= 1u << acc;
             pend_parity = (pend_parity & ~(1u << acc)) | (aphase << acc);
             if (++acc == NACC) {
@@ -331,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
               aphase ^= 1u;
             }
           }
-          mma_commit(&sh.empty[slot]);  // stage reusable once these MMAs are done
+          mma_commit_elect(&sh.empty[slot]);  // stage reusable once these MMAs are done
           if (++slot == (uint32_t)kNst) {
             slot = 0;
             phase ^= 1u;
