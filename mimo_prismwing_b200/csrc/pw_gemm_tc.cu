@@ -83,6 +83,17 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+// True on one lane of the converged calling warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(e));
+  return e != 0u;
+}
+
 __device__ __forceinline__ void tensormap_acquire(const CUtensorMap *map) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
 }
@@ -253,7 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   const bool qkv = KIND == 0 && a.layout != PW_LAYOUT_PLAIN;
 
   if (warp == kProducerWarp) {
-    if (lane == 0) {
+    // converged like the MMA warp: every lane waits, one elected lane issues
+    {
       uint32_t slot = 0, phase = 0, issued = 0, parity = 0;
       for (uint32_t u = u_begin; u < u_end; u += u_step) {
         const GemvGroup &g = a.groups[u / tpg];
@@ -275,18 +287,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
           const uint32_t m = st / kcs, kc = st % kcs;
           if (bwait(sh, &sh.empty[slot], phase ^ 1u, a.flags)) {
             uint8_t *dst = sh.ring + slot * kStage;
-            mbar_arrive_expect_tx(&sh.full[slot], bytes);
-            if (!qkv) {
-              tma_load_3d(dst, m == 0 ? m0 : g.tm1, 0, (int)row0, (int)(kc * 2u), &sh.full[slot]);
-            } else {
+            if (elect_one()) {
+              mbar_arrive_expect_tx(&sh.full[slot], bytes);
+              if (!qkv) {
+                tma_load_3d(dst, m == 0 ? m0 : g.tm1, 0, (int)row0, (int)(kc * 2u), &sh.full[slot]);
+              } else {
 #pragma unroll
-              for (uint32_t j = 0; j < 2; ++j) {
-                tma_load_3d(dst + j * (kTileRows * 128u), m0, 0, (int)src0, (int)(kc * 2u + j), &sh.full[slot]);
-                tma_load_3d(dst + j * (kTileRows * 128u) + 64u * 128u, m0, 0, (int)src1, (int)(kc * 2u + j),
-                            &sh.full[slot]);
+                for (uint32_t j = 0; j < 2; ++j) {
+                  tma_load_3d(dst + j * (kTileRows * 128u), m0, 0, (int)src0, (int)(kc * 2u + j), &sh.full[slot]);
+                  tma_load_3d(dst + j * (kTileRows * 128u) + 64u * 128u, m0, 0, (int)src1, (int)(kc * 2u + j),
+                              &sh.full[slot]);
+                }
               }
+              tma_load_3d(dst + kWBox, xm, 0, (int)g.tok_begin, (int)(kc * 2u), &sh.full[slot]);
             }
-            tma_load_3d(dst + kWBox, xm, 0, (int)g.tok_begin, (int)(kc * 2u), &sh.full[slot]);
+            __syncwarp();
             issued |= 1u << slot;
             parity = (parity & ~(1u << slot)) | (phase << slot);
           }
