@@ -554,12 +554,17 @@ __global__ void __launch_bounds__(kSchedThreads) k_sched_scan(uint32_t tokens, u
     return;
   }
   if (tid == 0) *summary = 0u;
-  // per-expert counts, four threads per expert (experts <= 256)
+  // per-expert counts, four threads per expert (experts <= 256), each with
+  // up to 16 mask words held in registers (all loads issued together)
   const uint32_t ex = tid / 4u, q = tid % 4u;
   const uint32_t per = (words + 3u) / 4u, w0 = min(words, q * per), w1 = min(words, w0 + per);
+  uint32_t mw[kSchedWords / 4u];
+#pragma unroll
+  for (uint32_t k = 0; k < kSchedWords / 4u; ++k)
+    mw[k] = ex < experts && w0 + k < w1 ? mask[ex * kSchedWords + w0 + k] : 0u;
   uint32_t local = 0;
-  if (ex < experts)
-    for (uint32_t wi = w0; wi < w1; ++wi) local += __popc(mask[ex * kSchedWords + wi]);
+#pragma unroll
+  for (uint32_t k = 0; k < kSchedWords / 4u; ++k) local += __popc(mw[k]);
   uint32_t incl = local;
 #pragma unroll
   for (uint32_t o = 1; o < 4u; o <<= 1) {
@@ -618,9 +623,10 @@ __global__ void __launch_bounds__(kSchedThreads) k_sched_scan(uint32_t tokens, u
   // placement index of the first token of every (expert, word)
   if (ex < experts) {
     uint32_t run = off[ex] + incl - local;
-    for (uint32_t wi = w0; wi < w1; ++wi) {
-      base[ex * kSchedWords + wi] = run;
-      run += __popc(mask[ex * kSchedWords + wi]);
+#pragma unroll
+    for (uint32_t k = 0; k < kSchedWords / 4u; ++k) {
+      if (w0 + k < w1) base[ex * kSchedWords + w0 + k] = run;
+      run += __popc(mw[k]);
     }
   }
   // GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
