@@ -288,6 +288,17 @@ __global__ void __launch_bounds__(256) k_ep_return(const EpArgs e, const float *
   pdl_launch_dependents();
 }
 
+// ------------------------------------------------------------- release
+// The down GEMM stored the rows into the sources' windows itself (fused
+// return); publish them: a system-scope fence, then flag_ret[rank] = epoch in
+// every window.
+__global__ void k_ep_release(const EpArgs e) {
+  pdl_wait();
+  __threadfence_system();
+  if (threadIdx.x < e.w.G) st_release_sys(win_at<uint32_t>(e, threadIdx.x, e.w.flag_ret) + e.rank, e.epoch);
+  pdl_launch_dependents();
+}
+
 // ------------------------------------------------------------------ wait
 __global__ void k_ep_wait_returns(const EpArgs e) {
   pdl_wait();
@@ -321,6 +332,10 @@ cudaError_t launch_ep_gather(const EpArgs &e, const uint32_t *perm, const uint32
 cudaError_t launch_ep_return(const EpArgs &e, const float *down, const uint32_t *src_rank, const uint32_t *src_place,
                              const uint32_t *p_recv, uint32_t *ctr, int grid, cudaStream_t stream) {
   return launch_kernel(k_ep_return, dim3(grid), dim3(256), 0, stream, e, down, src_rank, src_place, p_recv, ctr);
+}
+
+cudaError_t launch_ep_release(const EpArgs &e, cudaStream_t stream) {
+  return launch_kernel(k_ep_release, dim3(1), dim3(32), 0, stream, e);
 }
 
 cudaError_t launch_ep_wait_returns(const EpArgs &e, cudaStream_t stream) {

@@ -485,9 +485,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
             o[2 * i + 1] = rb ? round_bf16(acc[i].y) : acc[i].y;
             bad |= !finite(o[2 * i]) || !finite(o[2 * i + 1]);
           }
-          if (a.out_bf16) {  // exact: the values are bf16-rounded
-            uint4 *d16 = reinterpret_cast<uint4 *>(a.out_bf16 + (size_t)(grp.tok_begin + t_local) * a.out_stride +
-                                                   row0 + col0);
+          if (a.out_bf16 || a.peer_base) {  // exact: the values are bf16-rounded
+            const size_t p = grp.tok_begin + t_local;
+            uint16_t *row = a.peer_base ? reinterpret_cast<uint16_t *>(a.peer_base[a.row_rank[p]] + a.peer_off) +
+                                              (size_t)a.row_place[p] * a.out_stride
+                                        : a.out_bf16 + p * a.out_stride;
+            uint4 *d16 = reinterpret_cast<uint4 *>(row + row0 + col0);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               const float *oo = o + 8 * i;
@@ -536,6 +539,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     }
   }
 
+  // rows stored into other GPUs' memory are made visible before the release
+  // kernel that follows this one publishes them
+  if (KIND == 0 && a.peer_base) __threadfence_system();
   // free the accumulator columns once every role is done with them
   tc_fence_before();
   __syncthreads();

@@ -79,6 +79,10 @@ struct GemvArgs {
   uint16_t *up_bf16;             //   staged SwiGLU's inputs (k_swiglu_quant finishes it)
   uint16_t *out_bf16;            // tcgen05 kind 0 with round_bf16: the rounded result as bf16 bits
                                  //   [*, out_stride] instead of f32 in out
+  uint8_t *const *peer_base;     // tcgen05 kind 0, expert parallelism: bf16 row p goes to
+  uint64_t peer_off;             //   peer_base[row_rank[p]] + peer_off + row_place[p] * 2 * out_stride
+  const uint32_t *row_rank;      //   (another GPU's window, plain 16-byte stores over NVLink)
+  const uint32_t *row_place;
   uint32_t splits;               // GEMV split-K over the 8-leaf K tree: 1, 2, 4 or 8
   float *split_ws;               //   partial sums [tile][split][mats][128 rows][8 tokens]
   uint32_t *split_cnt;           //   per-tile arrival counters (zero; reset by the last CTA)
@@ -199,6 +203,9 @@ cudaError_t launch_ep_plan(const EpArgs &e, const BankTable &bank, uint32_t chun
                            uint32_t *p_recv, cudaStream_t stream);
 cudaError_t launch_ep_gather(const EpArgs &e, const uint32_t *perm, const uint32_t *p_recv, uint8_t *codes,
                              float *scales, int grid, cudaStream_t stream);
+// After a down GEMM that stored its rows into the peers' windows: make them
+// visible system-wide and release flag_ret[rank] = epoch in every window.
+cudaError_t launch_ep_release(const EpArgs &e, cudaStream_t stream);
 cudaError_t launch_ep_return(const EpArgs &e, const float *down, const uint32_t *src_rank, const uint32_t *src_place,
                              const uint32_t *p_recv, uint32_t *ctr, int grid, cudaStream_t stream);
 cudaError_t launch_ep_wait_returns(const EpArgs &e, cudaStream_t stream);

@@ -742,12 +742,20 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
 
 // The expert chain on the tcgen05 GEMM.  xg / xsg are the gate/up input codes
 // and scales laid out by group (tok_begin indexes rows directly).
+// Expert parallelism: the down projection's bf16 rows go straight to the
+// source ranks' windows (row p -> base[rank[p]] + off + place[p] * 2H).
+struct PeerRows {
+  uint8_t *const *base;
+  uint64_t off;
+  const uint32_t *rank, *place;
+};
+
 static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const GemvGroup *dn, uint32_t n_groups,
                                      const uint32_t *n_groups_dev, uint32_t slots, uint32_t H, uint32_t I,
                                      const uint8_t *xg, const float *xsg, float *hidden, float *gate_tmp,
                                      float *up_tmp, uint8_t *hc, float *hs, float *down, uint32_t down_round,
                                      uint64_t units_hint, const uint32_t *slots_dev = nullptr,
-                                     uint16_t *down16 = nullptr) {
+                                     uint16_t *down16 = nullptr, const PeerRows *peer = nullptr) {
   const int grid_gu = grid_for(rt, units_hint * (I / 128u));
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   if (fused && !rt->silu_lut) {
@@ -799,6 +807,12 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
   D.g.out_stride = H;
   D.g.round_bf16 = down_round;
   if (down16 && down_round) D.g.out_bf16 = down16;  // bf16 rows: half the bytes for the combine
+  if (peer && down_round) {
+    D.g.peer_base = peer->base;
+    D.g.peer_off = peer->off;
+    D.g.row_rank = peer->rank;
+    D.g.row_place = peer->place;
+  }
   if (!encode_act_maps(D.xmap, hc, slots, I))
     return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the hidden codes");
   ProfScope ps(rt, P_DOWN, 1);
@@ -1525,8 +1539,10 @@ int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_
       ProfScope ps(rt, P_QUANT, 1);
       CK(launch_ep_gather(ea, perm, p_recv, xg, xsg, rt->num_sms, rt->stream));
     }
+    // fused return: the down GEMM stores each bf16 row into its source's window
+    const PeerRows pr{ep->d_peers, w.ret_rows, src_rank, src_place};
     s = enqueue_expert_chain_wide(rt, gu, dn, max_groups, n_groups, cap, H, I, xg, xsg, hid, gt, ut, hc, hs, down, 1,
-                                  max_groups, p_recv);
+                                  max_groups, p_recv, nullptr, &pr);
   } else {
     s = enqueue_expert_chain(rt, gu, dn, max_groups, n_groups, cap, H, I, perm,
                              reinterpret_cast<const uint8_t *>(mine + w.recv_codes),
@@ -1536,7 +1552,10 @@ int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_
   if (s != PW_OK) return s;
   {
     ProfScope ps(rt, P_COMBINE, 3);
-    CK(launch_ep_return(ea, down, src_rank, src_place, p_recv, ep->d_ctr + 1, rt->num_sms, rt->stream));
+    if (wide)
+      CK(launch_ep_release(ea, rt->stream));
+    else
+      CK(launch_ep_return(ea, down, src_rank, src_place, p_recv, ep->d_ctr + 1, rt->num_sms, rt->stream));
     CK(launch_ep_wait_returns(ea, rt->stream));
     if (tokens)
       CK(launch_combine_bf16(reinterpret_cast<const uint16_t *>(mine + w.ret_rows), so.slot_place, so.placement_w,
