@@ -1489,6 +1489,7 @@ int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_
   // the tcgen05 GEMM when the layer is wide (judged from this rank's tokens:
   // the owners' row counts are known only on the device)
   const bool wide = (uint64_t)G * tokens >= kWideLayerTokens;
+  const bool fuse_return = wide && G <= 2u;  // see the down projection below
   const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
   const uint32_t max_groups = cap / chunk + L;
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
@@ -1539,10 +1540,14 @@ int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_
       ProfScope ps(rt, P_QUANT, 1);
       CK(launch_ep_gather(ea, perm, p_recv, xg, xsg, rt->num_sms, rt->stream));
     }
-    // fused return: the down GEMM stores each bf16 row into its source's window
+    // fused return (two ranks): the down GEMM stores each bf16 row into its
+    // source's window.  Measured: at 2 GPUs fused beats a separate return
+    // kernel (down + return + combine 308 vs 377 us per layer); at 4 GPUs the
+    // GEMM's stores to three peers slowed it from 133 to 200 us and the
+    // separate kernel wins (212 vs 252 us).
     const PeerRows pr{ep->d_peers, w.ret_rows, src_rank, src_place};
     s = enqueue_expert_chain_wide(rt, gu, dn, max_groups, n_groups, cap, H, I, xg, xsg, hid, gt, ut, hc, hs, down, 1,
-                                  max_groups, p_recv, nullptr, &pr);
+                                  max_groups, p_recv, nullptr, fuse_return ? &pr : nullptr);
   } else {
     s = enqueue_expert_chain(rt, gu, dn, max_groups, n_groups, cap, H, I, perm,
                              reinterpret_cast<const uint8_t *>(mine + w.recv_codes),
@@ -1552,7 +1557,7 @@ int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_
   if (s != PW_OK) return s;
   {
     ProfScope ps(rt, P_COMBINE, 3);
-    if (wide)
+    if (fuse_return)
       CK(launch_ep_release(ea, rt->stream));
     else
       CK(launch_ep_return(ea, down, src_rank, src_place, p_recv, ep->d_ctr + 1, rt->num_sms, rt->stream));
