@@ -54,11 +54,11 @@ PREFILL_TOKENS, STACK_LAYERS, DECODE_TOKENS = 2048, 48, 8
 METRIC = "EP prefill tok/s (2048-token batch through the 48-layer routed-MoE stack)"
 DECODE_METRIC = "routed FP8 MoE layer us @width 8"
 # DRAM traffic / algorithmic bytes of the fused gate/up GEMM, from one ncu
-# capture of a 64-expert, 512-token layer (profiles/k_gemm_tc_fused_prefill_small.md:
-# 1.129 GB read+written for 1.125 GB of algorithmic bytes); traffic grows in
-# proportion to the experts streamed.
+# capture of a 64-expert, 512-token layer (1.129 GB read+written for 1.125 GB
+# of algorithmic bytes); traffic grows in proportion to the experts streamed.
 GATE_UP_GEMM_TRAFFIC_RATIO = (1.094376 + 0.034642) / 1.12486
-GATE_UP_GEMV_TRAFFIC_RATIO = 507.55 / 503.84  # profiles/k_gemv_mma_c2_small.md
+# the same for the fused gate/up GEMV from one capture of the decode layer
+GATE_UP_GEMV_TRAFFIC_RATIO = 507.55 / 503.84
 
 
 def peaks():

@@ -1,9 +1,9 @@
 #!/usr/bin/env python3
 """Regenerate the golden vectors under tests/golden/ from the reference tree.
 
-Run in a container where the x3haloed/mimo-prismwing source is mounted (default
-/root/reference, or --reference PATH).  The GPU box never runs this script: the
-tests read only the JSON files it writes.
+Run where the x3haloed/mimo-prismwing source is checked out (its location is
+the --reference argument).  The GPU box never runs this script: the tests read
+only the JSON files it writes.
 
 Two kinds of golden data come out:
   * copies of the reference's own fixtures for the hot path (the files named in
