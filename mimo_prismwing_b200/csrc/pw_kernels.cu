@@ -923,38 +923,47 @@ __global__ void k_combine(const T *__restrict__ down, const uint32_t *__restrict
     wt[threadIdx.x] = placement_w[pl[threadIdx.x]];
   }
   __syncthreads();
-  for (uint32_t c4 = blockIdx.x * blockDim.x + threadIdx.x; c4 < hidden / 4u; c4 += gridDim.x * blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  // two 4-column groups per thread: all 16 row loads in flight together
+  for (uint32_t c8 = blockIdx.x * blockDim.x + threadIdx.x; c8 < hidden / 8u; c8 += gridDim.x * blockDim.x) {
+    float4 d[2][8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const float4 d = load4(down + (size_t)pl[k] * hidden, c4);
-      acc.x = __fadd_rn(acc.x, __fmul_rn(d.x, wt[k]));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(d.y, wt[k]));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(d.z, wt[k]));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(d.w, wt[k]));
+      d[0][k] = load4(down + (size_t)pl[k] * hidden, 2u * c8);
+      d[1][k] = load4(down + (size_t)pl[k] * hidden, 2u * c8 + 1u);
     }
-    acc.x = round_bf16(acc.x);
-    acc.y = round_bf16(acc.y);
-    acc.z = round_bf16(acc.z);
-    acc.w = round_bf16(acc.w);
-    if (!finite(acc.x) || !finite(acc.y) || !finite(acc.z) || !finite(acc.w))
-      raise_flag(flags, PW_FLAG_NONFINITE_COMBINE);
-    reinterpret_cast<float4 *>(y + (size_t)t * hidden)[c4] = acc;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        acc.x = __fadd_rn(acc.x, __fmul_rn(d[h][k].x, wt[k]));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(d[h][k].y, wt[k]));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(d[h][k].z, wt[k]));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(d[h][k].w, wt[k]));
+      }
+      acc.x = round_bf16(acc.x);
+      acc.y = round_bf16(acc.y);
+      acc.z = round_bf16(acc.z);
+      acc.w = round_bf16(acc.w);
+      if (!finite(acc.x) || !finite(acc.y) || !finite(acc.z) || !finite(acc.w))
+        raise_flag(flags, PW_FLAG_NONFINITE_COMBINE);
+      reinterpret_cast<float4 *>(y + (size_t)t * hidden)[2u * c8 + h] = acc;
+    }
   }
 }
 
 cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const float *placement_w,
                            uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream) {
-  if (hidden % 4u || tokens == 0) return cudaErrorInvalidValue;
-  dim3 grid((hidden / 4u + 255u) / 256u, tokens);
+  if (hidden % 8u || tokens == 0) return cudaErrorInvalidValue;
+  dim3 grid((hidden / 8u + 255u) / 256u, tokens);
   return launch_kernel(k_combine<float>, grid, dim3(256), 0, stream, down, slot_place, placement_w, tokens, hidden,
                        y, flags);
 }
 
 cudaError_t launch_combine_bf16(const uint16_t *down, const uint32_t *slot_place, const float *placement_w,
                                 uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream) {
-  if (hidden % 4u || tokens == 0) return cudaErrorInvalidValue;
-  dim3 grid((hidden / 4u + 255u) / 256u, tokens);
+  if (hidden % 8u || tokens == 0) return cudaErrorInvalidValue;
+  dim3 grid((hidden / 8u + 255u) / 256u, tokens);
   return launch_kernel(k_combine<uint16_t>, grid, dim3(256), 0, stream, down, slot_place, placement_w, tokens,
                        hidden, y, flags);
 }
