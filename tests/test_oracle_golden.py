@@ -322,3 +322,42 @@ def test_schedule_matches_reference_build_schedule():
         assert [int(p) // 8 for p in placements] == entry["positions"]
         assert np.allclose([wts.ravel()[p] for p in placements], entry["weights"], rtol=0, atol=0)
     assert sum(offsets[e + 1] - offsets[e] for e in range(256)) == 128 * 8
+
+
+def _fma_f32(a, b, c):
+    """fmaf: the exact a*b + c rounded once to the nearest f32 (ties to even)."""
+    from fractions import Fraction
+    exact = Fraction(float(a)) * Fraction(float(b)) + Fraction(float(c))
+    if exact == 0:
+        return np.float32(0.0) if (float(a) * float(b) >= 0 and float(c) >= 0) else np.float32(-0.0)
+    near = np.float32(float(exact))  # within one f32 step of the answer
+    best = None
+    for cand in (np.nextafter(near, np.float32(-np.inf)), near, np.nextafter(near, np.float32(np.inf))):
+        err = abs(Fraction(float(cand)) - exact)
+        if best is None or err < best[0] or (err == best[0] and (int(cand.view(np.uint32)) & 1) == 0):
+            best = (err, cand)
+    return np.float32(best[1])
+
+
+def test_router_logits_follow_the_pinned_slice_order():
+    # The pinned router order (the reference's SGEMM order is unspecified):
+    # per 256-column slice a chain of fmaf from +0 over its columns, then the
+    # slice sums added in slice order.  Restated here with exact rational
+    # arithmetic and checked bit for bit against the C oracle (which the GPU
+    # kernels are checked against in turn).
+    rng = np.random.default_rng(11)
+    tokens, experts, hidden = 2, 3, 1024
+    x = (rng.standard_normal((tokens, hidden)) * 3.0).astype(np.float32)
+    w = (rng.standard_normal((experts, hidden)) * 0.05).astype(np.float32)
+    wbits = (w.view(np.uint32) >> 16).astype(np.uint16)
+    wq = (wbits.astype(np.uint32) << 16).view(np.float32)
+    got = O.router_logits(x, wbits)
+    for t in range(tokens):
+        for e in range(experts):
+            logit = None
+            for s in range(hidden // 256):
+                c = np.float32(0.0)
+                for i in range(256 * s, 256 * (s + 1)):
+                    c = _fma_f32(x[t, i], wq[e, i], c)
+                logit = c if logit is None else np.float32(logit + c)
+            assert got[t, e].view(np.uint32) == np.float32(logit).view(np.uint32), (t, e, got[t, e], logit)
