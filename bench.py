@@ -33,8 +33,17 @@ decode     configs[2]: the 8-token decode/verifier layer (us per layer, HBM
 configs    (N = 1) configs[0] readable GEMV, configs[1] one expert at widths
            1/2/4/8, configs[3] fused QKV at widths 1/8/2048: device time per
            call and its HBM / FP8 tensor fraction.
-cpu_baseline  oracle/ (the reference's CPU path restated, f32 order, libm exp,
-           all host threads) on a bounded sample of the same layer.
+parity     before the timed region, layer 0 of the workload on this rank's
+           tokens: routes and route weights bit-exact against the oracle and
+           the output within the layer tolerance on 16 tokens (rank 0); at
+           N > 1 every rank also checks the expert-parallel layer bit for bit
+           against the single-GPU pw_moe_layer on the same tokens with the full
+           256-expert bank ("ep_parity": "ok"); a mismatch exits non-zero.
+cpu_baseline  the reference's own CPU implementation of the layer (its torch
+           helpers, restated in oracle/torch_layer.py: dequantize, dynamic
+           FP8 round trip, f32 SGEMM, staged SwiGLU, index_add_), all host
+           threads, one FULL 2048-token 256-expert layer, x 48 layers; plus
+           the bit-level C oracle (oracle/pw_oracle.c) on a sample of experts.
 """
 from __future__ import annotations
 
@@ -163,38 +172,56 @@ def fp8_peak_tflops(dev) -> float | None:
 
 
 # ------------------------------------------------------------- CPU samples
-_CPU_EXPERTS: dict = {}
+def host_bank(experts):
+    """Host copies of (gate, up, down) WideProjectionBindings for the CPU legs."""
+    return [tuple((p.weight.cpu(), p.scale.cpu()) for p in trio) for trio in experts]
 
 
-def cpu_layer_sample(tokens: int, seed: int, budget_s: float = 20.0):
-    """The reference's routed layer (src/text_endpoint.rs:5290) restated on
-    the CPU (oracle/, f32 reference order, libm exp, all host threads) over
-    `tokens` tokens of a 256-expert layer; returns (seconds per call, threads,
-    repeats, unique experts).  Experts are generated once and cached."""
-    import numpy as np
+def cpu_full_layer(bank, router, x, threads):
+    """One full routed layer through the reference's own CPU formulation
+    (oracle/torch_layer.py: router SGEMM + sigmoid top-8, then per expert
+    dequantize, dynamic FP8 round trip, f32 SGEMMs, staged SwiGLU,
+    index_add_), `threads` host threads.  Returns seconds (router, layer)."""
     import torch
-    from mimo_prismwing_b200 import synth
+    from oracle import torch_layer as TL
+    TL.set_threads(threads)
+    w, bias = router
+    t0 = time.perf_counter()
+    sel, wts = TL.route(x, w, bias)
+    t1 = time.perf_counter()
+    TL.routed_layer(x, sel, wts, bank)
+    t2 = time.perf_counter()
+    del torch
+    return t1 - t0, t2 - t0
+
+
+def cpu_oracle_experts(bank, router, x, n_experts, threads):
+    """The bit-level C oracle (oracle/pw_oracle.c, f32 reference order, libm
+    exp) on the first `n_experts` experts that the layer routes to, each over
+    all its placements of the full batch; returns (seconds per expert,
+    placements per expert)."""
+    import numpy as np
     from oracle import oracle as O
-    threads = os.cpu_count() or 1
+    from oracle import torch_layer as TL
     O.set_threads(threads)
-    w, bias = synth.router(EXPERTS, HIDDEN, 7, "cpu")
-    x = synth.activations(tokens, HIDDEN, seed, "cpu").numpy()
-    logits = O.router_logits(x, w.view(torch.int16).numpy().view(np.uint16))
-    sel, wts, _, _, _ = O.noaux_topk(logits, bias.numpy())
-    needed = sorted(set(sel.ravel().tolist()))
-    for e in needed:
-        if e not in _CPU_EXPERTS:
-            g, u, d = synth.expert(HIDDEN, INTER, 1000 + e, "cpu")
-            _CPU_EXPERTS[e] = tuple(a.numpy() for p in (g, u, d) for a in (p.weight, p.scale))
-    filler = _CPU_EXPERTS[needed[0]]
-    bank = [_CPU_EXPERTS.get(e, filler) for e in range(EXPERTS)]  # the oracle reads only selected experts
-    times = []
-    t_end = time.perf_counter() + budget_s
-    while not times or (time.perf_counter() < t_end and len(times) < 5):
-        t0 = time.perf_counter()
-        O.routed_layer(x, sel, wts, bank, O.ACC_F32, O.EXP_LIBM)
-        times.append(time.perf_counter() - t0)
-    return statistics.mean(times), threads, len(times), len(needed)
+    w, bias = router
+    sel, _ = TL.route(x, w, bias)
+    sel = sel.numpy()
+    xn = x.numpy()
+    experts = sorted(set(sel.ravel().tolist()))[:n_experts]
+    rows = 0
+    t0 = time.perf_counter()
+    for e in experts:
+        pos = np.nonzero((sel == e).any(axis=1))[0]
+        rows += len(pos)
+        (gw, gs), (uw, us), (dw, ds) = (tuple(t.numpy() for t in pair) for pair in bank[e])
+        codes, scales, _ = O.dynamic_fp8(xn[pos])
+        g = O.blockscaled_linear(gw, gs, codes, scales, mode=O.ACC_F32)
+        u = O.blockscaled_linear(uw, us, codes, scales, mode=O.ACC_F32)
+        h = O.staged_swiglu(g, u, O.EXP_LIBM)
+        hc, hs, _ = O.dynamic_fp8(h)
+        O.round_bf16(O.blockscaled_linear(dw, ds, hc, hs, mode=O.ACC_F32))
+    return (time.perf_counter() - t0) / len(experts), rows / len(experts)
 
 
 # ------------------------------------------------- configs[0], [1], [3]
@@ -256,37 +283,131 @@ def bench_configs(rt, dev, hbm, tflops_fp8, iters=20):
 
 # -------------------------------------------------------------- reference
 def run_reference(args, rank):
-    """--impl reference: the reference's CPU path (restated, oracle/) for this
-    arm's metric; rank 0 only.  A step is a bounded sample (16 tokens through
-    one layer); tok/s through the stack = sample tokens / (time x 48)."""
+    """--impl reference: the reference's own CPU implementation of this arm's
+    workload (its torch helpers, restated in oracle/torch_layer.py), all host
+    threads; rank 0 only (the other ranks exit without work).  The 2048-token
+    batch is routed once over 256 experts; a step runs one 32-expert slice of
+    that layer (all placements of experts [32 s, 32 s + 32), s = step mod 8)
+    and ms_per_step is that measured time.  tok/s through the stack = 2048 /
+    (router + 8 x mean slice time) / 48 layers.  32 distinct synthetic experts
+    stand in for every slice's weights (the arithmetic per expert does not
+    depend on the values)."""
     if rank != 0:
         return
-    sample_tokens = 16
+    import torch
+    from mimo_prismwing_b200 import synth
+    from oracle import torch_layer as TL
     threads = os.cpu_count() or 1
-    per_call = []
-    for i in range(max(1, args.warmup // 3) + args.steps):
-        sec, threads, _, uniq = cpu_layer_sample(sample_tokens, 2000 + i, budget_s=0.0)
-        if i >= max(1, args.warmup // 3):
-            per_call.append(sec)
-    sec = statistics.mean(per_call)
-    tok_s = sample_tokens / (sec * STACK_LAYERS)
+    TL.set_threads(threads)
+    slice_experts, slices = 32, EXPERTS // 32
+    base = [tuple((p.weight, p.scale) for p in synth.expert(HIDDEN, INTER, 1000 + e, "cpu"))
+            for e in range(slice_experts)]
+    bank = [base[e % slice_experts] for e in range(EXPERTS)]
+    w, bias = synth.router(EXPERTS, HIDDEN, 7, "cpu")
+    x = synth.activations(PREFILL_TOKENS, HIDDEN, 5000, "cpu")
+    t0 = time.perf_counter()
+    sel, wts = TL.route(x, w, bias)
+    router_s = time.perf_counter() - t0
+    times = []
+    for i in range(args.warmup + args.steps):
+        s_ = i % slices
+        t0 = time.perf_counter()
+        TL.routed_layer(x, sel, wts, bank, experts=range(slice_experts * s_, slice_experts * (s_ + 1)),
+                        finish=False)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    slice_s = statistics.mean(times)
+    layer_s = router_s + slices * slice_s
+    tok_s = PREFILL_TOKENS / (layer_s * STACK_LAYERS)
     line = {
         "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(sec * STACK_LAYERS * 1e3, 1), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": "configs[4] EP prefill, 2048 tokens x 48 layers (CPU: a 16-token sample of one layer "
-                               "per step, scaled to the stack)", "hidden": HIDDEN, "experts": EXPERTS,
-                   "top_k": TOPK},
+        "warmup": args.warmup, "ms_per_step": round(slice_s * 1e3, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32 (fp8 dequantized)", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "configs[4] EP prefill, 2048 tokens x 48 layers, 256 experts (CPU: one 32-expert "
+                               "slice of the full layer per step)", "hidden": HIDDEN, "intermediate": INTER,
+                   "experts": EXPERTS, "top_k": TOPK, "tokens": PREFILL_TOKENS, "layers": STACK_LAYERS},
+        "layer_s": round(layer_s, 3), "router_s": round(router_s, 4),
         "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"{sample_tokens} tokens through one 256-expert layer per step ({uniq} experts); "
-                                   "oracle/pw_oracle.c routed layer, f32 reference order, libm exp; tok/s = "
-                                   "tokens / (seconds x 48 layers)"},
+                         "sample": f"2048 tokens routed over 256 experts once; each step one 32-expert slice "
+                                   f"(all its placements); layer = router + 8 slices = {layer_s:.2f} s; "
+                                   "oracle/torch_layer.py (the reference's torch helpers: dequantize, dynamic FP8, "
+                                   "f32 SGEMM, staged SwiGLU, index_add_); tok/s = 2048 / (layer x 48)"},
         "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------- ours
+def parity_check(rt, layers, x, world, rank, local_rank, dev):
+    """Layer 0 of the workload on this rank's tokens, before anything is
+    timed.  Rank 0: routes and route weights bit-exact against the oracle and
+    the output within the layer tolerance (relative L2 <= 2e-3; elements
+    beyond 2e-3 of max|ref| only as <= 2-ulp bf16 flips on <= 0.5% of them)
+    on 16 of its tokens.  N > 1, every rank: the expert-parallel layer equals,
+    bit for bit, the single-GPU pw_moe_layer over the same tokens with the
+    full 256-expert bank (same seeds as bank 0).  Returns (ok, JSON fields)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from mimo_prismwing_b200 import synth
+    from mimo_prismwing_b200.runtime import WideMoeRuntime
+    from oracle import oracle as O
+    T = x.shape[0]
+    h0, w, bias = layers.layer(0)
+    y = torch.empty_like(x)
+    if world > 1:
+        ex = rt.ep_moe_layer(x, w, bias, h0, want_routes=True, out=y)
+    else:
+        ex = rt.moe_layer(x, w, bias, h0, want_routes=True, out=y)
+    out, ok = {}, True
+    bank = layers.keep[0]
+    if world > 1:
+        bank = [synth.expert(HIDDEN, INTER, 1000 + e, dev) for e in range(EXPERTS)]
+        single = WideMoeRuntime.compile_with_fused_gate_up(local_rank)
+        ref = single.moe_layer(x, w, bias, single.create_bank(bank), want_routes=True)
+        torch.cuda.synchronize()
+        same = bool(torch.equal(ref.output, y) and torch.equal(ref.selected, ex.selected))
+        single.close()
+        flag = torch.tensor([0 if same else 1], device=dev)
+        dist.all_reduce(flag)
+        bad = int(flag.item())
+        out["ep_parity"] = "ok" if bad == 0 else f"mismatch on {bad} rank(s)"
+        ok = bad == 0
+    if rank == 0:
+        take = np.linspace(0, T - 1, 16).astype(np.int64)
+        xn = x.cpu().numpy()[take]
+        logits = O.router_logits(xn, w.view(torch.int16).cpu().numpy().view(np.uint16))
+        osel, owts, _, _, _ = O.noaux_topk(logits, bias.cpu().numpy())
+        gsel = ex.selected.cpu().numpy().astype(np.uint32)[take]
+        gw = ex.weights.cpu().numpy()[take]
+        routes_ok = bool(np.array_equal(gsel, osel) and np.array_equal(gw.view(np.uint32), owts.view(np.uint32)))
+        needed = sorted(set(osel.ravel().tolist()))
+        arrays = {e: tuple(t.cpu().numpy() for p in bank[e] for t in (p.weight, p.scale)) for e in needed}
+        filler = arrays[needed[0]]
+        refo = O.routed_layer(xn, osel, owts, [arrays.get(e, filler) for e in range(EXPERTS)], O.ACC_F64,
+                              O.EXP_SLEEF)
+        g = y.cpu().numpy()[take].astype(np.float64)
+        d = np.abs(g - refo)
+        l2 = float(np.linalg.norm(g - refo) / max(np.linalg.norm(refo), 1e-30))
+        big = d > 2e-3 * np.max(np.abs(refo))
+        a = np.maximum(np.maximum(np.abs(refo), np.abs(g)), 2.0 ** -126)
+        ulps = d / 2.0 ** (np.floor(np.log2(a)) - 7)
+        out_ok = l2 <= 2e-3 and bool(np.all(ulps[big] <= 2 + 1e-9)) and float(np.mean(big)) <= 5e-3
+        out["parity"] = {"vs": "oracle/pw_oracle.c f64 routed layer", "layer": 0, "tokens": 16,
+                         "routes_bit_exact": routes_ok, "rel_l2": float(f"{l2:.3e}"),
+                         "flipped_frac": float(f"{float(np.mean(big)):.2e}"),
+                         "status": "ok" if routes_ok and out_ok else "mismatch"}
+        ok = ok and routes_ok and out_ok
+    del bank
+    torch.cuda.empty_cache()
+    if world > 1:
+        flag = torch.tensor([0 if ok else 1], device=dev)
+        dist.all_reduce(flag)  # also keeps the ranks together while rank 0 runs the oracle
+        ok = int(flag.item()) == 0
+    return ok, out
+
+
 class Layers:
     """The per-rank weights: --banks distinct layer banks of this rank's experts."""
 
@@ -347,6 +468,12 @@ def run_ours(args, rank, world, local_rank):
     T = PREFILL_TOKENS // world
     x = synth.activations(T, HIDDEN, 5000 + rank, dev)
     ys = [torch.empty((T, HIDDEN), device=dev) for _ in range(2)]
+
+    ok, parity = (True, {}) if args.no_parity else parity_check(rt, layers, x, world, rank, local_rank, dev)
+    if not ok:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "error": "parity check failed", **parity}), flush=True)
+        raise SystemExit(3)
 
     def step():
         for i in range(STACK_LAYERS):
@@ -487,11 +614,25 @@ def run_ours(args, rank, world, local_rank):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sec, threads, reps, su = cpu_layer_sample(16, 2000)
-        cpu_tok_s = 16 / (sec * STACK_LAYERS)
+        threads = os.cpu_count() or 1
+        hb = host_bank(layers.keep[0])
+        router_h = tuple(t.cpu() for t in layers.routers[0])
+        xh_cpu = x.cpu()
+        router_s, layer_s = cpu_full_layer(hb, router_h, xh_cpu, threads)
+        per_expert_s, rows_e = cpu_oracle_experts(hb, router_h, xh_cpu, 4, threads)
+        del hb
+        cpu_tok_s = PREFILL_TOKENS / (layer_s * STACK_LAYERS)
         cpu = {"value": round(cpu_tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"16 tokens through one 256-expert layer ({su} experts) x {reps}; oracle/pw_oracle.c "
-                         "routed layer, f32 reference order, libm exp; tok/s = tokens / (seconds x 48 layers)"}
+               "sample": f"one full configs[4] layer (2048 tokens, 256 experts, the bench's bank 0) in "
+                         f"{layer_s:.2f} s (router {router_s:.3f} s), x 48 identical layers; "
+                         "oracle/torch_layer.py = the reference's torch helpers (dequantize, dynamic FP8, f32 "
+                         "SGEMM, staged SwiGLU, index_add_)",
+               "layer_s": round(layer_s, 3),
+               "oracle_c": {"value": round(PREFILL_TOKENS / (per_expert_s * EXPERTS * STACK_LAYERS), 4),
+                            "unit": "tok/s", "cores": threads,
+                            "sample": f"oracle/pw_oracle.c expert path (f32 reference order, libm exp) on 4 of "
+                                      f"the layer's experts, {rows_e:.0f} rows each, {per_expert_s:.2f} s per "
+                                      "expert, x 256 experts x 48 layers"}}
 
     if rank == 0:
         value = PREFILL_TOKENS / (step_ms * 1e-3)
@@ -536,6 +677,7 @@ def run_ours(args, rank, world, local_rank):
                                     "unit": "GB/s", "frac": round(dgu_gbs / hbm, 4) if dgu_gbs else None,
                                     "traffic_ratio": round(GATE_UP_GEMV_TRAFFIC_RATIO, 4)}},
             "configs": configs,
+            **parity,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
@@ -553,6 +695,7 @@ def main():
     ap.add_argument("--banks", type=int, default=4, help="distinct synthetic layer banks the 48 layers cycle through")
     ap.add_argument("--decode-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the start-up parity check (profiling runs)")
     ap.add_argument("--skip-configs", action="store_true", help="skip the configs[0]/[1]/[3] sub-benchmarks")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange: peer-memory stores (default) or NCCL send/recv")

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define PW_ABI_VERSION 1
+#define PW_ABI_VERSION 2
 
 /* ---- status codes (reference: Result<_, String>, src/wide_metal_moe.rs) ---- */
 #define PW_OK 0
@@ -111,13 +111,21 @@ typedef struct pw_expert_binding {
   pw_expert_weights weights;    /* device pointers */
 } pw_expert_binding;
 
+/* Router weight storage (pw_router.weight_dtype).  The reference reads the
+ * checkpoint's model.layers.N.mlp.gate.weight as F32 and runs an f32 linear
+ * (src/text_endpoint.rs:4350-4358, f32_linear :3458-3476): pass that tensor as
+ * PW_ROUTER_F32.  PW_ROUTER_BF16 takes bf16 bits, widened to f32 exactly
+ * (a bf16 copy of the checkpoint's weight is a different router). */
+#define PW_ROUTER_F32 0u
+#define PW_ROUTER_BF16 1u
+
 /* Router (reference: route_mlp src/text_endpoint.rs:4342 with gate.weight
- * [256,4096] and e_score_correction_bias [256]).  The weight is bf16 bits
- * (the reference stores F32; bf16 values widen exactly). Device pointers. */
+ * [256,4096] and e_score_correction_bias [256]).  Device pointers. */
 typedef struct pw_router {
-  const uint16_t *weight_bf16; /* [experts, hidden] */
-  const float *bias;           /* [experts] */
+  const void *weight;    /* [experts, hidden], f32 or bf16 bits per weight_dtype */
+  const float *bias;     /* [experts] f32 */
   uint32_t experts, hidden, top_k;
+  uint32_t weight_dtype; /* PW_ROUTER_F32 or PW_ROUTER_BF16 */
 } pw_router;
 
 /* Per-call accounting (reference: WideMoeExecution / WideLinearExecution,
@@ -203,10 +211,14 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
 
 /* Reference: route_mlp src/text_endpoint.rs:4342 + pytorch_noaux_routes :4394
  * (f32 logits, SLEEF-u10 sigmoid, top-k of score+bias, weights = score /
- * (pairwise sum of the k chosen + 1e-20)).  top_k must be 8.  Logits are
- * accumulated in f64; selected experts are emitted in canonical order
- * (corrected score descending, index ascending).  selected u32 [tokens, 8],
- * weights f32 [tokens, 8]. */
+ * (pairwise sum of the k chosen + 1e-20)).  top_k must be 8.  Logits are f32
+ * in one fixed order: the hidden axis is cut into 256-column slices, each
+ * slice sum is a chain of fused multiply-adds from +0 over its columns in
+ * ascending order, and the logit adds the slice sums in slice order (the
+ * reference's SGEMM order is unspecified; this one is reproducible on CPU and
+ * GPU).  Selected experts are emitted in canonical order (corrected score
+ * descending, index ascending).  selected u32 [tokens, 8], weights f32
+ * [tokens, 8]. */
 int pw_route(pw_runtime *rt, const pw_router *router, const float *x, uint32_t tokens,
              uint32_t *selected, float *weights, uint32_t mem, pw_stats *stats);
 
@@ -311,9 +323,11 @@ int pw_ep_plan(const uint32_t *all_offsets, uint32_t world, uint32_t rank, uint3
  *
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture.  All calls share the one array and it keeps the last
- * call's contents, so calls that overlap on the GPU (different streams or
- * threads at once) race with each other: serialise them. */
+ * any stream capture.  The address is kept until the process exits: do not
+ * call this after cudaDeviceReset.  `cuda_stream` must belong to the current
+ * device (else PW_ERR_ARGUMENT).  All calls share the one array and it keeps
+ * the last call's contents, so calls that overlap on the GPU (different
+ * streams or threads at once) race with each other: serialise them. */
 int pw_expert_forward_static(const pw_expert_weights *w, const float *x, uint32_t width, float *y,
                              void *cuda_stream);
 

@@ -3,7 +3,12 @@
 // Every rank owns a window (one cudaMalloc, mapped into every other rank's
 // process through CUDA IPC; layout in EpWindow).  Per layer, with an epoch
 // number that all ranks advance together:
-//   k_ep_dispatch  stores this rank's per-expert counts and its FP8 rows
+//   k_ep_dispatch  first publishes flag_ready[r] = epoch in every window and
+//                  waits (bounded) until every peer's flag_ready has reached
+//                  this epoch in its own window: a peer that has left never
+//                  publishes it, so no row is ever stored into a departed
+//                  rank's window, and the wait times out instead; then it
+//                  stores this rank's per-expert counts and its FP8 rows
 //                  (codes + per-128 scales, in its expert-major placement
 //                  order) straight into each expert owner's window -- source
 //                  slot r, so no rank needs the others' counts to know where
@@ -67,12 +72,23 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const EpArgs e, const uint3
   const EpWindow &w = e.w;
   const uint32_t G = w.G, L = w.L, r = e.rank;
   __shared__ uint32_t gbeg[9];
-  __shared__ int last;
+  __shared__ int last, ready;
+  // readiness: this rank has finished the previous layer (its receive slots
+  // are free); every peer must say the same before any row goes to it.
+  // Every CTA publishes (the same value), so no CTA's wait depends on another
+  // CTA of this grid being resident.
+  if (threadIdx.x < G) st_release_sys(win_at<uint32_t>(e, threadIdx.x, w.flag_ready) + r, e.epoch);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ready = wait_flags(win_at<uint32_t>(e, r, w.flag_ready), G, e.epoch, e.deadline_ns) ? 1 : 0;
+    if (!ready) raise_flag(e.flags, PW_FLAG_WAIT_TIMEOUT);
+  }
   if (threadIdx.x <= G) gbeg[threadIdx.x] = offsets[threadIdx.x * L];
   __syncthreads();
+  const bool go = ready != 0;
   // the mailbox: this rank's counts for each owner's experts and the
   // placement index of its first row for that owner
-  if (blockIdx.x == 0) {
+  if (blockIdx.x == 0 && go) {
     for (uint32_t i = threadIdx.x; i < G * L + G; i += blockDim.x) {
       if (i < G * L) {
         const uint32_t g = i / L, le = i % L, ex = g * L + le;
@@ -87,7 +103,7 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const EpArgs e, const uint3
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32u, lane = threadIdx.x % 32u;
   const uint32_t nwarps = gridDim.x * blockDim.x / 32u;
   const uint32_t vc = w.H / 16u, vs = w.H / 128u / 4u;  // uint4 per row: codes, scales
-  for (uint32_t i = warp; i < P; i += nwarps) {
+  for (uint32_t i = warp; go && i < P; i += nwarps) {
     uint32_t g = 0;
     while (g + 1u < G && gbeg[g + 1] <= i) ++g;
     const uint64_t dst_row = (uint64_t)r * w.slot_rows + (i - gbeg[g]);
@@ -105,7 +121,7 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const EpArgs e, const uint3
   __syncthreads();
   if (last) {
     __threadfence_system();
-    if (threadIdx.x < G) st_release_sys(win_at<uint32_t>(e, threadIdx.x, w.flag_data) + r, e.epoch);
+    if (go && threadIdx.x < G) st_release_sys(win_at<uint32_t>(e, threadIdx.x, w.flag_data) + r, e.epoch);
     if (threadIdx.x == 0) *ctr = 0u;
   }
   pdl_launch_dependents();

@@ -117,9 +117,10 @@ cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_
 // Router logits (or, from 64 tokens, their per-slice sums) into `scratch`
 // (router_scratch_floats floats), then the sigmoid no-aux top-8.
 size_t router_scratch_floats(uint32_t tokens, uint32_t experts, uint32_t hidden);
-cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, const float *bias, uint32_t experts,
-                          uint32_t hidden, float *scratch, uint32_t *selected, float *weights, uint32_t *tie_rows,
-                          uint32_t *flags, int num_sms, cudaStream_t stream);
+// w: [experts, hidden] router weight, f32 or bf16 bits (w_dtype = PW_ROUTER_*).
+cudaError_t launch_router(const float *x, uint32_t tokens, const void *w, uint32_t w_dtype, const float *bias,
+                          uint32_t experts, uint32_t hidden, float *scratch, uint32_t *selected, float *weights,
+                          uint32_t *tie_rows, uint32_t *flags, int num_sms, cudaStream_t stream);
 
 // Device-side schedule for a routed layer: from selected [tokens, 8] build
 // placements ordered by (expert asc, position asc) and the GEMV groups.
@@ -179,12 +180,13 @@ cudaError_t launch_validate_fp8(const uint8_t *w, uint64_t n, const float *s, ui
                                 unsigned long long *first_bad, uint32_t *flags, cudaStream_t stream);
 
 // Expert-parallel window of one rank (byte offsets from its base): flags
-// written by peers, the mailbox (per-source per-local-expert counts and the
-// source's placement index of its first row for this owner), the receive
+// written by peers (ready for an epoch, data sent, rows returned), the
+// mailbox (per-source per-local-expert counts and the source's placement
+// index of its first row for this owner), the receive
 // slots (source s: rows [s * slot_rows, (s + 1) * slot_rows)) and the
 // returned bf16 rows of this rank's own placements.
 struct EpWindow {
-  uint64_t flag_data, flag_ret, mail_cnt, mail_base, recv_codes, recv_scales, ret_rows, total;
+  uint64_t flag_ready, flag_data, flag_ret, mail_cnt, mail_base, recv_codes, recv_scales, ret_rows, total;
   uint32_t G, L, H, slot_rows;
 };
 

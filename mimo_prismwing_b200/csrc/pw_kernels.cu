@@ -2,6 +2,7 @@
 // quantization, router logits + sigmoid no-aux top-8, the device-side expert
 // schedule, the weighted combine, bf16 rounding and weight validation.
 #include <cstdint>
+#include <type_traits>
 #include <cuda_runtime.h>
 
 #include "pw_device.cuh"
@@ -88,17 +89,24 @@ __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w &
 // slice's activation columns and weight rows in shared memory with coalesced
 // loads; thread (token, expert) then runs its chain from shared memory (the
 // warp shares a token: broadcast reads of x, consecutive experts' weights).
-// The slice sums go to the same partials as the prefill kernel.
+// The slice sums go to the same partials as the prefill kernel.  WT is the
+// router weight's storage type: float (the checkpoint's F32 gate.weight) or
+// uint16_t (bf16 bits, widened exactly); the f32 chain is the same.
 constexpr int kRouterTok = 8;
 constexpr uint32_t kRouterMaxSlices = 64;  // hidden <= 16384
 
+__device__ __forceinline__ float router_w(float v) { return v; }
+__device__ __forceinline__ float router_w(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+
+template <typename WT>
 __global__ void __launch_bounds__(256) k_router_slices_small(const float *__restrict__ x, uint32_t tokens,
-                                                             const uint16_t *__restrict__ w, uint32_t experts,
+                                                             const WT *__restrict__ w, uint32_t experts,
                                                              uint32_t hidden, float *__restrict__ part) {
   pdl_wait();
   pdl_launch_dependents();
+  constexpr uint32_t kPer = 16u / sizeof(WT);  // weight values per 16-byte load
   __shared__ __align__(16) float xs[kRouterTok][kRouterSlice];
-  __shared__ __align__(16) uint16_t ws[kRouterSlice][32];
+  __shared__ __align__(16) WT ws[kRouterSlice][32];
   const uint32_t s = blockIdx.x, e0 = blockIdx.y * 32u, t0 = blockIdx.z * kRouterTok;
   const uint32_t tid = threadIdx.x, col0 = kRouterSlice * s;
   for (uint32_t i = tid; i < (uint32_t)kRouterTok * kRouterSlice / 4u; i += 256u) {
@@ -107,23 +115,19 @@ __global__ void __launch_bounds__(256) k_router_slices_small(const float *__rest
         t0 + j < tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + j) * hidden + col0) + c4)
                         : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  for (uint32_t i = tid; i < 32u * kRouterSlice / 8u; i += 256u) {
-    const uint32_t el = i % 32u, c8 = i / 32u;  // lanes: consecutive experts (conflict-free stores)
-    const uint4 q = e0 + el < experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)(e0 + el) * hidden + col0) + c8)
+  for (uint32_t i = tid; i < 32u * kRouterSlice / kPer; i += 256u) {
+    const uint32_t el = i % 32u, cq = i / 32u;  // lanes: consecutive experts (conflict-free stores)
+    const uint4 q = e0 + el < experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)(e0 + el) * hidden + col0) + cq)
                                       : make_uint4(0u, 0u, 0u, 0u);
-    const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+    const WT *v = reinterpret_cast<const WT *>(&q);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      ws[8u * c8 + 2u * k][el] = (uint16_t)(qq[k] & 0xffffu);
-      ws[8u * c8 + 2u * k + 1u][el] = (uint16_t)(qq[k] >> 16);
-    }
+    for (uint32_t k = 0; k < kPer; ++k) ws[kPer * cq + k][el] = v[k];
   }
   __syncthreads();
   const uint32_t el = tid % 32u, j = tid / 32u;
   float acc = 0.0f;
 #pragma unroll 16
-  for (uint32_t i = 0; i < kRouterSlice; ++i)
-    acc = __fmaf_rn(xs[j][i], __uint_as_float((uint32_t)ws[i][el] << 16), acc);
+  for (uint32_t i = 0; i < kRouterSlice; ++i) acc = __fmaf_rn(xs[j][i], router_w(ws[i][el]), acc);
   if (t0 + j < tokens && e0 + el < experts) part[((size_t)s * tokens + t0 + j) * experts + e0 + el] = acc;
 }
 
@@ -168,13 +172,18 @@ struct RouterCursor {
   __device__ __forceinline__ uint32_t base() const { return kRouterSlice * s + rp::kCols * st; }
 };
 
+// One stage's global loads, fetched a stage ahead: 64 tokens x 32 columns of
+// x and 128 experts x 32 columns of the weight (8 KB as bf16, 16 KB as f32).
+template <bool F32W>
 struct RouterStage {
+  static constexpr int kW = F32W ? 8 : 4;  // 16-byte weight loads per thread
   float4 x[4];
-  uint4 w[4];
+  uint4 w[kW];
 };
 
-__device__ __forceinline__ void router_gload(const float *__restrict__ x, const uint16_t *__restrict__ w,
-                                             const RouterUnits &g, const RouterCursor &c, RouterStage &r) {
+template <bool F32W>
+__device__ __forceinline__ void router_gload(const float *__restrict__ x, const void *__restrict__ wv,
+                                             const RouterUnits &g, const RouterCursor &c, RouterStage<F32W> &r) {
   const uint32_t base = c.base();
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
@@ -182,13 +191,21 @@ __device__ __forceinline__ void router_gload(const float *__restrict__ x, const 
     const uint32_t tok = c.t0 + i % 64u, c4 = i / 64u;  // x: token, 4 columns
     r.x[m] = tok < g.tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)tok * g.hidden + base + 4u * c4))
                             : make_float4(0.f, 0.f, 0.f, 0.f);
-    const uint32_t e = c.e0 + i % 128u, c8 = i / 128u;  // w: expert, 8 columns
-    r.w[m] = e < g.experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)e * g.hidden + base + 8u * c8))
+  }
+  constexpr uint32_t kPer = F32W ? 4u : 8u;  // weight columns per 16-byte load
+  const unsigned char *w = static_cast<const unsigned char *>(wv);
+  const size_t esz = F32W ? 4u : 2u;
+#pragma unroll
+  for (int m = 0; m < RouterStage<F32W>::kW; ++m) {
+    const uint32_t i = threadIdx.x + rp::kThreads * m;
+    const uint32_t e = c.e0 + i % 128u, cq = i / 128u;  // w: expert, kPer columns
+    r.w[m] = e < g.experts ? __ldg(reinterpret_cast<const uint4 *>(w + ((size_t)e * g.hidden + base + kPer * cq) * esz))
                            : make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
-__device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterStage &r) {
+template <bool F32W>
+__device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterStage<F32W> &r) {
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
@@ -197,18 +214,27 @@ __device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterS
     sm.xs[b][4 * c4 + 1][tok] = r.x[m].y;
     sm.xs[b][4 * c4 + 2][tok] = r.x[m].z;
     sm.xs[b][4 * c4 + 3][tok] = r.x[m].w;
-    const uint32_t e = i % 128u, c8 = i / 128u;
+  }
+#pragma unroll
+  for (int m = 0; m < RouterStage<F32W>::kW; ++m) {
+    const uint32_t i = threadIdx.x + rp::kThreads * m;
+    const uint32_t e = i % 128u, cq = i / 128u;
     const uint32_t q[4] = {r.w[m].x, r.w[m].y, r.w[m].z, r.w[m].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      sm.ws[b][8 * c8 + 2 * j][e] = bf16lo(q[j]);
-      sm.ws[b][8 * c8 + 2 * j + 1][e] = bf16hi(q[j]);
+      if (F32W) {
+        sm.ws[b][4 * cq + j][e] = __uint_as_float(q[j]);
+      } else {
+        sm.ws[b][8 * cq + 2 * j][e] = bf16lo(q[j]);
+        sm.ws[b][8 * cq + 2 * j + 1][e] = bf16hi(q[j]);
+      }
     }
   }
 }
 
+template <bool F32W>
 __global__ void __launch_bounds__(rp::kThreads, 2)
-    k_router_partials(const float *__restrict__ x, const uint16_t *__restrict__ w, RouterUnits g,
+    k_router_partials(const float *__restrict__ x, const void *__restrict__ w, RouterUnits g,
                       float *__restrict__ part) {
   pdl_wait();
   pdl_launch_dependents();
@@ -220,7 +246,7 @@ __global__ void __launch_bounds__(rp::kThreads, 2)
   ld.decode(g);
   if (!ld.valid(g)) return;
   RouterCursor cp = ld;
-  RouterStage r;
+  RouterStage<F32W> r;
   router_gload(x, w, g, ld, r);
   ld.next(g);
   router_sstore(sm, 0, r);
@@ -417,31 +443,38 @@ __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ s
   }
 }
 
-cudaError_t launch_router(const float *x, uint32_t tokens, const uint16_t *w, const float *bias, uint32_t experts,
-                          uint32_t hidden, float *scratch, uint32_t *selected, float *weights, uint32_t *tie_rows,
-                          uint32_t *flags, int num_sms, cudaStream_t stream) {
-  if (hidden % 512u || hidden > kRouterSlice * kRouterMaxSlices || tokens == 0 || experts <= 8 || experts > 1024u)
-    return cudaErrorInvalidValue;
-  const RouterUnits g = router_units(tokens, experts, hidden);
-  cudaError_t st;
+template <bool F32W>
+static cudaError_t launch_router_logits(const float *x, uint32_t tokens, const void *w, const RouterUnits &g,
+                                        float *scratch, int num_sms, cudaStream_t stream) {
   if (tokens >= kRouterPartialMinTokens) {
     static bool configured = false;
     if (!configured) {
-      st = cudaFuncSetAttribute(k_router_partials, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(rp::Smem));
+      const cudaError_t st = cudaFuncSetAttribute(k_router_partials<F32W>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(rp::Smem));
       if (st != cudaSuccess) return st;
       configured = true;
     }
     // two 4-warp CTAs per SM: one warp per scheduler left the FMA pipe idle
     // on every short dependency (measured ~50% FMA-pipe activity)
     const uint32_t grid = g.n_units < 2u * (uint32_t)num_sms ? g.n_units : 2u * (uint32_t)num_sms;
-    st = launch_kernel(k_router_partials, dim3(grid), dim3(rp::kThreads), sizeof(rp::Smem), stream, x, w, g,
-                       scratch);
-  } else {
-    st = launch_kernel(k_router_slices_small,
-                       dim3(g.slices, (experts + 31u) / 32u, (tokens + kRouterTok - 1) / kRouterTok), dim3(256), 0,
-                       stream, x, tokens, w, experts, hidden, scratch);
+    return launch_kernel(k_router_partials<F32W>, dim3(grid), dim3(rp::kThreads), sizeof(rp::Smem), stream, x, w, g,
+                         scratch);
   }
+  using WT = typename std::conditional<F32W, float, uint16_t>::type;
+  return launch_kernel(k_router_slices_small<WT>,
+                       dim3(g.slices, (g.experts + 31u) / 32u, (tokens + kRouterTok - 1) / kRouterTok), dim3(256), 0,
+                       stream, x, tokens, static_cast<const WT *>(w), g.experts, g.hidden, scratch);
+}
+
+cudaError_t launch_router(const float *x, uint32_t tokens, const void *w, uint32_t w_dtype, const float *bias,
+                          uint32_t experts, uint32_t hidden, float *scratch, uint32_t *selected, float *weights,
+                          uint32_t *tie_rows, uint32_t *flags, int num_sms, cudaStream_t stream) {
+  if (hidden % 512u || hidden > kRouterSlice * kRouterMaxSlices || tokens == 0 || experts <= 8 || experts > 1024u ||
+      (w_dtype != PW_ROUTER_BF16 && w_dtype != PW_ROUTER_F32))
+    return cudaErrorInvalidValue;
+  const RouterUnits g = router_units(tokens, experts, hidden);
+  cudaError_t st = w_dtype == PW_ROUTER_F32 ? launch_router_logits<true>(x, tokens, w, g, scratch, num_sms, stream)
+                                            : launch_router_logits<false>(x, tokens, w, g, scratch, num_sms, stream);
   if (st != cudaSuccess) return st;
   const dim3 grid((tokens + 7u) / 8u);
   if (experts <= 256u)

@@ -886,8 +886,14 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
 }
 
 // ------------------------------------------------------------------- router
+static uint64_t router_bytes(const pw_router *r) {
+  return (uint64_t)r->experts * r->hidden * (r->weight_dtype == PW_ROUTER_F32 ? 4u : 2u) + r->experts * 4u;
+}
+
 static int check_router(pw_runtime *rt, const pw_router *r) {
-  if (!r || !r->weight_bf16 || !r->bias) return fail(rt, PW_ERR_ARGUMENT, "router descriptor is null");
+  if (!r || !r->weight || !r->bias) return fail(rt, PW_ERR_ARGUMENT, "router descriptor is null");
+  if (r->weight_dtype != PW_ROUTER_F32 && r->weight_dtype != PW_ROUTER_BF16)
+    return fail(rt, PW_ERR_ARGUMENT, "router weight_dtype must be PW_ROUTER_F32 or PW_ROUTER_BF16");
   if (r->top_k != 8) return fail(rt, PW_ERR_UNSUPPORTED, "top_k must be 8");
   if (r->experts <= 8 || r->experts > 256 || r->hidden == 0 || r->hidden % 512u || r->hidden > 16384u)
     return fail(rt, PW_ERR_SHAPE, "router shape mismatch (experts 9..256, hidden a multiple of 512 up to 16384)");
@@ -920,8 +926,8 @@ int pw_route(pw_runtime *rt, const pw_router *router, const float *x, uint32_t t
     CK(cudaMemsetAsync(rt->d_ties, 0, 4, rt->stream));
     {
       ProfScope ps(rt, P_ROUTER, 2);
-      CK(launch_router(dx, tokens, router->weight_bf16, router->bias, E, H, logits, dsel, dw, rt->d_ties,
-                       rt->d_flags, rt->num_sms, rt->stream));
+      CK(launch_router(dx, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, dsel, dw,
+                       rt->d_ties, rt->d_flags, rt->num_sms, rt->stream));
     }
     if (call.host()) {
       if ((s = call.stage_out(selected, dsel, (size_t)tokens * 32)) != PW_OK) return s;
@@ -930,7 +936,7 @@ int pw_route(pw_runtime *rt, const pw_router *router, const float *x, uint32_t t
   }
   uint32_t ties = 0;
   if (stats) CK(cudaMemcpyAsync(&ties, rt->d_ties, 4, cudaMemcpyDeviceToHost, rt->stream));
-  s = call.finish((uint64_t)E * H * 2 + E * 4);
+  s = call.finish(router_bytes(router));
   if (stats) stats->boundary_tie_rows = ties;
   return s;
 }
@@ -1243,8 +1249,8 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     }
     {
       ProfScope ps(rt, P_ROUTER, 2);
-      CK(launch_router(dx, tokens, router->weight_bf16, router->bias, E, H, logits, sel, wts, rt->d_ties,
-                       rt->d_flags, rt->num_sms, rt->stream));
+      CK(launch_router(dx, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, sel, wts,
+                       rt->d_ties, rt->d_flags, rt->num_sms, rt->stream));
     }
     {
       ProfScope ps(rt, P_SCHED, 3);
@@ -1294,7 +1300,7 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     stats->unique_experts = cnt[0];
     stats->expert_rows = cnt[1];
     stats->boundary_tie_rows = ties;
-    stats->weight_bytes = per_expert * cnt[0] + (uint64_t)E * H * 2 + E * 4;
+    stats->weight_bytes = per_expert * cnt[0] + router_bytes(router);
   }
   return s;
 }
@@ -1425,6 +1431,7 @@ int ep_window_setup(pw_runtime *rt, uint32_t L, uint32_t H) {
     off += (bytes + 255u) & ~uint64_t(255);
     return o;
   };
+  w.flag_ready = take(G * 4u);
   w.flag_data = take(G * 4u);
   w.flag_ret = take(G * 4u);
   w.mail_cnt = take((uint64_t)G * L * 4u);
@@ -1742,8 +1749,8 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
     }
     {
       ProfScope ps(rt, P_ROUTER, 2);
-      CK(launch_router(dx, tokens, router->weight_bf16, router->bias, E, H, logits, sel, wts, rt->d_ties,
-                       rt->d_flags, rt->num_sms, rt->stream));
+      CK(launch_router(dx, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, sel, wts,
+                       rt->d_ties, rt->d_flags, rt->num_sms, rt->stream));
     }
     {
       ProfScope ps(rt, P_SCHED, 4);

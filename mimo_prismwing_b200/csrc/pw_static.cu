@@ -58,7 +58,9 @@ std::mutex g_setup_mutex;
 void *g_scratch_ptr[kMaxDevices] = {};
 
 // Device address of g_static_scratch on the current device, looked up once
-// per device (with that device current) and cached.
+// per device (with that device current) and cached for the life of the
+// process.  cudaDeviceReset destroys the context that address belongs to, so
+// the entry point must not be called after a reset.
 cudaError_t scratch_base(int device, unsigned char **out) {
   if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_setup_mutex);
@@ -91,6 +93,10 @@ extern "C" int pw_expert_forward_static(const pw_expert_weights *w, const float 
 
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return PW_ERR_CUDA;
+  // the scratch used is the current device's, so the stream must belong to it
+  int stream_device = device;
+  if (cudaStreamGetDevice(stream, &stream_device) != cudaSuccess) return PW_ERR_CUDA;
+  if (stream_device != device) return PW_ERR_ARGUMENT;
   unsigned char *base = nullptr;
   if (scratch_base(device, &base) != cudaSuccess) return PW_ERR_CUDA;
   uint8_t *xc = base + kOffXCodes;

@@ -34,6 +34,8 @@ MEM_HOST = 1
 MEM_ASYNC = 2
 EP_NCCL_TRANSPORT = 1
 RUNTIME_FUSED_GATE_UP = 1
+ROUTER_F32 = 0
+ROUTER_BF16 = 1
 
 ERRORS = {
     -1: "argument", -2: "shape", -3: "nonfinite", -4: "device_flags", -5: "cuda", -6: "nccl",
@@ -65,8 +67,8 @@ class ExpertBinding(ctypes.Structure):
 
 
 class Router(ctypes.Structure):
-    _fields_ = [("weight_bf16", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("experts", ctypes.c_uint32),
-                ("hidden", ctypes.c_uint32), ("top_k", ctypes.c_uint32)]
+    _fields_ = [("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("experts", ctypes.c_uint32),
+                ("hidden", ctypes.c_uint32), ("top_k", ctypes.c_uint32), ("weight_dtype", ctypes.c_uint32)]
 
 
 class Stats(ctypes.Structure):
@@ -287,13 +289,14 @@ class WideMoeRuntime:
                                               ctypes.c_void_p(out.data_ptr()), mem, ctypes.byref(st)))
         return Execution(out, st.wall_ms, st.device_ms, weight_bytes=st.weight_bytes)
 
-    def route(self, x, router_weight_bf16: torch.Tensor, bias: torch.Tensor):
+    def route(self, x, router_weight: torch.Tensor, bias: torch.Tensor):
         """route_mlp + pytorch_noaux_routes (src/text_endpoint.rs:4342-4470).
 
-        router_weight_bf16: CUDA bf16 [E, H] (or int16/uint16 bits); bias CUDA f32 [E].
+        router_weight: CUDA [E, H], float32 (the checkpoint's F32 gate.weight) or
+        bf16 (or int16 bits); bias CUDA f32 [E].
         Returns (selected int64 [T, 8], weights f32 [T, 8], stats dict)."""
         x = _as_f32(x)
-        r = self._router(router_weight_bf16, bias)
+        r = self._router(router_weight, bias)
         mem = MEM_DEVICE if x.is_cuda else MEM_HOST
         sel = torch.empty((x.shape[0], 8), dtype=torch.int32, device=x.device)
         wts = torch.empty((x.shape[0], 8), dtype=torch.float32, device=x.device)
@@ -305,9 +308,18 @@ class WideMoeRuntime:
 
     @staticmethod
     def _router(w: torch.Tensor, bias: torch.Tensor) -> Router:
-        if not (w.is_cuda and bias.is_cuda and w.element_size() == 2 and bias.dtype == torch.float32):
-            raise PrismwingError(-1, "router weight must be CUDA bf16 bits and bias CUDA float32")
-        return Router(w.data_ptr(), bias.data_ptr(), w.shape[0], w.shape[1], 8)
+        """pw_router for a CUDA float32 (PW_ROUTER_F32) or bf16/int16 (PW_ROUTER_BF16) weight."""
+        if w.dtype == torch.float32:
+            dtype = ROUTER_F32
+        elif w.dtype in (torch.bfloat16, torch.int16):
+            dtype = ROUTER_BF16
+        else:
+            raise PrismwingError(-1, f"router weight must be float32 or bf16, not {w.dtype}")
+        if not (w.is_cuda and bias.is_cuda and bias.dtype == torch.float32):
+            raise PrismwingError(-1, "router weight and bias must be CUDA tensors, bias float32")
+        if not (w.is_contiguous() and bias.is_contiguous()):
+            raise PrismwingError(-1, "router tensors must be contiguous")
+        return Router(w.data_ptr(), bias.data_ptr(), w.shape[0], w.shape[1], 8, dtype)
 
     # ------------------------------------------------------------ layers
     def execute(self, x, experts: Sequence[WideExpertBinding]) -> Execution:
@@ -370,14 +382,14 @@ class WideMoeRuntime:
         self._check(self._L.pw_ep_init(self._rt, rank, world, buf, len(uid), timeout_ms, max_tokens, hidden,
                                        local_experts, EP_NCCL_TRANSPORT if nccl_transport else 0))
 
-    def ep_moe_layer(self, x, router_weight_bf16: torch.Tensor, bias: torch.Tensor, bank,
+    def ep_moe_layer(self, x, router_weight: torch.Tensor, bias: torch.Tensor, bank,
                      want_routes: bool = False, stats: bool = True, asynchronous: bool = False,
                      out: Optional[torch.Tensor] = None) -> Execution:
         """Collective routed layer over this rank's tokens; `bank` holds this
         rank's experts (rank g: experts [g n, (g + 1) n))."""
         x = _as_f32(x)
         T, H = x.shape
-        r = self._router(router_weight_bf16, bias)
+        r = self._router(router_weight, bias)
         mem = MEM_DEVICE if x.is_cuda else MEM_HOST
         if asynchronous:
             if not x.is_cuda:
@@ -398,13 +410,13 @@ class WideMoeRuntime:
         return Execution(out, st.wall_ms, st.device_ms, st.unique_experts, st.expert_rows, st.boundary_tie_rows,
                          st.weight_bytes, sel, wts)
 
-    def moe_layer(self, x, router_weight_bf16: torch.Tensor, bias: torch.Tensor, bank,
+    def moe_layer(self, x, router_weight: torch.Tensor, bias: torch.Tensor, bank,
                   want_routes: bool = False, stats: bool = True, asynchronous: bool = False,
                   out: Optional[torch.Tensor] = None) -> Execution:
         """routed_mlp_metal_wide_configured (src/text_endpoint.rs:4750) fully on the device."""
         x = _as_f32(x)
         T, H = x.shape
-        r = self._router(router_weight_bf16, bias)
+        r = self._router(router_weight, bias)
         mem = MEM_DEVICE if x.is_cuda else MEM_HOST
         if asynchronous:
             if not x.is_cuda:

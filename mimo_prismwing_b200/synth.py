@@ -80,7 +80,24 @@ def expert(hidden: int, inter: int, seed: int, device="cuda"):
 
 
 def router(experts: int, hidden: int, seed: int, device="cuda"):
+    """bf16 router weight N(0, 0.02) and f32 bias N(0, 0.01)."""
     g = _gen(device, seed)
     w = (torch.randn((experts, hidden), generator=g, device=device) * 0.02).to(torch.bfloat16).contiguous()
     bias = (torch.randn((experts,), generator=g, device=device) * 0.01).float().contiguous()
     return w, bias
+
+
+def router_f32(experts: int, hidden: int, seed: int, device="cuda"):
+    """F32 router weight N(0, 0.02), as the checkpoint stores gate.weight
+    (most values carry mantissa bits that bf16 cannot hold), and f32 bias."""
+    g = _gen(device, seed)
+    w = (torch.randn((experts, hidden), generator=g, device=device) * 0.02).float().contiguous()
+    bias = (torch.randn((experts,), generator=g, device=device) * 0.01).float().contiguous()
+    return w, bias
+
+
+def to_device(obj, device):
+    """Copy a WideProjectionBinding, or a tuple/list of them, to `device`."""
+    if isinstance(obj, WideProjectionBinding):
+        return WideProjectionBinding(obj.weight.to(device).contiguous(), obj.scale.to(device).contiguous())
+    return type(obj)(to_device(o, device) for o in obj)

@@ -30,11 +30,28 @@ EXP_LIBM = 1
 _lib = None
 
 
+def reference_root() -> str | None:
+    """Where the reference source tree is checked out, if anywhere: the
+    PW_REFERENCE_ROOT environment variable, else BASELINE.json's
+    "reference_path" at the repository root.  None when neither names an
+    existing tree (the GPU box has no reference tree)."""
+    root = os.environ.get("PW_REFERENCE_ROOT")
+    if not root:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                root = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            root = None
+    return root if root and os.path.isdir(os.path.join(root, "src")) else None
+
+
 def build() -> None:
     """Compile libpw_oracle.so (and the reference top-k bridge when the reference is present)."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if os.path.isdir("/root/reference/src"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    ref = reference_root()
+    if ref:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
 
 
 def lib() -> ctypes.CDLL:
@@ -77,6 +94,7 @@ def _bind(L: ctypes.CDLL) -> None:
     L.pwo_staged_swiglu.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_int]
     L.pwo_staged_swiglu.restype = ctypes.c_float
     L.pwo_router_logits.argtypes = [f32p, sz, u16p, sz, sz, f32p]
+    L.pwo_router_logits_f32.argtypes = [f32p, sz, f32p, sz, sz, f32p]
     L.pwo_noaux_topk.argtypes = [f32p, f32p, sz, sz, sz, u32p, f32p, f32p, f32p]
     L.pwo_routed_layer.argtypes = [f32p, sz, sz, sz, u32p, f32p, sz, _p(ctypes.c_void_p),
                                    ctypes.c_int, ctypes.c_int, f32p, f32p, f32p]
@@ -262,16 +280,25 @@ def swa_qkv_source_row(r: int) -> int:
     return v
 
 
-def router_logits(x: np.ndarray, weight_bf16_bits: np.ndarray) -> np.ndarray:
-    """Router logits, f32 fused-multiply-add chains over 256-column slices, added in slice order
-    (the pinned order; see pw_oracle.c)."""
+def router_logits(x: np.ndarray, weight: np.ndarray) -> np.ndarray:
+    """Router logits (src/text_endpoint.rs:4350-4358 route_mlp's f32 linear): f32
+    fused-multiply-add chains over 256-column slices, added in slice order (the
+    pinned order; see pw_oracle.c).  `weight` is the F32 gate.weight (float32)
+    or bf16 bits (uint16)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    w = np.ascontiguousarray(weight_bf16_bits, dtype=np.uint16)
     tokens, hidden = x.shape
-    experts = w.shape[0]
+    experts = weight.shape[0]
     out = np.empty((tokens, experts), np.float32)
-    rc = lib().pwo_router_logits(_ptr(x, ctypes.c_float), tokens, _ptr(w, ctypes.c_uint16), experts, hidden,
-                                 _ptr(out, ctypes.c_float))
+    if weight.dtype == np.float32:
+        w = np.ascontiguousarray(weight)
+        rc = lib().pwo_router_logits_f32(_ptr(x, ctypes.c_float), tokens, _ptr(w, ctypes.c_float), experts, hidden,
+                                         _ptr(out, ctypes.c_float))
+    elif weight.dtype in (np.uint16, np.int16):
+        w = np.ascontiguousarray(weight).view(np.uint16)
+        rc = lib().pwo_router_logits(_ptr(x, ctypes.c_float), tokens, _ptr(w, ctypes.c_uint16), experts, hidden,
+                                     _ptr(out, ctypes.c_float))
+    else:
+        raise TypeError(f"router weight must be float32 or bf16 bits (uint16), not {weight.dtype}")
     if rc != 0:
         raise ValueError("router logits shape mismatch")
     return out

@@ -445,28 +445,41 @@ float pwo_staged_swiglu(float gate, float up, int exp_kind) {
 /*   of fused multiply-adds in f32 (fmaf: one rounding per step) from   */
 /*   +0 over its columns in ascending order; the logit is the slice    */
 /*   sums added in slice order starting from slice 0's.  The weight is  */
-/*   bf16 bits (exact in f32).                                          */
+/*   the checkpoint's F32 gate.weight (src/text_endpoint.rs:4350-4358)  */
+/*   or bf16 bits (exact in f32); the chain is the same for both.       */
 /* ------------------------------------------------------------------ */
 static inline float bf16_bits_to_f32(uint16_t b) { return u2f((uint32_t)b << 16); }
 
-int pwo_router_logits(const float *x, size_t tokens, const uint16_t *weight_bf16, size_t experts,
-                      size_t hidden, float *logits) {
+static int router_logits_any(const float *x, size_t tokens, const float *w32, const uint16_t *w16,
+                             size_t experts, size_t hidden, float *logits) {
   if (hidden % 512 != 0) return -1;
   const size_t slices = hidden / 256;
 #pragma omp parallel for schedule(static)
   for (size_t te = 0; te < tokens * experts; ++te) {
     const size_t t = te / experts, e = te % experts;
     const float *xr = x + t * hidden;
-    const uint16_t *wr = weight_bf16 + e * hidden;
     float logit = 0.0f;
     for (size_t s = 0; s < slices; ++s) {
       float c = 0.0f;
-      for (size_t i = 256 * s; i < 256 * (s + 1); ++i) c = fmaf(xr[i], bf16_bits_to_f32(wr[i]), c);
+      for (size_t i = 256 * s; i < 256 * (s + 1); ++i) {
+        const float wv = w32 ? w32[e * hidden + i] : bf16_bits_to_f32(w16[e * hidden + i]);
+        c = fmaf(xr[i], wv, c);
+      }
       logit = s == 0 ? c : logit + c;
     }
     logits[t * experts + e] = logit;
   }
   return 0;
+}
+
+int pwo_router_logits(const float *x, size_t tokens, const uint16_t *weight_bf16, size_t experts,
+                      size_t hidden, float *logits) {
+  return router_logits_any(x, tokens, NULL, weight_bf16, experts, hidden, logits);
+}
+
+int pwo_router_logits_f32(const float *x, size_t tokens, const float *weight, size_t experts, size_t hidden,
+                          float *logits) {
+  return router_logits_any(x, tokens, weight, NULL, experts, hidden, logits);
 }
 
 /* ------------------------------------------------------------------ */

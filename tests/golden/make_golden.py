@@ -110,7 +110,9 @@ def torch_expert_goldens(reference: str) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    env = os.environ.get("PW_REFERENCE_ROOT")
+    ap.add_argument("--reference", default=env, required=not env,
+                    help="the reference source tree (default: $PW_REFERENCE_ROOT)")
     args = ap.parse_args()
     copy_fixtures(args.reference)
     torch_expert_goldens(args.reference)

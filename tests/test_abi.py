@@ -31,7 +31,20 @@ def test_library_exports_every_declared_symbol():
 def test_library_loads_and_reports_abi_version():
     import mimo_prismwing_b200 as m
     L = m.load()
-    assert L.pw_abi_version() == 1
+    assert L.pw_abi_version() == 2
+
+
+def test_router_descriptor_layout_matches_header():
+    # pw_router {const void *weight; const float *bias; uint32_t experts, hidden,
+    # top_k, weight_dtype;} and the dtype codes of include/pw_cuda.h
+    import re
+    from mimo_prismwing_b200 import _lib
+    from mimo_prismwing_b200.runtime import ROUTER_BF16, ROUTER_F32, Router
+    assert [f[0] for f in Router._fields_] == ["weight", "bias", "experts", "hidden", "top_k", "weight_dtype"]
+    assert ctypes.sizeof(Router) == 32
+    text = open(_lib.HEADER).read()
+    assert int(re.search(r"#define PW_ROUTER_F32 (\d+)u", text).group(1)) == ROUTER_F32
+    assert int(re.search(r"#define PW_ROUTER_BF16 (\d+)u", text).group(1)) == ROUTER_BF16
 
 
 def test_null_and_no_device_paths_fail_cleanly():

@@ -1,7 +1,7 @@
 """GPU parity: the CUDA path through the C ABI against the CPU oracle.
 
 Bit-exact: e4m3 dequantization, dynamic FP8 activation codes and scales,
-router logits (pinned f64 order), selected expert sets, route weights, the
+router logits (pinned f32 slice order), selected expert sets, route weights, the
 staged SwiGLU and the weighted combine.  Within relative 2e-3 (norm-wise and
 max|d|/max|ref|) of the f64-accumulated oracle: every projection and layer.
 """
@@ -106,6 +106,61 @@ def test_mapped_fp8_gemv_selects_row_and_column_scale_blocks(rt):
     s = torch.tensor([[1.0, 2.0], [3.0, 4.0]], device="cuda")
     y = H(rt.fp8_gemv(torch.ones(256, device="cuda"), WideProjectionBinding(w, s)).output)[0]
     assert np.all(y[:128] == 384.0) and np.all(y[128:] == 896.0)
+
+
+def _all_bytes_block():
+    """A 128x256 e4m3 block holding every non-NaN byte: W[r, 0] = r and
+    W[r, 1] = 128 + r (0x7f and 0xff, the NaNs, left as 0x00), scale 1."""
+    w = np.zeros((128, 256), np.uint8)
+    w[:, 0] = np.arange(128)
+    w[:, 1] = np.arange(128, 256)
+    w[0x7F, 0] = 0
+    w[0x7F, 1] = 0
+    return w, np.ones((1, 2), np.float32)
+
+
+def test_dequant_all_bytes_bit_exact_on_gpu(rt):
+    # src/lib.rs:8012 every_fp8_encoding_matches_oracle, on the GPU: one-hot
+    # inputs make y[t, r] = dec(W[r, c_t]) * 1 * 1 exactly, so the readable
+    # GEMV's output is the dequantized byte.  Sums start from +0, so the byte
+    # 0x80 (-0.0) reads back as +0.0, as in the reference's own projection.
+    from mimo_prismwing_b200.runtime import WideProjectionBinding
+    with open(os.path.join(GOLDEN, "f8_e4m3fn_all_bytes.json")) as f:
+        expected = np.asarray(json.load(f)["expected_f32_bits"], dtype=np.uint32)
+    assert len(expected) == 256
+    w, s = _all_bytes_block()
+    b = WideProjectionBinding(torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda())
+    x = torch.zeros((2, 256), device="cuda")
+    x[0, 0] = 1.0
+    x[1, 1] = 1.0
+    y = H(rt.fp8_gemv(x, b).output).view(np.uint32)  # [2, 128]
+    got = np.concatenate([y[0], y[1]])                  # byte b at index b
+    for byte in range(256):
+        if byte in (0x7F, 0xFF):
+            continue
+        want = expected[byte] if byte != 0x80 else np.uint32(0)
+        assert got[byte] == want, f"byte {byte:#04x}: {got[byte]:#010x} != {want:#010x}"
+
+
+@pytest.mark.parametrize("width", [2, 8, 32])
+def test_dequant_all_bytes_through_fp8_mma(rt, width):
+    # The block-scaled path feeds the e4m3 bytes to the tensor cores (the
+    # warp-level MMA at widths <= 8, tcgen05 from 32).  With one-hot tokens
+    # each output is a single product dec(W) * dec(code) * S * xs, rounded
+    # once: bit-exact against the oracle's equation.
+    from mimo_prismwing_b200.runtime import WideProjectionBinding
+    w, s = _all_bytes_block()
+    b = WideProjectionBinding(torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda())
+    x = np.zeros((width, 256), np.float32)
+    for t in range(width):
+        x[t, t % 2 if t < 2 else (t * 37) % 256] = 1.0 if t % 3 else -2.0
+    y = H(rt.execute_fp8_linear(torch.from_numpy(x).cuda(), b, f32_output=True).output)
+    codes, scales, _ = O.dynamic_fp8(x)
+    ref = O.blockscaled_linear(w, s, codes, scales, mode=O.ACC_F32)
+    # (+0 canonicalises signed zeros on both sides: a sum from +0 of -0 terms)
+    assert np.array_equal((y + np.float32(0)).view(np.uint32), (ref + np.float32(0)).view(np.uint32))
+    dec = O.decode_table()
+    assert np.array_equal(y[0] != 0, dec[w[:, 0]] != 0) and np.array_equal(y[1] != 0, dec[w[:, 1]] != 0)
 
 
 @pytest.mark.parametrize("width", [1, 2, 3, 5, 8])
@@ -245,6 +300,59 @@ def test_route_bit_exact_vs_oracle(rt, tokens):
     assert np.array_equal(H(sel).astype(np.uint32), osel)
     assert np.array_equal(H(wts).view(np.uint32), owts.view(np.uint32))
     assert st["boundary_tie_rows"] == ties
+
+
+@pytest.mark.parametrize("tokens", [1, 8, 128])
+def test_route_f32_weights_bit_exact_vs_oracle(rt, tokens):
+    # The checkpoint's gate.weight is F32 (src/text_endpoint.rs:4350-4358,
+    # f32_linear :3458): routed as F32, not through a bf16 copy.
+    from mimo_prismwing_b200 import synth
+    w, bias = synth.router_f32(256, 4096, 15, "cuda")
+    wn = H(w)
+    assert np.mean((wn.view(np.uint32) & 0xFFFF) != 0) > 0.99  # bits bf16 cannot hold
+    x = synth.activations(tokens, 4096, 510 + tokens, "cuda")
+    sel, wts, st = rt.route(x, w, bias)
+    logits = O.router_logits(H(x), wn)
+    osel, owts, _, _, ties = O.noaux_topk(logits, H(bias))
+    assert np.array_equal(H(sel).astype(np.uint32), osel)
+    assert np.array_equal(H(wts).view(np.uint32), owts.view(np.uint32))
+    assert st["boundary_tie_rows"] == ties
+    # a bf16 copy of the same weights is a different router
+    wb = H(w.to(torch.bfloat16).view(torch.int16)).view(np.uint16)
+    assert not np.array_equal(O.router_logits(H(x), wb), logits)
+
+
+def test_moe_layer_f32_router_vs_oracle(rt):
+    from gpu_helpers import assert_close_bf16, bank_arrays
+    from mimo_prismwing_b200 import synth
+    E, Hd, I, T = 64, 1024, 512, 8
+    bank = _small_bank(E, Hd, I, 19)
+    handle = rt.create_bank(bank)
+    w, bias = synth.router_f32(E, Hd, 20, "cuda")
+    x = synth.activations(T, Hd, 21, "cuda")
+    ex = rt.moe_layer(x, w, bias, handle, want_routes=True)
+    osel, owts, _, _, _ = O.noaux_topk(O.router_logits(H(x), H(w)), H(bias))
+    assert np.array_equal(H(ex.selected).astype(np.uint32), osel)
+    assert np.array_equal(H(ex.weights).view(np.uint32), owts.view(np.uint32))
+    ref = O.routed_layer(H(x), osel, owts, bank_arrays(bank), O.ACC_F64, O.EXP_SLEEF)
+    assert_close_bf16(H(ex.output), ref, what="moe layer f32 router")
+
+
+def test_route_rejects_bad_weight_dtype(rt):
+    import ctypes
+    from mimo_prismwing_b200 import synth
+    from mimo_prismwing_b200.runtime import PrismwingError
+    w, bias = synth.router_f32(16, 512, 22, "cuda")
+    r = rt._router(w, bias)
+    r.weight_dtype = 7
+    x = torch.zeros((1, 512), device="cuda")
+    sel = torch.empty((1, 8), dtype=torch.int32, device="cuda")
+    wts = torch.empty((1, 8), device="cuda")
+    st = rt._L.pw_route(rt._rt, ctypes.byref(r), ctypes.c_void_p(x.data_ptr()), 1, ctypes.c_void_p(sel.data_ptr()),
+                        ctypes.c_void_p(wts.data_ptr()), 0, None)
+    assert st == -1 and "weight_dtype" in rt.last_error()
+    with pytest.raises(PrismwingError):
+        rt.route(x, w.half(), bias)
 
 
 def test_route_host_io_matches_device_io(rt):

@@ -121,16 +121,53 @@ def test_wide_moe_layer_device_router_vs_oracle(rt, tokens):
     assert ex.expert_rows == tokens * 8
 
 
-@pytest.mark.parametrize("experts,hidden,tokens", [(256, 4096, 64), (256, 4096, 67), (100, 1024, 70),
-                                                   (256, 4096, 2048)])
-def test_wide_route_bit_exact_vs_oracle(rt, experts, hidden, tokens):
-    # >= 64 tokens take the tiled router (4 tokens x 8 experts per CTA);
-    # ragged token and expert tiles included
+def test_full_size_prefill_layer_vs_oracle(rt):
+    # The benchmarked layer itself (one layer): 2048
+    # tokens, 256 experts of [2048x4096] gate/up and [4096x2048] down, device
+    # router (src/text_endpoint.rs:5076-5103 gate the reference's layer-major
+    # slices the same way).  Routes and route weights are compared bit for bit
+    # on every token; the output against the f64 oracle on every 16th token
+    # (each token's output depends only on its own row and routes).
+    from gpu_helpers import assert_close_bf16
     from mimo_prismwing_b200 import synth
-    w, bias = synth.router(experts, hidden, 51, "cuda")
+    E, Hd, I, T = 256, 4096, 2048, 2048
+    bank = [synth.expert(Hd, I, 9000 + e, "cuda") for e in range(E)]
+    handle = rt.create_bank(bank)
+    w, bias = synth.router(E, Hd, 77, "cuda")
+    x = synth.activations(T, Hd, 78, "cuda")
+    ex = rt.moe_layer(x, w, bias, handle, want_routes=True)
+    logits = O.router_logits(H(x), H(w.view(torch.int16)).view(np.uint16))
+    osel, owts, _, _, _ = O.noaux_topk(logits, H(bias))
+    assert np.array_equal(H(ex.selected).astype(np.uint32), osel)
+    assert np.array_equal(H(ex.weights).view(np.uint32), owts.view(np.uint32))
+    assert ex.expert_rows == T * 8 and ex.unique_experts == E
+    take = np.arange(0, T, 16)
+    needed = sorted(set(osel[take].ravel().tolist()))
+    arrays = {e: tuple(H(t) for p in bank[e] for t in (p.weight, p.scale)) for e in needed}
+    filler = arrays[needed[0]]
+    oracle_bank = [arrays.get(e, filler) for e in range(E)]  # the oracle reads only selected experts
+    ref = O.routed_layer(H(x)[take], osel[take], owts[take], oracle_bank, O.ACC_F64, O.EXP_SLEEF)
+    assert_close_bf16(H(ex.output)[take], ref, what="configs[4] layer (every 16th token)")
+    # the asynchronous device call gives the same bits
+    out = torch.empty_like(x)
+    rt.moe_layer(x, w, bias, handle, asynchronous=True, out=out)
+    rt.synchronize()
+    assert torch.equal(out, ex.output)
+
+
+@pytest.mark.parametrize("experts,hidden,tokens,dtype", [(256, 4096, 64, "bf16"), (256, 4096, 67, "bf16"),
+                                                         (100, 1024, 70, "bf16"), (256, 4096, 2048, "bf16"),
+                                                         (256, 4096, 67, "f32"), (256, 4096, 2048, "f32")])
+def test_wide_route_bit_exact_vs_oracle(rt, experts, hidden, tokens, dtype):
+    # >= 64 tokens take the register-tiled router (64 tokens x 128 experts x
+    # one 256-column slice per unit); ragged token and expert tiles included;
+    # F32 weights are the checkpoint's gate.weight (src/text_endpoint.rs:4350)
+    from mimo_prismwing_b200 import synth
+    make = synth.router_f32 if dtype == "f32" else synth.router
+    w, bias = make(experts, hidden, 51, "cuda")
     x = synth.activations(tokens, hidden, 700 + tokens, "cuda")
     sel, wts, st = rt.route(x, w, bias)
-    logits = O.router_logits(H(x), H(w.view(torch.int16)).view(np.uint16))
+    logits = O.router_logits(H(x), H(w) if dtype == "f32" else H(w.view(torch.int16)).view(np.uint16))
     osel, owts, _, _, ties = O.noaux_topk(logits, H(bias))
     assert np.array_equal(H(sel).astype(np.uint32), osel)
     assert np.array_equal(H(wts).view(np.uint32), owts.view(np.uint32))

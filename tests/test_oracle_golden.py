@@ -361,3 +361,28 @@ def test_router_logits_follow_the_pinned_slice_order():
                     c = _fma_f32(x[t, i], wq[e, i], c)
                 logit = c if logit is None else np.float32(logit + c)
             assert got[t, e].view(np.uint32) == np.float32(logit).view(np.uint32), (t, e, got[t, e], logit)
+
+
+def test_router_logits_f32_weights_follow_the_pinned_slice_order():
+    # The same order over the checkpoint's F32 gate.weight (src/text_endpoint.rs:4350-4358):
+    # full f32 weights, mantissa bits below bf16's included.
+    rng = np.random.default_rng(12)
+    tokens, experts, hidden = 2, 2, 512
+    x = (rng.standard_normal((tokens, hidden)) * 3.0).astype(np.float32)
+    w = (rng.standard_normal((experts, hidden)) * 0.05).astype(np.float32)
+    got = O.router_logits(x, w)
+    for t in range(tokens):
+        for e in range(experts):
+            logit = None
+            for s in range(hidden // 256):
+                c = np.float32(0.0)
+                for i in range(256 * s, 256 * (s + 1)):
+                    c = _fma_f32(x[t, i], w[e, i], c)
+                logit = c if logit is None else np.float32(logit + c)
+            assert got[t, e].view(np.uint32) == np.float32(logit).view(np.uint32), (t, e)
+    # bf16-valued F32 weights route exactly like their bf16 bits
+    wbits = (w.view(np.uint32) >> 16).astype(np.uint16)
+    wq = (wbits.astype(np.uint32) << 16).view(np.float32)
+    assert np.array_equal(O.router_logits(x, wq).view(np.uint32), O.router_logits(x, wbits).view(np.uint32))
+    with pytest.raises(TypeError):
+        O.router_logits(x, w.astype(np.float64))

@@ -51,6 +51,35 @@ def test_static_scratch_expert_matches_allocating_entry_point():
     rt.close()
 
 
+def test_static_scratch_expert_allocates_no_device_memory():
+    # the property the entry point exists for: once a first round of calls
+    # has looked up the array's address and loaded each width's kernels
+    # (CUDA loads kernels lazily, on first launch), further calls at every
+    # width leave the device's free memory and torch's pool unchanged
+    import torch
+    from mimo_prismwing_b200 import synth
+    from mimo_prismwing_b200.runtime import ExpertWeights
+
+    static_forward = _bind()
+    g, u, d = synth.expert(4096, 2048, 79, "cuda")
+    weights = ExpertWeights(g.c(), u.c(), d.c())
+    xs = [synth.activations(w, 4096, 800 + w, "cuda") for w in range(1, 9)]
+    ys = [torch.empty((w, 4096), device="cuda") for w in range(1, 9)]
+    for w in range(1, 9):
+        assert static_forward(ctypes.byref(weights), ctypes.c_void_p(xs[w - 1].data_ptr()), w,
+                              ctypes.c_void_p(ys[w - 1].data_ptr()), None) == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    reserved0 = torch.cuda.memory_reserved()
+    for w in range(1, 9):
+        assert static_forward(ctypes.byref(weights), ctypes.c_void_p(xs[w - 1].data_ptr()), w,
+                              ctypes.c_void_p(ys[w - 1].data_ptr()), None) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, f"device free memory changed by {free0 - free1} bytes"
+    assert torch.cuda.memory_reserved() == reserved0
+
+
 def test_static_scratch_expert_rejects_sizes_beyond_its_array():
     import torch
     from mimo_prismwing_b200 import synth
