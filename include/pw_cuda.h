@@ -128,6 +128,21 @@ typedef struct pw_router {
   uint32_t weight_dtype; /* PW_ROUTER_F32 or PW_ROUTER_BF16 */
 } pw_router;
 
+/* RMSNorm weight storage (pw_norm.weight_dtype).  The checkpoint stores
+ * model.layers.N.post_attention_layernorm.weight as BF16 (read by bf16_vector,
+ * src/text_endpoint.rs:5507-5512). */
+#define PW_NORM_F32 0u
+#define PW_NORM_BF16 1u
+
+/* An RMSNorm (reference: rms_norm src/text_endpoint.rs:2939 with
+ * stable_rms_inverse src/lib.rs:1890).  Device pointer. */
+typedef struct pw_norm {
+  const void *weight;    /* [hidden], f32 or bf16 bits per weight_dtype */
+  uint32_t hidden;       /* a multiple of 256, at most 16384 */
+  uint32_t weight_dtype; /* PW_NORM_F32 or PW_NORM_BF16 */
+  float epsilon;         /* layernorm_epsilon (1e-5 for MiMo-V2.5), finite and > 0 */
+} pw_norm;
+
 /* Per-call accounting (reference: WideMoeExecution / WideLinearExecution,
  * src/wide_metal_moe.rs:97-111). */
 typedef struct pw_stats {
@@ -222,6 +237,15 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
 int pw_route(pw_runtime *rt, const pw_router *router, const float *x, uint32_t tokens,
              uint32_t *selected, float *weights, uint32_t mem, pw_stats *stats);
 
+/* Reference: rms_norm src/text_endpoint.rs:2939.  Per row of x f32 [rows,
+ * hidden]: inv = 1 / sqrt(sum(x^2) / hidden + epsilon), the sum in PyTorch's
+ * vectorised cascade order (pytorch_contiguous_inner_square_sum_f32,
+ * src/lib.rs:1905), then y = bf16(bf16(x * inv) * weight).  `inverse`
+ * (optional, same `mem` as x) receives each row's inv.  Non-finite input is
+ * PW_ERR_NONFINITE (stable_rms_inverse's Err). */
+int pw_rms_norm(pw_runtime *rt, const pw_norm *norm, const float *x, uint32_t rows, float *y, float *inverse,
+                uint32_t mem, pw_stats *stats);
+
 /* ------------------------------------------------------------ MoE layers */
 
 /* Reference: WideMetalMoeRuntime::execute / execute_fused_gate_up
@@ -247,6 +271,18 @@ void pw_bank_destroy(pw_expert_bank *bank);
 int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,
                  uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem,
                  pw_stats *stats);
+
+/* The MoE half of a decoder layer (reference: src/text_endpoint.rs:5507-5580):
+ *   moe_input = rms_norm(post_attention, post_attention_layernorm)
+ *   mlp       = routed layer of moe_input (as pw_moe_layer)
+ *   out       = bf16(post_attention + mlp)
+ * The RMSNorm runs fused with the experts' input quantization (one kernel
+ * writes the normalized rows for the router and their FP8 codes), and the
+ * residual add runs in the combine's epilogue.  residual = post_attention f32
+ * [tokens, H] (bf16-valued); out [tokens, H] may not alias it. */
+int pw_moe_block(pw_runtime *rt, const pw_norm *post_norm, const pw_router *router, const pw_expert_bank *bank,
+                 const float *residual, uint32_t tokens, float *out, uint32_t *selected, float *weights,
+                 uint32_t mem, pw_stats *stats);
 
 /* ------------------------------------------------- expert parallelism */
 
@@ -289,6 +325,12 @@ int pw_ep_rank(const pw_runtime *rt, int *rank, int *world);
 int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,
                     uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem,
                     pw_stats *stats);
+
+/* Collective form of pw_moe_block: the RMSNorm and the residual add run on
+ * each token's own rank, the routed layer as in pw_ep_moe_layer. */
+int pw_ep_moe_block(pw_runtime *rt, const pw_norm *post_norm, const pw_router *router, const pw_expert_bank *bank,
+                    const float *residual, uint32_t tokens, float *out, uint32_t *selected, float *weights,
+                    uint32_t mem, pw_stats *stats);
 
 /* Host-only helper (no GPU): the transfer plan pw_ep_moe_layer derives for
  * rank `rank` from every rank's expert offsets.  all_offsets[g * (E + 1) + e]

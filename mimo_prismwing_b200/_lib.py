@@ -59,6 +59,9 @@ def _bind(L: ctypes.CDLL) -> None:
     L.pw_ep_rank.argtypes = [vp, _p(i32), _p(i32)]
     L.pw_ep_plan.argtypes = [vp, u32, u32, u32, vp, vp, vp, vp, vp]
     L.pw_ep_moe_layer.argtypes = [vp, vp, vp, vp, u32, vp, vp, vp, u32, vp]
+    L.pw_rms_norm.argtypes = [vp, vp, vp, u32, vp, vp, u32, vp]
+    L.pw_moe_block.argtypes = [vp, vp, vp, vp, vp, u32, vp, vp, vp, u32, vp]
+    L.pw_ep_moe_block.argtypes = [vp, vp, vp, vp, vp, u32, vp, vp, vp, u32, vp]
     L.pw_set_profiling.argtypes = [vp, i32]
     L.pw_last_profile.argtypes = [vp, vp]
     for name in header_symbols():

@@ -157,12 +157,23 @@ uint32_t map_box_rows(uint32_t layout);
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
                             const BankTable &bank, const ScheduleOut &out, uint32_t *flags, uint32_t chunk,
                             cudaStream_t stream);
+// residual (optional, [tokens, hidden]): y = bf16(residual + bf16(sum)), the
+// decoder layer's residual add, instead of y = bf16(sum).
 cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const float *placement_w,
-                           uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream);
+                           uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream,
+                           const float *residual = nullptr);
 // The same combine over bf16 down rows (the expert-parallel return path; the
 // rows are bf16-rounded, so the result is identical).
 cudaError_t launch_combine_bf16(const uint16_t *down, const uint32_t *slot_place, const float *placement_w,
-                                uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream);
+                                uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream,
+                                const float *residual = nullptr);
+// RMSNorm (src/text_endpoint.rs:2939) of x [rows, cols] fused with the dynamic
+// FP8 quantization of its output: xn (optional) receives the normalized f32
+// rows, codes/scales (optional) their per-128 FP8 encoding, inv (optional)
+// each row's inverse RMS.  cols % 256 == 0, cols <= 16384; w_dtype PW_NORM_*.
+cudaError_t launch_rms_quantize(const float *x, uint32_t rows, uint32_t cols, const void *weight, uint32_t w_dtype,
+                                float eps, float *xn, uint8_t *codes, float *scales, float *inv, uint32_t *flags,
+                                cudaStream_t stream);
 // out[idx[j]] = bf16 bits of rows[j] (rows already bf16-rounded), j < n.
 cudaError_t launch_scatter_rows_bf16(const float *rows, const uint32_t *idx, uint32_t n, uint32_t cols,
                                      uint16_t *out, cudaStream_t stream);

@@ -56,6 +56,122 @@ cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_
                        rows_dev, cols / 128u);
 }
 
+// ------------------------------------------------- RMSNorm + quantization
+// The decoder layer's post-attention RMSNorm (src/text_endpoint.rs:2939
+// rms_norm; stable_rms_inverse src/lib.rs:1890) fused with the dynamic FP8
+// quantization of its output, the routed experts' first step.  One CTA per
+// row.  The sum of squares follows PyTorch's vectorised cascade
+// (pytorch_contiguous_inner_square_sum_f32, src/lib.rs:1905) exactly: with
+// cols % 256 == 0 it is 16 accumulators j = 4 * register + lane, each summing
+// the squares of columns c = j (mod 16); level 0 sums 16 steps of one 256-
+// column block from zero and is added into level 1 after every block, level 1
+// into level 2 when the step count is a multiple of 256, level 2 into level 3
+// at multiples of 4096; then levels fold into level 0, registers into
+// register 0, lanes into the result.  Here the 16 x (cols / 256) block sums
+// run in parallel (one thread each) and 16 threads replay the level cascade.
+// Products and sums round separately.  Then out = bf16(bf16(x * inv) * w[c])
+// and its per-128 FP8 codes and scales (as k_quantize).
+constexpr uint32_t kRmsMaxBlocks = 64;  // cols <= 16384
+
+template <bool F32W>
+__global__ void __launch_bounds__(256) k_rms_quantize(const float *__restrict__ x, uint32_t cols,
+                                                      const void *__restrict__ weight, float eps,
+                                                      float *__restrict__ xn, uint8_t *__restrict__ codes,
+                                                      float *__restrict__ scales, float *__restrict__ inv_out,
+                                                      uint32_t *flags) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float blk[kRmsMaxBlocks][16];
+  __shared__ float lvl[16];
+  __shared__ float inv_s;
+  const uint32_t row = blockIdx.x, tid = threadIdx.x, nb = cols / 256u;
+  const float *xr = x + (size_t)row * cols;
+  bool ok = true;
+  for (uint32_t pr = tid; pr < nb * 16u; pr += blockDim.x) {
+    const uint32_t b = pr / 16u, j = pr % 16u;
+    float sacc = 0.0f;
+#pragma unroll
+    for (uint32_t i = 0; i < 16u; ++i) {
+      const float v = __ldg(xr + 256u * b + 16u * i + j);
+      ok = ok && finite(v);
+      sacc = __fadd_rn(sacc, __fmul_rn(v, v));
+    }
+    blk[b][j] = sacc;
+  }
+  if (!ok) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
+  __syncthreads();
+  if (tid < 16u) {
+    float a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    for (uint32_t b = 0; b < nb; ++b) {
+      const uint32_t index = 16u * (b + 1u);
+      a1 = __fadd_rn(a1, blk[b][tid]);  // level 0 -> 1 (level 0 restarts from zero)
+      if (index & (15u << 4)) continue;
+      a2 = __fadd_rn(a2, a1);
+      a1 = 0.0f;
+      if (index & (15u << 8)) continue;
+      a3 = __fadd_rn(a3, a2);
+      a2 = 0.0f;
+    }
+    lvl[tid] = __fadd_rn(__fadd_rn(__fadd_rn(0.0f, a1), a2), a3);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float result = 0.0f;
+#pragma unroll
+    for (uint32_t l = 0; l < 4u; ++l) {
+      const float t = __fadd_rn(__fadd_rn(__fadd_rn(lvl[l], lvl[4u + l]), lvl[8u + l]), lvl[12u + l]);
+      result = __fadd_rn(result, t);
+    }
+    const float variance = __fdiv_rn(result, (float)cols);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
+    inv_s = inv;
+    if (inv_out) inv_out[row] = inv;
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  const uint32_t lane = tid % 32u, warp = tid / 32u, nwarps = blockDim.x / 32u;
+  for (uint32_t g = warp; g < cols / 128u; g += nwarps) {
+    const uint32_t c0 = 128u * g + 4u * lane;
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(xr + c0));
+    float wv[4];
+    if (F32W) {
+      const float4 w4 = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(weight) + c0));
+      wv[0] = w4.x, wv[1] = w4.y, wv[2] = w4.z, wv[3] = w4.w;
+    } else {
+      const uint2 w2 = __ldg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(weight) + c0));
+      wv[0] = __uint_as_float(w2.x << 16), wv[1] = __uint_as_float(w2.x & 0xffff0000u);
+      wv[2] = __uint_as_float(w2.y << 16), wv[3] = __uint_as_float(w2.y & 0xffff0000u);
+    }
+    const float xv[4] = {v.x, v.y, v.z, v.w};
+    float o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(xv[k], inv)), wv[k]));
+    if (xn) *reinterpret_cast<float4 *>(xn + (size_t)row * cols + c0) = make_float4(o[0], o[1], o[2], o[3]);
+    float m = fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3])));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const float scale = __fdiv_rn(fmaxf(m, 1.0e-10f), 448.0f);
+    auto q = [&](float val) { return fminf(fmaxf(__fdiv_rn(val, scale), -448.0f), 448.0f); };
+    const uint32_t lo = encode2(q(o[0]), q(o[1]));
+    const uint32_t hi = encode2(q(o[2]), q(o[3]));
+    if (codes) reinterpret_cast<uint32_t *>(codes + (size_t)row * cols + 128u * g)[lane] = lo | (hi << 16);
+    if (scales && lane == 0) scales[(size_t)row * (cols / 128u) + g] = scale;
+  }
+}
+
+cudaError_t launch_rms_quantize(const float *x, uint32_t rows, uint32_t cols, const void *weight, uint32_t w_dtype,
+                                float eps, float *xn, uint8_t *codes, float *scales, float *inv, uint32_t *flags,
+                                cudaStream_t stream) {
+  if (cols == 0 || cols % 256u || cols / 256u > kRmsMaxBlocks || (w_dtype != PW_NORM_F32 && w_dtype != PW_NORM_BF16))
+    return cudaErrorInvalidValue;
+  if (rows == 0) return cudaSuccess;
+  if (w_dtype == PW_NORM_F32)
+    return launch_kernel(k_rms_quantize<true>, dim3(rows), dim3(256), 0, stream, x, cols, weight, eps, xn, codes,
+                         scales, inv, flags);
+  return launch_kernel(k_rms_quantize<false>, dim3(rows), dim3(256), 0, stream, x, cols, weight, eps, xn, codes, scales,
+                       inv, flags);
+}
+
 // --------------------------------------------------------------- bf16 round
 __global__ void k_round_bf16(float *v, uint32_t n, uint32_t *flags) {
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -945,7 +1061,7 @@ __device__ __forceinline__ float4 load4(const uint16_t *row, uint32_t c4) {
 template <typename T>
 __global__ void k_combine(const T *__restrict__ down, const uint32_t *__restrict__ slot_place,
                           const float *__restrict__ placement_w, uint32_t tokens, uint32_t hidden,
-                          float *__restrict__ y, uint32_t *flags) {
+                          const float *__restrict__ residual, float *__restrict__ y, uint32_t *flags) {
   pdl_wait();
   pdl_launch_dependents();
   const uint32_t t = blockIdx.y;
@@ -980,25 +1096,34 @@ __global__ void k_combine(const T *__restrict__ down, const uint32_t *__restrict
       acc.w = round_bf16(acc.w);
       if (!finite(acc.x) || !finite(acc.y) || !finite(acc.z) || !finite(acc.w))
         raise_flag(flags, PW_FLAG_NONFINITE_COMBINE);
+      if (residual) {  // the decoder layer's residual add: bf16(residual + mlp) (src/text_endpoint.rs:5576-5580)
+        const float4 r = __ldg(reinterpret_cast<const float4 *>(residual + (size_t)t * hidden) + 2u * c8 + h);
+        acc.x = round_bf16(__fadd_rn(r.x, acc.x));
+        acc.y = round_bf16(__fadd_rn(r.y, acc.y));
+        acc.z = round_bf16(__fadd_rn(r.z, acc.z));
+        acc.w = round_bf16(__fadd_rn(r.w, acc.w));
+      }
       reinterpret_cast<float4 *>(y + (size_t)t * hidden)[2u * c8 + h] = acc;
     }
   }
 }
 
 cudaError_t launch_combine(const float *down, const uint32_t *slot_place, const float *placement_w,
-                           uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream) {
+                           uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream,
+                           const float *residual) {
   if (hidden % 8u || tokens == 0) return cudaErrorInvalidValue;
   dim3 grid((hidden / 8u + 255u) / 256u, tokens);
   return launch_kernel(k_combine<float>, grid, dim3(256), 0, stream, down, slot_place, placement_w, tokens, hidden,
-                       y, flags);
+                       residual, y, flags);
 }
 
 cudaError_t launch_combine_bf16(const uint16_t *down, const uint32_t *slot_place, const float *placement_w,
-                                uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream) {
+                                uint32_t tokens, uint32_t hidden, float *y, uint32_t *flags, cudaStream_t stream,
+                                const float *residual) {
   if (hidden % 8u || tokens == 0) return cudaErrorInvalidValue;
   dim3 grid((hidden / 8u + 255u) / 256u, tokens);
   return launch_kernel(k_combine<uint16_t>, grid, dim3(256), 0, stream, down, slot_place, placement_w, tokens,
-                       hidden, y, flags);
+                       hidden, residual, y, flags);
 }
 
 // ------------------------------------------------------ bf16 row scatter

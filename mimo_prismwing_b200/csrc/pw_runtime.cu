@@ -9,6 +9,7 @@
 // scheduled on the host for pw_moe_layer: routing, scheduling and combine all
 // run on the device.
 #include <chrono>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -555,6 +556,55 @@ int pw_quantize_fp8(pw_runtime *rt, const float *x, uint32_t rows, uint32_t cols
     CK(launch_quantize(x, rows, cols, codes, scales, rt->d_flags, rt->stream));
   }
   return call.finish(0);
+}
+
+// ------------------------------------------------------------------ rms norm
+static int check_norm(pw_runtime *rt, const pw_norm *n, uint32_t hidden) {
+  if (!n || !n->weight) return fail(rt, PW_ERR_ARGUMENT, "norm descriptor is null");
+  if (n->weight_dtype != PW_NORM_F32 && n->weight_dtype != PW_NORM_BF16)
+    return fail(rt, PW_ERR_ARGUMENT, "norm weight_dtype must be PW_NORM_F32 or PW_NORM_BF16");
+  if (!std::isfinite(n->epsilon) || n->epsilon <= 0.0f)
+    return fail(rt, PW_ERR_ARGUMENT, "invalid RMSNorm epsilon");
+  if (n->hidden != hidden || hidden == 0 || hidden % 256u || hidden > 16384u)
+    return fail(rt, PW_ERR_SHAPE, "RMSNorm shape mismatch (hidden %u, a multiple of 256 up to 16384)", n->hidden);
+  return PW_OK;
+}
+
+int pw_rms_norm(pw_runtime *rt, const pw_norm *norm, const float *x, uint32_t rows, float *y, float *inverse,
+                uint32_t mem, pw_stats *stats) {
+  if (!rt) return PW_ERR_ARGUMENT;
+  if (!x || !y) return fail(rt, PW_ERR_ARGUMENT, "null argument");
+  int s;
+  if (!norm) return fail(rt, PW_ERR_ARGUMENT, "norm descriptor is null");
+  if ((s = check_norm(rt, norm, norm->hidden)) != PW_OK) return s;
+  if (rows == 0) return fail(rt, PW_ERR_SHAPE, "RMSNorm needs at least one row");
+  CK(cudaSetDevice(rt->device));
+  const uint32_t H = norm->hidden;
+  const size_t n = (size_t)rows * H;
+  Call call{rt, mem, stats, 0};
+  if ((s = call.begin()) != PW_OK) return s;
+  Arena ar;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1) {
+      if ((s = ensure_scratch(rt, ar.off)) != PW_OK) return s;
+      ar = Arena{static_cast<char *>(rt->scratch), 0};
+    }
+    float *dx = call.host() ? ar.take<float>(n) : const_cast<float *>(x);
+    float *dy = call.host() ? ar.take<float>(n) : y;
+    float *dinv = inverse && call.host() ? ar.take<float>(rows) : inverse;
+    if (pass == 0) continue;
+    if (call.host() && (s = call.stage_in(dx, x, n * 4)) != PW_OK) return s;
+    {
+      ProfScope ps(rt, P_QUANT, 1);
+      CK(launch_rms_quantize(dx, rows, H, norm->weight, norm->weight_dtype, norm->epsilon, dy, nullptr, nullptr,
+                             dinv, rt->d_flags, rt->stream));
+    }
+    if (call.host()) {
+      if ((s = call.stage_out(y, dy, n * 4)) != PW_OK) return s;
+      if (inverse && (s = call.stage_out(inverse, dinv, (size_t)rows * 4)) != PW_OK) return s;
+    }
+  }
+  return call.finish((uint64_t)H * (norm->weight_dtype == PW_NORM_F32 ? 4u : 2u));
 }
 
 // ------------------------------------------------------------------ validate
@@ -1185,14 +1235,20 @@ void pw_bank_destroy(pw_expert_bank *bank) {
 }
 
 // ------------------------------------------------------ device-routed layer
-int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x, uint32_t tokens,
-                 float *y, uint32_t *selected, float *weights, uint32_t mem, pw_stats *stats) {
+// The routed layer, optionally as the MoE half of a decoder layer: with
+// `norm`, x is the post-attention residual stream, the layer's input is
+// rms_norm(x) (fused with its FP8 quantization) and y = bf16(x + layer).
+static int moe_layer_impl(pw_runtime *rt, const pw_norm *norm, const pw_router *router, const pw_expert_bank *bank,
+                          const float *x, uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem,
+                          pw_stats *stats) {
   if (!rt) return PW_ERR_ARGUMENT;
   if (!x || !y || !bank) return fail(rt, PW_ERR_ARGUMENT, "null argument");
   int s;
   if ((s = check_router(rt, router)) != PW_OK) return s;
   if (bank->n != router->experts || bank->hidden != router->hidden)
     return fail(rt, PW_ERR_SHAPE, "router and expert bank disagree");
+  if (norm && (s = check_norm(rt, norm, bank->hidden)) != PW_OK) return s;
+  if (norm && x == y) return fail(rt, PW_ERR_ARGUMENT, "the block's output may not alias its residual input");
   if (tokens == 0) return fail(rt, PW_ERR_SHAPE, "routed layer needs at least one token");
   if (tokens > 2048u) return fail(rt, PW_ERR_UNSUPPORTED, "routed layer supports at most 2048 tokens per call");
   CK(cudaSetDevice(rt->device));
@@ -1214,6 +1270,7 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     }
     float *dx = call.host() ? ar.take<float>((size_t)tokens * H) : const_cast<float *>(x);
     float *dy = call.host() ? ar.take<float>((size_t)tokens * H) : y;
+    float *dn = norm ? ar.take<float>((size_t)tokens * H) : dx;  // the layer input the router reads
     uint8_t *xc = ar.take<uint8_t>((size_t)tokens * H);
     float *xs = ar.take<float>((size_t)tokens * H / 128u);
     float *logits = ar.take<float>(router_scratch_floats(tokens, E, H));
@@ -1245,11 +1302,15 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     PdlScope pdl(!rt->profiling);
     {
       ProfScope ps(rt, P_QUANT, 1);
-      CK(launch_quantize(dx, tokens, H, xc, xs, rt->d_flags, rt->stream));
+      if (norm)
+        CK(launch_rms_quantize(dx, tokens, H, norm->weight, norm->weight_dtype, norm->epsilon, dn, xc, xs, nullptr,
+                               rt->d_flags, rt->stream));
+      else
+        CK(launch_quantize(dx, tokens, H, xc, xs, rt->d_flags, rt->stream));
     }
     {
       ProfScope ps(rt, P_ROUTER, 2);
-      CK(launch_router(dx, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, sel, wts,
+      CK(launch_router(dn, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, sel, wts,
                        rt->d_ties, rt->d_flags, rt->num_sms, rt->stream));
     }
     {
@@ -1271,11 +1332,12 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     if (s != PW_OK) return s;
     {
       ProfScope ps(rt, P_COMBINE, 1);
+      const float *residual = norm ? dx : nullptr;
       if (wide)
         CK(launch_combine_bf16(reinterpret_cast<const uint16_t *>(down), so.slot_place, so.placement_w, tokens, H, dy,
-                               rt->d_flags, rt->stream));
+                               rt->d_flags, rt->stream, residual));
       else
-        CK(launch_combine(down, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream));
+        CK(launch_combine(down, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream, residual));
     }
     if (call.host()) {
       if ((s = call.stage_out(y, dy, (size_t)tokens * H * 4)) != PW_OK) return s;
@@ -1303,6 +1365,18 @@ int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *
     stats->weight_bytes = per_expert * cnt[0] + router_bytes(router);
   }
   return s;
+}
+
+int pw_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x, uint32_t tokens,
+                 float *y, uint32_t *selected, float *weights, uint32_t mem, pw_stats *stats) {
+  return moe_layer_impl(rt, nullptr, router, bank, x, tokens, y, selected, weights, mem, stats);
+}
+
+int pw_moe_block(pw_runtime *rt, const pw_norm *post_norm, const pw_router *router, const pw_expert_bank *bank,
+                 const float *residual, uint32_t tokens, float *out, uint32_t *selected, float *weights,
+                 uint32_t mem, pw_stats *stats) {
+  if (rt && !post_norm) return fail(rt, PW_ERR_ARGUMENT, "norm descriptor is null");
+  return moe_layer_impl(rt, post_norm, router, bank, residual, tokens, out, selected, weights, mem, stats);
 }
 
 }  // extern "C"
@@ -1488,7 +1562,7 @@ int ep_window_setup(pw_runtime *rt, uint32_t L, uint32_t H) {
 // local routing and the gathered send rows stays on the device.
 int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_t tokens,
                  float *y, uint32_t *selected, float *weights, const ScheduleOut &so, float *dy, uint32_t *sel,
-                 float *wts, const uint8_t *xsend, const float *ssend) {
+                 float *wts, const uint8_t *xsend, const float *ssend, const float *residual) {
   EpState *ep = rt->ep;
   const EpWindow &w = ep->w;
   const uint32_t G = w.G, L = w.L, H = bank->hidden, I = bank->inter, P = tokens * 8u;
@@ -1571,7 +1645,7 @@ int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_
     CK(launch_ep_wait_returns(ea, rt->stream));
     if (tokens)
       CK(launch_combine_bf16(reinterpret_cast<const uint16_t *>(mine + w.ret_rows), so.slot_place, so.placement_w,
-                             tokens, H, dy, rt->d_flags, rt->stream));
+                             tokens, H, dy, rt->d_flags, rt->stream, residual));
   }
   if (tokens) {
     if (call.host()) {
@@ -1679,8 +1753,11 @@ int pw_ep_init(pw_runtime *rt, int rank, int world, const void *id, uint32_t byt
   return s;
 }
 
-int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,
-                    uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem, pw_stats *stats) {
+// With `norm` (pw_ep_moe_block) x is the residual stream: the RMSNorm runs
+// fused with the input quantization and the combine adds the residual.
+static int ep_moe_layer_impl(pw_runtime *rt, const pw_norm *norm, const pw_router *router, const pw_expert_bank *bank,
+                             const float *x, uint32_t tokens, float *y, uint32_t *selected, float *weights,
+                             uint32_t mem, pw_stats *stats) {
   if (!rt) return PW_ERR_ARGUMENT;
   EpState *ep = rt->ep;
   if (!ep || !ep->comm)
@@ -1688,6 +1765,8 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
   if (!bank || (tokens && (!x || !y))) return fail(rt, PW_ERR_ARGUMENT, "null argument");
   int s;
   if ((s = check_router(rt, router)) != PW_OK) return s;
+  if (norm && (s = check_norm(rt, norm, bank->hidden)) != PW_OK) return s;
+  if (norm && tokens && x == y) return fail(rt, PW_ERR_ARGUMENT, "the block's output may not alias its residual input");
   const uint32_t G = (uint32_t)ep->world, r = (uint32_t)ep->rank;
   const uint32_t L = bank->n, E = router->experts, H = bank->hidden, I = bank->inter;
   if (E != L * G) return fail(rt, PW_ERR_SHAPE, "router has %u experts; %u ranks x %u local experts", E, G, L);
@@ -1706,7 +1785,7 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
 
   // ---- phase 1: local routing, schedule, send rows (runtime scratch)
   Arena ar;
-  float *dx = nullptr, *dy = nullptr;
+  float *dx = nullptr, *dy = nullptr, *dnorm = nullptr;
   uint32_t *sel = nullptr, *alloff = nullptr;
   float *wts = nullptr;
   uint8_t *xsend = nullptr;
@@ -1720,6 +1799,7 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
     }
     dx = call.host() ? ar.take<float>((size_t)tokens * H) : const_cast<float *>(x);
     dy = call.host() ? ar.take<float>((size_t)tokens * H) : y;
+    dnorm = norm ? ar.take<float>((size_t)tokens * H) : dx;  // the layer input the router reads
     uint8_t *xc = ar.take<uint8_t>((size_t)tokens * H);
     float *xs = ar.take<float>((size_t)tokens * Hs);
     float *logits = ar.take<float>(router_scratch_floats(tokens, E, H));
@@ -1745,11 +1825,15 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
     CK(cudaMemsetAsync(rt->d_ties, 0, 4, rt->stream));
     {
       ProfScope ps(rt, P_QUANT, 1);
-      CK(launch_quantize(dx, tokens, H, xc, xs, rt->d_flags, rt->stream));
+      if (norm)
+        CK(launch_rms_quantize(dx, tokens, H, norm->weight, norm->weight_dtype, norm->epsilon, dnorm, xc, xs,
+                               nullptr, rt->d_flags, rt->stream));
+      else
+        CK(launch_quantize(dx, tokens, H, xc, xs, rt->d_flags, rt->stream));
     }
     {
       ProfScope ps(rt, P_ROUTER, 2);
-      CK(launch_router(dx, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, sel, wts,
+      CK(launch_router(dnorm, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, sel, wts,
                        rt->d_ties, rt->d_flags, rt->num_sms, rt->stream));
     }
     {
@@ -1758,7 +1842,9 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
       CK(launch_gather_rows(xc, xs, so.placement_tok, P, H, xsend, ssend, rt->stream));
     }
   }
-  if (ep->p2p) return ep_layer_p2p(rt, call, bank, tokens, y, selected, weights, so, dy, sel, wts, xsend, ssend);
+  const float *residual = norm ? dx : nullptr;
+  if (ep->p2p)
+    return ep_layer_p2p(rt, call, bank, tokens, y, selected, weights, so, dy, sel, wts, xsend, ssend, residual);
   if ((s = ep_pinned(rt, ep->h_off, ep->h_off_cap, (size_t)G * (E + 1) * 4)) != PW_OK) return s;
   NK(pw::nccl::all_gather(so.offsets, alloff, E + 1, ncclUint32, ep->comm, rt->stream, ep->timeout_s),
      "ncclAllGather of expert offsets");
@@ -1905,7 +1991,7 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
   if (tokens) {
     {
       ProfScope ps(rt, P_COMBINE, 1);
-      CK(launch_combine_bf16(ret, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream));
+      CK(launch_combine_bf16(ret, so.slot_place, so.placement_w, tokens, H, dy, rt->d_flags, rt->stream, residual));
     }
     if (call.host()) {
       if ((s = call.stage_out(y, dy, (size_t)tokens * H * 4)) != PW_OK) return s;
@@ -1929,6 +2015,18 @@ int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_ban
     stats->expert_rows = P_recv;
   }
   return s;
+}
+
+int pw_ep_moe_layer(pw_runtime *rt, const pw_router *router, const pw_expert_bank *bank, const float *x,
+                    uint32_t tokens, float *y, uint32_t *selected, float *weights, uint32_t mem, pw_stats *stats) {
+  return ep_moe_layer_impl(rt, nullptr, router, bank, x, tokens, y, selected, weights, mem, stats);
+}
+
+int pw_ep_moe_block(pw_runtime *rt, const pw_norm *post_norm, const pw_router *router, const pw_expert_bank *bank,
+                    const float *residual, uint32_t tokens, float *out, uint32_t *selected, float *weights,
+                    uint32_t mem, pw_stats *stats) {
+  if (rt && !post_norm) return fail(rt, PW_ERR_ARGUMENT, "norm descriptor is null");
+  return ep_moe_layer_impl(rt, post_norm, router, bank, residual, tokens, out, selected, weights, mem, stats);
 }
 
 int pw_ep_plan(const uint32_t *all_offsets, uint32_t world, uint32_t rank, uint32_t experts, uint32_t *n_send,

@@ -36,6 +36,8 @@ EP_NCCL_TRANSPORT = 1
 RUNTIME_FUSED_GATE_UP = 1
 ROUTER_F32 = 0
 ROUTER_BF16 = 1
+NORM_F32 = 0
+NORM_BF16 = 1
 
 ERRORS = {
     -1: "argument", -2: "shape", -3: "nonfinite", -4: "device_flags", -5: "cuda", -6: "nccl",
@@ -69,6 +71,11 @@ class ExpertBinding(ctypes.Structure):
 class Router(ctypes.Structure):
     _fields_ = [("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("experts", ctypes.c_uint32),
                 ("hidden", ctypes.c_uint32), ("top_k", ctypes.c_uint32), ("weight_dtype", ctypes.c_uint32)]
+
+
+class Norm(ctypes.Structure):
+    _fields_ = [("weight", ctypes.c_void_p), ("hidden", ctypes.c_uint32), ("weight_dtype", ctypes.c_uint32),
+                ("epsilon", ctypes.c_float)]
 
 
 class Stats(ctypes.Structure):
@@ -321,6 +328,29 @@ class WideMoeRuntime:
             raise PrismwingError(-1, "router tensors must be contiguous")
         return Router(w.data_ptr(), bias.data_ptr(), w.shape[0], w.shape[1], 8, dtype)
 
+    @staticmethod
+    def _norm(weight: torch.Tensor, epsilon: float) -> Norm:
+        """pw_norm for a CUDA float32 (PW_NORM_F32) or bf16/int16 (PW_NORM_BF16) weight."""
+        if weight.dtype == torch.float32:
+            dtype = NORM_F32
+        elif weight.dtype in (torch.bfloat16, torch.int16):
+            dtype = NORM_BF16
+        else:
+            raise PrismwingError(-1, f"norm weight must be float32 or bf16, not {weight.dtype}")
+        if not (weight.is_cuda and weight.is_contiguous() and weight.dim() == 1):
+            raise PrismwingError(-1, "norm weight must be a contiguous 1-D CUDA tensor")
+        return Norm(weight.data_ptr(), weight.shape[0], dtype, float(epsilon))
+
+    def rms_norm(self, x, weight: torch.Tensor, epsilon: float = 1e-5):
+        """rms_norm (src/text_endpoint.rs:2939): (y f32 [rows, H], inverse f32 [rows])."""
+        x = _as_f32(x)
+        n = self._norm(weight, epsilon)
+        x, out, mem = self._io(x, tuple(x.shape))
+        inv = torch.empty((x.shape[0],), dtype=torch.float32, device=out.device)
+        self._check(self._L.pw_rms_norm(self._rt, ctypes.byref(n), ctypes.c_void_p(x.data_ptr()), x.shape[0],
+                                        ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(inv.data_ptr()), mem, None))
+        return out, inv
+
     # ------------------------------------------------------------ layers
     def execute(self, x, experts: Sequence[WideExpertBinding]) -> Execution:
         """src/wide_metal_moe.rs:836 execute: host-built schedule, whole layer on device."""
@@ -433,5 +463,36 @@ class WideMoeRuntime:
             ctypes.c_void_p(sel.data_ptr() if sel is not None else 0),
             ctypes.c_void_p(wts.data_ptr() if wts is not None else 0), mem,
             ctypes.byref(st) if stats else None))
+        return Execution(out, st.wall_ms, st.device_ms, st.unique_experts, st.expert_rows, st.boundary_tie_rows,
+                         st.weight_bytes, sel, wts)
+
+    def moe_block(self, residual, norm_weight: torch.Tensor, epsilon: float, router_weight: torch.Tensor,
+                  bias: torch.Tensor, bank, want_routes: bool = False, stats: bool = True,
+                  asynchronous: bool = False, out: Optional[torch.Tensor] = None, expert_parallel: bool = False
+                  ) -> Execution:
+        """The MoE half of a decoder layer (src/text_endpoint.rs:5507-5580):
+        out = bf16(residual + routed_layer(rms_norm(residual))).  With
+        expert_parallel the call is pw_ep_moe_block (collective)."""
+        x = _as_f32(residual)
+        T, H = x.shape
+        n = self._norm(norm_weight, epsilon)
+        r = self._router(router_weight, bias)
+        mem = MEM_DEVICE if x.is_cuda else MEM_HOST
+        if asynchronous:
+            if not x.is_cuda:
+                raise PrismwingError(-1, "asynchronous calls need device I/O")
+            mem |= MEM_ASYNC
+            stats = False
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.float32, device=x.device)
+        sel = torch.empty((T, 8), dtype=torch.int32, device=x.device) if want_routes else None
+        wts = torch.empty((T, 8), dtype=torch.float32, device=x.device) if want_routes else None
+        st = Stats()
+        fn = self._L.pw_ep_moe_block if expert_parallel else self._L.pw_moe_block
+        self._check(fn(self._rt, ctypes.byref(n), ctypes.byref(r), bank, ctypes.c_void_p(x.data_ptr() if T else 0), T,
+                       ctypes.c_void_p(out.data_ptr() if T else 0),
+                       ctypes.c_void_p(sel.data_ptr() if sel is not None and T else 0),
+                       ctypes.c_void_p(wts.data_ptr() if wts is not None and T else 0), mem,
+                       ctypes.byref(st) if stats else None))
         return Execution(out, st.wall_ms, st.device_ms, st.unique_experts, st.expert_rows, st.boundary_tie_rows,
                          st.weight_bytes, sel, wts)

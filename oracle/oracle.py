@@ -95,6 +95,11 @@ def _bind(L: ctypes.CDLL) -> None:
     L.pwo_staged_swiglu.restype = ctypes.c_float
     L.pwo_router_logits.argtypes = [f32p, sz, u16p, sz, sz, f32p]
     L.pwo_router_logits_f32.argtypes = [f32p, sz, f32p, sz, sz, f32p]
+    L.pwo_rms_square_sum.argtypes = [f32p, sz]
+    L.pwo_rms_square_sum.restype = ctypes.c_float
+    L.pwo_rms_inverse.argtypes = [f32p, sz, ctypes.c_float, f32p]
+    L.pwo_rms_norm.argtypes = [f32p, sz, sz, f32p, ctypes.c_float, f32p, f32p]
+    L.pwo_residual_add.argtypes = [f32p, f32p, sz, f32p]
     L.pwo_noaux_topk.argtypes = [f32p, f32p, sz, sz, sz, u32p, f32p, f32p, f32p]
     L.pwo_routed_layer.argtypes = [f32p, sz, sz, sz, u32p, f32p, sz, _p(ctypes.c_void_p),
                                    ctypes.c_int, ctypes.c_int, f32p, f32p, f32p]
@@ -301,6 +306,45 @@ def router_logits(x: np.ndarray, weight: np.ndarray) -> np.ndarray:
         raise TypeError(f"router weight must be float32 or bf16 bits (uint16), not {weight.dtype}")
     if rc != 0:
         raise ValueError("router logits shape mismatch")
+    return out
+
+
+def rms_square_sum(values: np.ndarray) -> np.float32:
+    """pytorch_contiguous_inner_square_sum_f32 (src/lib.rs:1905): PyTorch's cascade order."""
+    v = np.ascontiguousarray(values, dtype=np.float32).ravel()
+    return np.float32(lib().pwo_rms_square_sum(_ptr(v, ctypes.c_float), v.size))
+
+
+def rms_inverse(values: np.ndarray, epsilon: float) -> np.float32:
+    """stable_rms_inverse (src/lib.rs:1890); raises ValueError where the reference returns Err."""
+    v = np.ascontiguousarray(values, dtype=np.float32).ravel()
+    out = np.zeros(1, np.float32)
+    if lib().pwo_rms_inverse(_ptr(v, ctypes.c_float), v.size, ctypes.c_float(epsilon), _ptr(out, ctypes.c_float)):
+        raise ValueError("invalid RMSNorm input")
+    return out[0]
+
+
+def rms_norm(x: np.ndarray, weight: np.ndarray, epsilon: float = 1e-5):
+    """rms_norm (src/text_endpoint.rs:2939) -> (out f32 [rows, cols], inverse f32 [rows])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    w = np.ascontiguousarray(weight, dtype=np.float32)
+    if w.shape != (cols,):
+        raise ValueError("RMSNorm shape mismatch")
+    out = np.empty_like(x)
+    inv = np.empty(rows, np.float32)
+    if lib().pwo_rms_norm(_ptr(x, ctypes.c_float), rows, cols, _ptr(w, ctypes.c_float), ctypes.c_float(epsilon),
+                          _ptr(out, ctypes.c_float), _ptr(inv, ctypes.c_float)):
+        raise ValueError("invalid RMSNorm input")
+    return out, inv
+
+
+def residual_add(residual: np.ndarray, projected: np.ndarray) -> np.ndarray:
+    """src/text_endpoint.rs:5576-5580: bf16(residual + projected)."""
+    r = np.ascontiguousarray(residual, dtype=np.float32)
+    p = np.ascontiguousarray(projected, dtype=np.float32)
+    out = np.empty_like(r)
+    lib().pwo_residual_add(_ptr(r, ctypes.c_float), _ptr(p, ctypes.c_float), r.size, _ptr(out, ctypes.c_float))
     return out
 
 

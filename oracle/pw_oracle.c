@@ -657,3 +657,113 @@ int pwo_schedule(const uint32_t *selected, size_t tokens, size_t experts, uint32
   free(fill);
   return 0;
 }
+
+/* ------------------------------------------------------------------ */
+/* RMSNorm (src/text_endpoint.rs:2939 rms_norm, with stable_rms_inverse */
+/* src/lib.rs:1890 and its sum of squares                               */
+/* pytorch_contiguous_inner_square_sum_f32 src/lib.rs:1905).  The sum  */
+/* runs in PyTorch's vectorised cascade order: 4 lanes x 4 interleaved  */
+/* registers x 4 levels of f32 accumulators; level 0 takes              */
+/* 2^level_power steps of 16 squares, then each level is added into the */
+/* next (and cleared) until the step count is not a multiple of that   */
+/* level's span; leftovers go to level 0, levels fold into level 0,     */
+/* registers into register 0, and lanes into the scalar tail's sum.     */
+/* Products and sums round separately (no fused multiply-add).          */
+/* ------------------------------------------------------------------ */
+float pwo_rms_square_sum(const float *values, size_t n) {
+  enum { LANES = 4, INTERLEAVE = 4, LEVELS = 4 };
+  const size_t vector_count = n / LANES;
+  const size_t cascade_size = vector_count / INTERLEAVE;
+  size_t ceil_log2 = 0;
+  if (cascade_size > 1) {
+    size_t v = cascade_size - 1;
+    while (v) { ++ceil_log2; v >>= 1; }
+  }
+  const size_t level_power = ceil_log2 / LEVELS > 4 ? ceil_log2 / LEVELS : 4;
+  const size_t level_step = (size_t)1 << level_power;
+  const size_t level_mask = level_step - 1;
+  float acc[LEVELS][INTERLEAVE][LANES];
+  memset(acc, 0, sizeof acc);
+  size_t index = 0;
+  while (index + level_step <= cascade_size) {
+    for (size_t s = 0; s < level_step; ++s) {
+      for (int r = 0; r < INTERLEAVE; ++r) {
+        const size_t base = (index * INTERLEAVE + r) * LANES;
+        for (int l = 0; l < LANES; ++l) {
+          const float sq = values[base + l] * values[base + l];
+          acc[0][r][l] += sq;
+        }
+      }
+      ++index;
+    }
+    for (int level = 1; level < LEVELS; ++level) {
+      for (int r = 0; r < INTERLEAVE; ++r)
+        for (int l = 0; l < LANES; ++l) {
+          acc[level][r][l] += acc[level - 1][r][l];
+          acc[level - 1][r][l] = 0.0f;
+        }
+      if (index & (level_mask << (level * level_power))) break;
+    }
+  }
+  while (index < cascade_size) {
+    for (int r = 0; r < INTERLEAVE; ++r) {
+      const size_t base = (index * INTERLEAVE + r) * LANES;
+      for (int l = 0; l < LANES; ++l) {
+        const float sq = values[base + l] * values[base + l];
+        acc[0][r][l] += sq;
+      }
+    }
+    ++index;
+  }
+  for (int level = 1; level < LEVELS; ++level)
+    for (int r = 0; r < INTERLEAVE; ++r)
+      for (int l = 0; l < LANES; ++l) acc[0][r][l] += acc[level][r][l];
+  for (size_t vec = cascade_size * INTERLEAVE; vec < vector_count; ++vec)
+    for (int l = 0; l < LANES; ++l) {
+      const float v = values[vec * LANES + l];
+      const float sq = v * v;
+      acc[0][0][l] += sq;
+    }
+  for (int r = 1; r < INTERLEAVE; ++r)
+    for (int l = 0; l < LANES; ++l) acc[0][0][l] += acc[0][r][l];
+  float result = 0.0f;
+  for (size_t i = vector_count * LANES; i < n; ++i) {
+    const float sq = values[i] * values[i];
+    result += sq;
+  }
+  for (int l = 0; l < LANES; ++l) result += acc[0][0][l];
+  return result;
+}
+
+/* stable_rms_inverse (src/lib.rs:1890): 1 / sqrt(sum/n + eps); -1 on   */
+/* empty or non-finite input or a non-positive / non-finite epsilon.    */
+int pwo_rms_inverse(const float *values, size_t n, float epsilon, float *inverse) {
+  if (n == 0 || !isfinite(epsilon) || epsilon <= 0.0f) return -1;
+  for (size_t i = 0; i < n; ++i)
+    if (!isfinite(values[i])) return -1;
+  const float variance = pwo_rms_square_sum(values, n) / (float)n;
+  *inverse = 1.0f / sqrtf(variance + epsilon);
+  return 0;
+}
+
+/* rms_norm (src/text_endpoint.rs:2939): per row, out = bf16(bf16(x*inv) */
+/* * weight[c]); inverse (optional) receives each row's inverse.         */
+int pwo_rms_norm(const float *x, size_t rows, size_t cols, const float *weight, float epsilon, float *out,
+                 float *inverse) {
+  for (size_t r = 0; r < rows; ++r) {
+    float inv;
+    if (pwo_rms_inverse(x + r * cols, cols, epsilon, &inv) != 0) return -1;
+    if (inverse) inverse[r] = inv;
+    for (size_t c = 0; c < cols; ++c) {
+      const float normalized = pwo_round_bf16(x[r * cols + c] * inv);
+      out[r * cols + c] = pwo_round_bf16(normalized * weight[c]);
+    }
+  }
+  return 0;
+}
+
+/* Residual add of the decoder layer (src/text_endpoint.rs:5576-5580): */
+/* out = bf16(residual + projected).                                    */
+void pwo_residual_add(const float *residual, const float *projected, size_t n, float *out) {
+  for (size_t i = 0; i < n; ++i) out[i] = pwo_round_bf16(residual[i] + projected[i]);
+}

@@ -40,6 +40,9 @@ COPIES = {
     "mtp_gate_fp8_gemv.json": ("evals/fixtures/real/mtp-gate-fp8-gemv.json",
                                ["rows", "columns", "block_columns", "raw_u8", "scale_inv", "input",
                                 "expected_f32", "oracle", "tensor"]),
+    "pw0079_rms_cascade.json": ("evals/fixtures/tiny/pw0079-pytorch-rms-cascade.json",
+                                ["epsilon_f32_u32", "high_precision_variance_f32_u32", "input_bf16_u16",
+                                 "inverse_f32_u32", "semantic", "torch_version", "variance_f32_u32", "width"]),
     "mtp_gate_fp8_block.json": ("evals/fixtures/real/mtp-gate-fp8-block.json",
                                 ["raw_u8", "decoded_fp8", "dequantized", "scale_inv"]),
 }

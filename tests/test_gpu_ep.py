@@ -66,6 +66,10 @@ def _worker(rank, world, uid_q, res_q, tokens_per_rank, mode, nccl=False):
         y_async = torch.empty((T, HID), device=dev)
         rt.ep_moe_layer(x, w, bias, local, asynchronous=True, out=y_async)
         rt.ep_moe_layer(x, w, bias, local)
+        # the decoder-layer block (RMSNorm before, residual add after) on the
+        # same ranks: collective too
+        nw = (1.0 + 0.1 * torch.randn(HID, generator=torch.Generator().manual_seed(5))).to(torch.bfloat16).cuda(rank)
+        blk = rt.moe_block(x, nw, 1e-5, w, bias, local, expert_parallel=True)
         if T == 0:
             res_q.put((rank, "ok"))
             return
@@ -80,13 +84,17 @@ def _worker(rank, world, uid_q, res_q, tokens_per_rank, mode, nccl=False):
         from oracle import oracle as O
         full_bank = _bank(dev, range(E))
         rt1 = WideMoeRuntime.compile_with_fused_gate_up(rank)
-        single = rt1.moe_layer(x, w, bias, rt1.create_bank(full_bank)).output.cpu().numpy()
+        full_handle = rt1.create_bank(full_bank)
+        single = rt1.moe_layer(x, w, bias, full_handle).output.cpu().numpy()
+        single_blk = rt1.moe_block(x, nw, 1e-5, w, bias, full_handle).output.cpu().numpy()
         # bit-identical when both pick the same expert kernels: the single-GPU
         # layer runs the tcgen05 GEMM from 256 tokens, the expert-parallel one
         # when an expert receives > 16 rows (GEMV and GEMM sum in different orders)
         total = sum(tokens_per_rank)
         if T >= 256 or total * 8 <= 16 * E // 4:
             assert np.array_equal(y.view(np.uint32), single.view(np.uint32)), "EP != single GPU"
+            assert np.array_equal(blk.output.cpu().numpy().view(np.uint32), single_blk.view(np.uint32)), \
+                "EP block != single-GPU block"
         # ... and the oracle
         ref = O.routed_layer(x.cpu().numpy(), sel, wts, bank_arrays(full_bank), O.ACC_F64, O.EXP_SLEEF)
         assert_close_bf16(y, ref, what=f"EP layer rank {rank}")

@@ -386,3 +386,55 @@ def test_router_logits_f32_weights_follow_the_pinned_slice_order():
     assert np.array_equal(O.router_logits(x, wq).view(np.uint32), O.router_logits(x, wbits).view(np.uint32))
     with pytest.raises(TypeError):
         O.router_logits(x, w.astype(np.float64))
+
+
+def test_rms_cascade_matches_pytorch_row():
+    # src/lib.rs:7917 pytorch_rms_cascade_matches_real_row: a real 4096-wide
+    # post-attention row; PyTorch's cascade order gives these variance bits
+    # (and not the high-precision ones) and this inverse.
+    fx = load("pw0079_rms_cascade.json")
+    values = (np.asarray(fx["input_bf16_u16"], dtype=np.uint32) << 16).view(np.float32)
+    assert values.size == 4096
+    variance = np.float32(O.rms_square_sum(values) / np.float32(values.size))
+    assert int(variance.view(np.uint32)) == fx["variance_f32_u32"]
+    assert int(variance.view(np.uint32)) != fx["high_precision_variance_f32_u32"]
+    eps = np.uint32(fx["epsilon_f32_u32"]).view(np.float32)
+    assert int(O.rms_inverse(values, float(eps)).view(np.uint32)) == fx["inverse_f32_u32"]
+
+
+def test_stable_rms_inverse_known_answer_and_rejections():
+    # src/lib.rs:7906 stable_rms_inverse_matches_high_precision_reduction
+    values = np.array([1.0, 2.0, 3.0, 4.0], np.float32)
+    expected = np.float32(1.0) / np.sqrt(np.float32(7.5) + np.float32(1e-5))
+    assert O.rms_inverse(values, 1e-5).view(np.uint32) == np.float32(expected).view(np.uint32)
+    with pytest.raises(ValueError):
+        O.rms_inverse(np.zeros(0, np.float32), 1e-5)
+    with pytest.raises(ValueError):
+        O.rms_inverse(values, 0.0)
+    with pytest.raises(ValueError):
+        O.rms_inverse(np.array([1.0, np.nan, 0.0, 0.0], np.float32), 1e-5)
+
+
+@pytest.mark.parametrize("n", [4, 17, 64, 256, 1000, 4096, 4100, 16384])
+def test_rms_cascade_sum_is_a_reassociation_of_the_exact_sum(n):
+    # the cascade visits every square once: within f32 reassociation error
+    # of the exact sum, for sizes with every kind of tail
+    rng = np.random.default_rng(n)
+    v = rng.standard_normal(n).astype(np.float32)
+    exact = float(np.sum(v.astype(np.float64) ** 2))
+    got = float(O.rms_square_sum(v))
+    assert abs(got - exact) <= 1e-5 * exact
+
+
+def test_rms_norm_rounds_twice_to_bf16():
+    # src/text_endpoint.rs:2951-2954: bf16(bf16(x * inv) * weight)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((3, 512)).astype(np.float32)
+    w = O.round_bf16(rng.standard_normal(512).astype(np.float32))
+    out, inv = O.rms_norm(x, w, 1e-5)
+    for r in range(3):
+        assert inv[r] == O.rms_inverse(x[r], 1e-5)
+        expect = O.round_bf16(O.round_bf16(x[r] * inv[r]) * w)
+        assert np.array_equal(out[r].view(np.uint32), expect.view(np.uint32))
+    y = O.residual_add(x, out)
+    assert np.array_equal(y, O.round_bf16(x + out))
