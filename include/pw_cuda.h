@@ -46,6 +46,8 @@ extern "C" {
 #define PW_ERR_TIMEOUT (-7)      /* a bounded device wait gave up              */
 #define PW_ERR_SCHEDULE (-8)     /* invalid expert schedule / route table      */
 #define PW_ERR_UNSUPPORTED (-9)  /* valid request outside this build's limits  */
+#define PW_ERR_FORMAT (-10)      /* malformed or inconsistent checkpoint file  */
+#define PW_ERR_IO (-11)          /* file open / read / write failure           */
 
 /* ---- device error-flag bits (reference kernels/block_fp8_gemv.metal:40-229;
  *      bits 1..128 keep the reference meanings, 256+ are new) ---- */
@@ -341,6 +343,66 @@ int pw_ep_moe_block(pw_runtime *rt, const pw_norm *post_norm, const pw_router *r
  * then source rank, then the source's order) and expert_begin[E / world + 1]. */
 int pw_ep_plan(const uint32_t *all_offsets, uint32_t world, uint32_t rank, uint32_t experts, uint32_t *n_send,
                uint32_t *n_recv, uint32_t *recv_base, uint32_t *perm, uint32_t *expert_begin);
+
+/* ------------------------------------------------- checkpoint ingestion */
+
+/* A read-only mapped tensor file: a safetensors checkpoint shard or a PWEXPRT1
+ * expert container.  Tensor bytes stay in the mapping (host memory) until
+ * uploaded. */
+typedef struct pw_tensor_file pw_tensor_file;
+
+typedef struct pw_tensor_view {
+  const char *name;   /* valid while the file is open */
+  const char *dtype;  /* safetensors dtype string: "F8_E4M3", "F32", "BF16", ... */
+  uint32_t rank;
+  uint64_t shape[8];
+  const void *data;   /* host pointer into the mapping */
+  uint64_t bytes;
+} pw_tensor_view;
+
+/* Reference: MappedSafetensors::open (src/lib.rs:784-905), fail-closed: the
+ * 8-byte header length (non-zero, <= 256 MiB, a multiple of 8, inside the
+ * file), a strict JSON header with unique keys, known dtypes, non-empty
+ * shapes without zero dimensions, byte counts matching shape x dtype,
+ * in-range non-overlapping payloads, at least one tensor.  `err` (optional)
+ * receives the reason on failure.  Returns PW_ERR_FORMAT / PW_ERR_IO. */
+int pw_safetensors_open(const char *path, pw_tensor_file **out, char *err, size_t err_len);
+/* Reference: verify_expert_container (src/lib.rs:7282-7345) and
+ * docs/EXPERT_CONTAINER.md: PWEXPRT1 magic, schema 1, 64-byte aligned
+ * increasing payloads, every tensor's SHA-256, no trailing bytes. */
+int pw_container_open(const char *path, pw_tensor_file **out, char *err, size_t err_len);
+/* Reference: repack_expert_container (src/lib.rs:7190-7280): copy the named
+ * tensors of a safetensors file, byte for byte, into a new PWEXPRT1 file;
+ * refuses to overwrite; writes a same-directory temporary file, verifies it
+ * and publishes it with a hard link. */
+int pw_container_repack(const char *source, const char *output, const char *const *names, uint32_t n_names,
+                        char *err, size_t err_len);
+void pw_tensor_file_close(pw_tensor_file *f);
+int pw_tensor_file_count(const pw_tensor_file *f, uint32_t *n);
+/* i-th tensor in name order. */
+int pw_tensor_file_at(const pw_tensor_file *f, uint32_t i, pw_tensor_view *out);
+/* Reference: MappedSafetensors::tensor (src/lib.rs:907).  PW_ERR_FORMAT if absent. */
+int pw_tensor_file_find(const pw_tensor_file *f, const char *name, pw_tensor_view *out);
+
+/* Copy one tensor, found in exactly one of `files`, into a new device buffer
+ * on the runtime's device (free it with pw_device_free).  dtype / shape
+ * (optional) must match.  The router's model.layers.N.mlp.gate.weight (F32)
+ * and e_score_correction_bias (F32), and post_attention_layernorm.weight
+ * (BF16) load this way. */
+int pw_tensor_upload(pw_runtime *rt, const pw_tensor_file *const *files, uint32_t n_files, const char *name,
+                     const char *dtype, const uint64_t *shape, uint32_t rank, void **device_ptr, char *err,
+                     size_t err_len);
+int pw_device_free(pw_runtime *rt, void *device_ptr);
+
+/* Load routed experts [first_expert, first_expert + n_experts) of `layer`
+ * from the checkpoint's tensors model.layers.{layer}.mlp.experts.{e}.
+ * {gate,up,down}_proj.weight (F8_E4M3) and their "_scale_inv" grids (F32)
+ * (src/text_endpoint.rs:3067), found across `files`, into one device
+ * allocation, and register them as a bank (pw_bank_create, which validates
+ * every weight byte and scale).  The bank owns that memory; pw_bank_destroy
+ * frees it.  Shapes must agree across experts: gate/up [I, H], down [H, I]. */
+int pw_bank_load(pw_runtime *rt, const pw_tensor_file *const *files, uint32_t n_files, uint32_t layer,
+                 uint32_t first_expert, uint32_t n_experts, pw_expert_bank **out, char *err, size_t err_len);
 
 /* ------------------------------------------------- allocation-free variant */
 

@@ -1,6 +1,7 @@
 """Build the sm_100a CUDA library behind include/pw_cuda.h.
 
-Compiles every mimo_prismwing_b200/csrc/*.cu for sm_100a (`-gencode
+Compiles every mimo_prismwing_b200/csrc/*.cu for sm_100a, and the host-only
+csrc/*.cpp (checkpoint ingestion) with the same driver (`-gencode
 arch=compute_100a,code=sm_100a -lineinfo`, no fast-math: the quantizer and the
 staged SwiGLU rely on IEEE division and rounding) and links
 mimo_prismwing_b200/lib/libpw_cuda.so in-tree.  Objects go to
@@ -35,13 +36,13 @@ def _stale(target: str, deps: list[str]) -> bool:
 def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     os.makedirs(os.path.dirname(LIB), exist_ok=True)
-    sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
     headers = glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
         glob.glob(os.path.join(ROOT, "include", "*.h"))
     objects = []
     jobs = []
     for src in sources:
-        obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+        obj = os.path.join(BUILD, os.path.splitext(os.path.basename(src))[0] + ".o")
         objects.append(obj)
         if force or _stale(obj, [src] + headers):
             cmd = [NVCC] + ARCH + FLAGS + ["-c", src, "-o", obj]

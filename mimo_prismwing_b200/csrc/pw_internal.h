@@ -12,6 +12,12 @@
 
 namespace pw {
 
+// The CUDA device of a runtime (PW_ERR_ARGUMENT for a null runtime).
+int runtime_device(const pw_runtime *rt, int *device);
+// A bank loaded from checkpoint files owns its weights' device memory
+// (one allocation, freed by pw_bank_destroy).
+void bank_adopt_memory(pw_expert_bank *bank, void *device_block);
+
 // Launch a kernel, marked for programmatic dependent launch when the calling
 // thread has enabled it (routed-layer chains); otherwise a plain launch.
 bool pdl_enabled();

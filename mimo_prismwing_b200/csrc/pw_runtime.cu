@@ -134,6 +134,14 @@ struct pw_runtime {
   uint16_t *silu_lut = nullptr;   // staged silu of every bf16 pattern (built on first use)
 };
 
+namespace pw {
+int runtime_device(const pw_runtime *rt, int *device) {
+  if (!rt || !device) return PW_ERR_ARGUMENT;
+  *device = rt->device;
+  return PW_OK;
+}
+}  // namespace pw
+
 namespace {
 enum ProfClass { P_QUANT, P_ROUTER, P_SCHED, P_GATEUP, P_DOWN, P_COMBINE, P_PROJ };
 
@@ -156,6 +164,7 @@ struct ProfScope {
 
 struct pw_expert_bank {
   pw_runtime *rt = nullptr;
+  void *owned = nullptr;  // weights uploaded by pw_bank_load (freed with the bank)
   uint32_t n = 0;
   uint32_t hidden = 0, inter = 0;
   void *d_table = nullptr;  // 6 arrays of n pointers
@@ -163,6 +172,12 @@ struct pw_expert_bank {
   BankTable table{};
   std::vector<pw_expert_weights> host;
 };
+
+namespace pw {
+void bank_adopt_memory(pw_expert_bank *bank, void *device_block) {
+  if (bank) bank->owned = device_block;
+}
+}  // namespace pw
 
 namespace {
 
@@ -1226,10 +1241,11 @@ int pw_bank_create(pw_runtime *rt, const pw_expert_weights *experts, uint32_t n_
 
 void pw_bank_destroy(pw_expert_bank *bank) {
   if (!bank) return;
-  if (bank->d_table || bank->d_maps) {
+  if (bank->d_table || bank->d_maps || bank->owned) {
     cudaSetDevice(bank->rt->device);
     if (bank->d_table) cudaFree(bank->d_table);
     if (bank->d_maps) cudaFree(bank->d_maps);
+    if (bank->owned) cudaFree(bank->owned);
   }
   delete bank;
 }
