@@ -226,6 +226,16 @@ int pw_fp8_linear(pw_runtime *rt, const pw_fp8_tensor *w, uint32_t layout, const
 int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x, uint32_t width,
                       float *y, uint32_t mem, pw_stats *stats);
 
+/* Reference: dense_mlp src/text_endpoint.rs:4266, the dense MLP of layer 0:
+ * gate and up [I, H], staged bf16 SwiGLU, down [H, I], each projection an
+ * fp8_linear (dynamic FP8 input, block-scaled, bf16-rounded output); for
+ * MiMo-V2.5 I = 16384, H = 4096.  x [rows, H] -> y [rows, H].  The same
+ * arithmetic as pw_expert_forward; intermediate sizes above 4096 (up to
+ * 65536) run the down projection over 4096-column slices of its input axis,
+ * whose sums are added in slice order before the bf16 round. */
+int pw_dense_mlp(pw_runtime *rt, const pw_expert_weights *w, const float *x, uint32_t rows, float *y, uint32_t mem,
+                 pw_stats *stats);
+
 /* Reference: route_mlp src/text_endpoint.rs:4342 + pytorch_noaux_routes :4394
  * (f32 logits, SLEEF-u10 sigmoid, top-k of score+bias, weights = score /
  * (pairwise sum of the k chosen + 1e-20)).  top_k must be 8.  Logits are f32

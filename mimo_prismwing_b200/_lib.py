@@ -60,6 +60,7 @@ def _bind(L: ctypes.CDLL) -> None:
     L.pw_ep_plan.argtypes = [vp, u32, u32, u32, vp, vp, vp, vp, vp]
     L.pw_ep_moe_layer.argtypes = [vp, vp, vp, vp, u32, vp, vp, vp, u32, vp]
     L.pw_rms_norm.argtypes = [vp, vp, vp, u32, vp, vp, u32, vp]
+    L.pw_dense_mlp.argtypes = [vp, vp, vp, u32, vp, u32, vp]
     L.pw_moe_block.argtypes = [vp, vp, vp, vp, vp, u32, vp, vp, vp, u32, vp]
     L.pw_ep_moe_block.argtypes = [vp, vp, vp, vp, vp, u32, vp, vp, vp, u32, vp]
     L.pw_set_profiling.argtypes = [vp, i32]

@@ -155,9 +155,14 @@ struct BankTable {
 };
 
 // Host: encode the 2-D TMA map of one row-major e4m3 matrix [rows, cols]
-// (box 128 B x box_rows, 128B swizzle).  Returns false on failure.
+// (box 128 B x box_rows, 128B swizzle).  row_stride (bytes, 0 = cols) lets the
+// map cover a column slice of a wider matrix.  Returns false on failure.
 bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows,
-                       uint32_t box_kb = 0);
+                       uint32_t box_kb = 0, uint32_t row_stride = 0);
+// y[i] = (bf16-rounded if round) sum over the n_parts partials p[k * n + i],
+// added in k order.
+cudaError_t launch_sum_partials(const float *p, uint32_t n_parts, uint64_t n, float *y, uint32_t round,
+                                uint32_t *flags, cudaStream_t stream);
 uint32_t map_box_rows(uint32_t layout);
 // chunk: tokens per GEMV/GEMM group (8 for the GEMV, gemm_tc_tokens(2) for the GEMM)
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,

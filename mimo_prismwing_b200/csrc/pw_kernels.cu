@@ -172,6 +172,31 @@ cudaError_t launch_rms_quantize(const float *x, uint32_t rows, uint32_t cols, co
                        inv, flags);
 }
 
+// ---------------------------------------------------------- partial sums
+// A projection computed over slices of its K axis (the dense MLP's 16384-wide
+// down projection): the slice sums are added in slice order, then rounded.
+__global__ void k_sum_partials(const float *__restrict__ p, uint32_t n_parts, uint64_t n, float *__restrict__ y,
+                               uint32_t round, uint32_t *flags) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    float acc = p[i];
+    for (uint32_t k = 1; k < n_parts; ++k) acc = __fadd_rn(acc, p[k * n + i]);
+    if (round) acc = round_bf16(acc);
+    if (!finite(acc)) raise_flag(flags, PW_FLAG_NONFINITE_ROUND);
+    y[i] = acc;
+  }
+}
+
+cudaError_t launch_sum_partials(const float *p, uint32_t n_parts, uint64_t n, float *y, uint32_t round,
+                                uint32_t *flags, cudaStream_t stream) {
+  if (n_parts == 0) return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+  uint64_t blocks = (n + 255u) / 256u;
+  if (blocks > 148u * 8u) blocks = 148u * 8u;
+  return launch_kernel(k_sum_partials, dim3((unsigned)blocks), dim3(256), 0, stream, p, n_parts, n, y, round, flags);
+}
+
 // --------------------------------------------------------------- bf16 round
 __global__ void k_round_bf16(float *v, uint32_t n, uint32_t *flags) {
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {

@@ -71,11 +71,11 @@ bool encode_act_maps(CUtensorMap (&out)[4], const void *base, uint32_t rows, uin
 // box_kb != 0 overrides the k-blocks per box (the tcgen05 GEMM's QKV tiles
 // load {128, 64, 1} boxes).
 bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32_t cols, uint32_t box_rows,
-                       uint32_t box_kb) {
+                       uint32_t box_kb, uint32_t row_stride) {
   EncodeTiledFn fn = encode_fn();
-  if (!fn || cols % 128u) return false;
+  if (!fn || cols % 128u || (row_stride && (row_stride < cols || row_stride % 16u))) return false;
   cuuint64_t dims[3] = {128u, rows, cols / 128u};
-  cuuint64_t strides[2] = {cols, 128u};
+  cuuint64_t strides[2] = {row_stride ? row_stride : cols, 128u};
   cuuint32_t box[3] = {128u, box_rows, box_kb ? box_kb : 256u / box_rows};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
@@ -787,6 +787,7 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
     ProfScope ps(rt, P_QUANT, 1);
     CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream, slots_dev));
   }
+  if (!dn) return PW_OK;  // the caller runs the down projection itself
   GemvArgs d = gemv_args(rt, dn, n_groups, H, I, PW_LAYOUT_PLAIN);
   d.n_groups_dev = n_groups_dev;
   d.x_codes = hc;
@@ -863,6 +864,7 @@ static int enqueue_expert_chain_wide(pw_runtime *rt, const GemvGroup *gu, const 
     else
       CK(launch_quantize(hidden, slots, I, hc, hs, rt->d_flags, rt->stream, slots_dev));
   }
+  if (!dn) return PW_OK;  // the caller runs the down projection itself
   GemmArgs D{};
   D.g = gemv_args(rt, dn, n_groups, H, I, PW_LAYOUT_PLAIN);
   D.g.n_groups_dev = n_groups_dev;
@@ -947,6 +949,136 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
   }
   const uint64_t wb = 3ull * H * I + 4ull * (w->gate.scale_rows * w->gate.scale_cols * 2u +
                                              w->down.scale_rows * w->down.scale_cols);
+  return call.finish(wb);
+}
+
+// --------------------------------------------------------------- dense MLP
+// Reference: dense_mlp src/text_endpoint.rs:4266 (layer 0: gate and up
+// [16384, 4096], staged SwiGLU, down [4096, 16384], each an fp8_linear).  The
+// same chain as a routed expert at weight 1; an intermediate size above 4096
+// runs the down projection over 4096-column slices of its K axis (the
+// hidden's codes for a slice are copied contiguous, the weight slice is read
+// in place through a strided TMA map) and adds the slice sums in slice order
+// before the bf16 round.
+constexpr uint32_t kDenseSlice = 4096;
+
+int pw_dense_mlp(pw_runtime *rt, const pw_expert_weights *w, const float *x, uint32_t rows, float *y, uint32_t mem,
+                 pw_stats *stats) {
+  if (!rt) return PW_ERR_ARGUMENT;
+  if (!x || !y || !w) return fail(rt, PW_ERR_ARGUMENT, "null argument");
+  int s;
+  if ((s = check_projection(rt, &w->gate, PW_LAYOUT_PLAIN)) != PW_OK) return s;
+  if ((s = check_projection(rt, &w->up, PW_LAYOUT_PLAIN)) != PW_OK) return s;
+  const uint32_t H = w->gate.cols, I = w->gate.rows;
+  if (w->up.rows != I || w->up.cols != H) return fail(rt, PW_ERR_SHAPE, "gate and up shapes disagree");
+  const pw_fp8_tensor &dw = w->down;
+  if (!tensor_ok(&dw) || dw.rows != H || dw.cols != I || H % 128u || dw.scale_rows != H / 128u ||
+      dw.scale_cols != I / 128u)
+    return fail(rt, PW_ERR_SHAPE, "down projection must be [%u, %u] with a [%u, %u] scale grid", H, I, H / 128u,
+                I / 128u);
+  if (I > 65536u) return fail(rt, PW_ERR_UNSUPPORTED, "intermediate sizes above 65536 are not supported");
+  if (rows == 0) return fail(rt, PW_ERR_SHAPE, "dense MLP needs at least one row");
+  if (I <= kDenseSlice) return pw_expert_forward(rt, w, x, rows, y, mem, stats);
+  CK(cudaSetDevice(rt->device));
+  const uint32_t nsl = (I + kDenseSlice - 1u) / kDenseSlice;
+  std::vector<CUtensorMap> hmaps(2 + nsl);
+  {
+    const pw_fp8_tensor *ts[2] = {&w->gate, &w->up};
+    if (!encode_maps(rt, ts, 2, PW_LAYOUT_PLAIN, hmaps.data())) return PW_ERR_CUDA;
+    for (uint32_t c = 0; c < nsl; ++c) {
+      const uint32_t Kc = I - c * kDenseSlice < kDenseSlice ? I - c * kDenseSlice : kDenseSlice;
+      if (!encode_weight_map(&hmaps[2 + c], dw.weight + (size_t)c * kDenseSlice, H, Kc, 128u, 0u, I))
+        return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for a down-projection slice");
+    }
+  }
+  const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
+  const bool wide = rows >= kWideProjection;
+  Call call{rt, mem, stats, 0};
+  if ((s = call.begin()) != PW_OK) return s;
+  Arena ar;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1) {
+      if ((s = ensure_scratch(rt, ar.off)) != PW_OK) return s;
+      ar = Arena{static_cast<char *>(rt->scratch), 0};
+    }
+    float *dx = call.host() ? ar.take<float>((size_t)rows * H) : const_cast<float *>(x);
+    float *dy = call.host() ? ar.take<float>((size_t)rows * H) : y;
+    uint8_t *xc = ar.take<uint8_t>((size_t)rows * H);
+    float *xs = ar.take<float>((size_t)rows * H / 128u);
+    float *hid = fused ? nullptr : ar.take<float>((size_t)rows * I);
+    float *gt = fused && !wide ? nullptr : ar.take<float>((size_t)rows * I);
+    float *ut = fused && !wide ? nullptr : ar.take<float>((size_t)rows * I);
+    uint8_t *hc = ar.take<uint8_t>((size_t)rows * I);
+    float *hs = ar.take<float>((size_t)rows * I / 128u);
+    uint8_t *hcc = ar.take<uint8_t>((size_t)rows * kDenseSlice);
+    float *hsc = ar.take<float>((size_t)rows * kDenseSlice / 128u);
+    float *part = ar.take<float>((size_t)nsl * rows * H);
+    CUtensorMap *dm = ar.take<CUtensorMap>(2 + nsl);
+    const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
+    std::vector<GemvGroup> gu = width_groups(rows, w->gate, &w->up, dm, dm ? dm + 1 : nullptr, chunk);
+    std::vector<std::vector<GemvGroup>> dn(nsl);
+    for (uint32_t c = 0; c < nsl; ++c) {
+      pw_fp8_tensor sl = dw;
+      sl.weight = dw.weight + (size_t)c * kDenseSlice;
+      sl.scale = dw.scale + (size_t)c * (kDenseSlice / 128u);
+      dn[c] = width_groups(rows, sl, nullptr, dm ? dm + 2 + c : nullptr, nullptr,
+                           wide ? (uint32_t)gemm_tc_tokens(0) : 8u);
+    }
+    GemvGroup *dgu = ar.take<GemvGroup>(gu.size());
+    std::vector<GemvGroup *> ddn(nsl);
+    for (uint32_t c = 0; c < nsl; ++c) ddn[c] = ar.take<GemvGroup>(dn[c].size());
+    if (pass == 0) continue;
+    if (call.host() && (s = call.stage_in(dx, x, (size_t)rows * H * 4)) != PW_OK) return s;
+    CK(cudaMemcpyAsync(dm, hmaps.data(), hmaps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, rt->stream));
+    CK(cudaMemcpyAsync(dgu, gu.data(), gu.size() * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
+    for (uint32_t c = 0; c < nsl; ++c)
+      CK(cudaMemcpyAsync(ddn[c], dn[c].data(), dn[c].size() * sizeof(GemvGroup), cudaMemcpyHostToDevice,
+                         rt->stream));
+    {
+      ProfScope ps(rt, P_QUANT, 1);
+      CK(launch_quantize(dx, rows, H, xc, xs, rt->d_flags, rt->stream));
+    }
+    // gate/up, staged SwiGLU and the hidden's FP8 codes (no down projection)
+    if (wide)
+      s = enqueue_expert_chain_wide(rt, dgu, nullptr, (uint32_t)gu.size(), nullptr, rows, H, I, xc, xs, hid, gt, ut,
+                                    hc, hs, nullptr, 1, gu.size());
+    else
+      s = enqueue_expert_chain(rt, dgu, nullptr, (uint32_t)gu.size(), nullptr, rows, H, I, nullptr, xc, xs, hid, gt,
+                               ut, hc, hs, nullptr, 1, gu.size());
+    if (s != PW_OK) return s;
+    for (uint32_t c = 0; c < nsl; ++c) {
+      const uint32_t Kc = I - c * kDenseSlice < kDenseSlice ? I - c * kDenseSlice : kDenseSlice;
+      CK(cudaMemcpy2DAsync(hcc, Kc, hc + (size_t)c * kDenseSlice, I, Kc, rows, cudaMemcpyDeviceToDevice,
+                           rt->stream));
+      CK(cudaMemcpy2DAsync(hsc, (Kc / 128u) * 4u, hs + (size_t)c * (kDenseSlice / 128u), (I / 128u) * 4u,
+                           (Kc / 128u) * 4u, rows, cudaMemcpyDeviceToDevice, rt->stream));
+      GemvArgs d = gemv_args(rt, ddn[c], (uint32_t)dn[c].size(), H, Kc, PW_LAYOUT_PLAIN);
+      d.scale_cols = I / 128u;  // the slice's scales are columns of the full grid
+      d.x_codes = hcc;
+      d.x_scales = hsc;
+      d.out = part + (size_t)c * rows * H;
+      d.out_stride = H;
+      d.round_bf16 = 0;
+      ProfScope ps(rt, P_DOWN, 1);
+      if (wide) {
+        GemmArgs D{};
+        D.g = d;
+        if (!encode_act_maps(D.xmap, hcc, rows, Kc))
+          return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for the hidden codes");
+        CK(launch_gemm_tc(0, D, grid_for(rt, (uint64_t)dn[c].size() * (H / 128u)), rt->stream));
+      } else {
+        int grid = 0;
+        if ((s = gemv_launch_setup(rt, d, (uint64_t)dn[c].size() * (H / 128u), 1, grid)) != PW_OK) return s;
+        CK(launch_gemv(0, d, grid, rt->stream));
+      }
+    }
+    {
+      ProfScope ps(rt, P_COMBINE, 1);
+      CK(launch_sum_partials(part, nsl, (uint64_t)rows * H, dy, 1u, rt->d_flags, rt->stream));
+    }
+    if (call.host() && (s = call.stage_out(y, dy, (size_t)rows * H * 4)) != PW_OK) return s;
+  }
+  const uint64_t wb = 3ull * H * I + 4ull * (w->gate.scale_rows * w->gate.scale_cols * 2u + dw.scale_rows * dw.scale_cols);
   return call.finish(wb);
 }
 

@@ -296,6 +296,18 @@ class WideMoeRuntime:
                                               ctypes.c_void_p(out.data_ptr()), mem, ctypes.byref(st)))
         return Execution(out, st.wall_ms, st.device_ms, weight_bytes=st.weight_bytes)
 
+    def dense_mlp(self, x, gate: WideProjectionBinding, up: WideProjectionBinding,
+                  down: WideProjectionBinding) -> Execution:
+        """dense_mlp (src/text_endpoint.rs:4266): layer 0's dense FP8 MLP
+        (gate/up [16384, 4096], down [4096, 16384] for MiMo-V2.5)."""
+        x = _as_f32(x)
+        x, out, mem = self._io(x, (x.shape[0], down.rows))
+        w = ExpertWeights(gate.c(), up.c(), down.c())
+        st = Stats()
+        self._check(self._L.pw_dense_mlp(self._rt, ctypes.byref(w), ctypes.c_void_p(x.data_ptr()), x.shape[0],
+                                         ctypes.c_void_p(out.data_ptr()), mem, ctypes.byref(st)))
+        return Execution(out, st.wall_ms, st.device_ms, weight_bytes=st.weight_bytes)
+
     def route(self, x, router_weight: torch.Tensor, bias: torch.Tensor):
         """route_mlp + pytorch_noaux_routes (src/text_endpoint.rs:4342-4470).
 

@@ -138,3 +138,34 @@ def test_moe_block_rejects_aliasing_and_bad_norm(rt):
     with pytest.raises(PrismwingError) as e:  # epsilon must be positive
         rt.moe_block(x, _bf16_weight(512, 1).cuda(), -1.0, w, bias, handle)
     assert e.value.kind == "argument"
+
+
+@pytest.mark.parametrize("width", [1, 8, 40])
+def test_dense_mlp_layer0_shape_vs_oracle(rt, width):
+    # dense_mlp (src/text_endpoint.rs:4266): gate/up [16384, 4096], staged
+    # SwiGLU, down [4096, 16384]; widths 1 and 8 on the GEMV, 40 on the
+    # tcgen05 GEMM; the 16384-wide down projection runs in 4096-column slices
+    from gpu_helpers import assert_close_bf16, bank_arrays
+    from mimo_prismwing_b200 import synth
+    g, u, d = synth.expert(4096, 16384, 44, "cuda")
+    x = synth.activations(width, 4096, 90 + width, "cuda")
+    ex = rt.dense_mlp(x, g, u, d)
+    y = H(ex.output)
+    (gw, gs, uw, us, dw, ds), = bank_arrays([(g, u, d)])
+    take = slice(None) if width <= 8 else slice(0, width, 5)  # keep the f64 oracle quick
+    xc, xs, _ = O.dynamic_fp8(H(x)[take])
+    act = O.staged_swiglu(O.blockscaled_linear(gw, gs, xc, xs), O.blockscaled_linear(uw, us, xc, xs), O.EXP_SLEEF)
+    hc, hs, _ = O.dynamic_fp8(act)
+    ref = O.round_bf16(O.blockscaled_linear(dw, ds, hc, hs))
+    assert_close_bf16(y[take], ref, what=f"dense MLP w{width}")
+    assert ex.weight_bytes == 3 * 16384 * 4096 + 4 * (2 * 128 * 32 + 32 * 128)
+    # host I/O: same bits
+    assert np.array_equal(rt.dense_mlp(x.cpu(), g, u, d).output.numpy(), y)
+
+
+def test_dense_mlp_small_intermediate_equals_expert_forward(rt):
+    # at I <= 4096 the dense MLP is the routed expert's chain exactly
+    from mimo_prismwing_b200 import synth
+    g, u, d = synth.expert(1024, 2048, 45, "cuda")
+    x = synth.activations(5, 1024, 46, "cuda")
+    assert torch.equal(rt.dense_mlp(x, g, u, d).output, rt.expert_forward(x, g, u, d).output)
