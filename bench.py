@@ -225,57 +225,108 @@ def cpu_oracle_experts(bank, router, x, n_experts, threads):
 
 
 # ------------------------------------------------- configs[0], [1], [3]
-def bench_configs(rt, dev, hbm, tflops_fp8, iters=20):
-    """The single-projection configs on one GPU, device time per call from
-    CUDA events around each kernel class (the runtime's profiler); weights
-    rotate over copies that together exceed 2x L2 (126 MB)."""
+def bench_configs(rt, dev, hbm, tflops_fp8, stream, iters=30):
+    """The single-projection configs on one GPU.  Each call is measured two
+    ways: per launch (CUDA events on the runtime's stream around back-to-back
+    asynchronous calls through the C ABI; each call is its whole kernel chain,
+    so launch latency between calls counts) and as a CUDA graph (one pass over
+    every weight copy captured once and replayed; per call = replay time /
+    calls).  Weights rotate over copies that together exceed 2x L2 (126 MB),
+    so every call streams its weights from HBM.  `kernels_us` is the device
+    time the runtime's profiler attributes to each kernel class (events
+    around each launch group, no PDL)."""
     import torch
     from mimo_prismwing_b200 import synth
     out = {}
 
-    def timed(fn, keys, n):
+    def timed_events(fn, n):
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                fn(i)
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(n):
+                fn(i)
+            e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / n * 1e3
+
+    def timed_graph(fn, copies, reps=8):
+        with torch.cuda.stream(stream):
+            for i in range(copies):  # every call's descriptors exist before the capture
+                fn(i)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(copies):
+                fn(i)
+        with torch.cuda.stream(stream):
+            g.replay()
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        e1.synchronize()
+        del g
+        return e0.elapsed_time(e1) / (reps * copies) * 1e3
+
+    def profiled(fn, keys, n=10):
         for i in range(3):
             fn(i)
         rt.set_profiling(True)
-        tot = 0.0
+        tot = {k: 0.0 for k in keys}
         for i in range(n):
             fn(i)
             p = rt.last_profile()
-            tot += sum(p[k] for k in keys)
+            for k in keys:
+                tot[k] += p[k]
         rt.set_profiling(False)
-        return tot / n * 1e3  # us
+        return {k.replace("_ms", ""): round(v / n * 1e3, 2) for k, v in tot.items()}
+
+    def row(b, us_launch, us_graph, kern, flops=None):
+        best = min(us_launch, us_graph)
+        r = {"us_per_launch": round(us_launch, 2), "us_graph": round(us_graph, 2), "bytes": b,
+             "gbs": round(b / best / 1e3, 1), "hbm_frac": round(b / best / 1e3 / hbm, 4), "kernels_us": kern}
+        if flops:
+            r["tflops"] = round(flops / best / 1e6, 1)
+            if tflops_fp8:
+                r["tensor_frac"] = round(flops / best / 1e6 / tflops_fp8, 4)
+        return r
 
     # configs[0]: readable GEMV [2048 x 4096], x [1 x 4096] f32 (src/lib.rs:1272)
     c0 = [synth.projection(2048, 4096, 100 + i, dev) for i in range(32)]
     x1 = synth.activations(1, 4096, 5, dev)
-    us = timed(lambda i: rt.fp8_gemv(x1, c0[i % 32]), ["projection_ms"], iters)
-    b0 = 8407040
-    out["c0_gemv_2048x4096_w1"] = {"us": round(us, 2), "gbs": round(b0 / us / 1e3, 1),
-                                   "hbm_frac": round(b0 / us / 1e3 / hbm, 4), "bytes": b0}
+    y1 = torch.empty((1, 2048), device=dev)
+    f0 = lambda i: rt.fp8_gemv(x1, c0[i % 32], asynchronous=True, out=y1)
+    out["c0_gemv_2048x4096_w1"] = row(8407040, timed_events(f0, iters * 4), timed_graph(f0, 32),
+                                      profiled(lambda i: rt.fp8_gemv(x1, c0[i % 32]), ["projection_ms"]))
     del c0
     # configs[1]: one routed expert at widths 1, 2, 4, 8 (quantize, fused gate/up, down)
     ex = [synth.expert(HIDDEN, INTER, 200 + i, dev) for i in range(12)]
     gu_b, dn_b = expert_bytes()
     for w in (1, 2, 4, 8):
         xw = synth.activations(w, HIDDEN, 6 + w, dev)
-        us = timed(lambda i: rt.expert_forward(xw, *ex[i % 12]), ["quantize_ms", "gate_up_ms", "down_ms"], iters)
-        b = gu_b + dn_b + w * (8192 + 16384)
-        out[f"c1_expert_w{w}"] = {"us": round(us, 2), "gbs": round(b / us / 1e3, 1),
-                                  "hbm_frac": round(b / us / 1e3 / hbm, 4), "bytes": b}
+        yw = torch.empty((w, HIDDEN), device=dev)
+        f1 = lambda i: rt.expert_forward(xw, *ex[i % 12], asynchronous=True, out=yw)
+        out[f"c1_expert_w{w}"] = row(gu_b + dn_b + w * (8192 + 16384), timed_events(f1, iters * 2),
+                                     timed_graph(f1, 12),
+                                     profiled(lambda i: rt.expert_forward(xw, *ex[i % 12]),
+                                              ["quantize_ms", "gate_up_ms", "down_ms"]))
     del ex
     # configs[3]: fused QKV [13568 x 4096] (full layout) at widths 1, 8, 2048
     qk = [synth.full_qkv(300 + i, dev) for i in range(6)]
     for w in (1, 8, 2048):
         xw = synth.activations(w, HIDDEN, 9 + w, dev)
-        us = timed(lambda i: rt.execute_fp8_linear(xw, qk[i % 6], full_qkv_layout=True),
-                   ["quantize_ms", "projection_ms"], iters if w < 2048 else 10)
-        b = 55574528 + 13824 + w * (8192 + 4 * 13568)
-        flops = 2 * w * 13568 * 4096
-        row = {"us": round(us, 2), "gbs": round(b / us / 1e3, 1), "hbm_frac": round(b / us / 1e3 / hbm, 4),
-               "tflops": round(flops / us / 1e6, 1)}
-        if w == 2048 and tflops_fp8:
-            row["tensor_frac"] = round(flops / us / 1e6 / tflops_fp8, 4)
-        out[f"c3_qkv_full_w{w}"] = row
+        yw = torch.empty((w, 13568), device=dev)
+        f3 = lambda i: rt.execute_fp8_linear(xw, qk[i % 6], full_qkv_layout=True, asynchronous=True, out=yw)
+        out[f"c3_qkv_full_w{w}"] = row(55574528 + 13824 + w * (8192 + 4 * 13568),
+                                       timed_events(f3, iters if w < 2048 else 12), timed_graph(f3, 6),
+                                       profiled(lambda i: rt.execute_fp8_linear(xw, qk[i % 6], full_qkv_layout=True),
+                                                ["quantize_ms", "projection_ms"]),
+                                       flops=2 * w * 13568 * 4096)
     del qk
     torch.cuda.empty_cache()
     return out
@@ -444,11 +495,16 @@ def run_ours(args, rank, world, local_rank):
         dist.broadcast_object_list(box, src=0)
         rt.ep_init(rank, world, box[0], timeout_ms=120000, max_tokens=PREFILL_TOKENS // world, hidden=HIDDEN,
                    local_experts=EXPERTS // world, nccl_transport=args.ep_transport == "nccl")
-    layers = Layers(rt, rank, world, args.banks, dev)
     stream = torch.cuda.Stream(device=dev)
     rt.set_stream(stream)
     hbm, peak_kind = peaks()
     tflops_fp8 = fp8_peak_tflops(dev) if rank == 0 else None
+    if args.configs_only:  # configs[0]/[1]/[3] alone (one GPU), for profiling runs
+        print(json.dumps({"configs": bench_configs(rt, dev, hbm, tflops_fp8, stream),
+                          "fp8_peak_tflops": tflops_fp8}), flush=True)
+        rt.close()
+        return
+    layers = Layers(rt, rank, world, args.banks, dev)
 
     def barrier():
         if world > 1:
@@ -610,7 +666,7 @@ def run_ours(args, rank, world, local_rank):
 
     configs = None
     if world == 1 and not args.skip_configs:
-        configs = bench_configs(rt, dev, hbm, tflops_fp8)
+        configs = bench_configs(rt, dev, hbm, tflops_fp8, stream)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -697,6 +753,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the start-up parity check (profiling runs)")
     ap.add_argument("--skip-configs", action="store_true", help="skip the configs[0]/[1]/[3] sub-benchmarks")
+    ap.add_argument("--configs-only", action="store_true", help="run only the configs[0]/[1]/[3] sub-benchmarks")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange: peer-memory stores (default) or NCCL send/recv")
     # smaller cases for ncu captures only; the metric is quoted at the defaults

@@ -128,7 +128,8 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const EpArgs e, const uint3
 }
 
 // ---------------------------------------------------------------------- plan
-// One CTA.  Outputs (expert order j): perm[j] = received row (slot s, row),
+// One CTA (the plan is a few hundred words; what takes time is the wait for
+// the slowest source's rows).  Outputs (expert order j): perm[j] = received row (slot s, row),
 // src_rank[j], src_place[j]; groups over each local expert's rows in chunks
 // of `chunk`; *n_groups; *p_recv = rows received and p_recv[1] = local
 // experts with at least one row.  Rows beyond `cap` are an error.
@@ -202,18 +203,22 @@ __global__ void __launch_bounds__(1024) k_ep_plan(const EpArgs e, BankTable bank
     }
     return;
   }
-  for (uint32_t le = threadIdx.x; le < L; le += blockDim.x) {
-    uint32_t j = beg[le];
+  // a warp per local expert: its rows (source rank, then the source's
+  // order) and its groups, lanes striding over them
+  const uint32_t lane = threadIdx.x % 32u, nwarps = blockDim.x / 32u;
+  for (uint32_t le = threadIdx.x / 32u; le < L; le += nwarps) {
+    uint32_t j0 = beg[le];
     for (uint32_t s = 0; s < G; ++s) {
       const uint32_t c = cnt[s * L + le], p0 = pre[s * L + le];
-      for (uint32_t k = 0; k < c; ++k, ++j) {
-        perm[j] = s * w.slot_rows + p0 + k;
-        src_rank[j] = s;
-        src_place[j] = base[s] + p0 + k;
+      for (uint32_t k = lane; k < c; k += 32u) {
+        perm[j0 + k] = s * w.slot_rows + p0 + k;
+        src_rank[j0 + k] = s;
+        src_place[j0 + k] = base[s] + p0 + k;
       }
+      j0 += c;
     }
     const uint32_t t = beg[le + 1] - beg[le];
-    for (uint32_t c = 0; c * chunk < t; ++c) {
+    for (uint32_t c = lane; c * chunk < t; c += 32u) {
       GemvGroup g;
       g.tok_begin = beg[le] + c * chunk;
       g.count = min(chunk, t - c * chunk);

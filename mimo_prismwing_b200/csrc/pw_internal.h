@@ -89,6 +89,7 @@ struct GemvArgs {
   uint64_t peer_off;             //   peer_base[row_rank[p]] + peer_off + row_place[p] * 2 * out_stride
   const uint32_t *row_rank;      //   (another GPU's window, plain 16-byte stores over NVLink)
   const uint32_t *row_place;
+  uint32_t max_count;            // largest group token count (readable GEMV width bucket; 0: up to 8)
   uint32_t splits;               // GEMV split-K over the 8-leaf K tree: 1, 2, 4 or 8
   float *split_ws;               //   partial sums [tile][split][mats][128 rows][8 tokens]
   uint32_t *split_cnt;           //   per-tile arrival counters (zero; reset by the last CTA)
@@ -111,8 +112,11 @@ cudaError_t launch_gather_rows(const uint8_t *codes, const float *scales, const 
 // Kernel launchers (pw_kernels.cu).  All enqueue on `stream` and return the
 // launch status.
 // rows_dev (optional): the row count lives on the device; `rows` bounds it.
+// zero (optional): n_zero words cleared by the kernel before anything after it
+// in a PDL chain reads them (the chain's split-K counters).
 cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_t *codes, float *scales,
-                            uint32_t *flags, cudaStream_t stream, const uint32_t *rows_dev = nullptr);
+                            uint32_t *flags, cudaStream_t stream, const uint32_t *rows_dev = nullptr,
+                            uint32_t *zero = nullptr, uint32_t n_zero = 0);
 // kind: 0 = block-scaled (quantized x) over each group's w0/s0, 1 = readable
 // (f32 x), 2 = fused gate/up SwiGLU over w0/s0 and w1/s1, 3 = block-scaled
 // over w1/s1 (the unfused up projection)

@@ -21,9 +21,12 @@ void set_pdl(bool on) { t_pdl = on; }
 // bit-exact with the reference; lane l holds values 4l..4l+3.
 __global__ void k_quantize(const float *__restrict__ x, uint64_t groups, uint8_t *__restrict__ codes,
                            float *__restrict__ scales, uint32_t *flags, const uint32_t *rows_dev,
-                           uint32_t groups_per_row) {
+                           uint32_t groups_per_row, uint32_t *zero, uint32_t n_zero) {
   pdl_wait();
   pdl_launch_dependents();
+  // the first kernel of a chain clears the next kernels' split-K counters
+  if (zero && blockIdx.x == 0)
+    for (uint32_t i = threadIdx.x; i < n_zero; i += blockDim.x) zero[i] = 0u;
   if (rows_dev) groups = min(groups, (uint64_t)*rows_dev * groups_per_row);
   const uint64_t warp_global = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32u;
   const uint32_t lane = threadIdx.x % 32u;
@@ -45,15 +48,17 @@ __global__ void k_quantize(const float *__restrict__ x, uint64_t groups, uint8_t
 }
 
 cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_t *codes, float *scales,
-                            uint32_t *flags, cudaStream_t stream, const uint32_t *rows_dev) {
+                            uint32_t *flags, cudaStream_t stream, const uint32_t *rows_dev, uint32_t *zero,
+                            uint32_t n_zero) {
   if (cols % 128u) return cudaErrorInvalidValue;
   const uint64_t groups = (uint64_t)rows * (cols / 128u);
-  if (groups == 0) return cudaSuccess;
+  if (groups == 0 && !zero) return cudaSuccess;
   const int threads = 256;
   uint64_t blocks = (groups * 32u + threads - 1) / threads;
   if (blocks > 148u * 16u) blocks = 148u * 16u;
+  if (blocks == 0) blocks = 1;
   return launch_kernel(k_quantize, dim3((unsigned)blocks), dim3(threads), 0, stream, x, groups, codes, scales, flags,
-                       rows_dev, cols / 128u);
+                       rows_dev, cols / 128u, zero, n_zero);
 }
 
 // ------------------------------------------------- RMSNorm + quantization

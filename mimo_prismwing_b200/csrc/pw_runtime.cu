@@ -16,6 +16,7 @@
 #include <new>
 #include <string>
 #include <thread>
+#include <unordered_map>
 #include <vector>
 
 #include <cuda.h>
@@ -132,6 +133,14 @@ struct pw_runtime {
   float *split_ws = nullptr;      // GEMV split-K partial sums (allocated on first use)
   uint32_t *split_cnt = nullptr;  // and per-tile arrival counters
   uint16_t *silu_lut = nullptr;   // staged silu of every bf16 pattern (built on first use)
+  // Device-resident launch descriptors (TMA maps + group records) of the
+  // projections and experts called so far, keyed by what they are built
+  // from, so a repeated call enqueues only its kernels.
+  static constexpr uint32_t kDescSlots = 512, kDescSlotBytes = 4096;
+  uint8_t *desc = nullptr;
+  std::unordered_map<std::string, uint32_t> desc_index;
+  std::vector<std::string> desc_key;
+  uint32_t desc_next = 0;
 };
 
 namespace pw {
@@ -413,7 +422,19 @@ uint32_t gemv_splits(const pw_runtime *rt, uint64_t tiles, uint32_t K, uint32_t 
 
 // Set up a GEMV launch over `tiles` (group, row-tile) pairs: split-K state
 // and the grid.
-int gemv_launch_setup(pw_runtime *rt, GemvArgs &a, uint64_t tiles, int mats, int &grid) {
+int ensure_split_ws(pw_runtime *rt) {
+  if (!rt->split_ws) {
+    CK(cudaMalloc(&rt->split_ws, kSplitWsBytes));
+    CK(cudaMalloc(&rt->split_cnt, kSplitCounters * sizeof(uint32_t)));
+    CK(cudaMemset(rt->split_cnt, 0, kSplitCounters * sizeof(uint32_t)));
+  }
+  return PW_OK;
+}
+
+// counters_cleared: an earlier kernel of the same chain zeroes the counters
+// (launch_quantize's `zero`), so no memset breaks the PDL chain here.
+int gemv_launch_setup(pw_runtime *rt, GemvArgs &a, uint64_t tiles, int mats, int &grid,
+                      bool counters_cleared = false) {
   const uint32_t S = gemv_splits(rt, tiles, a.K, a.layout, mats);
   grid = grid_for(rt, tiles * S);
   if (S == 1u) return PW_OK;
@@ -421,16 +442,101 @@ int gemv_launch_setup(pw_runtime *rt, GemvArgs &a, uint64_t tiles, int mats, int
     grid = grid_for(rt, tiles);
     return PW_OK;
   }
-  if (!rt->split_ws) {
-    CK(cudaMalloc(&rt->split_ws, kSplitWsBytes));
-    CK(cudaMalloc(&rt->split_cnt, kSplitCounters * sizeof(uint32_t)));
-  }
+  int s;
+  if ((s = ensure_split_ws(rt)) != PW_OK) return s;
   // the last CTA of every tile resets its counter; clear them anyway in case
   // an earlier call was cut short
-  CK(cudaMemsetAsync(rt->split_cnt, 0, tiles * sizeof(uint32_t), rt->stream));
+  if (!counters_cleared) CK(cudaMemsetAsync(rt->split_cnt, 0, tiles * sizeof(uint32_t), rt->stream));
   a.splits = S;
   a.split_ws = rt->split_ws;
   a.split_cnt = rt->split_cnt;
+  return PW_OK;
+}
+
+// Launch descriptors of a projection (one matrix) or an expert (gate, up,
+// down) at a given width: TMA maps first, then the group records, whose map
+// pointers point at the maps in the same device slot.
+struct Descs {
+  const CUtensorMap *maps = nullptr;
+  const GemvGroup *gu = nullptr, *dn = nullptr;  // dn: the expert's down groups
+  uint32_t n_gu = 0, n_dn = 0;
+};
+
+// Looks up (or builds and uploads) the descriptors.  `b` (optional) is the
+// second matrix of a fused pair (up), `c` (optional) an expert's down
+// projection.  Maps use `box_rows` rows (and `box_kb` k-blocks when nonzero).
+// Falls back to false when they do not fit a slot; a miss while the stream
+// is being captured is an error (warm the call up first).
+int get_descs(pw_runtime *rt, uint32_t tag, uint32_t width, uint32_t chunk, const pw_fp8_tensor &a,
+              const pw_fp8_tensor *b, const pw_fp8_tensor *c, uint32_t box_rows, uint32_t box_kb, Descs &out,
+              bool &cached) {
+  cached = false;
+  const uint32_t nmaps = 1u + (b ? 1u : 0u) + (c ? 1u : 0u);
+  const uint32_t ng = (width + chunk - 1u) / chunk;
+  const size_t bytes = nmaps * sizeof(CUtensorMap) + (size_t)ng * (c ? 2u : 1u) * sizeof(GemvGroup);
+  if (bytes > pw_runtime::kDescSlotBytes) return PW_OK;
+  std::string key(reinterpret_cast<const char *>(&tag), 4);
+  auto put = [&key](const void *p, size_t n) { key.append(static_cast<const char *>(p), n); };
+  put(&width, 4);
+  put(&chunk, 4);
+  put(&box_rows, 4);
+  put(&box_kb, 4);
+  for (const pw_fp8_tensor *t : {&a, b, c}) {
+    if (t) put(t, sizeof *t);
+    else key.append(sizeof(pw_fp8_tensor), '\0');
+  }
+  auto fill = [&](uint8_t *base) {
+    const CUtensorMap *m = reinterpret_cast<const CUtensorMap *>(base);
+    out.maps = m;
+    const GemvGroup *g = reinterpret_cast<const GemvGroup *>(base + nmaps * sizeof(CUtensorMap));
+    out.gu = g;
+    out.n_gu = ng;
+    out.dn = c ? g + ng : nullptr;
+    out.n_dn = c ? ng : 0u;
+  };
+  auto it = rt->desc_index.find(key);
+  if (it != rt->desc_index.end()) {
+    fill(rt->desc + (size_t)it->second * pw_runtime::kDescSlotBytes);
+    cached = true;
+    return PW_OK;
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  CK(cudaStreamIsCapturing(rt->stream, &cap));
+  if (cap != cudaStreamCaptureStatusNone)
+    return fail(rt, PW_ERR_ARGUMENT, "first call of this shape inside a stream capture: call it once before capturing");
+  if (!rt->desc) {
+    CK(cudaMalloc(&rt->desc, (size_t)pw_runtime::kDescSlots * pw_runtime::kDescSlotBytes));
+    rt->desc_key.assign(pw_runtime::kDescSlots, std::string());
+  }
+  const uint32_t slot = rt->desc_next;
+  rt->desc_next = (rt->desc_next + 1u) % pw_runtime::kDescSlots;
+  if (!rt->desc_key[slot].empty()) {
+    // evicting: kernels enqueued earlier may still read this slot
+    CK(cudaStreamSynchronize(rt->stream));
+    rt->desc_index.erase(rt->desc_key[slot]);
+  }
+  uint8_t *base = rt->desc + (size_t)slot * pw_runtime::kDescSlotBytes;
+  std::vector<uint8_t> host(bytes);
+  CUtensorMap *hm = reinterpret_cast<CUtensorMap *>(host.data());
+  const pw_fp8_tensor *ts[3] = {&a, b ? b : c, b ? c : nullptr};
+  for (uint32_t i = 0; i < nmaps; ++i)
+    if (!encode_weight_map(&hm[i], ts[i]->weight, ts[i]->rows, ts[i]->cols, box_rows, box_kb))
+      return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for a [%u, %u] weight", ts[i]->rows, ts[i]->cols);
+  const CUtensorMap *dm = reinterpret_cast<const CUtensorMap *>(base);
+  std::vector<GemvGroup> g1 = width_groups(width, a, b, dm, b ? dm + 1 : nullptr, chunk);
+  memcpy(host.data() + nmaps * sizeof(CUtensorMap), g1.data(), g1.size() * sizeof(GemvGroup));
+  if (c) {
+    std::vector<GemvGroup> g2 = width_groups(width, *c, nullptr, dm + nmaps - 1u, nullptr, chunk);
+    memcpy(host.data() + nmaps * sizeof(CUtensorMap) + ng * sizeof(GemvGroup), g2.data(),
+           g2.size() * sizeof(GemvGroup));
+  }
+  // synchronous: the host buffer is temporary; a miss is a one-time cost
+  CK(cudaStreamSynchronize(rt->stream));
+  CK(cudaMemcpy(base, host.data(), bytes, cudaMemcpyHostToDevice));
+  rt->desc_index[key] = slot;
+  rt->desc_key[slot] = key;
+  fill(base);
+  cached = true;
   return PW_OK;
 }
 
@@ -496,6 +602,7 @@ void pw_runtime_destroy(pw_runtime *rt) {
   if (rt->split_ws) cudaFree(rt->split_ws);
   if (rt->split_cnt) cudaFree(rt->split_cnt);
   if (rt->silu_lut) cudaFree(rt->silu_lut);
+  if (rt->desc) cudaFree(rt->desc);
   if (rt->d_flags) cudaFree(rt->d_flags);
   if (rt->ev0) cudaEventDestroy(rt->ev0);
   if (rt->ev1) cudaEventDestroy(rt->ev1);
@@ -661,16 +768,18 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
   // wide block-scaled projections run on the tcgen05 GEMM (all layouts; the
   // QKV layouts load each 128-row tile as two 64-row source runs)
   const bool wide = kind != 1 && width >= kWideProjection;
+  const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(0) : 8u;
+  const uint32_t box_rows = wide && layout != PW_LAYOUT_PLAIN ? 64u : map_box_rows(layout);
+  const uint32_t box_kb = wide && layout != PW_LAYOUT_PLAIN ? 1u : 0u;
+  // device-resident map and groups (built on the first call of this shape)
+  Descs D;
+  bool cached = false;
+  if ((s = get_descs(rt, 2u + (uint32_t)kind, width, chunk, *w, nullptr, nullptr, box_rows, box_kb, D, cached)) !=
+      PW_OK)
+    return s;
   CUtensorMap hmap;
-  if (kind != 1) {
-    const pw_fp8_tensor *ts[1] = {w};
-    if (wide && layout != PW_LAYOUT_PLAIN) {
-      if (!encode_weight_map(&hmap, w->weight, w->rows, w->cols, 64u, 1u))
-        return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for a [%u, %u] weight", w->rows, w->cols);
-    } else if (!encode_maps(rt, ts, 1, layout, &hmap)) {
-      return PW_ERR_CUDA;
-    }
-  }
+  if (!cached && !encode_weight_map(&hmap, w->weight, w->rows, w->cols, box_rows, box_kb))
+    return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for a [%u, %u] weight", w->rows, w->cols);
   Call call{rt, mem, stats, 0};
   if ((s = call.begin()) != PW_OK) return s;
   Arena ar;
@@ -683,20 +792,28 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
     float *dy = call.host() ? ar.take<float>(ny) : y;
     uint8_t *dc = kind == 1 ? nullptr : ar.take<uint8_t>(nx);
     float *ds = kind == 1 ? nullptr : ar.take<float>(nx / 128u);
-    CUtensorMap *dm = ar.take<CUtensorMap>(1);
-    std::vector<GemvGroup> groups =
-        width_groups(width, *w, nullptr, kind == 1 ? nullptr : dm, nullptr, wide ? (uint32_t)gemm_tc_tokens(0) : 8u);
-    GemvGroup *dg = ar.take<GemvGroup>(groups.size());
+    CUtensorMap *dm = cached ? nullptr : ar.take<CUtensorMap>(1);
+    std::vector<GemvGroup> groups;
+    const GemvGroup *dg = D.gu;
+    if (!cached) {
+      groups = width_groups(width, *w, nullptr, dm, nullptr, chunk);
+      dg = ar.take<GemvGroup>(groups.size());
+    }
+    const uint32_t n_groups = cached ? D.n_gu : (uint32_t)groups.size();
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, nx * 4)) != PW_OK) return s;
-    if (kind != 1) CK(cudaMemcpyAsync(dm, &hmap, sizeof hmap, cudaMemcpyHostToDevice, rt->stream));
-    CK(cudaMemcpyAsync(dg, groups.data(), groups.size() * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
-    GemvArgs a = gemv_args(rt, dg, (uint32_t)groups.size(), N, K, layout);
+    if (!cached) {
+      CK(cudaMemcpyAsync(dm, &hmap, sizeof hmap, cudaMemcpyHostToDevice, rt->stream));
+      CK(cudaMemcpyAsync(const_cast<GemvGroup *>(dg), groups.data(), groups.size() * sizeof(GemvGroup),
+                         cudaMemcpyHostToDevice, rt->stream));
+    }
+    GemvArgs a = gemv_args(rt, dg, n_groups, N, K, layout);
     a.out = dy;
     a.out_stride = N;
     if (kind == 1) {
       a.x_f32 = dx;
       a.round_bf16 = 0;
+      a.max_count = width < 8u ? width : 8u;
     } else {
       ProfScope ps(rt, P_QUANT, 1);
       CK(launch_quantize(dx, width, K, dc, ds, rt->d_flags, rt->stream));
@@ -706,8 +823,8 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
     }
     {
       ProfScope ps(rt, P_PROJ, 1);
-      int grid = grid_for(rt, (uint64_t)groups.size() * (N / (kind == 1 ? 64u : 128u)));
-      if (!wide && kind != 1 && (s = gemv_launch_setup(rt, a, (uint64_t)groups.size() * (N / 128u), 1, grid)) != PW_OK)
+      int grid = grid_for(rt, (uint64_t)n_groups * (N / (kind == 1 ? 64u : 128u)));
+      if (!wide && kind != 1 && (s = gemv_launch_setup(rt, a, (uint64_t)n_groups * (N / 128u), 1, grid)) != PW_OK)
         return s;
       if (wide) {
         GemmArgs A{};
@@ -745,7 +862,8 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
                                 const uint32_t *n_groups_dev, uint32_t slots, uint32_t H, uint32_t I,
                                 const uint32_t *tok_list, const uint8_t *xc, const float *xs, float *hidden,
                                 float *gate_tmp, float *up_tmp, uint8_t *hc, float *hs, float *down,
-                                uint32_t down_round, uint64_t units_hint, const uint32_t *slots_dev = nullptr) {
+                                uint32_t down_round, uint64_t units_hint, const uint32_t *slots_dev = nullptr,
+                                bool early = false) {
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   int s = PW_OK, grid_gu = 0;
   {
@@ -761,7 +879,10 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
     a.out_stride = I;
     a.q_codes = hc;
     a.q_scales = hs;
-    if ((s = gemv_launch_setup(rt, a, units_hint * (I / 128u), 2, grid_gu)) != PW_OK) return s;
+    // early: the weights and groups were final before the chain started, so
+    // under PDL the producer streams weights while the quantizer still runs
+    a.early_weights = early && pdl_enabled() ? 1u : 0u;
+    if ((s = gemv_launch_setup(rt, a, units_hint * (I / 128u), 2, grid_gu, early)) != PW_OK) return s;
     CK(launch_gemv(2, a, grid_gu, rt->stream));
   } else {
     // gate and up as two block-scaled projections, then the staged SwiGLU
@@ -799,7 +920,7 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
   // kernel's producer streams weights during gate/up's last wave
   d.early_weights = (pdl_enabled() && fused) ? 1u : 0u;
   int grid_dn = 0;
-  if ((s = gemv_launch_setup(rt, d, units_hint * (H / 128u), 1, grid_dn)) != PW_OK) return s;
+  if ((s = gemv_launch_setup(rt, d, units_hint * (H / 128u), 1, grid_dn, early && fused)) != PW_OK) return s;
   ProfScope ps(rt, P_DOWN, 1);
   CK(launch_gemv(0, d, grid_dn, rt->stream));
   return PW_OK;
@@ -898,12 +1019,18 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
   if (width == 0) return fail(rt, PW_ERR_SHAPE, "expert width must be at least one");
   CK(cudaSetDevice(rt->device));
   const uint32_t H = w->gate.cols, I = w->gate.rows;
+  const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
+  const bool wide = width >= kWideProjection;
+  const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
+  // device-resident maps and groups (built on the first call of this shape)
+  Descs D;
+  bool cached = false;
+  if ((s = get_descs(rt, 1u, width, chunk, w->gate, &w->up, &w->down, 128u, 0u, D, cached)) != PW_OK) return s;
   CUtensorMap hmaps[3];
-  {
+  if (!cached) {
     const pw_fp8_tensor *ts[3] = {&w->gate, &w->up, &w->down};
     if (!encode_maps(rt, ts, 3, PW_LAYOUT_PLAIN, hmaps)) return PW_ERR_CUDA;
   }
-  const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
   Call call{rt, mem, stats, 0};
   if ((s = call.begin()) != PW_OK) return s;
   Arena ar;
@@ -916,34 +1043,49 @@ int pw_expert_forward(pw_runtime *rt, const pw_expert_weights *w, const float *x
     float *dy = call.host() ? ar.take<float>((size_t)width * H) : y;
     uint8_t *xc = ar.take<uint8_t>((size_t)width * H);
     float *xs = ar.take<float>((size_t)width * H / 128u);
-    const bool wide = width >= kWideProjection;
     float *hid = fused ? nullptr : ar.take<float>((size_t)width * I);
     // the wide fused chain stages bf16 gate/up here
     float *gt = fused && !wide ? nullptr : ar.take<float>((size_t)width * I);
     float *ut = fused && !wide ? nullptr : ar.take<float>((size_t)width * I);
     uint8_t *hc = ar.take<uint8_t>((size_t)width * I);
     float *hs = ar.take<float>((size_t)width * I / 128u);
-    CUtensorMap *dm = ar.take<CUtensorMap>(3);
-    const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
-    std::vector<GemvGroup> gu = width_groups(width, w->gate, &w->up, dm, dm ? dm + 1 : nullptr, chunk);
-    std::vector<GemvGroup> dn = width_groups(width, w->down, nullptr, dm ? dm + 2 : nullptr, nullptr, chunk);
-    GemvGroup *dgu = ar.take<GemvGroup>(gu.size());
-    GemvGroup *ddn = ar.take<GemvGroup>(dn.size());
+    const GemvGroup *dgu = D.gu, *ddn = D.dn;
+    std::vector<GemvGroup> gu, dn;
+    CUtensorMap *dm = nullptr;
+    if (!cached) {
+      dm = ar.take<CUtensorMap>(3);
+      gu = width_groups(width, w->gate, &w->up, dm, dm ? dm + 1 : nullptr, chunk);
+      dn = width_groups(width, w->down, nullptr, dm ? dm + 2 : nullptr, nullptr, chunk);
+      dgu = ar.take<GemvGroup>(gu.size());
+      ddn = ar.take<GemvGroup>(dn.size());
+    }
+    const uint32_t n_groups = cached ? D.n_gu : (uint32_t)gu.size();
     if (pass == 0) continue;
     if (call.host() && (s = call.stage_in(dx, x, (size_t)width * H * 4)) != PW_OK) return s;
-    CK(cudaMemcpyAsync(dm, hmaps, sizeof hmaps, cudaMemcpyHostToDevice, rt->stream));
-    CK(cudaMemcpyAsync(dgu, gu.data(), gu.size() * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
-    CK(cudaMemcpyAsync(ddn, dn.data(), dn.size() * sizeof(GemvGroup), cudaMemcpyHostToDevice, rt->stream));
+    if (!cached) {
+      CK(cudaMemcpyAsync(dm, hmaps, sizeof hmaps, cudaMemcpyHostToDevice, rt->stream));
+      CK(cudaMemcpyAsync(const_cast<GemvGroup *>(dgu), gu.data(), gu.size() * sizeof(GemvGroup),
+                         cudaMemcpyHostToDevice, rt->stream));
+      CK(cudaMemcpyAsync(const_cast<GemvGroup *>(ddn), dn.data(), dn.size() * sizeof(GemvGroup),
+                         cudaMemcpyHostToDevice, rt->stream));
+    }
+    // quantize -> gate/up -> down as one PDL chain: the quantizer clears the
+    // GEMVs' split-K counters, and each GEMV's producer streams its weights
+    // while the kernel before it finishes
+    const bool chain = !wide && fused && !rt->profiling;
+    if (chain && (s = ensure_split_ws(rt)) != PW_OK) return s;
+    PdlScope pdl(chain);
     {
       ProfScope ps(rt, P_QUANT, 1);
-      CK(launch_quantize(dx, width, H, xc, xs, rt->d_flags, rt->stream));
+      CK(launch_quantize(dx, width, H, xc, xs, rt->d_flags, rt->stream, nullptr, chain ? rt->split_cnt : nullptr,
+                         chain ? kSplitCounters : 0u));
     }
     if (wide)
-      s = enqueue_expert_chain_wide(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, width, H, I, xc, xs, hid, gt, ut, hc,
-                                    hs, dy, 1, gu.size());
+      s = enqueue_expert_chain_wide(rt, dgu, ddn, n_groups, nullptr, width, H, I, xc, xs, hid, gt, ut, hc, hs, dy, 1,
+                                    n_groups);
     else
-      s = enqueue_expert_chain(rt, dgu, ddn, (uint32_t)gu.size(), nullptr, width, H, I, nullptr, xc, xs, hid, gt, ut,
-                               hc, hs, dy, 1, gu.size());
+      s = enqueue_expert_chain(rt, dgu, ddn, n_groups, nullptr, width, H, I, nullptr, xc, xs, hid, gt, ut, hc, hs, dy,
+                               1, n_groups, nullptr, chain);
     if (s != PW_OK) return s;
     if (call.host() && (s = call.stage_out(y, dy, (size_t)width * H * 4)) != PW_OK) return s;
   }

@@ -249,20 +249,35 @@ class WideMoeRuntime:
         bad = ctypes.c_uint64()
         self._check(self._L.pw_validate_fp8(self._rt, ctypes.byref(t), ctypes.byref(bad)))
 
-    def fp8_gemv(self, x, binding: WideProjectionBinding) -> Execution:
+    def _io_async(self, x, out_shape, asynchronous, out):
+        """(x, out, mem, stats pointer) for a call that may be enqueued without
+        waiting (PW_MEM_ASYNC: device I/O, no stats; CUDA-graph capturable once
+        the same call has run before)."""
+        if asynchronous:
+            if not x.is_cuda:
+                raise PrismwingError(-1, "asynchronous calls need device I/O")
+            if out is None:
+                out = torch.empty(out_shape, dtype=torch.float32, device=x.device)
+            return x, out, MEM_DEVICE | MEM_ASYNC, None
+        x, o, mem = self._io(x, out_shape)
+        return x, (out if out is not None and x.is_cuda else o), mem, Stats()
+
+    def fp8_gemv(self, x, binding: WideProjectionBinding, asynchronous: bool = False,
+                 out: Optional[torch.Tensor] = None) -> Execution:
         """Readable projection (src/lib.rs:1272 mapped_fp8_gemv): x f32 [w, cols] -> f32 [w, rows]."""
         x = _as_f32(x)
         if x.dim() == 1:
             x = x.unsqueeze(0)
-        x, out, mem = self._io(x, (x.shape[0], binding.rows))
+        x, out, mem, st = self._io_async(x, (x.shape[0], binding.rows), asynchronous, out)
         t = binding.c()
-        st = Stats()
         self._check(self._L.pw_fp8_gemv(self._rt, ctypes.byref(t), ctypes.c_void_p(x.data_ptr()), x.shape[0],
-                                        ctypes.c_void_p(out.data_ptr()), mem, ctypes.byref(st)))
-        return Execution(out, st.wall_ms, st.device_ms, weight_bytes=st.weight_bytes)
+                                        ctypes.c_void_p(out.data_ptr()), mem, ctypes.byref(st) if st else None))
+        return Execution(out, st.wall_ms if st else 0.0, st.device_ms if st else 0.0,
+                         weight_bytes=st.weight_bytes if st else 0)
 
     def execute_fp8_linear(self, x, binding: WideProjectionBinding, full_qkv_layout: bool = False,
-                           layout: Optional[int] = None, f32_output: bool = False) -> Execution:
+                           layout: Optional[int] = None, f32_output: bool = False, asynchronous: bool = False,
+                           out: Optional[torch.Tensor] = None) -> Execution:
         """src/wide_metal_moe.rs:241: quantize, block-scaled projection, bf16 round.
 
         Like the reference, a [14848, 4096] projection selects the SWA-QKV row map
@@ -278,23 +293,26 @@ class WideMoeRuntime:
                 layout = LAYOUT_PLAIN
         if f32_output:
             layout |= OUTPUT_F32
-        x, out, mem = self._io(x, (x.shape[0], binding.rows))
+        x, out, mem, st = self._io_async(x, (x.shape[0], binding.rows), asynchronous, out)
         t = binding.c()
-        st = Stats()
         self._check(self._L.pw_fp8_linear(self._rt, ctypes.byref(t), layout, ctypes.c_void_p(x.data_ptr()),
-                                          x.shape[0], ctypes.c_void_p(out.data_ptr()), mem, ctypes.byref(st)))
-        return Execution(out, st.wall_ms, st.device_ms, weight_bytes=st.weight_bytes)
+                                          x.shape[0], ctypes.c_void_p(out.data_ptr()), mem,
+                                          ctypes.byref(st) if st else None))
+        return Execution(out, st.wall_ms if st else 0.0, st.device_ms if st else 0.0,
+                         weight_bytes=st.weight_bytes if st else 0)
 
     def expert_forward(self, x, gate: WideProjectionBinding, up: WideProjectionBinding,
-                       down: WideProjectionBinding) -> Execution:
+                       down: WideProjectionBinding, asynchronous: bool = False,
+                       out: Optional[torch.Tensor] = None) -> Execution:
         """One routed expert at weight 1 (src/text_endpoint.rs:5311-5346)."""
         x = _as_f32(x)
-        x, out, mem = self._io(x, (x.shape[0], down.rows))
+        x, out, mem, st = self._io_async(x, (x.shape[0], down.rows), asynchronous, out)
         w = ExpertWeights(gate.c(), up.c(), down.c())
-        st = Stats()
         self._check(self._L.pw_expert_forward(self._rt, ctypes.byref(w), ctypes.c_void_p(x.data_ptr()), x.shape[0],
-                                              ctypes.c_void_p(out.data_ptr()), mem, ctypes.byref(st)))
-        return Execution(out, st.wall_ms, st.device_ms, weight_bytes=st.weight_bytes)
+                                              ctypes.c_void_p(out.data_ptr()), mem,
+                                              ctypes.byref(st) if st else None))
+        return Execution(out, st.wall_ms if st else 0.0, st.device_ms if st else 0.0,
+                         weight_bytes=st.weight_bytes if st else 0)
 
     def dense_mlp(self, x, gate: WideProjectionBinding, up: WideProjectionBinding,
                   down: WideProjectionBinding) -> Execution:

@@ -438,3 +438,55 @@ def test_bank_rejects_nonfinite_weight_byte(rt):
     with pytest.raises(PrismwingError) as e:
         rt.create_bank(bank)
     assert e.value.kind == "nonfinite" and "4" in str(e.value)
+
+
+def test_repeated_calls_are_graph_capturable(rt):
+    # After a first call of a shape (which uploads its launch descriptors),
+    # asynchronous projection and expert calls enqueue only kernels: captured
+    # into a CUDA graph and replayed they give the same bits as direct calls.
+    from mimo_prismwing_b200 import synth
+    s = torch.cuda.Stream()
+    rt.set_stream(s)
+    try:
+        b = synth.projection(2048, 4096, 81, "cuda")
+        g, u, d = synth.expert(4096, 2048, 82, "cuda")
+        x1 = synth.activations(1, 4096, 83, "cuda")
+        x8 = synth.activations(8, 4096, 84, "cuda")
+        ref_gemv = rt.fp8_gemv(x1, b).output.clone()
+        ref_lin = rt.execute_fp8_linear(x8, b).output.clone()
+        ref_exp = rt.expert_forward(x8, g, u, d).output.clone()
+        y_gemv = torch.empty_like(ref_gemv)
+        y_lin = torch.empty_like(ref_lin)
+        y_exp = torch.empty_like(ref_exp)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            rt.fp8_gemv(x1, b, asynchronous=True, out=y_gemv)
+            rt.execute_fp8_linear(x8, b, asynchronous=True, out=y_lin)
+            rt.expert_forward(x8, g, u, d, asynchronous=True, out=y_exp)
+        for _ in range(3):
+            with torch.cuda.stream(s):
+                graph.replay()
+            s.synchronize()
+            assert torch.equal(y_gemv, ref_gemv) and torch.equal(y_lin, ref_lin) and torch.equal(y_exp, ref_exp)
+        assert rt.error_flags() == 0
+        del graph
+    finally:
+        rt.set_stream(None)
+
+
+def test_first_call_of_a_shape_inside_capture_is_refused(rt):
+    from mimo_prismwing_b200 import synth
+    from mimo_prismwing_b200.runtime import PrismwingError
+    s = torch.cuda.Stream()
+    rt.set_stream(s)
+    try:
+        b = synth.projection(256, 512, 85, "cuda")
+        x = synth.activations(3, 512, 86, "cuda")
+        y = torch.empty((3, 256), device="cuda")
+        graph = torch.cuda.CUDAGraph()
+        with pytest.raises(PrismwingError) as e:
+            with torch.cuda.graph(graph, stream=s):
+                rt.execute_fp8_linear(x, b, asynchronous=True, out=y)
+        assert "before capturing" in str(e.value)
+    finally:
+        rt.set_stream(None)
