@@ -514,78 +514,95 @@ __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ s
                                                      uint32_t *flags) {
   pdl_wait();
   pdl_launch_dependents();
+  // Persistent warps loop over tokens: the code stays hot in the instruction
+  // cache (a warp per token and launch ran each instruction once, and stalled
+  // on instruction fetch: ~22 us per call at any token count).
   const uint32_t lane = threadIdx.x % 32u;
-  const uint32_t t = blockIdx.x * 8u + threadIdx.x / 32u;
-  if (t >= tokens) return;
+  const uint32_t nwarps = gridDim.x * (blockDim.x / 32u);
   const float ninf = -__int_as_float(0x7f800000);
-  float score[NPL], corr[NPL];
   const size_t plane = (size_t)tokens * experts;
+  float bias_r[NPL];
 #pragma unroll
   for (int k = 0; k < NPL; ++k) {
     const uint32_t e = lane + 32u * k;
-    score[k] = 0.0f;
-    corr[k] = ninf;
-    if (e < experts) {
-      const float *p = src + (size_t)t * experts + e;
-      float lg;
-      if (slices <= 16u) {  // independent loads first, then the ordered sum
-        float v[16];
-#pragma unroll
-        for (uint32_t s = 0; s < 16u; ++s) v[s] = s < slices ? p[s * plane] : 0.0f;
-        lg = v[0];
-#pragma unroll
-        for (uint32_t s = 1; s < 16u; ++s)
-          if (s < slices) lg = __fadd_rn(lg, v[s]);
-      } else {
-        lg = p[0];
-        for (uint32_t s = 1; s < slices; ++s) lg = __fadd_rn(lg, p[s * plane]);
-      }
-      const float b = __ldg(bias + e);
-      if (!finite(lg) || !finite(b)) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
-      score[k] = sigmoid_sleef(lg);
-      corr[k] = __fadd_rn(score[k], b);
-    }
+    bias_r[k] = e < experts ? __ldg(bias + e) : 0.0f;
   }
-  uint32_t taken = 0;
-  float pv[9], ps[9];
-  uint32_t pi[9];
-#pragma unroll
-  for (int round = 0; round < 9; ++round) {
-    float bv = ninf, bs = 0.0f;
-    uint32_t bi = 0xffffffffu;
+  for (uint32_t t = blockIdx.x * (blockDim.x / 32u) + threadIdx.x / 32u; t < tokens; t += nwarps) {
+    float score[NPL], corr[NPL];
+    bool bad = false;
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
       const uint32_t e = lane + 32u * k;
-      if (e < experts && !((taken >> k) & 1u) && better(corr[k], e, bv, bi)) {
-        bv = corr[k];
-        bi = e;
-        bs = score[k];
+      score[k] = 0.0f;
+      corr[k] = ninf;
+      if (e < experts) {
+        const float *p = src + (size_t)t * experts + e;
+        float lg;
+        if (slices <= 16u) {  // independent loads first, then the ordered sum
+          float v[16];
+#pragma unroll
+          for (uint32_t q = 0; q < 16u; ++q) v[q] = q < slices ? __ldcs(p + q * plane) : 0.0f;
+          lg = v[0];
+#pragma unroll
+          for (uint32_t q = 1; q < 16u; ++q)
+            if (q < slices) lg = __fadd_rn(lg, v[q]);
+        } else {
+          lg = p[0];
+          for (uint32_t q = 1; q < slices; ++q) lg = __fadd_rn(lg, p[q * plane]);
+        }
+        bad |= !finite(lg) || !finite(bias_r[k]);
+        score[k] = sigmoid_sleef(lg);
+        corr[k] = __fadd_rn(score[k], bias_r[k]);
       }
     }
-    argmax_shfl(bv, bi, bs);
-    pv[round] = bv;
-    pi[round] = bi;
-    ps[round] = bs;
-    if (round < 8 && bi != 0xffffffffu && bi % 32u == lane) taken |= 1u << (bi / 32u);
-  }
-  if (lane == 0) {
-    const float l0 = __fadd_rn(ps[0], ps[4]);
-    const float l1 = __fadd_rn(ps[1], ps[5]);
-    const float l2 = __fadd_rn(ps[2], ps[6]);
-    const float l3 = __fadd_rn(ps[3], ps[7]);
-    const float den = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, l0), l1), l2), l3), 1.0e-20f);
-    float sum = 0.0f;
-    bool ok = true;
+    if (bad) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
+    // 9 rounds of warp argmax (ties -> lower index): lane r keeps round r's
+    // pick (corrected value, expert, unbiased score)
+    uint32_t taken = 0;
+    float my_v = ninf, my_s = 0.0f;
+    uint32_t my_i = 0xffffffffu;
+#pragma unroll 1
+    for (uint32_t round = 0; round < 9u; ++round) {
+      float bv = ninf, bs = 0.0f;
+      uint32_t bi = 0xffffffffu;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float wk = __fdiv_rn(ps[k], den);
-      ok = ok && finite(wk) && wk >= 0.0f && pi[k] < experts;
-      sum = __fadd_rn(sum, wk);
-      selected[(size_t)t * 8 + k] = pi[k];
-      weights[(size_t)t * 8 + k] = wk;
+      for (int k = 0; k < NPL; ++k) {
+        const uint32_t e = lane + 32u * k;
+        if (e < experts && !((taken >> k) & 1u) && better(corr[k], e, bv, bi)) {
+          bv = corr[k];
+          bi = e;
+          bs = score[k];
+        }
+      }
+      argmax_shfl(bv, bi, bs);
+      if (lane == round) {
+        my_v = bv;
+        my_i = bi;
+        my_s = bs;
+      }
+      if (round < 8u && bi != 0xffffffffu && bi % 32u == lane) taken |= 1u << (bi / 32u);
     }
-    if (!ok || fabsf(__fsub_rn(sum, 1.0f)) > 1.0e-6f) raise_flag(flags, PW_FLAG_ROUTE_WEIGHTS);
-    if (pv[7] == pv[8] && tie_rows) atomicAdd(tie_rows, 1u);
+    // weight_k = score_k / (pairwise sum of the 8 + 1e-20), src/text_endpoint.rs:4382
+    const float s4 = __shfl_down_sync(0xffffffffu, my_s, 4);  // lane k < 4: score of pick k + 4
+    const float lk = __fadd_rn(my_s, s4);                      // lane k < 4: l_k
+    const float l0 = __shfl_sync(0xffffffffu, lk, 0), l1 = __shfl_sync(0xffffffffu, lk, 1);
+    const float l2 = __shfl_sync(0xffffffffu, lk, 2), l3 = __shfl_sync(0xffffffffu, lk, 3);
+    const float den = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, l0), l1), l2), l3), 1.0e-20f);
+    const float wk = __fdiv_rn(my_s, den);
+    const bool ok_k = lane >= 8u || (finite(wk) && wk >= 0.0f && my_i < experts);
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, wk, k));
+    const bool all_ok = __all_sync(0xffffffffu, ok_k);
+    if (lane < 8u) {
+      selected[(size_t)t * 8 + lane] = my_i;
+      weights[(size_t)t * 8 + lane] = wk;
+    }
+    const float v7 = __shfl_sync(0xffffffffu, my_v, 7), v8 = __shfl_sync(0xffffffffu, my_v, 8);
+    if (lane == 0) {
+      if (!all_ok || fabsf(__fsub_rn(sum, 1.0f)) > 1.0e-6f) raise_flag(flags, PW_FLAG_ROUTE_WEIGHTS);
+      if (v7 == v8 && tie_rows) atomicAdd(tie_rows, 1u);
+    }
   }
 }
 
@@ -622,7 +639,10 @@ cudaError_t launch_router(const float *x, uint32_t tokens, const void *w, uint32
   cudaError_t st = w_dtype == PW_ROUTER_F32 ? launch_router_logits<true>(x, tokens, w, g, scratch, num_sms, stream)
                                             : launch_router_logits<false>(x, tokens, w, g, scratch, num_sms, stream);
   if (st != cudaSuccess) return st;
-  const dim3 grid((tokens + 7u) / 8u);
+  // persistent: up to two 8-warp CTAs per SM, each warp looping over tokens
+  uint32_t blocks = (tokens + 7u) / 8u;
+  if (blocks > 2u * (uint32_t)num_sms) blocks = 2u * (uint32_t)num_sms;
+  const dim3 grid(blocks);
   if (experts <= 256u)
     return launch_kernel(k_router_topk<8>, grid, dim3(256), 0, stream, (const float *)scratch, g.slices, bias,
                          tokens, experts, selected, weights, tie_rows, flags);
