@@ -278,13 +278,16 @@ __global__ void __launch_bounds__(256) k_router_slices_small(const float *__rest
 }
 
 // Prefill widths: the slice chains as a register-tiled product.  Work unit:
-// 64 tokens x 128 experts x one slice (256 columns, 8 stages of 32); thread
-// (tg, eg) owns tokens 8tg..8tg+7 and experts 4eg..4eg+3, 64+4eg..64+4eg+3,
-// one f32 chain each (packed f32x2 FMAs over expert pairs; each lane of a
-// pair rounds like fmaf).  Stages are double-buffered in shared memory and
-// fetched one stage ahead into registers; persistent CTAs walk the units and
-// store each unit's slice sums to partials [slice][token][expert], which
-// k_router_topk adds in slice order.
+// 64 tokens x EXPT experts (128, or 64 when 128-expert units would leave SMs
+// idle: the expert-parallel ranks' few hundred tokens) x one slice (256
+// columns, 8 stages of 32); thread (tg, eg) owns tokens 8tg..8tg+7 and
+// experts 4eg..4eg+3 (+ 64 + the same for EXPT = 128), one f32 chain each
+// (packed f32x2 FMAs over expert pairs; each lane of a pair rounds like
+// fmaf).  Stages are double-buffered in shared memory and fetched one stage
+// ahead into registers; persistent CTAs walk the units and store each unit's
+// slice sums to partials [slice][token][expert], which k_router_topk adds in
+// slice order.  The tile shape changes which thread computes a chain, never
+// the chain.
 namespace rp {
 constexpr int kTok = 64, kExp = 128, kCols = 32, kThreads = 128;
 constexpr uint32_t kStages = kRouterSlice / kCols;
@@ -295,7 +298,7 @@ struct Smem {
 }  // namespace rp
 
 struct RouterUnits {
-  uint32_t tokens, experts, hidden, slices, tiles_e, n_units;
+  uint32_t tokens, experts, hidden, slices, tiles_e, n_units, exp_tile;
 };
 
 struct RouterCursor {
@@ -304,7 +307,7 @@ struct RouterCursor {
     if (u >= g.n_units) return;
     s = u % g.slices;
     const uint32_t tile = u / g.slices;
-    e0 = (tile % g.tiles_e) * rp::kExp;
+    e0 = (tile % g.tiles_e) * g.exp_tile;
     t0 = (tile / g.tiles_e) * rp::kTok;
   }
   __device__ __forceinline__ bool valid(const RouterUnits &g) const { return u < g.n_units; }
@@ -319,17 +322,18 @@ struct RouterCursor {
 };
 
 // One stage's global loads, fetched a stage ahead: 64 tokens x 32 columns of
-// x and 128 experts x 32 columns of the weight (8 KB as bf16, 16 KB as f32).
-template <bool F32W>
+// x and EXPT experts x 32 columns of the weight.
+template <bool F32W, int EXPT>
 struct RouterStage {
-  static constexpr int kW = F32W ? 8 : 4;  // 16-byte weight loads per thread
+  static constexpr int kW = EXPT * rp::kCols * (F32W ? 4 : 2) / 16 / rp::kThreads;  // 16-byte weight loads
   float4 x[4];
   uint4 w[kW];
 };
 
-template <bool F32W>
+template <bool F32W, int EXPT>
 __device__ __forceinline__ void router_gload(const float *__restrict__ x, const void *__restrict__ wv,
-                                             const RouterUnits &g, const RouterCursor &c, RouterStage<F32W> &r) {
+                                             const RouterUnits &g, const RouterCursor &c,
+                                             RouterStage<F32W, EXPT> &r) {
   const uint32_t base = c.base();
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
@@ -342,16 +346,16 @@ __device__ __forceinline__ void router_gload(const float *__restrict__ x, const 
   const unsigned char *w = static_cast<const unsigned char *>(wv);
   const size_t esz = F32W ? 4u : 2u;
 #pragma unroll
-  for (int m = 0; m < RouterStage<F32W>::kW; ++m) {
+  for (int m = 0; m < RouterStage<F32W, EXPT>::kW; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
-    const uint32_t e = c.e0 + i % 128u, cq = i / 128u;  // w: expert, kPer columns
+    const uint32_t e = c.e0 + i % (uint32_t)EXPT, cq = i / (uint32_t)EXPT;  // w: expert, kPer columns
     r.w[m] = e < g.experts ? __ldg(reinterpret_cast<const uint4 *>(w + ((size_t)e * g.hidden + base + kPer * cq) * esz))
                            : make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
-template <bool F32W>
-__device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterStage<F32W> &r) {
+template <bool F32W, int EXPT>
+__device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterStage<F32W, EXPT> &r) {
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
@@ -362,9 +366,9 @@ __device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterS
     sm.xs[b][4 * c4 + 3][tok] = r.x[m].w;
   }
 #pragma unroll
-  for (int m = 0; m < RouterStage<F32W>::kW; ++m) {
+  for (int m = 0; m < RouterStage<F32W, EXPT>::kW; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
-    const uint32_t e = i % 128u, cq = i / 128u;
+    const uint32_t e = i % (uint32_t)EXPT, cq = i / (uint32_t)EXPT;
     const uint32_t q[4] = {r.w[m].x, r.w[m].y, r.w[m].z, r.w[m].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -378,10 +382,11 @@ __device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterS
   }
 }
 
-template <bool F32W>
+template <bool F32W, int EXPT>
 __global__ void __launch_bounds__(rp::kThreads, 2)
     k_router_partials(const float *__restrict__ x, const void *__restrict__ w, RouterUnits g,
                       float *__restrict__ part) {
+  constexpr int NP = EXPT / 32;  // f32x2 expert pairs per thread and token
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char router_smem[];
@@ -392,7 +397,7 @@ __global__ void __launch_bounds__(rp::kThreads, 2)
   ld.decode(g);
   if (!ld.valid(g)) return;
   RouterCursor cp = ld;
-  RouterStage<F32W> r;
+  RouterStage<F32W, EXPT> r;
   router_gload(x, w, g, ld, r);
   ld.next(g);
   router_sstore(sm, 0, r);
@@ -403,27 +408,30 @@ __global__ void __launch_bounds__(rp::kThreads, 2)
   }
   __syncthreads();
 
-  float2 acc[8][4];
+  float2 acc[8][NP];
 #pragma unroll
   for (int t = 0; t < 8; ++t)
 #pragma unroll
-    for (int p = 0; p < 4; ++p) acc[t][p] = make_float2(0.f, 0.f);
+    for (int p = 0; p < NP; ++p) acc[t][p] = make_float2(0.f, 0.f);
   int b = 0;
   while (cp.valid(g)) {
 #pragma unroll 4
     for (int k = 0; k < rp::kCols; ++k) {
       const float4 xa = *reinterpret_cast<const float4 *>(&sm.xs[b][k][8 * tg]);
       const float4 xb = *reinterpret_cast<const float4 *>(&sm.xs[b][k][8 * tg + 4]);
-      const float4 wa = *reinterpret_cast<const float4 *>(&sm.ws[b][k][4 * eg]);
-      const float4 wb = *reinterpret_cast<const float4 *>(&sm.ws[b][k][64 + 4 * eg]);
       const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-      const float2 wv[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
-                            make_float2(wb.z, wb.w)};
+      float2 wv[NP];
+#pragma unroll
+      for (int h = 0; h < NP / 2; ++h) {
+        const float4 wq = *reinterpret_cast<const float4 *>(&sm.ws[b][k][64 * h + 4 * eg]);
+        wv[2 * h] = make_float2(wq.x, wq.y);
+        wv[2 * h + 1] = make_float2(wq.z, wq.w);
+      }
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         const float2 xd = make_float2(xv[t], xv[t]);
 #pragma unroll
-        for (int p = 0; p < 4; ++p) acc[t][p] = __ffma2_rn(wv[p], xd, acc[t][p]);
+        for (int p = 0; p < NP; ++p) acc[t][p] = __ffma2_rn(wv[p], xd, acc[t][p]);
       }
     }
     if (cp.st == rp::kStages - 1u) {  // the unit's slice chains are complete
@@ -434,7 +442,7 @@ __global__ void __launch_bounds__(rp::kThreads, 2)
         if (tok < g.tokens) {
           float *row = dst + (size_t)tok * g.experts;
 #pragma unroll
-          for (int hlf = 0; hlf < 2; ++hlf) {
+          for (int hlf = 0; hlf < NP / 2; ++hlf) {
             const uint32_t e = cp.e0 + 64u * hlf + 4u * eg;
             const float v[4] = {acc[t][2 * hlf].x, acc[t][2 * hlf].y, acc[t][2 * hlf + 1].x, acc[t][2 * hlf + 1].y};
             if ((g.experts & 3u) == 0u && e + 3u < g.experts) {
@@ -447,7 +455,7 @@ __global__ void __launch_bounds__(rp::kThreads, 2)
           }
         }
 #pragma unroll
-        for (int p = 0; p < 4; ++p) acc[t][p] = make_float2(0.f, 0.f);
+        for (int p = 0; p < NP; ++p) acc[t][p] = make_float2(0.f, 0.f);
       }
     }
     const bool next_ok = have;
@@ -463,13 +471,14 @@ __global__ void __launch_bounds__(rp::kThreads, 2)
   }
 }
 
-static RouterUnits router_units(uint32_t tokens, uint32_t experts, uint32_t hidden) {
+static RouterUnits router_units(uint32_t tokens, uint32_t experts, uint32_t hidden, uint32_t exp_tile = 128u) {
   RouterUnits g{};
   g.tokens = tokens;
   g.experts = experts;
   g.hidden = hidden;
   g.slices = hidden / kRouterSlice;
-  g.tiles_e = (experts + rp::kExp - 1) / rp::kExp;
+  g.exp_tile = exp_tile;
+  g.tiles_e = (experts + exp_tile - 1) / exp_tile;
   const uint32_t tiles_t = (tokens + rp::kTok - 1) / rp::kTok;
   g.n_units = tiles_t * g.tiles_e * g.slices;
   return g;
@@ -606,22 +615,31 @@ __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ s
   }
 }
 
+template <bool F32W, int EXPT>
+static cudaError_t launch_partials(const float *x, const void *w, const RouterUnits &g, float *scratch, int num_sms,
+                                   cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t st = cudaFuncSetAttribute(k_router_partials<F32W, EXPT>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(rp::Smem));
+    if (st != cudaSuccess) return st;
+    configured = true;
+  }
+  // two 4-warp CTAs per SM: one warp per scheduler left the FMA pipe idle
+  // on every short dependency (measured ~50% FMA-pipe activity)
+  const uint32_t grid = g.n_units < 2u * (uint32_t)num_sms ? g.n_units : 2u * (uint32_t)num_sms;
+  return launch_kernel(k_router_partials<F32W, EXPT>, dim3(grid), dim3(rp::kThreads), sizeof(rp::Smem), stream, x, w,
+                       g, scratch);
+}
+
 template <bool F32W>
 static cudaError_t launch_router_logits(const float *x, uint32_t tokens, const void *w, const RouterUnits &g,
                                         float *scratch, int num_sms, cudaStream_t stream) {
   if (tokens >= kRouterPartialMinTokens) {
-    static bool configured = false;
-    if (!configured) {
-      const cudaError_t st = cudaFuncSetAttribute(k_router_partials<F32W>,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(rp::Smem));
-      if (st != cudaSuccess) return st;
-      configured = true;
-    }
-    // two 4-warp CTAs per SM: one warp per scheduler left the FMA pipe idle
-    // on every short dependency (measured ~50% FMA-pipe activity)
-    const uint32_t grid = g.n_units < 2u * (uint32_t)num_sms ? g.n_units : 2u * (uint32_t)num_sms;
-    return launch_kernel(k_router_partials<F32W>, dim3(grid), dim3(rp::kThreads), sizeof(rp::Smem), stream, x, w, g,
-                         scratch);
+    // 128-expert units unless they would leave CTA slots idle
+    if (g.n_units >= 2u * (uint32_t)num_sms) return launch_partials<F32W, 128>(x, w, g, scratch, num_sms, stream);
+    const RouterUnits g64 = router_units(g.tokens, g.experts, g.hidden, 64u);
+    return launch_partials<F32W, 64>(x, w, g64, scratch, num_sms, stream);
   }
   using WT = typename std::conditional<F32W, float, uint16_t>::type;
   return launch_kernel(k_router_slices_small<WT>,
