@@ -165,19 +165,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 32 lanes x 16 consecutive f32 columns.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 consecutive f32 columns from registers into TMEM.
@@ -426,96 +413,61 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       }
     };
     float wn0 = 0.0f, wn1 = 0.0f;
-    uint32_t gcount_n = 0, gtok_n = 0;  // the next tile's group (count, first token)
     if (u_begin < u_end) {
       ws_load(u_begin, wn0, wn1);
       xs_fetch(u_begin, 0u);
-      gcount_n = a.groups[u_begin / tpg].count;
-      gtok_n = a.groups[u_begin / tpg].tok_begin;
     }
     uint32_t ti = 0;  // tile ordinal: token-scale buffer ti & 1
     for (uint32_t u = u_begin; u < u_end; u += u_step, ++ti) {
+      const uint32_t gi = u / tpg;
+      const GemvGroup grp = a.groups[gi];
       const uint32_t row0 = (u % tpg) * kTileRows;
-      const uint32_t gcount = gcount_n, gtok = gtok_n;
-      const uint32_t cnt = min(gcount, (uint32_t)kTN);
+      const uint32_t cnt = min(grp.count, (uint32_t)kTN);
       const bool active = quarter * 32u < cnt;  // this warp's lane quarter holds tokens
       // this tile's token scales have landed (both warps), the other buffer is free
       cp_async_wait_all();
       named_bar_sync(2u + quarter, 64u);
       const float *xsb = sh.xs + ((ti & 1u) * 4u + quarter) * 1024u;
-      if (u + u_step < u_end) {
-        // everything the next tile needs besides its accumulators, fetched now
-        xs_fetch(u + u_step, (ti & 1u) ^ 1u);
-        gcount_n = a.groups[(u + u_step) / tpg].count;
-        gtok_n = a.groups[(u + u_step) / tpg].tok_begin;
-      }
+      if (u + u_step < u_end) xs_fetch(u + u_step, (ti & 1u) ^ 1u);
       const float wc0 = wn0, wc1 = wn1;
       if (u + u_step < u_end) ws_load(u + u_step, wn0, wn1);
 
-      // Promotion of this tile's k-blocks (all gate blocks, then all up
-      // blocks for the fused kind), software-pipelined in 16-column chunks:
-      // the TMEM load of the next chunk (the next k-block's first, once its
-      // slot is full) is in flight while the current chunk's FMAs run, and a
-      // k-block's slot is released as soon as its last chunk sits in
-      // registers.  (tcgen05.wait::ld waits for every load of the thread, so
-      // the pipeline is one chunk deep.)
       float2 acc[32];  // weight rows col0 + 2i, col0 + 2i + 1
 #pragma unroll
-      for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
-      const uint32_t steps = kblocks * (uint32_t)MATS;
-      float b0[16], b1[16];
-      bool ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
-      tc_fence_after();
-      if (ok && active) tmem_ld16(tmem + lane_base + acc_slot * (uint32_t)kTN + col0, b0);
-      for (uint32_t st = 0; st < steps; ++st) {
-        const uint32_t m = st / kblocks, kb = st % kblocks;
-        if (MATS == 2 && st == kblocks) {
+      for (int m = 0; m < MATS; ++m) {
+        if (m == 1 && active) {
           // gate finished: park its sums in the stash slot, start the up sums
-          // (the first up block's load is issued after the stash)
-          if (active) {
-            tmem_st32(stash, *reinterpret_cast<const float2(*)[16]>(&acc[0]));
-            tmem_st32(stash + 32u, *reinterpret_cast<const float2(*)[16]>(&acc[16]));
-            tmem_wait_st();
-          }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
-          ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
-          tc_fence_after();
-          if (ok && active) tmem_ld16(tmem + lane_base + acc_slot * (uint32_t)kTN + col0, b0);
+          tmem_st32(stash, *reinterpret_cast<const float2(*)[16]>(&acc[0]));
+          tmem_st32(stash + 32u, *reinterpret_cast<const float2(*)[16]>(&acc[16]));
+          tmem_wait_st();
         }
-        const uint32_t sel = qkv ? half : m;
-        const float ws = __shfl_sync(0xffffffffu, sel == 0u ? wc0 : wc1, kb);
-        const float c = __fmul_rn(ws, xsb[kb * 32u + lane]);
-        const float2 c2 = make_float2(c, c);
-        const bool cur_ok = ok && active;
-        const uint32_t slot_addr = tmem + lane_base + acc_slot * (uint32_t)kTN + col0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float(&cur)[16] = (q & 1) ? b1 : b0;
-          float(&nxt)[16] = (q & 1) ? b0 : b1;
-          if (cur_ok) tmem_wait_ld();  // chunk q of this k-block is in registers
-          if (q < 3) {
-            if (cur_ok) tmem_ld16(slot_addr + 16u * (uint32_t)(q + 1), nxt);
-          } else {
-            // every chunk of this k-block is in registers: release its slot,
-            // then start the next k-block's first chunk
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sh.tempty[acc_slot]);
-            if (++acc_slot == NACC) {
-              acc_slot = 0;
-              aphase ^= 1u;
-            }
-            if (st + 1u < steps && !(MATS == 2 && st + 1u == kblocks)) {
-              ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
-              tc_fence_after();
-              if (ok && active) tmem_ld16(tmem + lane_base + acc_slot * (uint32_t)kTN + col0, nxt);
+        for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
+        const uint32_t sel = qkv ? half : (uint32_t)m;
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+          const float ws = __shfl_sync(0xffffffffu, sel == 0u ? wc0 : wc1, kb);
+          const bool ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
+          tc_fence_after();
+          if (ok && active) {
+            const float c = __fmul_rn(ws, xsb[kb * 32u + lane]);
+            const float2 c2 = make_float2(c, c);
+            const uint32_t src = tmem + lane_base + acc_slot * (uint32_t)kTN + col0;
+            float v0[32], v1[32];
+            tmem_ld32(src, v0);
+            tmem_ld32(src + 32u, v1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              acc[i] = __ffma2_rn(make_float2(v0[2 * i], v0[2 * i + 1]), c2, acc[i]);
+              acc[16 + i] = __ffma2_rn(make_float2(v1[2 * i], v1[2 * i + 1]), c2, acc[16 + i]);
             }
           }
-          if (cur_ok) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              acc[8 * q + i] = __ffma2_rn(make_float2(cur[2 * i], cur[2 * i + 1]), c2, acc[8 * q + i]);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.tempty[acc_slot]);
+          if (++acc_slot == NACC) {
+            acc_slot = 0;
+            aphase ^= 1u;
           }
         }
       }
@@ -534,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
             bad |= !finite(o[2 * i]) || !finite(o[2 * i + 1]);
           }
           if (a.out_bf16 || a.peer_base) {  // exact: the values are bf16-rounded
-            const size_t p = gtok + t_local;
+            const size_t p = grp.tok_begin + t_local;
             uint16_t *row = a.peer_base ? reinterpret_cast<uint16_t *>(a.peer_base[a.row_rank[p]] + a.peer_off) +
                                               (size_t)a.row_place[p] * a.out_stride
                                         : a.out_bf16 + p * a.out_stride;
@@ -548,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
                                   (__float_as_uint(oo[6]) >> 16) | (__float_as_uint(oo[7]) & 0xffff0000u));
             }
           } else {
-            float *dst = a.out + (size_t)(gtok + t_local) * a.out_stride + row0 + col0;
+            float *dst = a.out + (size_t)(grp.tok_begin + t_local) * a.out_stride + row0 + col0;
             if ((a.out_stride & 3u) == 0u && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0u) {
 #pragma unroll
               for (int i = 0; i < 16; ++i)
@@ -563,29 +515,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       } else if (active) {
         // bf16(gate) (from the stash) and bf16(up) (registers): the staged
         // SwiGLU's first roundings; k_swiglu_quant finishes the hidden
-        // the gate sums come back from the stash 16 columns at a time
-        const uint32_t I = a.rows;
-        const bool mine = t_local < cnt;
-        uint4 *gd = reinterpret_cast<uint4 *>(a.gate_bf16 + (size_t)(gtok + t_local) * I + row0 + col0);
-        uint4 *ud = reinterpret_cast<uint4 *>(a.up_bf16 + (size_t)(gtok + t_local) * I + row0 + col0);
-        auto pack = [](float lo, float hi) {
-          return (__float_as_uint(round_bf16(lo)) >> 16) | (__float_as_uint(round_bf16(hi)) & 0xffff0000u);
-        };
+        float g0[32], g1[32];
+        tmem_ld32(stash, g0);
+        tmem_ld32(stash + 32u, g1);
+        tmem_wait_ld();
+        if (t_local < cnt) {
+          const uint32_t I = a.rows;
+          uint4 *gd = reinterpret_cast<uint4 *>(a.gate_bf16 + (size_t)(grp.tok_begin + t_local) * I + row0 + col0);
+          uint4 *ud = reinterpret_cast<uint4 *>(a.up_bf16 + (size_t)(grp.tok_begin + t_local) * I + row0 + col0);
+          auto pack = [](float lo, float hi) {
+            return (__float_as_uint(round_bf16(lo)) >> 16) | (__float_as_uint(round_bf16(hi)) & 0xffff0000u);
+          };
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float g[16];
-          tmem_ld16(stash + 16u * (uint32_t)j, g);
-          tmem_wait_ld();
-          if (mine) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const float *gs = g + 8 * h;
-              gd[2 * j + h] =
-                  make_uint4(pack(gs[0], gs[1]), pack(gs[2], gs[3]), pack(gs[4], gs[5]), pack(gs[6], gs[7]));
-              const float2 *us = acc + 8 * j + 4 * h;
-              ud[2 * j + h] = make_uint4(pack(us[0].x, us[0].y), pack(us[1].x, us[1].y), pack(us[2].x, us[2].y),
-                                         pack(us[3].x, us[3].y));
-            }
+          for (int i = 0; i < 8; ++i) {
+            const float *gs = i < 4 ? g0 + 8 * i : g1 + 8 * (i - 4);
+            gd[i] = make_uint4(pack(gs[0], gs[1]), pack(gs[2], gs[3]), pack(gs[4], gs[5]), pack(gs[6], gs[7]));
+            const float2 *us = acc + 4 * i;
+            ud[i] = make_uint4(pack(us[0].x, us[0].y), pack(us[1].x, us[1].y), pack(us[2].x, us[2].y),
+                               pack(us[3].x, us[3].y));
           }
         }
       }
