@@ -520,6 +520,63 @@ def run_ours(args, rank, world, local_rank):
             return rt.moe_layer(x, w, bias, h, stats=profile, out=out)
         return rt.moe_layer(x, w, bias, h, asynchronous=True, out=out)
 
+    def decode_bench():
+        """the 8-token layer, µs per layer (CUDA events over
+        decode_steps layer calls), and the fused gate/up GEMV's HBM rate
+        from profiled calls."""
+        gu_b, _ = expert_bytes()
+        Td = DECODE_TOKENS // world + (rank < DECODE_TOKENS % world)
+        xd = [synth.activations(max(Td, 1), HIDDEN, 7000 + 97 * i + rank, dev)[:Td]
+              for i in range(args.decode_steps + 3)]
+        yd = torch.empty((max(Td, 1), HIDDEN), device=dev)[:Td]
+        rt.set_stream(stream)
+        for i in range(3):
+            layer_call(xd[args.decode_steps + i], 0, out=yd)
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            d0.record(stream)
+            for i in range(args.decode_steps):
+                layer_call(xd[i], i % len(layers.handles), out=yd)
+            d1.record(stream)
+        stream.synchronize()
+        barrier()
+        dec_us = d0.elapsed_time(d1) * 1e3 / args.decode_steps
+        rt.set_profiling(True)
+        dprof = {"gate_up_ms": 0.0}
+        dgu_bytes = 0.0
+        duniq = []
+        for i in range(min(args.decode_steps, 20)):
+            ex = layer_call(xd[i], i % len(layers.handles), out=yd, profile=True)
+            p = rt.last_profile()
+            dprof["gate_up_ms"] += p["gate_up_ms"]
+            P = ex.expert_rows
+            dgu_bytes += ex.unique_experts * gu_b + P * (HIDDEN + HIDDEN // 128 * 4) + P * (INTER + INTER // 128 * 4)
+            duniq.append(ex.unique_experts)
+        rt.set_profiling(False)
+        nd = min(args.decode_steps, 20)
+        dgu_gbs = (dgu_bytes / nd) / (dprof["gate_up_ms"] / nd * 1e-3) / 1e9 if dprof["gate_up_ms"] else None
+        return dec_us, dgu_gbs, duniq
+
+    def decode_json(dec_us, dgu_gbs, duniq):
+        return {"metric": DECODE_METRIC, "value": round(dec_us, 2), "unit": "us", "higher_is_better": False,
+                "workload": "configs[2]: 8 tokens, 256 experts, device router"
+                            + (f", expert-parallel x{world}" if ep else ""),
+                "unique_experts_mean": round(statistics.mean(duniq), 2) if duniq else None,
+                "roofline": {"bound": "hbm", "kernel": "k_gemv_mma fused gate/up + SwiGLU",
+                             "achieved": round(dgu_gbs, 1) if dgu_gbs else None, "peak": hbm,
+                             "unit": "GB/s", "frac": round(dgu_gbs / hbm, 4) if dgu_gbs else None,
+                             "traffic_ratio": round(GATE_UP_GEMV_TRAFFIC_RATIO, 4)}}
+
+    if args.decode_only:  # configs[2] alone, for profiling runs
+        dec = decode_json(*decode_bench())
+        if rank == 0:
+            print(json.dumps({"decode": dec}), flush=True)
+        rt.close()
+        return
+
     # ================================================================ prefill
     T = PREFILL_TOKENS // world
     x = synth.activations(T, HIDDEN, 5000 + rank, dev)
@@ -620,38 +677,7 @@ def run_ours(args, rank, world, local_rank):
     barrier()
 
     # ================================================================= decode
-    Td = DECODE_TOKENS // world if DECODE_TOKENS % world == 0 else (DECODE_TOKENS // world + (rank < DECODE_TOKENS % world))
-    xd = [synth.activations(max(Td, 1), HIDDEN, 7000 + 97 * i + rank, dev)[:Td] for i in range(args.decode_steps + 3)]
-    yd = torch.empty((max(Td, 1), HIDDEN), device=dev)[:Td]
-    rt.set_stream(stream)
-    for i in range(3):
-        layer_call(xd[args.decode_steps + i], 0, out=yd)
-    stream.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        d0.record(stream)
-        for i in range(args.decode_steps):
-            layer_call(xd[i], i % len(layers.handles), out=yd)
-        d1.record(stream)
-    stream.synchronize()
-    barrier()
-    dec_us = d0.elapsed_time(d1) * 1e3 / args.decode_steps
-    rt.set_profiling(True)
-    dprof = {"gate_up_ms": 0.0}
-    dgu_bytes = 0.0
-    duniq = []
-    for i in range(min(args.decode_steps, 20)):
-        ex = layer_call(xd[i], i % len(layers.handles), out=yd, profile=True)
-        p = rt.last_profile()
-        dprof["gate_up_ms"] += p["gate_up_ms"]
-        P = ex.expert_rows
-        dgu_bytes += ex.unique_experts * gu_b + P * (HIDDEN + HIDDEN // 128 * 4) + P * (INTER + INTER // 128 * 4)
-        duniq.append(ex.unique_experts)
-    rt.set_profiling(False)
-    nd = min(args.decode_steps, 20)
-    dgu_gbs = (dgu_bytes / nd) / (dprof["gate_up_ms"] / nd * 1e-3) / 1e9 if dprof["gate_up_ms"] else None
+    dec_us, dgu_gbs, duniq = decode_bench()
 
     # ================================================================ gather
     vals = torch.tensor([step_ms, e2e_s, dec_us, layer_gbs, gu_gbs, dgu_gbs or 0.0, e2e_layer_io_s], device=dev,
@@ -724,14 +750,7 @@ def run_ours(args, rank, world, local_rank):
                       "tensor_frac": round(layer_tflops / tflops_fp8, 4) if tflops_fp8 else None,
                       "experts_per_rank_run": round(uniq, 1), "rows_per_rank": round(rows, 1)},
             "kernels_us_per_layer": {k.replace("_ms", ""): round(v * 1e3, 2) for k, v in prof.items()},
-            "decode": {"metric": DECODE_METRIC, "value": round(dec_us, 2), "unit": "us", "higher_is_better": False,
-                       "workload": "configs[2]: 8 tokens, 256 experts, device router"
-                                   + (f", expert-parallel x{world}" if ep else ""),
-                       "unique_experts_mean": round(statistics.mean(duniq), 2) if duniq else None,
-                       "roofline": {"bound": "hbm", "kernel": "k_gemv_mma fused gate/up + SwiGLU",
-                                    "achieved": round(dgu_gbs, 1) if dgu_gbs else None, "peak": hbm,
-                                    "unit": "GB/s", "frac": round(dgu_gbs / hbm, 4) if dgu_gbs else None,
-                                    "traffic_ratio": round(GATE_UP_GEMV_TRAFFIC_RATIO, 4)}},
+            "decode": decode_json(dec_us, dgu_gbs, duniq),
             "configs": configs,
             **parity,
             "clocks": clocks.summary(),
@@ -754,6 +773,7 @@ def main():
     ap.add_argument("--no-parity", action="store_true", help="skip the start-up parity check (profiling runs)")
     ap.add_argument("--skip-configs", action="store_true", help="skip the configs[0]/[1]/[3] sub-benchmarks")
     ap.add_argument("--configs-only", action="store_true", help="run only the configs[0]/[1]/[3] sub-benchmarks")
+    ap.add_argument("--decode-only", action="store_true", help="run only the configs[2] decode layer")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange: peer-memory stores (default) or NCCL send/recv")
     # smaller cases for ncu captures only; the metric is quoted at the defaults
