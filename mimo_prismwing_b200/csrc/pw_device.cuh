@@ -27,6 +27,20 @@ __device__ __forceinline__ float round_bf16(float v) {
   return __uint_as_float(a > 0x7f800000u ? qnan : (a == 0x7f800000u ? bits : rn));
 }
 
+// bf16(lo) | bf16(hi) << 16 with one conversion instruction, round to nearest
+// even: for every non-NaN input the same bits as round_bf16 (a NaN becomes
+// the canonical quiet NaN; callers treat any NaN as an error).
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// Smallest |f32| bit pattern that bf16 rounding turns into an infinity: the
+// halfway point above the largest finite bf16 (0x7f7f, odd), where round to
+// nearest even goes up to 0x7f80.
+constexpr uint32_t kBf16OverflowBits = 0x7f7f8000u;
+
 // 4 packed e4m3 bytes -> 4 floats (byte 0 -> out[0]).  Exact.
 __device__ __forceinline__ void decode4(uint32_t w, float &o0, float &o1, float &o2, float &o3) {
   uint32_t h01, h23;

@@ -472,68 +472,121 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
         }
       }
 
-      // outputs: this thread's token, weight rows row0 + col0 .. + 63 (one
-      // contiguous run of the output row)
+      if (!active) continue;
+
+      // outputs: this warp's tokens, weight rows row0 + col0 .. + 63 (one
+      // contiguous run of each output row).  They leave through staging rows
+      // in this tile's token-scale buffer, which the quarter no longer needs
+      // once both of its warps are past the last k-block (the next tile's
+      // scales are in the other buffer; this one is refilled only after the
+      // next tile's barrier): each thread writes a 64-byte piece of its row
+      // (16-byte chunk i at position i ^ ((row >> 1) & 3), so neither the
+      // row-wise writes nor the column-wise reads conflict), and each store
+      // instruction then covers 8 rows x 64 B instead of 32 rows x 16 B.
+      named_bar_sync(2u + quarter, 64u);
+      uint8_t *stg = reinterpret_cast<uint8_t *>(sh.xs + ((ti & 1u) * 4u + quarter) * 1024u) + half * 2048u;
+      const uint32_t rows_here = min(cnt - quarter * 32u, 32u);
+      const size_t p0 = grp.tok_begin + quarter * 32u;  // the warp's first token row
+      // dst(r): byte address of row r's piece (r < rows_here)
+      auto put_rows = [&](const uint4 (&w)[4], auto &&dst) {
+#pragma unroll
+        for (uint32_t i = 0; i < 4; ++i)
+          *reinterpret_cast<uint4 *>(stg + lane * 64u + ((i ^ ((lane >> 1) & 3u)) << 4)) = w[i];
+        __syncwarp();
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          const uint32_t r = 8u * j + lane / 4u, c = lane % 4u;
+          const uint4 v = *reinterpret_cast<const uint4 *>(stg + r * 64u + ((c ^ ((r >> 1) & 3u)) << 4));
+          if (r < rows_here) *reinterpret_cast<uint4 *>(dst(r) + c * 16u) = v;
+        }
+        __syncwarp();  // the staging rows are rewritten by the next piece
+      };
       if (KIND != 2) {
-        if (t_local < cnt) {
-          const bool rb = a.round_bf16 != 0u;
+        // bf16 rounding by the conversion instruction; an output is non-finite
+        // when its f32 sum is, or when rounding carries it past the largest bf16
+        const bool rb = a.round_bf16 != 0u;
+        uint32_t mx = 0u;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          mx = max(mx, max(__float_as_uint(acc[i].x) & 0x7fffffffu, __float_as_uint(acc[i].y) & 0x7fffffffu));
+        if (mx >= (rb ? kBf16OverflowBits : 0x7f800000u) && t_local < cnt) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
+        uint32_t pk[32];  // bf16 pairs of weight rows col0 + 2i, col0 + 2i + 1
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2_rn(acc[i].x, acc[i].y);
+        if (a.out_bf16 || a.peer_base) {  // exact: the values are bf16-rounded
+          const size_t seg = (size_t)(row0 + col0) * 2u;
+#pragma unroll
+          for (uint32_t h = 0; h < 2; ++h) {
+            uint4 w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = make_uint4(pk[16 * h + 4 * i], pk[16 * h + 4 * i + 1], pk[16 * h + 4 * i + 2],
+                                pk[16 * h + 4 * i + 3]);
+            if (a.peer_base) {
+              put_rows(w, [&](uint32_t r) {
+                const size_t p = p0 + r;
+                return a.peer_base[a.row_rank[p]] + a.peer_off + (size_t)a.row_place[p] * a.out_stride * 2u + seg +
+                       h * 64u;
+              });
+            } else {
+              uint8_t *base = reinterpret_cast<uint8_t *>(a.out_bf16) + p0 * a.out_stride * 2u + seg + h * 64u;
+              put_rows(w, [&](uint32_t r) { return base + (size_t)r * a.out_stride * 2u; });
+            }
+          }
+        } else {
           float o[64];
-          bool bad = false;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            o[2 * i] = rb ? round_bf16(acc[i].x) : acc[i].x;
-            o[2 * i + 1] = rb ? round_bf16(acc[i].y) : acc[i].y;
-            bad |= !finite(o[2 * i]) || !finite(o[2 * i + 1]);
+            o[2 * i] = rb ? __uint_as_float(pk[i] << 16) : acc[i].x;
+            o[2 * i + 1] = rb ? __uint_as_float(pk[i] & 0xffff0000u) : acc[i].y;
           }
-          if (a.out_bf16 || a.peer_base) {  // exact: the values are bf16-rounded
-            const size_t p = grp.tok_begin + t_local;
-            uint16_t *row = a.peer_base ? reinterpret_cast<uint16_t *>(a.peer_base[a.row_rank[p]] + a.peer_off) +
-                                              (size_t)a.row_place[p] * a.out_stride
-                                        : a.out_bf16 + p * a.out_stride;
-            uint4 *d16 = reinterpret_cast<uint4 *>(row + row0 + col0);
+          if ((a.out_stride & 3u) == 0u && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0u) {
+            uint8_t *base = reinterpret_cast<uint8_t *>(a.out + p0 * a.out_stride + row0 + col0);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float *oo = o + 8 * i;
-              d16[i] = make_uint4((__float_as_uint(oo[0]) >> 16) | (__float_as_uint(oo[1]) & 0xffff0000u),
-                                  (__float_as_uint(oo[2]) >> 16) | (__float_as_uint(oo[3]) & 0xffff0000u),
-                                  (__float_as_uint(oo[4]) >> 16) | (__float_as_uint(oo[5]) & 0xffff0000u),
-                                  (__float_as_uint(oo[6]) >> 16) | (__float_as_uint(oo[7]) & 0xffff0000u));
+            for (uint32_t h = 0; h < 4; ++h) {
+              uint4 w[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                w[i] = make_uint4(__float_as_uint(o[16 * h + 4 * i]), __float_as_uint(o[16 * h + 4 * i + 1]),
+                                  __float_as_uint(o[16 * h + 4 * i + 2]), __float_as_uint(o[16 * h + 4 * i + 3]));
+              put_rows(w, [&](uint32_t r) { return base + (size_t)r * a.out_stride * 4u + h * 64u; });
             }
-          } else {
+          } else if (t_local < cnt) {
             float *dst = a.out + (size_t)(grp.tok_begin + t_local) * a.out_stride + row0 + col0;
-            if ((a.out_stride & 3u) == 0u && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0u) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i)
-                reinterpret_cast<float4 *>(dst)[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 64; ++i) dst[i] = o[i];
-            }
+            for (int i = 0; i < 64; ++i) dst[i] = o[i];
           }
-          if (bad) raise_flag(a.flags, PW_FLAG_NONFINITE_ROUND);
         }
-      } else if (active) {
+      } else {
         // bf16(gate) (from the stash) and bf16(up) (registers): the staged
         // SwiGLU's first roundings; k_swiglu_quant finishes the hidden
-        float g0[32], g1[32];
-        tmem_ld32(stash, g0);
-        tmem_ld32(stash + 32u, g1);
-        tmem_wait_ld();
-        if (t_local < cnt) {
-          const uint32_t I = a.rows;
-          uint4 *gd = reinterpret_cast<uint4 *>(a.gate_bf16 + (size_t)(grp.tok_begin + t_local) * I + row0 + col0);
-          uint4 *ud = reinterpret_cast<uint4 *>(a.up_bf16 + (size_t)(grp.tok_begin + t_local) * I + row0 + col0);
-          auto pack = [](float lo, float hi) {
-            return (__float_as_uint(round_bf16(lo)) >> 16) | (__float_as_uint(round_bf16(hi)) & 0xffff0000u);
-          };
+        const uint32_t I = a.rows;
+        const size_t seg = (size_t)(row0 + col0) * 2u;
+        uint8_t *gbase = reinterpret_cast<uint8_t *>(a.gate_bf16) + p0 * I * 2u + seg;
+        uint8_t *ubase = reinterpret_cast<uint8_t *>(a.up_bf16) + p0 * I * 2u + seg;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float *gs = i < 4 ? g0 + 8 * i : g1 + 8 * (i - 4);
-            gd[i] = make_uint4(pack(gs[0], gs[1]), pack(gs[2], gs[3]), pack(gs[4], gs[5]), pack(gs[6], gs[7]));
-            const float2 *us = acc + 4 * i;
-            ud[i] = make_uint4(pack(us[0].x, us[0].y), pack(us[1].x, us[1].y), pack(us[2].x, us[2].y),
-                               pack(us[3].x, us[3].y));
+        for (uint32_t h = 0; h < 2; ++h) {
+          float g[32];
+          tmem_ld32(stash + h * 32u, g);
+          tmem_wait_ld();
+          uint4 w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            w[i] = make_uint4(pack_bf16x2_rn(g[8 * i], g[8 * i + 1]), pack_bf16x2_rn(g[8 * i + 2], g[8 * i + 3]),
+                              pack_bf16x2_rn(g[8 * i + 4], g[8 * i + 5]),
+                              pack_bf16x2_rn(g[8 * i + 6], g[8 * i + 7]));
+          put_rows(w, [&](uint32_t r) { return gbase + (size_t)r * I * 2u + h * 64u; });
+        }
+#pragma unroll
+        for (uint32_t h = 0; h < 2; ++h) {
+          uint4 w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 *us = acc + 16 * h + 4 * i;
+            w[i] = make_uint4(pack_bf16x2_rn(us[0].x, us[0].y), pack_bf16x2_rn(us[1].x, us[1].y),
+                              pack_bf16x2_rn(us[2].x, us[2].y), pack_bf16x2_rn(us[3].x, us[3].y));
           }
+          put_rows(w, [&](uint32_t r) { return ubase + (size_t)r * I * 2u + h * 64u; });
         }
       }
     }
