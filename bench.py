@@ -224,6 +224,28 @@ def cpu_oracle_experts(bank, router, x, n_experts, threads):
     return (time.perf_counter() - t0) / len(experts), rows / len(experts)
 
 
+# ------------------------------------------------------ the router alone
+def bench_route(rt, dev, stream, iters=20):
+    """The device router (pw_route: f32 logits in the pinned slice order,
+    sigmoid, no-aux top-8) on the prefill batch: 2048 tokens x 4096 over 256
+    experts, bf16 weights and the checkpoint's F32 weights.  us
+    per call (median device time of `iters` calls) and FP32 FMA rate."""
+    import torch
+    from mimo_prismwing_b200 import synth
+    x = synth.activations(PREFILL_TOKENS, HIDDEN, 5000, dev)
+    out = {}
+    for name, (w, bias) in (("bf16", synth.router(EXPERTS, HIDDEN, 7, dev)),
+                            ("f32", synth.router_f32(EXPERTS, HIDDEN, 7, dev))):
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                rt.route(x, w, bias)
+            # device time of each call (events around its kernels; the call
+            # itself synchronises to read the device flags)
+            us = statistics.median(rt.route(x, w, bias)[2]["device_ms"] * 1e3 for _ in range(iters))
+        out[name] = {"us": round(us, 2), "fma_tflops": round(2.0 * PREFILL_TOKENS * EXPERTS * HIDDEN / us / 1e6, 2)}
+    return out
+
+
 # ------------------------------------------------- configs[0], [1], [3]
 def bench_configs(rt, dev, hbm, tflops_fp8, stream, iters=30):
     """The single-projection configs on one GPU.  Each call is measured two
@@ -499,6 +521,10 @@ def run_ours(args, rank, world, local_rank):
     rt.set_stream(stream)
     hbm, peak_kind = peaks()
     tflops_fp8 = fp8_peak_tflops(dev) if rank == 0 else None
+    if args.route_only:  # the router alone (one GPU), for profiling runs
+        print(json.dumps({"route": bench_route(rt, dev, stream)}), flush=True)
+        rt.close()
+        return
     if args.configs_only:  # configs[0]/[1]/[3] alone (one GPU), for profiling runs
         print(json.dumps({"configs": bench_configs(rt, dev, hbm, tflops_fp8, stream),
                           "fp8_peak_tflops": tflops_fp8}), flush=True)
@@ -774,6 +800,7 @@ def main():
     ap.add_argument("--skip-configs", action="store_true", help="skip the configs[0]/[1]/[3] sub-benchmarks")
     ap.add_argument("--configs-only", action="store_true", help="run only the configs[0]/[1]/[3] sub-benchmarks")
     ap.add_argument("--decode-only", action="store_true", help="run only the configs[2] decode layer")
+    ap.add_argument("--route-only", action="store_true", help="run only the prefill batch's router")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange: peer-memory stores (default) or NCCL send/recv")
     # smaller cases for ncu captures only; the metric is quoted at the defaults
