@@ -102,7 +102,7 @@ struct GemmArgs {
   GemvArgs g;
   CUtensorMap xmap[4];
 };
-// Tokens per group (TN) of the tcgen05 GEMM for a kind (0: 128, 2: 64, 3: 128).
+// Tokens per group (TN) of the tcgen05 GEMM (128 for every kind).
 int gemm_tc_tokens(int kind);
 cudaError_t launch_gemm_tc(int kind, const GemmArgs &args, int grid, cudaStream_t stream);
 bool encode_act_maps(CUtensorMap (&out)[4], const void *base, uint32_t rows, uint32_t cols);
@@ -128,9 +128,10 @@ cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_
 // (router_scratch_floats floats), then the sigmoid no-aux top-8.
 size_t router_scratch_floats(uint32_t tokens, uint32_t experts, uint32_t hidden);
 // w: [experts, hidden] router weight, f32 or bf16 bits (w_dtype = PW_ROUTER_*).
+// work: two words, zero before the first launch; the kernels leave them zero.
 cudaError_t launch_router(const float *x, uint32_t tokens, const void *w, uint32_t w_dtype, const float *bias,
                           uint32_t experts, uint32_t hidden, float *scratch, uint32_t *selected, float *weights,
-                          uint32_t *tie_rows, uint32_t *flags, int num_sms, cudaStream_t stream);
+                          uint32_t *tie_rows, uint32_t *flags, uint32_t *work, int num_sms, cudaStream_t stream);
 
 // Device-side schedule for a routed layer: from selected [tokens, 8] build
 // placements ordered by (expert asc, position asc) and the GEMV groups.

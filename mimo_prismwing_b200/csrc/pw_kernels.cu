@@ -311,12 +311,15 @@ struct RouterCursor {
     t0 = (tile / g.tiles_e) * rp::kTok;
   }
   __device__ __forceinline__ bool valid(const RouterUnits &g) const { return u < g.n_units; }
-  __device__ __forceinline__ void next(const RouterUnits &g) {
-    if (++st == rp::kStages) {
-      st = 0;
-      u += gridDim.x;
-      decode(g);
-    }
+  // one stage on; true when the unit is finished (the caller enters the next)
+  __device__ __forceinline__ bool step() {
+    if (++st < rp::kStages) return false;
+    st = 0;
+    return true;
+  }
+  __device__ __forceinline__ void enter(uint32_t unit, const RouterUnits &g) {
+    u = unit;
+    decode(g);
   }
   __device__ __forceinline__ uint32_t base() const { return kRouterSlice * s + rp::kCols * st; }
 };
@@ -382,29 +385,45 @@ __device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterS
   }
 }
 
+// Units (64 tokens x EXPT experts x one 256-column slice) are handed out
+// dynamically: each CTA starts on unit blockIdx.x and takes the next free one
+// from work[0] when it finishes a unit, so the SMs finish together (a fixed
+// round-robin left the last wave ~15% idle).  Results do not depend on which
+// CTA runs a unit.  The last CTA to exit zeroes work[0..1] for the next launch.
 template <bool F32W, int EXPT>
-__global__ void __launch_bounds__(rp::kThreads, 2)
+__global__ void __launch_bounds__(rp::kThreads, 3)
     k_router_partials(const float *__restrict__ x, const void *__restrict__ w, RouterUnits g,
-                      float *__restrict__ part) {
+                      float *__restrict__ part, uint32_t *__restrict__ work) {
   constexpr int NP = EXPT / 32;  // f32x2 expert pairs per thread and token
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char router_smem[];
+  __shared__ uint32_t next_unit;  // written by thread 0 one stage after each unit change
   rp::Smem &sm = *reinterpret_cast<rp::Smem *>(router_smem);
   const uint32_t lane = threadIdx.x % 32u, wp = threadIdx.x / 32u;
   const uint32_t eg = lane % 16u, tg = 2u * wp + lane / 16u;
+  if (threadIdx.x == 0) next_unit = gridDim.x + atomicAdd(work, 1u);
   RouterCursor ld{blockIdx.x, 0, 0, 0, 0};
   ld.decode(g);
-  if (!ld.valid(g)) return;
   RouterCursor cp = ld;
   RouterStage<F32W, EXPT> r;
-  router_gload(x, w, g, ld, r);
-  ld.next(g);
-  router_sstore(sm, 0, r);
+  if (ld.valid(g)) router_gload(x, w, g, ld, r);
+  __syncthreads();  // next_unit
+  bool refresh = false;
+  auto advance_ld = [&]() {
+    if (ld.step()) {
+      ld.enter(next_unit, g);
+      refresh = true;
+    }
+  };
+  if (ld.valid(g)) {
+    advance_ld();
+    router_sstore(sm, 0, r);
+  }
   bool have = ld.valid(g);
   if (have) {
     router_gload(x, w, g, ld, r);
-    ld.next(g);
+    advance_ld();
   }
   __syncthreads();
 
@@ -458,16 +477,30 @@ __global__ void __launch_bounds__(rp::kThreads, 2)
         for (int p = 0; p < NP; ++p) acc[t][p] = make_float2(0.f, 0.f);
       }
     }
-    const bool next_ok = have;
-    if (next_ok) router_sstore(sm, b ^ 1, r);
+    if (have) router_sstore(sm, b ^ 1, r);
     have = ld.valid(g);
     if (have) {
       router_gload(x, w, g, ld, r);
-      ld.next(g);
+      advance_ld();
     }
     __syncthreads();
+    // every thread has read next_unit for the unit ld entered before this
+    // barrier; the next read is a whole unit (8 stages, 8 barriers) away
+    if (refresh) {
+      if (threadIdx.x == 0) next_unit = gridDim.x + atomicAdd(work, 1u);
+      refresh = false;
+    }
     b ^= 1;
-    cp.next(g);
+    // the loader runs two stages ahead and a unit has eight: the unit the
+    // compute cursor enters is the one the loader is in
+    if (cp.step()) cp.enter(ld.u, g);
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(work + 1, 1u) == gridDim.x - 1u) {
+      work[0] = 0u;
+      work[1] = 0u;
+    }
   }
 }
 
@@ -485,6 +518,7 @@ static RouterUnits router_units(uint32_t tokens, uint32_t experts, uint32_t hidd
 }
 
 constexpr uint32_t kRouterPartialMinTokens = 64;  // below: k_router_slices_small
+constexpr uint32_t kRouterCtasPerSm = 3;
 
 size_t router_scratch_floats(uint32_t tokens, uint32_t experts, uint32_t hidden) {
   return (size_t)tokens * experts * (hidden / kRouterSlice);
@@ -616,8 +650,8 @@ __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ s
 }
 
 template <bool F32W, int EXPT>
-static cudaError_t launch_partials(const float *x, const void *w, const RouterUnits &g, float *scratch, int num_sms,
-                                   cudaStream_t stream) {
+static cudaError_t launch_partials(const float *x, const void *w, const RouterUnits &g, float *scratch, uint32_t *work,
+                                   int num_sms, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     const cudaError_t st = cudaFuncSetAttribute(k_router_partials<F32W, EXPT>,
@@ -625,21 +659,23 @@ static cudaError_t launch_partials(const float *x, const void *w, const RouterUn
     if (st != cudaSuccess) return st;
     configured = true;
   }
-  // two 4-warp CTAs per SM: one warp per scheduler left the FMA pipe idle
-  // on every short dependency (measured ~50% FMA-pipe activity)
-  const uint32_t grid = g.n_units < 2u * (uint32_t)num_sms ? g.n_units : 2u * (uint32_t)num_sms;
+  // three 4-warp CTAs per SM: with fewer warps per scheduler the FMA pipe
+  // idled on every short dependency (one CTA: ~50% FMA-pipe activity, two: 58%)
+  const uint32_t slots = kRouterCtasPerSm * (uint32_t)num_sms;
+  const uint32_t grid = g.n_units < slots ? g.n_units : slots;
   return launch_kernel(k_router_partials<F32W, EXPT>, dim3(grid), dim3(rp::kThreads), sizeof(rp::Smem), stream, x, w,
-                       g, scratch);
+                       g, scratch, work);
 }
 
 template <bool F32W>
 static cudaError_t launch_router_logits(const float *x, uint32_t tokens, const void *w, const RouterUnits &g,
-                                        float *scratch, int num_sms, cudaStream_t stream) {
+                                        float *scratch, uint32_t *work, int num_sms, cudaStream_t stream) {
   if (tokens >= kRouterPartialMinTokens) {
     // 128-expert units unless they would leave CTA slots idle
-    if (g.n_units >= 2u * (uint32_t)num_sms) return launch_partials<F32W, 128>(x, w, g, scratch, num_sms, stream);
+    if (g.n_units >= kRouterCtasPerSm * (uint32_t)num_sms)
+      return launch_partials<F32W, 128>(x, w, g, scratch, work, num_sms, stream);
     const RouterUnits g64 = router_units(g.tokens, g.experts, g.hidden, 64u);
-    return launch_partials<F32W, 64>(x, w, g64, scratch, num_sms, stream);
+    return launch_partials<F32W, 64>(x, w, g64, scratch, work, num_sms, stream);
   }
   using WT = typename std::conditional<F32W, float, uint16_t>::type;
   return launch_kernel(k_router_slices_small<WT>,
@@ -649,13 +685,14 @@ static cudaError_t launch_router_logits(const float *x, uint32_t tokens, const v
 
 cudaError_t launch_router(const float *x, uint32_t tokens, const void *w, uint32_t w_dtype, const float *bias,
                           uint32_t experts, uint32_t hidden, float *scratch, uint32_t *selected, float *weights,
-                          uint32_t *tie_rows, uint32_t *flags, int num_sms, cudaStream_t stream) {
+                          uint32_t *tie_rows, uint32_t *flags, uint32_t *work, int num_sms, cudaStream_t stream) {
   if (hidden % 512u || hidden > kRouterSlice * kRouterMaxSlices || tokens == 0 || experts <= 8 || experts > 1024u ||
       (w_dtype != PW_ROUTER_BF16 && w_dtype != PW_ROUTER_F32))
     return cudaErrorInvalidValue;
   const RouterUnits g = router_units(tokens, experts, hidden);
-  cudaError_t st = w_dtype == PW_ROUTER_F32 ? launch_router_logits<true>(x, tokens, w, g, scratch, num_sms, stream)
-                                            : launch_router_logits<false>(x, tokens, w, g, scratch, num_sms, stream);
+  cudaError_t st = w_dtype == PW_ROUTER_F32
+                       ? launch_router_logits<true>(x, tokens, w, g, scratch, work, num_sms, stream)
+                       : launch_router_logits<false>(x, tokens, w, g, scratch, work, num_sms, stream);
   if (st != cudaSuccess) return st;
   // persistent: up to two 8-warp CTAs per SM, each warp looping over tokens
   uint32_t blocks = (tokens + 7u) / 8u;

@@ -117,6 +117,7 @@ struct pw_runtime {
   uint32_t *d_flags = nullptr;            // error-flag word
   unsigned long long *d_bad = nullptr;    // validation: first bad byte
   uint32_t *d_ties = nullptr;             // router tie rows
+  uint32_t *d_router_work = nullptr;      // router unit counters (two words, left zero)
   void *scratch = nullptr;
   size_t scratch_cap = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -572,6 +573,7 @@ int pw_runtime_create(int device, uint32_t flags, pw_runtime **out) {
   if ((e = cudaMalloc(&rt->d_flags, 256)) != cudaSuccess) return bail(e);
   rt->d_bad = reinterpret_cast<unsigned long long *>(reinterpret_cast<char *>(rt->d_flags) + 64);
   rt->d_ties = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(rt->d_flags) + 128);
+  rt->d_router_work = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(rt->d_flags) + 192);
   if ((e = cudaMemset(rt->d_flags, 0, 256)) != cudaSuccess) return bail(e);
   if ((e = cudaEventCreate(&rt->ev0)) != cudaSuccess) return bail(e);
   if ((e = cudaEventCreate(&rt->ev1)) != cudaSuccess) return bail(e);
@@ -1266,7 +1268,7 @@ int pw_route(pw_runtime *rt, const pw_router *router, const float *x, uint32_t t
     {
       ProfScope ps(rt, P_ROUTER, 2);
       CK(launch_router(dx, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, dsel, dw,
-                       rt->d_ties, rt->d_flags, rt->num_sms, rt->stream));
+                       rt->d_ties, rt->d_flags, rt->d_router_work, rt->num_sms, rt->stream));
     }
     if (call.host()) {
       if ((s = call.stage_out(selected, dsel, (size_t)tokens * 32)) != PW_OK) return s;
@@ -1601,7 +1603,7 @@ static int moe_layer_impl(pw_runtime *rt, const pw_norm *norm, const pw_router *
     {
       ProfScope ps(rt, P_ROUTER, 2);
       CK(launch_router(dn, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, sel, wts,
-                       rt->d_ties, rt->d_flags, rt->num_sms, rt->stream));
+                       rt->d_ties, rt->d_flags, rt->d_router_work, rt->num_sms, rt->stream));
     }
     {
       ProfScope ps(rt, P_SCHED, 3);
@@ -2124,7 +2126,7 @@ static int ep_moe_layer_impl(pw_runtime *rt, const pw_norm *norm, const pw_route
     {
       ProfScope ps(rt, P_ROUTER, 2);
       CK(launch_router(dnorm, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, sel, wts,
-                       rt->d_ties, rt->d_flags, rt->num_sms, rt->stream));
+                       rt->d_ties, rt->d_flags, rt->d_router_work, rt->num_sms, rt->stream));
     }
     {
       ProfScope ps(rt, P_SCHED, 4);
