@@ -1388,13 +1388,22 @@ __device__ __forceinline__ void swiglu_chunk_finish(const SwigluChunk &c, const 
   bool fin = true;
   float m = 0.0f;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const uint32_t gb = (k & 1) ? (gw[k / 2] >> 16) : (gw[k / 2] & 0xffffu);
-    const float silu = __uint_as_float((uint32_t)slut[gb] << 16);
-    const float u = __uint_as_float((k & 1) ? (uw[k / 2] & 0xffff0000u) : (uw[k / 2] << 16));
-    v[k] = round_bf16(__fmul_rn(silu, round_bf16(u)));
-    fin = fin && finite(v[k]);
-    m = fmaxf(m, fabsf(v[k]));
+  for (int k = 0; k < 8; k += 2) {
+    // h = bf16(silu * u); u is already a bf16 value, so its own rounding is
+    // the identity (a NaN anywhere is an error)
+    float p[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t gb = ((k + j) & 1) ? (gw[(k + j) / 2] >> 16) : (gw[(k + j) / 2] & 0xffffu);
+      const float silu = __uint_as_float((uint32_t)slut[gb] << 16);
+      const float u = __uint_as_float(((k + j) & 1) ? (uw[(k + j) / 2] & 0xffff0000u) : (uw[(k + j) / 2] << 16));
+      p[j] = __fmul_rn(silu, u);
+    }
+    const uint32_t hb = pack_bf16x2_rn(p[0], p[1]);
+    v[k] = __uint_as_float(hb << 16);
+    v[k + 1] = __uint_as_float(hb & 0xffff0000u);
+    fin = fin && finite(v[k]) && finite(v[k + 1]);
+    m = fmaxf(m, fmaxf(fabsf(v[k]), fabsf(v[k + 1])));
   }
   if (ok && !fin) raise_flag(flags, PW_FLAG_NONFINITE_FUSED);
 #pragma unroll
@@ -1406,7 +1415,20 @@ __device__ __forceinline__ void swiglu_chunk_finish(const SwigluChunk &c, const 
     hp[1] = make_float4(v[4], v[5], v[6], v[7]);
   }
   const float scale = __fdiv_rn(fmaxf(m, 1.0e-10f), 448.0f);
-  auto q = [&](float val) { return fminf(fmaxf(__fdiv_rn(val, scale), -448.0f), 448.0f); };
+  // val / scale, correctly rounded, without a division per value: Markstein's
+  // method (P. Markstein, IBM J. Res. Dev. 34(1), 1990; the division theorem
+  // in Muller et al., Handbook of Floating-Point Arithmetic): with r = RN(1/scale),
+  // q1 = q0 + (val - q0 scale) r is a faithful quotient, and one more
+  // correction from the exact FMA remainder of a faithful quotient is
+  // RN(val / scale).  No overflow (|val| <= scale * 448) and no underflow that
+  // could reach a code (|quotient| < 2^-10 encodes to zero either way).
+  const float rcp = __frcp_rn(scale);
+  auto q = [&](float val) {
+    const float q0 = __fmul_rn(val, rcp);
+    const float q1 = __fmaf_rn(__fmaf_rn(-q0, scale, val), rcp, q0);
+    const float qr = __fmaf_rn(__fmaf_rn(-q1, scale, val), rcp, q1);
+    return fminf(fmaxf(qr, -448.0f), 448.0f);
+  };
   const uint32_t w0 = encode2(q(v[0]), q(v[1])) | (encode2(q(v[2]), q(v[3])) << 16);
   const uint32_t w1 = encode2(q(v[4]), q(v[5])) | (encode2(q(v[6]), q(v[7])) << 16);
   reinterpret_cast<uint2 *>(codes)[chunk] = make_uint2(w0, w1);

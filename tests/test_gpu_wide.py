@@ -80,6 +80,22 @@ def test_wide_fused_gate_up_is_exact_against_unfused(rt, rt_unfused):
         assert np.array_equal(a, b), f"width {width}"
 
 
+def test_wide_fused_quantizer_exact_over_magnitudes(rt, rt_unfused):
+    # The fused path quantizes the SwiGLU output with reciprocal-based
+    # quotients; the unfused path divides (pw_quantize semantics).  Token rows
+    # scaled by 2^-40 .. 2^40 put the hidden values and their group scales
+    # across ~80 binades; every hidden code, hence every down row, must match.
+    from mimo_prismwing_b200 import synth
+    g, u, d = synth.expert(2048, 1024, 23, "cuda")
+    width = 512
+    x = synth.activations(width, 2048, 77, "cuda")
+    k = torch.arange(width, device="cuda", dtype=torch.float32)
+    x = x * torch.exp2(torch.remainder(k * 37.0, 81.0) - 40.0).unsqueeze(1)
+    a = H(rt.expert_forward(x, g, u, d).output)
+    b = H(rt_unfused.expert_forward(x, g, u, d).output)
+    assert np.array_equal(a, b)
+
+
 def test_wide_host_schedule_vs_oracle(rt):
     # every token routed to all 8 experts: 64 placements per expert (> 16)
     from gpu_helpers import assert_close_bf16, bank_arrays
