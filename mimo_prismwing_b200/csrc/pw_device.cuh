@@ -36,10 +36,44 @@ __device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
   return d;
 }
 
+// Four values bf16-rounded (as f32) by two conversion instructions.
+__device__ __forceinline__ float4 round_bf16x4(float4 v) {
+  const uint32_t a = pack_bf16x2_rn(v.x, v.y), b = pack_bf16x2_rn(v.z, v.w);
+  return make_float4(__uint_as_float(a << 16), __uint_as_float(a & 0xffff0000u), __uint_as_float(b << 16),
+                     __uint_as_float(b & 0xffff0000u));
+}
+
 // Smallest |f32| bit pattern that bf16 rounding turns into an infinity: the
 // halfway point above the largest finite bf16 (0x7f7f, odd), where round to
 // nearest even goes up to 0x7f80.
 constexpr uint32_t kBf16OverflowBits = 0x7f7f8000u;
+
+// Dynamic FP8 quantization of a 128-value group (src/text_endpoint.rs:3008):
+// scale = max(absmax, 1e-10) / 448 and code = e4m3(clamp(value / scale)).
+// The quotients are correctly rounded without a division per value, by
+// Markstein's method (P. Markstein, IBM J. Res. Dev. 34(1), 1990; the division
+// theorem in Muller et al., Handbook of Floating-Point Arithmetic): with
+// rcp = RN(1/scale), q1 = q0 + (value - q0 scale) rcp is a faithful quotient,
+// and one more correction from the exact FMA remainder of a faithful quotient
+// gives RN(value / scale).  In range: |value| <= 448 scale (no overflow), and
+// quotients small enough to meet underflow (< 2^-10) encode to zero either way.
+// The sign is the value's (scale > 0): the corrections can turn -0 into +0.
+struct Fp8GroupScale {
+  float scale, rcp;
+  __device__ __forceinline__ static Fp8GroupScale of(float absmax) {
+    Fp8GroupScale g;
+    g.scale = __fdiv_rn(fmaxf(absmax, 1.0e-10f), 448.0f);
+    g.rcp = __frcp_rn(g.scale);
+    return g;
+  }
+  // clamp(RN(value / scale), -448, 448)
+  __device__ __forceinline__ float quotient(float value) const {
+    const float q0 = __fmul_rn(value, rcp);
+    const float q1 = __fmaf_rn(__fmaf_rn(-q0, scale, value), rcp, q0);
+    const float q = copysignf(__fmaf_rn(__fmaf_rn(-q1, scale, value), rcp, q1), value);
+    return fminf(fmaxf(q, -448.0f), 448.0f);
+  }
+};
 
 // 4 packed e4m3 bytes -> 4 floats (byte 0 -> out[0]).  Exact.
 __device__ __forceinline__ void decode4(uint32_t w, float &o0, float &o1, float &o2, float &o3) {

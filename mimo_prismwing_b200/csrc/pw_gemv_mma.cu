@@ -504,15 +504,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, cons
         M0 = fmaxf(M0, sh.amax[w * 8 + tig * 2u]);
         M1 = fmaxf(M1, sh.amax[w * 8 + tig * 2u + 1u]);
       }
-      const float sc0 = __fdiv_rn(fmaxf(M0, 1.0e-10f), 448.0f);
-      const float sc1 = __fdiv_rn(fmaxf(M1, 1.0e-10f), 448.0f);
+      const Fp8GroupScale g0 = Fp8GroupScale::of(M0), g1 = Fp8GroupScale::of(M1);
+      const float sc0 = g0.scale, sc1 = g1.scale;
       const uint32_t I = a.rows;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint32_t t = tig * 2u + (i & 1u);
         if (t < grp.count) {
-          const float sc = (i & 1) ? sc1 : sc0;
-          const float q = fminf(fmaxf(__fdiv_rn(outv[i], sc), -448.0f), 448.0f);
+          const float q = (i & 1) ? g1.quotient(outv[i]) : g0.quotient(outv[i]);
           const uint32_t r = row0 + warp * 16u + gid + (i >= 2 ? 8u : 0u);
           a.q_codes[(size_t)(grp.tok_begin + t) * I + r] = (uint8_t)(encode2(q, 0.0f) & 0xffu);
         }

@@ -17,8 +17,9 @@ void set_pdl(bool on) { t_pdl = on; }
 // ------------------------------------------------------------ quantization
 // One warp per 128-value group (src/text_endpoint.rs:3008,
 // kernels/block_fp8_gemv.metal:84): absmax, scale = max(absmax,1e-10)/448,
-// code = RNE_e4m3(clamp(x/scale, +-448)).  IEEE divisions (__fdiv_rn) keep it
-// bit-exact with the reference; lane l holds values 4l..4l+3.
+// code = RNE_e4m3(clamp(x/scale, +-448)).  The scale is an IEEE division and
+// the quotients are correctly rounded (Fp8GroupScale), so the bytes match the
+// reference's; lane l holds values 4l..4l+3.
 __global__ void k_quantize(const float *__restrict__ x, uint64_t groups, uint8_t *__restrict__ codes,
                            float *__restrict__ scales, uint32_t *flags, const uint32_t *rows_dev,
                            uint32_t groups_per_row, uint32_t *zero, uint32_t n_zero) {
@@ -38,8 +39,9 @@ __global__ void k_quantize(const float *__restrict__ x, uint64_t groups, uint8_t
     float m = ok ? fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))) : 0.0f;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float scale = __fdiv_rn(fmaxf(m, 1.0e-10f), 448.0f);
-    auto q = [&](float val) { return fminf(fmaxf(__fdiv_rn(val, scale), -448.0f), 448.0f); };
+    const Fp8GroupScale gs = Fp8GroupScale::of(m);
+    const float scale = gs.scale;
+    auto q = [&](float val) { return gs.quotient(val); };
     const uint32_t lo = encode2(q(v.x), q(v.y));
     const uint32_t hi = encode2(q(v.z), q(v.w));
     reinterpret_cast<uint32_t *>(codes + g * 128u)[lane] = lo | (hi << 16);
@@ -155,8 +157,9 @@ __global__ void __launch_bounds__(256) k_rms_quantize(const float *__restrict__ 
     float m = fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3])));
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    const float scale = __fdiv_rn(fmaxf(m, 1.0e-10f), 448.0f);
-    auto q = [&](float val) { return fminf(fmaxf(__fdiv_rn(val, scale), -448.0f), 448.0f); };
+    const Fp8GroupScale gs = Fp8GroupScale::of(m);
+    const float scale = gs.scale;
+    auto q = [&](float val) { return gs.quotient(val); };
     const uint32_t lo = encode2(q(o[0]), q(o[1]));
     const uint32_t hi = encode2(q(o[2]), q(o[3]));
     if (codes) reinterpret_cast<uint32_t *>(codes + (size_t)row * cols + 128u * g)[lane] = lo | (hi << 16);
@@ -1195,18 +1198,13 @@ __global__ void k_combine(const T *__restrict__ down, const uint32_t *__restrict
         acc.z = __fadd_rn(acc.z, __fmul_rn(d[h][k].z, wt[k]));
         acc.w = __fadd_rn(acc.w, __fmul_rn(d[h][k].w, wt[k]));
       }
-      acc.x = round_bf16(acc.x);
-      acc.y = round_bf16(acc.y);
-      acc.z = round_bf16(acc.z);
-      acc.w = round_bf16(acc.w);
+      acc = round_bf16x4(acc);
       if (!finite(acc.x) || !finite(acc.y) || !finite(acc.z) || !finite(acc.w))
         raise_flag(flags, PW_FLAG_NONFINITE_COMBINE);
       if (residual) {  // the decoder layer's residual add: bf16(residual + mlp) (src/text_endpoint.rs:5576-5580)
         const float4 r = __ldg(reinterpret_cast<const float4 *>(residual + (size_t)t * hidden) + 2u * c8 + h);
-        acc.x = round_bf16(__fadd_rn(r.x, acc.x));
-        acc.y = round_bf16(__fadd_rn(r.y, acc.y));
-        acc.z = round_bf16(__fadd_rn(r.z, acc.z));
-        acc.w = round_bf16(__fadd_rn(r.w, acc.w));
+        acc = round_bf16x4(make_float4(__fadd_rn(r.x, acc.x), __fadd_rn(r.y, acc.y), __fadd_rn(r.z, acc.z),
+                                       __fadd_rn(r.w, acc.w)));
       }
       reinterpret_cast<float4 *>(y + (size_t)t * hidden)[2u * c8 + h] = acc;
     }
@@ -1414,21 +1412,9 @@ __device__ __forceinline__ void swiglu_chunk_finish(const SwigluChunk &c, const 
     hp[0] = make_float4(v[0], v[1], v[2], v[3]);
     hp[1] = make_float4(v[4], v[5], v[6], v[7]);
   }
-  const float scale = __fdiv_rn(fmaxf(m, 1.0e-10f), 448.0f);
-  // val / scale, correctly rounded, without a division per value: Markstein's
-  // method (P. Markstein, IBM J. Res. Dev. 34(1), 1990; the division theorem
-  // in Muller et al., Handbook of Floating-Point Arithmetic): with r = RN(1/scale),
-  // q1 = q0 + (val - q0 scale) r is a faithful quotient, and one more
-  // correction from the exact FMA remainder of a faithful quotient is
-  // RN(val / scale).  No overflow (|val| <= scale * 448) and no underflow that
-  // could reach a code (|quotient| < 2^-10 encodes to zero either way).
-  const float rcp = __frcp_rn(scale);
-  auto q = [&](float val) {
-    const float q0 = __fmul_rn(val, rcp);
-    const float q1 = __fmaf_rn(__fmaf_rn(-q0, scale, val), rcp, q0);
-    const float qr = __fmaf_rn(__fmaf_rn(-q1, scale, val), rcp, q1);
-    return fminf(fmaxf(qr, -448.0f), 448.0f);
-  };
+  const Fp8GroupScale gs = Fp8GroupScale::of(m);
+  const float scale = gs.scale;
+  auto q = [&](float val) { return gs.quotient(val); };
   const uint32_t w0 = encode2(q(v[0]), q(v[1])) | (encode2(q(v[2]), q(v[3])) << 16);
   const uint32_t w1 = encode2(q(v[4]), q(v[5])) | (encode2(q(v[6]), q(v[7])) << 16);
   reinterpret_cast<uint2 *>(codes)[chunk] = make_uint2(w0, w1);
