@@ -63,9 +63,9 @@ PREFILL_TOKENS, STACK_LAYERS, DECODE_TOKENS = 2048, 48, 8
 METRIC = "EP prefill tok/s (2048-token batch through the 48-layer routed-MoE stack)"
 DECODE_METRIC = "routed FP8 MoE layer us @width 8"
 # DRAM traffic / algorithmic bytes of the fused gate/up GEMM, from one ncu
-# capture of a 64-expert, 512-token layer (1.129 GB read+written for 1.125 GB
+# capture of a 64-expert, 512-token layer (1.1275 GB read+written for 1.1249 GB
 # of algorithmic bytes); traffic grows in proportion to the experts streamed.
-GATE_UP_GEMM_TRAFFIC_RATIO = (1.094376 + 0.034642) / 1.12486
+GATE_UP_GEMM_TRAFFIC_RATIO = (1.094637 + 0.032880) / 1.12486
 # the same for the fused gate/up GEMV from one capture of the decode layer
 GATE_UP_GEMV_TRAFFIC_RATIO = 507.55 / 503.84
 
