@@ -435,30 +435,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvArgs a, cons
       named_bar_sync(1, kConsumerThreads);
       if (!*sh.last) continue;
       __threadfence();
-#pragma unroll 1
-      for (uint32_t sp = 0; sp < geo.splits; ++sp) {
+      // every other subtree in one round of loads, then the fixed pairwise
+      // tree over the splits (each split is a whole subtree of the 8 leaves)
+      float part[8][MATS][4];
+#pragma unroll
+      for (uint32_t sp = 0; sp < 8u; ++sp) {
         const float *src = a.split_ws + ((size_t)(tile * geo.splits + sp) * MATS) * 1024u;
 #pragma unroll
         for (int m = 0; m < MATS; ++m)
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            acc[m][i] = __ldcg(src + m * 1024 + (warp * 16u + gid + (i >= 2 ? 8u : 0u)) * 8u + tig * 2u + (i & 1u));
-        if ((sp & 1u) == 0u) {
-          if (sp + 1u < geo.splits) tree_copy<MATS>(s0, acc);
-        } else {
-          tree_add<MATS>(acc, s0);
-          if ((sp & 2u) == 0u) {
-            if (sp + 1u < geo.splits) tree_copy<MATS>(s1, acc);
-          } else {
-            tree_add<MATS>(acc, s1);
-            if ((sp & 4u) == 0u) {
-              if (sp + 1u < geo.splits) tree_copy<MATS>(s2, acc);
-            } else {
-              tree_add<MATS>(acc, s2);
-            }
-          }
-        }
+            part[sp][m][i] = sp == split ? acc[m][i]
+                             : sp < geo.splits
+                                 ? __ldcg(src + m * 1024 + (warp * 16u + gid + (i >= 2 ? 8u : 0u)) * 8u + tig * 2u +
+                                          (i & 1u))
+                                 : 0.0f;
       }
+#pragma unroll
+      for (int m = 0; m < MATS; ++m)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float p01 = __fadd_rn(part[0][m][i], part[1][m][i]);
+          const float p23 = __fadd_rn(part[2][m][i], part[3][m][i]);
+          const float p45 = __fadd_rn(part[4][m][i], part[5][m][i]);
+          const float p67 = __fadd_rn(part[6][m][i], part[7][m][i]);
+          acc[m][i] = geo.splits == 2u   ? p01
+                      : geo.splits == 4u ? __fadd_rn(p01, p23)
+                                         : __fadd_rn(__fadd_rn(p01, p23), __fadd_rn(p45, p67));
+        }
       if (threadIdx.x == 0) a.split_cnt[tile] = 0u;  // ready for the next call
     }
 

@@ -729,6 +729,7 @@ constexpr uint32_t kSchedMaxTokens = 2048;
 constexpr uint32_t kSchedMaxExperts = 256;
 constexpr uint32_t kSchedWords = kSchedMaxTokens / 32u;
 constexpr uint32_t kSchedThreads = 1024;
+static_assert(kSchedMaxExperts * 4u <= kSchedThreads, "four scan threads and one group writer per expert");
 
 size_t schedule_work_words(uint32_t experts) { return 2u * (size_t)experts * kSchedWords + kSchedWords + 1u; }
 
@@ -801,7 +802,28 @@ __global__ void __launch_bounds__(kSchedThreads) k_sched_scan(uint32_t tokens, u
     uniq = 0;
     maxc = 0;
   }
-  const int bad = __syncthreads_or(tid < words && badw[tid] != 0u);
+  // every global load this kernel needs is issued up front, so its latency
+  // is paid once: the per-word error flags, the mask words (four threads per
+  // expert, experts <= 256, up to 16 words each) and the expert's bank entries
+  const uint32_t ex = tid / 4u, q = tid % 4u;
+  const uint32_t per = (words + 3u) / 4u, w0 = min(words, q * per), w1 = min(words, w0 + per);
+  const bool badword = tid < words && badw[tid] != 0u;
+  uint32_t mw[kSchedWords / 4u];
+#pragma unroll
+  for (uint32_t k = 0; k < kSchedWords / 4u; ++k)
+    mw[k] = ex < experts && w0 + k < w1 ? mask[ex * kSchedWords + w0 + k] : 0u;
+  const bool has_bank = out.gu_groups && tid < experts;
+  const uint8_t *bw[3] = {nullptr, nullptr, nullptr};
+  const float *bs[3] = {nullptr, nullptr, nullptr};
+  if (has_bank) {
+    bw[0] = bank.gate_w[tid];
+    bs[0] = bank.gate_s[tid];
+    bw[1] = bank.up_w[tid];
+    bs[1] = bank.up_s[tid];
+    bw[2] = bank.down_w[tid];
+    bs[2] = bank.down_s[tid];
+  }
+  const int bad = __syncthreads_or(badword);
   if (bad) {
     if (tid == 0) {
       raise_flag(flags, PW_FLAG_BAD_EXPERT_COUNT);
@@ -811,14 +833,6 @@ __global__ void __launch_bounds__(kSchedThreads) k_sched_scan(uint32_t tokens, u
     return;
   }
   if (tid == 0) *summary = 0u;
-  // per-expert counts, four threads per expert (experts <= 256), each with
-  // up to 16 mask words held in registers (all loads issued together)
-  const uint32_t ex = tid / 4u, q = tid % 4u;
-  const uint32_t per = (words + 3u) / 4u, w0 = min(words, q * per), w1 = min(words, w0 + per);
-  uint32_t mw[kSchedWords / 4u];
-#pragma unroll
-  for (uint32_t k = 0; k < kSchedWords / 4u; ++k)
-    mw[k] = ex < experts && w0 + k < w1 ? mask[ex * kSchedWords + w0 + k] : 0u;
   uint32_t local = 0;
 #pragma unroll
   for (uint32_t k = 0; k < kSchedWords / 4u; ++k) local += __popc(mw[k]);
@@ -887,8 +901,10 @@ __global__ void __launch_bounds__(kSchedThreads) k_sched_scan(uint32_t tokens, u
     }
   }
   // GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
-  // (skipped when the caller runs the experts elsewhere: no group arrays)
-  for (uint32_t e = tid; e < experts && out.gu_groups; e += kSchedThreads) {
+  // (skipped when the caller runs the experts elsewhere: no group arrays);
+  // thread e writes expert e's (experts <= kSchedMaxExperts <= threads)
+  if (has_bank) {
+    const uint32_t e = tid;
     const uint32_t c = off[e + 1] - off[e];
     for (uint32_t j = 0; j * chunk < c; ++j) {
       GemvGroup g;
@@ -896,16 +912,16 @@ __global__ void __launch_bounds__(kSchedThreads) k_sched_scan(uint32_t tokens, u
       g.count = min(chunk, c - chunk * j);
       g.expert = e;
       g.pad = 0;
-      g.w0 = bank.gate_w[e];
-      g.s0 = bank.gate_s[e];
-      g.w1 = bank.up_w[e];
-      g.s1 = bank.up_s[e];
+      g.w0 = bw[0];
+      g.s0 = bs[0];
+      g.w1 = bw[1];
+      g.s1 = bs[1];
       g.tm0 = bank.gate_tm + e;
       g.tm1 = bank.up_tm + e;
       out.gu_groups[grp_off[e] + j] = g;
       GemvGroup d = g;
-      d.w0 = bank.down_w[e];
-      d.s0 = bank.down_s[e];
+      d.w0 = bw[2];
+      d.s0 = bs[2];
       d.w1 = nullptr;
       d.s1 = nullptr;
       d.tm0 = bank.down_tm + e;

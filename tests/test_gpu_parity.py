@@ -431,6 +431,33 @@ def test_moe_layer_device_router_vs_oracle(rt, tokens, E, Hd, I):
     assert np.array_equal(ex2.output.numpy(), H(ex.output))
 
 
+@pytest.mark.parametrize("tokens", [1, 8])
+def test_moe_layer_equals_host_schedule_bitwise(rt, tokens):
+    # The device-routed decode layer (device router, schedule and groups) and
+    # the host-scheduled execute (src/wide_metal_moe.rs:836) over the same
+    # routes run the same GEMVs and combine order: bit-identical outputs.
+    from mimo_prismwing_b200 import synth
+    from mimo_prismwing_b200.runtime import WideExpertBinding
+    E, Hd, I = 256, 4096, 2048
+    bank = _small_bank(E, Hd, I, 12)
+    handle = rt.create_bank(bank)
+    w, bias = synth.router(E, Hd, 13, "cuda")
+    x = synth.activations(tokens, Hd, 14 + tokens, "cuda")
+    ex = rt.moe_layer(x, w, bias, handle, want_routes=True)
+    sel = H(ex.selected).astype(np.uint32)
+    wts = H(ex.weights)
+    offsets, order = O.schedule(sel, E)
+    bindings = []
+    for e in range(E):
+        pl = order[offsets[e]:offsets[e + 1]]
+        if len(pl):
+            g, u, d = bank[e]
+            bindings.append(WideExpertBinding(e, [int(p) // 8 for p in pl], [float(wts.ravel()[p]) for p in pl],
+                                              g, u, d))
+    ref = rt.execute_fused_gate_up(x, bindings)
+    assert np.array_equal(H(ex.output), H(ref.output))
+
+
 def test_bank_rejects_nonfinite_weight_byte(rt):
     from mimo_prismwing_b200.runtime import PrismwingError
     bank = _small_bank(9, 256, 256, 12)
