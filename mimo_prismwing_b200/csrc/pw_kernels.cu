@@ -674,8 +674,12 @@ template <bool F32W>
 static cudaError_t launch_router_logits(const float *x, uint32_t tokens, const void *w, const RouterUnits &g,
                                         float *scratch, uint32_t *work, int num_sms, cudaStream_t stream) {
   if (tokens >= kRouterPartialMinTokens) {
-    // 128-expert units unless they would leave CTA slots idle
-    if (g.n_units >= kRouterCtasPerSm * (uint32_t)num_sms)
+    // 128-expert units when there are at least two per CTA slot; with fewer,
+    // most slots would run one or two whole units and the 64-expert units
+    // (twice as many, a bit over half the time each) finish first (measured
+    // at 1024 tokens: 132 vs 104 us; at 2048 tokens 128-expert units win,
+    // 145 vs 182 us)
+    if (g.n_units >= 2u * kRouterCtasPerSm * (uint32_t)num_sms)
       return launch_partials<F32W, 128>(x, w, g, scratch, work, num_sms, stream);
     const RouterUnits g64 = router_units(g.tokens, g.experts, g.hidden, 64u);
     return launch_partials<F32W, 64>(x, w, g64, scratch, work, num_sms, stream);
