@@ -292,16 +292,17 @@ __global__ void __launch_bounds__(256) k_router_slices_small(const float *__rest
 // slice order.  The tile shape changes which thread computes a chain, never
 // the chain.
 namespace rp {
-constexpr int kTok = 64, kExp = 128, kCols = 32, kThreads = 128;
+constexpr int kCols = 32, kThreads = 128;
 constexpr uint32_t kStages = kRouterSlice / kCols;
+template <int EXPT, int TOK>
 struct Smem {
-  float xs[2][kCols][kTok];  // activation [column][token]
-  float ws[2][kCols][kExp];  // router weight widened to f32 [column][expert]
+  float xs[2][kCols][TOK];   // activation [column][token]
+  float ws[2][kCols][EXPT];  // router weight widened to f32 [column][expert]
 };
 }  // namespace rp
 
 struct RouterUnits {
-  uint32_t tokens, experts, hidden, slices, tiles_e, n_units, exp_tile;
+  uint32_t tokens, experts, hidden, slices, tiles_e, n_units, exp_tile, tok_tile;
 };
 
 struct RouterCursor {
@@ -311,7 +312,7 @@ struct RouterCursor {
     s = u % g.slices;
     const uint32_t tile = u / g.slices;
     e0 = (tile % g.tiles_e) * g.exp_tile;
-    t0 = (tile / g.tiles_e) * rp::kTok;
+    t0 = (tile / g.tiles_e) * g.tok_tile;
   }
   __device__ __forceinline__ bool valid(const RouterUnits &g) const { return u < g.n_units; }
   // one stage on; true when the unit is finished (the caller enters the next)
@@ -327,24 +328,25 @@ struct RouterCursor {
   __device__ __forceinline__ uint32_t base() const { return kRouterSlice * s + rp::kCols * st; }
 };
 
-// One stage's global loads, fetched a stage ahead: 64 tokens x 32 columns of
+// One stage's global loads, fetched a stage ahead: TOK tokens x 32 columns of
 // x and EXPT experts x 32 columns of the weight.
-template <bool F32W, int EXPT>
+template <bool F32W, int EXPT, int TOK>
 struct RouterStage {
+  static constexpr int kX = TOK * rp::kCols / 4 / rp::kThreads;                      // float4 x loads
   static constexpr int kW = EXPT * rp::kCols * (F32W ? 4 : 2) / 16 / rp::kThreads;  // 16-byte weight loads
-  float4 x[4];
+  float4 x[kX];
   uint4 w[kW];
 };
 
-template <bool F32W, int EXPT>
+template <bool F32W, int EXPT, int TOK>
 __device__ __forceinline__ void router_gload(const float *__restrict__ x, const void *__restrict__ wv,
                                              const RouterUnits &g, const RouterCursor &c,
-                                             RouterStage<F32W, EXPT> &r) {
+                                             RouterStage<F32W, EXPT, TOK> &r) {
   const uint32_t base = c.base();
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
+  for (int m = 0; m < RouterStage<F32W, EXPT, TOK>::kX; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
-    const uint32_t tok = c.t0 + i % 64u, c4 = i / 64u;  // x: token, 4 columns
+    const uint32_t tok = c.t0 + i % (uint32_t)TOK, c4 = i / (uint32_t)TOK;  // x: token, 4 columns
     r.x[m] = tok < g.tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)tok * g.hidden + base + 4u * c4))
                             : make_float4(0.f, 0.f, 0.f, 0.f);
   }
@@ -352,7 +354,7 @@ __device__ __forceinline__ void router_gload(const float *__restrict__ x, const 
   const unsigned char *w = static_cast<const unsigned char *>(wv);
   const size_t esz = F32W ? 4u : 2u;
 #pragma unroll
-  for (int m = 0; m < RouterStage<F32W, EXPT>::kW; ++m) {
+  for (int m = 0; m < RouterStage<F32W, EXPT, TOK>::kW; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
     const uint32_t e = c.e0 + i % (uint32_t)EXPT, cq = i / (uint32_t)EXPT;  // w: expert, kPer columns
     r.w[m] = e < g.experts ? __ldg(reinterpret_cast<const uint4 *>(w + ((size_t)e * g.hidden + base + kPer * cq) * esz))
@@ -360,19 +362,19 @@ __device__ __forceinline__ void router_gload(const float *__restrict__ x, const 
   }
 }
 
-template <bool F32W, int EXPT>
-__device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterStage<F32W, EXPT> &r) {
+template <bool F32W, int EXPT, int TOK>
+__device__ __forceinline__ void router_sstore(rp::Smem<EXPT, TOK> &sm, int b, const RouterStage<F32W, EXPT, TOK> &r) {
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
+  for (int m = 0; m < RouterStage<F32W, EXPT, TOK>::kX; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
-    const uint32_t tok = i % 64u, c4 = i / 64u;
+    const uint32_t tok = i % (uint32_t)TOK, c4 = i / (uint32_t)TOK;
     sm.xs[b][4 * c4 + 0][tok] = r.x[m].x;
     sm.xs[b][4 * c4 + 1][tok] = r.x[m].y;
     sm.xs[b][4 * c4 + 2][tok] = r.x[m].z;
     sm.xs[b][4 * c4 + 3][tok] = r.x[m].w;
   }
 #pragma unroll
-  for (int m = 0; m < RouterStage<F32W, EXPT>::kW; ++m) {
+  for (int m = 0; m < RouterStage<F32W, EXPT, TOK>::kW; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
     const uint32_t e = i % (uint32_t)EXPT, cq = i / (uint32_t)EXPT;
     const uint32_t q[4] = {r.w[m].x, r.w[m].y, r.w[m].z, r.w[m].w};
@@ -388,28 +390,35 @@ __device__ __forceinline__ void router_sstore(rp::Smem &sm, int b, const RouterS
   }
 }
 
-// Units (64 tokens x EXPT experts x one 256-column slice) are handed out
+// Units (TOK tokens x EXPT experts x one 256-column slice) are handed out
 // dynamically: each CTA starts on unit blockIdx.x and takes the next free one
 // from work[0] when it finishes a unit, so the SMs finish together (a fixed
 // round-robin left the last wave ~15% idle).  Results do not depend on which
 // CTA runs a unit.  The last CTA to exit zeroes work[0..1] for the next launch.
-template <bool F32W, int EXPT>
-__global__ void __launch_bounds__(rp::kThreads, 3)
+// Thread (tg, eg) owns tokens TT tg .. TT tg + TT - 1 (TT = TOK / 8).
+template <int EXPT, int TOK>
+constexpr int router_ctas_per_sm() {
+  return TOK == 64 ? 3 : 4;
+}
+
+template <bool F32W, int EXPT, int TOK>
+__global__ void __launch_bounds__(rp::kThreads, router_ctas_per_sm<EXPT, TOK>())
     k_router_partials(const float *__restrict__ x, const void *__restrict__ w, RouterUnits g,
                       float *__restrict__ part, uint32_t *__restrict__ work) {
   constexpr int NP = EXPT / 32;  // f32x2 expert pairs per thread and token
+  constexpr int TT = TOK / 8;    // tokens per thread
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char router_smem[];
   __shared__ uint32_t next_unit;  // written by thread 0 one stage after each unit change
-  rp::Smem &sm = *reinterpret_cast<rp::Smem *>(router_smem);
+  rp::Smem<EXPT, TOK> &sm = *reinterpret_cast<rp::Smem<EXPT, TOK> *>(router_smem);
   const uint32_t lane = threadIdx.x % 32u, wp = threadIdx.x / 32u;
   const uint32_t eg = lane % 16u, tg = 2u * wp + lane / 16u;
   if (threadIdx.x == 0) next_unit = gridDim.x + atomicAdd(work, 1u);
   RouterCursor ld{blockIdx.x, 0, 0, 0, 0};
   ld.decode(g);
   RouterCursor cp = ld;
-  RouterStage<F32W, EXPT> r;
+  RouterStage<F32W, EXPT, TOK> r;
   if (ld.valid(g)) router_gload(x, w, g, ld, r);
   __syncthreads();  // next_unit
   bool refresh = false;
@@ -430,18 +439,24 @@ __global__ void __launch_bounds__(rp::kThreads, 3)
   }
   __syncthreads();
 
-  float2 acc[8][NP];
+  float2 acc[TT][NP];
 #pragma unroll
-  for (int t = 0; t < 8; ++t)
+  for (int t = 0; t < TT; ++t)
 #pragma unroll
     for (int p = 0; p < NP; ++p) acc[t][p] = make_float2(0.f, 0.f);
   int b = 0;
   while (cp.valid(g)) {
 #pragma unroll 4
     for (int k = 0; k < rp::kCols; ++k) {
-      const float4 xa = *reinterpret_cast<const float4 *>(&sm.xs[b][k][8 * tg]);
-      const float4 xb = *reinterpret_cast<const float4 *>(&sm.xs[b][k][8 * tg + 4]);
-      const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      float xv[TT];
+#pragma unroll
+      for (int q = 0; q < TT / 4; ++q) {
+        const float4 xq = *reinterpret_cast<const float4 *>(&sm.xs[b][k][TT * tg + 4 * q]);
+        xv[4 * q] = xq.x;
+        xv[4 * q + 1] = xq.y;
+        xv[4 * q + 2] = xq.z;
+        xv[4 * q + 3] = xq.w;
+      }
       float2 wv[NP];
 #pragma unroll
       for (int h = 0; h < NP / 2; ++h) {
@@ -450,7 +465,7 @@ __global__ void __launch_bounds__(rp::kThreads, 3)
         wv[2 * h + 1] = make_float2(wq.z, wq.w);
       }
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
+      for (int t = 0; t < TT; ++t) {
         const float2 xd = make_float2(xv[t], xv[t]);
 #pragma unroll
         for (int p = 0; p < NP; ++p) acc[t][p] = __ffma2_rn(wv[p], xd, acc[t][p]);
@@ -459,8 +474,8 @@ __global__ void __launch_bounds__(rp::kThreads, 3)
     if (cp.st == rp::kStages - 1u) {  // the unit's slice chains are complete
       float *dst = part + (size_t)cp.s * g.tokens * g.experts;
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const uint32_t tok = cp.t0 + 8u * tg + (uint32_t)t;
+      for (int t = 0; t < TT; ++t) {
+        const uint32_t tok = cp.t0 + (uint32_t)(TT * tg + t);
         if (tok < g.tokens) {
           float *row = dst + (size_t)tok * g.experts;
 #pragma unroll
@@ -507,21 +522,22 @@ __global__ void __launch_bounds__(rp::kThreads, 3)
   }
 }
 
-static RouterUnits router_units(uint32_t tokens, uint32_t experts, uint32_t hidden, uint32_t exp_tile = 128u) {
+static RouterUnits router_units(uint32_t tokens, uint32_t experts, uint32_t hidden, uint32_t exp_tile = 128u,
+                                uint32_t tok_tile = 64u) {
   RouterUnits g{};
   g.tokens = tokens;
   g.experts = experts;
   g.hidden = hidden;
   g.slices = hidden / kRouterSlice;
   g.exp_tile = exp_tile;
+  g.tok_tile = tok_tile;
   g.tiles_e = (experts + exp_tile - 1) / exp_tile;
-  const uint32_t tiles_t = (tokens + rp::kTok - 1) / rp::kTok;
+  const uint32_t tiles_t = (tokens + tok_tile - 1) / tok_tile;
   g.n_units = tiles_t * g.tiles_e * g.slices;
   return g;
 }
 
 constexpr uint32_t kRouterPartialMinTokens = 64;  // below: k_router_slices_small
-constexpr uint32_t kRouterCtasPerSm = 3;
 
 size_t router_scratch_floats(uint32_t tokens, uint32_t experts, uint32_t hidden) {
   return (size_t)tokens * experts * (hidden / kRouterSlice);
@@ -652,21 +668,23 @@ __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ s
   }
 }
 
-template <bool F32W, int EXPT>
+template <bool F32W, int EXPT, int TOK>
 static cudaError_t launch_partials(const float *x, const void *w, const RouterUnits &g, float *scratch, uint32_t *work,
                                    int num_sms, cudaStream_t stream) {
+  using Sm = rp::Smem<EXPT, TOK>;
   static bool configured = false;
   if (!configured) {
-    const cudaError_t st = cudaFuncSetAttribute(k_router_partials<F32W, EXPT>,
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(rp::Smem));
+    const cudaError_t st = cudaFuncSetAttribute(k_router_partials<F32W, EXPT, TOK>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Sm));
     if (st != cudaSuccess) return st;
     configured = true;
   }
-  // three 4-warp CTAs per SM: with fewer warps per scheduler the FMA pipe
-  // idled on every short dependency (one CTA: ~50% FMA-pipe activity, two: 58%)
-  const uint32_t slots = kRouterCtasPerSm * (uint32_t)num_sms;
+  // three or four 4-warp CTAs per SM: with fewer warps per scheduler the FMA
+  // pipe idled on every short dependency (one CTA: ~50% FMA-pipe activity,
+  // two: 58%)
+  const uint32_t slots = (uint32_t)router_ctas_per_sm<EXPT, TOK>() * (uint32_t)num_sms;
   const uint32_t grid = g.n_units < slots ? g.n_units : slots;
-  return launch_kernel(k_router_partials<F32W, EXPT>, dim3(grid), dim3(rp::kThreads), sizeof(rp::Smem), stream, x, w,
+  return launch_kernel(k_router_partials<F32W, EXPT, TOK>, dim3(grid), dim3(rp::kThreads), sizeof(Sm), stream, x, w,
                        g, scratch, work);
 }
 
@@ -674,15 +692,20 @@ template <bool F32W>
 static cudaError_t launch_router_logits(const float *x, uint32_t tokens, const void *w, const RouterUnits &g,
                                         float *scratch, uint32_t *work, int num_sms, cudaStream_t stream) {
   if (tokens >= kRouterPartialMinTokens) {
-    // 128-expert units when there are at least two per CTA slot; with fewer,
-    // most slots would run one or two whole units and the 64-expert units
-    // (twice as many, a bit over half the time each) finish first (measured
-    // at 1024 tokens: 132 vs 104 us; at 2048 tokens 128-expert units win,
-    // 145 vs 182 us)
-    if (g.n_units >= 2u * kRouterCtasPerSm * (uint32_t)num_sms)
-      return launch_partials<F32W, 128>(x, w, g, scratch, work, num_sms, stream);
-    const RouterUnits g64 = router_units(g.tokens, g.experts, g.hidden, 64u);
-    return launch_partials<F32W, 64>(x, w, g64, scratch, work, num_sms, stream);
+    // The largest unit that still gives every CTA slot two or more units:
+    // 64 tokens x 128 experts, then 64 x 64, then 32 x 64.  With fewer units
+    // most slots run one or two whole units and the smaller ones finish first
+    // (measured per pw_route call: 2048 tokens, 145 us with 128-expert units
+    // vs 182 with 64; 1024 tokens, 132 vs 100 vs 121 with 32-token units;
+    // 512 tokens, 97 with 64 x 64 vs 84 with 32 x 64).
+    const uint32_t sms = (uint32_t)num_sms;
+    if (g.n_units >= 2u * (uint32_t)router_ctas_per_sm<128, 64>() * sms)
+      return launch_partials<F32W, 128, 64>(x, w, g, scratch, work, num_sms, stream);
+    const RouterUnits g64 = router_units(g.tokens, g.experts, g.hidden, 64u, 64u);
+    if (g64.n_units >= 2u * (uint32_t)router_ctas_per_sm<64, 64>() * sms)
+      return launch_partials<F32W, 64, 64>(x, w, g64, scratch, work, num_sms, stream);
+    const RouterUnits g32 = router_units(g.tokens, g.experts, g.hidden, 64u, 32u);
+    return launch_partials<F32W, 64, 32>(x, w, g32, scratch, work, num_sms, stream);
   }
   using WT = typename std::conditional<F32W, float, uint16_t>::type;
   return launch_kernel(k_router_slices_small<WT>,
