@@ -546,12 +546,12 @@ def run_ours(args, rank, world, local_rank):
             return rt.moe_layer(x, w, bias, h, stats=profile, out=out)
         return rt.moe_layer(x, w, bias, h, asynchronous=True, out=out)
 
-    def decode_bench():
-        """the 8-token layer, µs per layer (CUDA events over
-        decode_steps layer calls), and the fused gate/up GEMV's HBM rate
-        from profiled calls."""
+    def decode_bench(tokens=DECODE_TOKENS):
+        """the decode layer (8 tokens; also 1), µs per layer (CUDA
+        events over decode_steps layer calls), and the fused gate/up GEMV's
+        HBM rate from profiled calls."""
         gu_b, _ = expert_bytes()
-        Td = DECODE_TOKENS // world + (rank < DECODE_TOKENS % world)
+        Td = tokens // world + (rank < tokens % world)
         xd = [synth.activations(max(Td, 1), HIDDEN, 7000 + 97 * i + rank, dev)[:Td]
               for i in range(args.decode_steps + 3)]
         yd = torch.empty((max(Td, 1), HIDDEN), device=dev)[:Td]
@@ -586,20 +586,28 @@ def run_ours(args, rank, world, local_rank):
         dgu_gbs = (dgu_bytes / nd) / (dprof["gate_up_ms"] / nd * 1e-3) / 1e9 if dprof["gate_up_ms"] else None
         return dec_us, dgu_gbs, duniq
 
-    def decode_json(dec_us, dgu_gbs, duniq):
-        return {"metric": DECODE_METRIC, "value": round(dec_us, 2), "unit": "us", "higher_is_better": False,
-                "workload": "configs[2]: 8 tokens, 256 experts, device router"
-                            + (f", expert-parallel x{world}" if ep else ""),
-                "unique_experts_mean": round(statistics.mean(duniq), 2) if duniq else None,
-                "roofline": {"bound": "hbm", "kernel": "k_gemv_mma fused gate/up + SwiGLU",
-                             "achieved": round(dgu_gbs, 1) if dgu_gbs else None, "peak": hbm,
-                             "unit": "GB/s", "frac": round(dgu_gbs / hbm, 4) if dgu_gbs else None,
-                             "traffic_ratio": round(GATE_UP_GEMV_TRAFFIC_RATIO, 4)}}
+    def decode_json(dec_us, dgu_gbs, duniq, tokens=DECODE_TOKENS):
+        gu_b, dn_b = expert_bytes()
+        uniq = statistics.mean(duniq) if duniq else None
+        out = {"metric": DECODE_METRIC if tokens == DECODE_TOKENS else f"routed FP8 MoE layer us @width {tokens}",
+               "value": round(dec_us, 2), "unit": "us", "higher_is_better": False,
+               "workload": f"configs[2]: {tokens} token{'s' if tokens > 1 else ''}, 256 experts, device router"
+                           + (f", expert-parallel x{world}" if ep else ""),
+               "unique_experts_mean": round(uniq, 2) if uniq else None,
+               "roofline": {"bound": "hbm", "kernel": "k_gemv_mma fused gate/up + SwiGLU",
+                            "achieved": round(dgu_gbs, 1) if dgu_gbs else None, "peak": hbm,
+                            "unit": "GB/s", "frac": round(dgu_gbs / hbm, 4) if dgu_gbs else None,
+                            "traffic_ratio": round(GATE_UP_GEMV_TRAFFIC_RATIO, 4)}}
+        if uniq and world == 1:  # the whole layer's weight stream over its time
+            out["layer_weight_gbs"] = round(uniq * (gu_b + dn_b) / (dec_us * 1e-6) / 1e9, 1)
+            out["layer_hbm_frac"] = round(out["layer_weight_gbs"] / hbm, 4)
+        return out
 
     if args.decode_only:  # configs[2] alone, for profiling runs
         dec = decode_json(*decode_bench())
+        dec1 = decode_json(*decode_bench(1), tokens=1)
         if rank == 0:
-            print(json.dumps({"decode": dec}), flush=True)
+            print(json.dumps({"decode": dec, "decode_w1": dec1}), flush=True)
         rt.close()
         return
 
@@ -704,6 +712,7 @@ def run_ours(args, rank, world, local_rank):
 
     # ================================================================= decode
     dec_us, dgu_gbs, duniq = decode_bench()
+    dec1 = decode_json(*decode_bench(1), tokens=1)
 
     # ================================================================ gather
     vals = torch.tensor([step_ms, e2e_s, dec_us, layer_gbs, gu_gbs, dgu_gbs or 0.0, e2e_layer_io_s], device=dev,
@@ -777,6 +786,7 @@ def run_ours(args, rank, world, local_rank):
                       "experts_per_rank_run": round(uniq, 1), "rows_per_rank": round(rows, 1)},
             "kernels_us_per_layer": {k.replace("_ms", ""): round(v * 1e3, 2) for k, v in prof.items()},
             "decode": decode_json(dec_us, dgu_gbs, duniq),
+            "decode_w1": dec1,
             "configs": configs,
             **parity,
             "clocks": clocks.summary(),
