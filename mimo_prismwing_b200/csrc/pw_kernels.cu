@@ -538,6 +538,7 @@ static RouterUnits router_units(uint32_t tokens, uint32_t experts, uint32_t hidd
 }
 
 constexpr uint32_t kRouterPartialMinTokens = 64;  // below: k_router_slices_small
+constexpr uint32_t kRouterTopkCtaMaxTokens = 256;  // below: k_router_topk_cta
 
 size_t router_scratch_floats(uint32_t tokens, uint32_t experts, uint32_t hidden) {
   return (size_t)tokens * experts * (hidden / kRouterSlice);
@@ -668,6 +669,129 @@ __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ s
   }
 }
 
+// The same selection with a whole CTA per token (experts <= 256, one expert
+// per thread): every thread loads its expert's slice sums at once, each warp
+// keeps its 9 best (corrected value, expert) under the same total order
+// (value descending, then expert ascending), and warp 0 picks the 9 best of
+// those 72.  The top 9 of the union of per-warp top 9s is the top 9 overall,
+// so picks, weights and the tie test equal k_router_topk's; the token's
+// critical path is one round of loads and two 9-round selections instead of
+// 8 expert columns per lane in sequence.  CTAs loop over tokens.
+__global__ void __launch_bounds__(256) k_router_topk_cta(const float *__restrict__ src, uint32_t slices,
+                                                         const float *__restrict__ bias, uint32_t tokens,
+                                                         uint32_t experts, uint32_t *__restrict__ selected,
+                                                         float *__restrict__ weights, uint32_t *tie_rows,
+                                                         uint32_t *flags) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float cv[8][9], cs[8][9];
+  __shared__ uint32_t ci[8][9];
+  const uint32_t tid = threadIdx.x, lane = tid % 32u, warp = tid / 32u;
+  const float ninf = -__int_as_float(0x7f800000);
+  const size_t plane = (size_t)tokens * experts;
+  const uint32_t e = tid;
+  const bool valid = e < experts;
+  const float b = valid ? __ldg(bias + e) : 0.0f;
+  for (uint32_t t = blockIdx.x; t < tokens; t += gridDim.x) {
+    float score = 0.0f, corr = ninf;
+    uint32_t idx = 0xffffffffu;
+    if (valid) {
+      const float *p = src + (size_t)t * experts + e;
+      float lg;
+      if (slices <= 16u) {  // independent loads first, then the ordered sum
+        float v[16];
+#pragma unroll
+        for (uint32_t q = 0; q < 16u; ++q) v[q] = q < slices ? __ldcs(p + q * plane) : 0.0f;
+        lg = v[0];
+#pragma unroll
+        for (uint32_t q = 1; q < 16u; ++q)
+          if (q < slices) lg = __fadd_rn(lg, v[q]);
+      } else {
+        lg = p[0];
+        for (uint32_t q = 1; q < slices; ++q) lg = __fadd_rn(lg, p[q * plane]);
+      }
+      if (!finite(lg) || !finite(b)) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
+      score = sigmoid_sleef(lg);
+      corr = __fadd_rn(score, b);
+      idx = e;
+    }
+    // this warp's 9 best: lane r keeps round r's pick
+    bool taken = false;
+#pragma unroll 1
+    for (uint32_t round = 0; round < 9u; ++round) {
+      float bv = taken ? ninf : corr, bs = taken ? 0.0f : score;
+      uint32_t bi = taken ? 0xffffffffu : idx;
+      argmax_shfl(bv, bi, bs);
+      if (lane == round) {
+        cv[warp][round] = bv;
+        ci[warp][round] = bi;
+        cs[warp][round] = bs;
+      }
+      if (bi != 0xffffffffu && bi == idx) taken = true;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // 72 candidates, slots lane, lane + 32, lane + 64
+      float v[3], sc[3];
+      uint32_t ix[3];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const uint32_t c = lane + 32u * (uint32_t)k;
+        const bool in = c < 72u;
+        v[k] = in ? cv[c / 9u][c % 9u] : ninf;
+        ix[k] = in ? ci[c / 9u][c % 9u] : 0xffffffffu;
+        sc[k] = in ? cs[c / 9u][c % 9u] : 0.0f;
+      }
+      uint32_t took = 0;
+      float my_v = ninf, my_s = 0.0f;
+      uint32_t my_i = 0xffffffffu;
+#pragma unroll 1
+      for (uint32_t round = 0; round < 9u; ++round) {
+        float bv = ninf, bs = 0.0f;
+        uint32_t bi = 0xffffffffu;
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+          if (!((took >> k) & 1u) && ix[k] != 0xffffffffu && better(v[k], ix[k], bv, bi)) {
+            bv = v[k];
+            bi = ix[k];
+            bs = sc[k];
+          }
+        argmax_shfl(bv, bi, bs);
+        if (lane == round) {
+          my_v = bv;
+          my_i = bi;
+          my_s = bs;
+        }
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+          if (bi != 0xffffffffu && ix[k] == bi) took |= 1u << k;
+      }
+      // weight_k = score_k / (pairwise sum of the 8 + 1e-20), src/text_endpoint.rs:4382
+      const float s4 = __shfl_down_sync(0xffffffffu, my_s, 4);
+      const float lk = __fadd_rn(my_s, s4);
+      const float l0 = __shfl_sync(0xffffffffu, lk, 0), l1 = __shfl_sync(0xffffffffu, lk, 1);
+      const float l2 = __shfl_sync(0xffffffffu, lk, 2), l3 = __shfl_sync(0xffffffffu, lk, 3);
+      const float den = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, l0), l1), l2), l3), 1.0e-20f);
+      const float wk = __fdiv_rn(my_s, den);
+      const bool ok_k = lane >= 8u || (finite(wk) && wk >= 0.0f && my_i < experts);
+      float sum = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, wk, k));
+      const bool all_ok = __all_sync(0xffffffffu, ok_k);
+      if (lane < 8u) {
+        selected[(size_t)t * 8 + lane] = my_i;
+        weights[(size_t)t * 8 + lane] = wk;
+      }
+      const float v7 = __shfl_sync(0xffffffffu, my_v, 7), v8 = __shfl_sync(0xffffffffu, my_v, 8);
+      if (lane == 0) {
+        if (!all_ok || fabsf(__fsub_rn(sum, 1.0f)) > 1.0e-6f) raise_flag(flags, PW_FLAG_ROUTE_WEIGHTS);
+        if (v7 == v8 && tie_rows) atomicAdd(tie_rows, 1u);
+      }
+    }
+    __syncthreads();  // the candidates are rewritten by the next token
+  }
+}
+
 template <bool F32W, int EXPT, int TOK>
 static cudaError_t launch_partials(const float *x, const void *w, const RouterUnits &g, float *scratch, uint32_t *work,
                                    int num_sms, cudaStream_t stream) {
@@ -724,6 +848,12 @@ cudaError_t launch_router(const float *x, uint32_t tokens, const void *w, uint32
                        ? launch_router_logits<true>(x, tokens, w, g, scratch, work, num_sms, stream)
                        : launch_router_logits<false>(x, tokens, w, g, scratch, work, num_sms, stream);
   if (st != cudaSuccess) return st;
+  if (experts <= 256u && tokens < kRouterTopkCtaMaxTokens) {
+    // decode widths: a CTA per token (a shorter critical path per token; at
+    // 2048 tokens the warp-per-token kernel is faster, 145 vs 170 us per call)
+    return launch_kernel(k_router_topk_cta, dim3(tokens), dim3(256), 0, stream, (const float *)scratch, g.slices,
+                         bias, tokens, experts, selected, weights, tie_rows, flags);
+  }
   // persistent: up to two 8-warp CTAs per SM, each warp looping over tokens
   uint32_t blocks = (tokens + 7u) / 8u;
   if (blocks > 2u * (uint32_t)num_sms) blocks = 2u * (uint32_t)num_sms;
