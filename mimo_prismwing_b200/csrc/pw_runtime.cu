@@ -1862,7 +1862,7 @@ int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_
   // the tcgen05 GEMM when the layer is wide (judged from this rank's tokens:
   // the owners' row counts are known only on the device)
   const bool wide = (uint64_t)G * tokens >= kWideLayerTokens;
-  const bool fuse_return = wide && G <= 2u;  // see the down projection below
+  const bool fuse_return = wide;  // see the down projection below
   const uint32_t chunk = wide ? (uint32_t)gemm_tc_tokens(2) : 8u;
   const uint32_t max_groups = cap / chunk + L;
   const bool fused = (rt->flags & PW_RUNTIME_FUSED_GATE_UP) != 0;
@@ -1913,11 +1913,12 @@ int ep_layer_p2p(pw_runtime *rt, Call &call, const pw_expert_bank *bank, uint32_
       ProfScope ps(rt, P_QUANT, 1);
       CK(launch_ep_gather(ea, perm, p_recv, xg, xsg, rt->num_sms, rt->stream));
     }
-    // fused return (two ranks): the down GEMM stores each bf16 row into its
-    // source's window.  Measured: at 2 GPUs fused beats a separate return
-    // kernel (down + return + combine 308 vs 377 us per layer); at 4 GPUs the
-    // GEMM's stores to three peers slowed it from 133 to 200 us and the
-    // separate kernel wins (212 vs 252 us).
+    // fused return: the down GEMM's epilogue stores each bf16 row into its
+    // source's window (8 rows x 64 B per store instruction, through the
+    // staging rows).  Measured at 4 GPUs: down 117 -> 131 us, return + wait +
+    // combine 76 -> 30 us, 69-72k -> 75-76k tok/s against a separate return
+    // kernel.  (With per-thread 16-byte row stores the fused form lost at 4
+    // GPUs: down 133 -> 200 us.)
     const PeerRows pr{ep->d_peers, w.ret_rows, src_rank, src_place};
     s = enqueue_expert_chain_wide(rt, gu, dn, max_groups, n_groups, cap, H, I, xg, xsg, hid, gt, ut, hc, hs, down, 1,
                                   max_groups, p_recv, nullptr, fuse_return ? &pr : nullptr);
