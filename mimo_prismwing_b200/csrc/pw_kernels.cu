@@ -338,6 +338,19 @@ struct RouterStage {
   uint4 w[kW];
 };
 
+// Shared-memory layout: xs[column][token] and ws[column][expert] (f32), read
+// by the product as float4 runs of 4 tokens / 4 experts.  The global loads are
+// row-wise coalesced: a warp loads 4 token rows x 128 B of x, and 8 expert rows
+// x 64 B (bf16) or 4 x 128 B (f32) of the weight.  Storing them column-wise
+// would put a warp's stores in few banks, so each row's float4 slots are
+// permuted by an XOR with a function of the row (xs_slot / ws_slot): the
+// stores become conflict-free and the product's float4 reads stay whole.
+__device__ __forceinline__ uint32_t xs_slot(uint32_t col, uint32_t slot) { return slot ^ ((col >> 2) & 7u); }
+template <bool F32W>
+__device__ __forceinline__ uint32_t ws_slot(uint32_t col, uint32_t slot) {
+  return F32W ? slot ^ ((col >> 2) & 7u) : slot ^ (2u * ((col >> 3) & 3u));
+}
+
 template <bool F32W, int EXPT, int TOK>
 __device__ __forceinline__ void router_gload(const float *__restrict__ x, const void *__restrict__ wv,
                                              const RouterUnits &g, const RouterCursor &c,
@@ -346,17 +359,18 @@ __device__ __forceinline__ void router_gload(const float *__restrict__ x, const 
 #pragma unroll
   for (int m = 0; m < RouterStage<F32W, EXPT, TOK>::kX; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
-    const uint32_t tok = c.t0 + i % (uint32_t)TOK, c4 = i / (uint32_t)TOK;  // x: token, 4 columns
+    const uint32_t tok = c.t0 + i / 8u, c4 = i % 8u;  // x: 8 lanes per token row
     r.x[m] = tok < g.tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)tok * g.hidden + base + 4u * c4))
                             : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  constexpr uint32_t kPer = F32W ? 4u : 8u;  // weight columns per 16-byte load
+  constexpr uint32_t kPer = F32W ? 4u : 8u;       // weight columns per 16-byte load
+  constexpr uint32_t kLoadsRow = 32u / kPer;       // 16-byte loads per expert row of the stage
   const unsigned char *w = static_cast<const unsigned char *>(wv);
   const size_t esz = F32W ? 4u : 2u;
 #pragma unroll
   for (int m = 0; m < RouterStage<F32W, EXPT, TOK>::kW; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
-    const uint32_t e = c.e0 + i % (uint32_t)EXPT, cq = i / (uint32_t)EXPT;  // w: expert, kPer columns
+    const uint32_t e = c.e0 + i / kLoadsRow, cq = i % kLoadsRow;  // w: consecutive lanes along the row
     r.w[m] = e < g.experts ? __ldg(reinterpret_cast<const uint4 *>(w + ((size_t)e * g.hidden + base + kPer * cq) * esz))
                            : make_uint4(0u, 0u, 0u, 0u);
   }
@@ -367,24 +381,29 @@ __device__ __forceinline__ void router_sstore(rp::Smem<EXPT, TOK> &sm, int b, co
 #pragma unroll
   for (int m = 0; m < RouterStage<F32W, EXPT, TOK>::kX; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
-    const uint32_t tok = i % (uint32_t)TOK, c4 = i / (uint32_t)TOK;
-    sm.xs[b][4 * c4 + 0][tok] = r.x[m].x;
-    sm.xs[b][4 * c4 + 1][tok] = r.x[m].y;
-    sm.xs[b][4 * c4 + 2][tok] = r.x[m].z;
-    sm.xs[b][4 * c4 + 3][tok] = r.x[m].w;
+    const uint32_t tok = i / 8u, c4 = i % 8u;
+    const float v[4] = {r.x[m].x, r.x[m].y, r.x[m].z, r.x[m].w};
+#pragma unroll
+    for (uint32_t j = 0; j < 4u; ++j) {
+      const uint32_t col = 4u * c4 + j;
+      sm.xs[b][col][4u * xs_slot(col, tok / 4u) + tok % 4u] = v[j];
+    }
   }
+  constexpr uint32_t kLoadsRow = F32W ? 8u : 4u;
 #pragma unroll
   for (int m = 0; m < RouterStage<F32W, EXPT, TOK>::kW; ++m) {
     const uint32_t i = threadIdx.x + rp::kThreads * m;
-    const uint32_t e = i % (uint32_t)EXPT, cq = i / (uint32_t)EXPT;
+    const uint32_t e = i / kLoadsRow, cq = i % kLoadsRow;
     const uint32_t q[4] = {r.w[m].x, r.w[m].y, r.w[m].z, r.w[m].w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (uint32_t j = 0; j < 4u; ++j) {
       if (F32W) {
-        sm.ws[b][4 * cq + j][e] = __uint_as_float(q[j]);
+        const uint32_t col = 4u * cq + j;
+        sm.ws[b][col][4u * ws_slot<F32W>(col, e / 4u) + e % 4u] = __uint_as_float(q[j]);
       } else {
-        sm.ws[b][8 * cq + 2 * j][e] = bf16lo(q[j]);
-        sm.ws[b][8 * cq + 2 * j + 1][e] = bf16hi(q[j]);
+        const uint32_t c0 = 8u * cq + 2u * j, c1 = c0 + 1u;
+        sm.ws[b][c0][4u * ws_slot<F32W>(c0, e / 4u) + e % 4u] = bf16lo(q[j]);
+        sm.ws[b][c1][4u * ws_slot<F32W>(c1, e / 4u) + e % 4u] = bf16hi(q[j]);
       }
     }
   }
@@ -451,7 +470,7 @@ __global__ void __launch_bounds__(rp::kThreads, router_ctas_per_sm<EXPT, TOK>())
       float xv[TT];
 #pragma unroll
       for (int q = 0; q < TT / 4; ++q) {
-        const float4 xq = *reinterpret_cast<const float4 *>(&sm.xs[b][k][TT * tg + 4 * q]);
+        const float4 xq = *reinterpret_cast<const float4 *>(&sm.xs[b][k][4u * xs_slot(k, (TT * tg) / 4u + q)]);
         xv[4 * q] = xq.x;
         xv[4 * q + 1] = xq.y;
         xv[4 * q + 2] = xq.z;
@@ -460,7 +479,7 @@ __global__ void __launch_bounds__(rp::kThreads, router_ctas_per_sm<EXPT, TOK>())
       float2 wv[NP];
 #pragma unroll
       for (int h = 0; h < NP / 2; ++h) {
-        const float4 wq = *reinterpret_cast<const float4 *>(&sm.ws[b][k][64 * h + 4 * eg]);
+        const float4 wq = *reinterpret_cast<const float4 *>(&sm.ws[b][k][4u * ws_slot<F32W>(k, 16u * h + eg)]);
         wv[2 * h] = make_float2(wq.x, wq.y);
         wv[2 * h + 1] = make_float2(wq.z, wq.w);
       }
