@@ -167,6 +167,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// tcgen05.wait::ld that also names the 32 registers a tmem_ld32 filled, so the
+// compiler cannot move their uses above the wait (the load is asynchronous
+// while other registers are computed on).
+__device__ __forceinline__ void tmem_wait_ld(float (&v)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7]),
+                 "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]), "+f"(v[12]), "+f"(v[13]), "+f"(v[14]),
+                 "+f"(v[15]), "+f"(v[16]), "+f"(v[17]), "+f"(v[18]), "+f"(v[19]), "+f"(v[20]), "+f"(v[21]),
+                 "+f"(v[22]), "+f"(v[23]), "+f"(v[24]), "+f"(v[25]), "+f"(v[26]), "+f"(v[27]), "+f"(v[28]),
+                 "+f"(v[29]), "+f"(v[30]), "+f"(v[31])
+               :
+               : "memory");
+}
+
 // 32 lanes x 32 consecutive f32 columns from registers into TMEM.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float2 (&v)[16]) {
   asm volatile(
@@ -433,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       if (u + u_step < u_end) ws_load(u + u_step, wn0, wn1);
 
       float2 acc[32];  // weight rows col0 + 2i, col0 + 2i + 1
-#pragma unroll
+#pragma unroll 1
       for (int m = 0; m < MATS; ++m) {
         if (m == 1 && active) {
           // gate finished: park its sums in the stash slot, start the up sums
@@ -444,30 +458,56 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
         const uint32_t sel = qkv ? half : (uint32_t)m;
-        for (uint32_t kb = 0; kb < kblocks; ++kb) {
-          const float ws = __shfl_sync(0xffffffffu, sel == 0u ? wc0 : wc1, kb);
-          const bool ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
+        const uint32_t cols = tmem + lane_base + col0;
+        // Two-deep software pipeline over the k-blocks: the second 32 columns
+        // of a block load while the first 32 are promoted, and the first 32
+        // of the next block load while the second 32 are.  The slot goes
+        // back to the MMA as soon as both halves sit in registers.  Every
+        // value still gets the same single FMA per k-block, in k order.
+        if (active) {
+          float v0[32], v1[32];
+          bool ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
           tc_fence_after();
-          if (ok && active) {
-            const float c = __fmul_rn(ws, xsb[kb * 32u + lane]);
+          tmem_ld32(cols + acc_slot * (uint32_t)kTN, v0);
+          tmem_wait_ld(v0);
+          for (uint32_t kb = 0; kb < kblocks; ++kb) {
+            const float ws = __shfl_sync(0xffffffffu, sel == 0u ? wc0 : wc1, kb);
+            const float c = ok ? __fmul_rn(ws, xsb[kb * 32u + lane]) : 0.0f;
             const float2 c2 = make_float2(c, c);
-            const uint32_t src = tmem + lane_base + acc_slot * (uint32_t)kTN + col0;
-            float v0[32], v1[32];
-            tmem_ld32(src, v0);
-            tmem_ld32(src + 32u, v1);
-            tmem_wait_ld();
+            tmem_ld32(cols + acc_slot * (uint32_t)kTN + 32u, v1);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              acc[i] = __ffma2_rn(make_float2(v0[2 * i], v0[2 * i + 1]), c2, acc[i]);
-              acc[16 + i] = __ffma2_rn(make_float2(v1[2 * i], v1[2 * i + 1]), c2, acc[16 + i]);
+            for (int i = 0; i < 16; ++i) acc[i] = __ffma2_rn(make_float2(v0[2 * i], v0[2 * i + 1]), c2, acc[i]);
+            tmem_wait_ld(v1);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.tempty[acc_slot]);
+            if (++acc_slot == NACC) {
+              acc_slot = 0;
+              aphase ^= 1u;
             }
+            const bool more = kb + 1u < kblocks;
+            if (more) {
+              ok = bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
+              tc_fence_after();
+              tmem_ld32(cols + acc_slot * (uint32_t)kTN, v0);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              acc[16 + i] = __ffma2_rn(make_float2(v1[2 * i], v1[2 * i + 1]), c2, acc[16 + i]);
+            if (more) tmem_wait_ld(v0);
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sh.tempty[acc_slot]);
-          if (++acc_slot == NACC) {
-            acc_slot = 0;
-            aphase ^= 1u;
+        } else {
+          // no tokens in this lane quarter: keep the slot handshake only
+          for (uint32_t kb = 0; kb < kblocks; ++kb) {
+            bwait(sh, &sh.tfull[acc_slot], aphase, a.flags);
+            tc_fence_after();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.tempty[acc_slot]);
+            if (++acc_slot == NACC) {
+              acc_slot = 0;
+              aphase ^= 1u;
+            }
           }
         }
       }
