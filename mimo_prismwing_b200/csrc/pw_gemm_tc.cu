@@ -40,6 +40,7 @@
 
 #include "pw_device.cuh"
 #include "pw_internal.h"
+#include "pw_tc.cuh"
 
 namespace pw {
 namespace tc {
@@ -73,127 +74,6 @@ struct Cfg {
   static_assert((NACC + (FUSED ? 1 : 0)) * kTN <= kTmemCols, "TMEM holds 512 columns");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
-
-// ------------------------------------------------------------------ PTX
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-          smem_addr(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
-      : "memory");
-}
-
-// True on one lane of the converged calling warp.
-__device__ __forceinline__ bool elect_one() {
-  uint32_t e;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "elect.sync _|p, 0xffffffff;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(e));
-  return e != 0u;
-}
-
-__device__ __forceinline__ void tensormap_acquire(const CUtensorMap *map) {
-  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
-}
-
-// 4-byte asynchronous copy global -> shared (completion: cp.async.wait_group).
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major operand, 128B swizzle: rows are 128-byte lines, 8-row groups 1024 B
-// apart (SBO), LBO unused (1), version 1, base offset 0 (1024-aligned tiles).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3fffu);        // start address
-  d |= (uint64_t)1u << 16;                         // leading byte offset (unused for SW128 K-major)
-  d |= (uint64_t)(1024u >> 4) << 32;               // stride byte offset
-  d |= (uint64_t)1u << 46;                         // descriptor version (sm_100)
-  d |= (uint64_t)2u << 61;                         // SWIZZLE_128B
-  return d;
-}
-
-// kind::f8f6f4 instruction descriptor: D f32, A/B e4m3, both K-major, M=128, N=n.
-// (A: token rows, B: weight rows.)
-__device__ __forceinline__ uint32_t instr_desc(uint32_t n) {
-  return (1u << 4)                   // c_format F32
-         | (0u << 7) | (0u << 10)    // a, b: E4M3
-         | (0u << 15) | (0u << 16)   // K-major
-         | ((n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-
-// One MMA (M=128, N, K=32) issued by one lane elected from the (converged)
-// calling warp; accum = 0 starts a fresh accumulator.
-__device__ __forceinline__ void mma_f8_elect(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accum), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit_elect(uint64_t *bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_addr(bar))
-      : "memory");
-}
-
-
-// 32 lanes x 32 consecutive f32 columns (one per register) of the warp's lane quarter.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// tcgen05.wait::ld that also names the 32 registers a tmem_ld32 filled, so the
-// compiler cannot move their uses above the wait (the load is asynchronous
-// while other registers are computed on).
-__device__ __forceinline__ void tmem_wait_ld(float (&v)[32]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7]),
-                 "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]), "+f"(v[12]), "+f"(v[13]), "+f"(v[14]),
-                 "+f"(v[15]), "+f"(v[16]), "+f"(v[17]), "+f"(v[18]), "+f"(v[19]), "+f"(v[20]), "+f"(v[21]),
-                 "+f"(v[22]), "+f"(v[23]), "+f"(v[24]), "+f"(v[25]), "+f"(v[26]), "+f"(v[27]), "+f"(v[28]),
-                 "+f"(v[29]), "+f"(v[30]), "+f"(v[31])
-               :
-               : "memory");
-}
-
-// 32 lanes x 32 consecutive f32 columns from registers into TMEM.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float2 (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "f"(v[0].x), "f"(v[0].y), "f"(v[1].x), "f"(v[1].y), "f"(v[2].x), "f"(v[2].y), "f"(v[3].x), "f"(v[3].y),
-      "f"(v[4].x), "f"(v[4].y), "f"(v[5].x), "f"(v[5].y), "f"(v[6].x), "f"(v[6].y), "f"(v[7].x), "f"(v[7].y),
-      "f"(v[8].x), "f"(v[8].y), "f"(v[9].x), "f"(v[9].y), "f"(v[10].x), "f"(v[10].y), "f"(v[11].x), "f"(v[11].y),
-      "f"(v[12].x), "f"(v[12].y), "f"(v[13].x), "f"(v[13].y), "f"(v[14].x), "f"(v[14].y), "f"(v[15].x), "f"(v[15].y)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 struct Shared {
   uint8_t *ring;
@@ -342,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       for (uint32_t u = u_begin; u < u_end; u += u_step) {
         const uint32_t n = n_next;  // token rows loaded
         if (u + u_step < u_end) n_next = mma_cols(a.groups[(u + u_step) / tpg].count);
-        const uint32_t idesc = instr_desc((uint32_t)kTileRows);
+        const uint32_t idesc = instr_desc((uint32_t)kTileRows, 128u);
         for (uint32_t st = 0; st < per_tile; ++st) {
           const uint32_t kc = st % kcs;
           const bool ok_full = bwait(sh, &sh.full[slot], phase, a.flags);

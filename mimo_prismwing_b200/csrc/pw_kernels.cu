@@ -251,26 +251,44 @@ template <typename WT>
 __global__ void __launch_bounds__(256) k_router_slices_small(const float *__restrict__ x, uint32_t tokens,
                                                              const WT *__restrict__ w, uint32_t experts,
                                                              uint32_t hidden, float *__restrict__ part) {
-  pdl_wait();
-  pdl_launch_dependents();
   constexpr uint32_t kPer = 16u / sizeof(WT);  // weight values per 16-byte load
   __shared__ __align__(16) float xs[kRouterTok][kRouterSlice];
   __shared__ __align__(16) WT ws[kRouterSlice][32];
   const uint32_t s = blockIdx.x, e0 = blockIdx.y * 32u, t0 = blockIdx.z * kRouterTok;
   const uint32_t tid = threadIdx.x, col0 = kRouterSlice * s;
-  for (uint32_t i = tid; i < (uint32_t)kRouterTok * kRouterSlice / 4u; i += 256u) {
-    const uint32_t j = i / (kRouterSlice / 4u), c4 = i % (kRouterSlice / 4u);
-    reinterpret_cast<float4 *>(&xs[j][0])[c4] =
-        t0 + j < tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + j) * hidden + col0) + c4)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  for (uint32_t i = tid; i < 32u * kRouterSlice / kPer; i += 256u) {
-    const uint32_t el = i % 32u, cq = i / 32u;  // lanes: consecutive experts (conflict-free stores)
-    const uint4 q = e0 + el < experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)(e0 + el) * hidden + col0) + cq)
-                                      : make_uint4(0u, 0u, 0u, 0u);
-    const WT *v = reinterpret_cast<const WT *>(&q);
+  // every 16-byte load of the CTA is in flight before the first store (one
+  // memory round trip instead of one per loop iteration)
+  constexpr uint32_t kXLoads = (uint32_t)kRouterTok * kRouterSlice / 4u / 256u;
+  constexpr uint32_t kWLoads = 32u * kRouterSlice / kPer / 256u;
+  float4 xv[kXLoads];
+  uint4 wv[kWLoads];
+  // the router weight is not written by the kernels before this one, so
+  // under programmatic dependent launch it is fetched before the wait
 #pragma unroll
-    for (uint32_t k = 0; k < kPer; ++k) ws[kPer * cq + k][el] = v[k];
+  for (uint32_t k = 0; k < kWLoads; ++k) {
+    const uint32_t i = tid + 256u * k, el = i % 32u, cq = i / 32u;  // lanes: consecutive experts
+    wv[k] = e0 + el < experts ? __ldg(reinterpret_cast<const uint4 *>(w + (size_t)(e0 + el) * hidden + col0) + cq)
+                              : make_uint4(0u, 0u, 0u, 0u);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+#pragma unroll
+  for (uint32_t k = 0; k < kXLoads; ++k) {
+    const uint32_t i = tid + 256u * k, j = i / (kRouterSlice / 4u), c4 = i % (kRouterSlice / 4u);
+    xv[k] = t0 + j < tokens ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + j) * hidden + col0) + c4)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (uint32_t k = 0; k < kXLoads; ++k) {
+    const uint32_t i = tid + 256u * k;
+    reinterpret_cast<float4 *>(&xs[i / (kRouterSlice / 4u)][0])[i % (kRouterSlice / 4u)] = xv[k];
+  }
+#pragma unroll
+  for (uint32_t k = 0; k < kWLoads; ++k) {
+    const uint32_t i = tid + 256u * k, el = i % 32u, cq = i / 32u;  // conflict-free stores
+    const WT *v = reinterpret_cast<const WT *>(&wv[k]);
+#pragma unroll
+    for (uint32_t q = 0; q < kPer; ++q) ws[kPer * cq + q][el] = v[q];
   }
   __syncthreads();
   const uint32_t el = tid % 32u, j = tid / 32u;
