@@ -114,7 +114,14 @@ cudaError_t launch_gemv(int kind, const GemvArgs &a, int grid, cudaStream_t stre
     }
     case 0:
     case 2:
-    case 3: return launch_gemv_mma(kind, a, grid, stream);
+    case 3:
+      // Plain row-major weights, whole-K units: the tcgen05 GEMV (decode
+      // layer at width 8: 282 -> 264 us).  Fused-QKV shard maps (64-row
+      // boxes) and split-K launches (a lone expert: 1/8-tile units, where the
+      // tcgen05 pipeline's fill latency cost 19 -> 24 us) keep the
+      // warp-level MMA kernel.
+      return a.layout == PW_LAYOUT_PLAIN && a.splits <= 1u ? launch_gemv_tc(kind, a, grid, stream)
+                                                           : launch_gemv_mma(kind, a, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -123,6 +123,8 @@ cudaError_t launch_quantize(const float *x, uint32_t rows, uint32_t cols, uint8_
 cudaError_t launch_gemv(int kind, const GemvArgs &args, int grid, cudaStream_t stream);
 int gemv_max_ctas(int num_sms);
 cudaError_t launch_gemv_mma(int kind, const GemvArgs &args, int grid, cudaStream_t stream);
+// The same kinds on tcgen05 / TMEM for PW_LAYOUT_PLAIN weights (pw_gemv_tc.cu).
+cudaError_t launch_gemv_tc(int kind, const GemvArgs &args, int grid, cudaStream_t stream);
 cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_t stream);
 // Router logits (or, from 64 tokens, their per-slice sums) into `scratch`
 // (router_scratch_floats floats), then the sigmoid no-aux top-8.
