@@ -1,4 +1,8 @@
-// pw_gemv_mma.cu -- block-scaled FP8 GEMV on the FP8 tensor-core MMA (widths 1..8).
+// pw_gemv_mma.cu -- block-scaled FP8 GEMV on the warp-level FP8 MMA (widths 1..8).
+//
+// Used where the tcgen05 GEMV (pw_gemv_tc.cu) is not: fused-QKV shard maps
+// (64-row TMA boxes) and split-K launches (a lone expert's 1/8-tile units,
+// whose short pipelines this kernel fills faster).
 //
 // Equation (src/wide_metal_moe.rs:404-423, kernels/block_fp8_gemv.metal:935-1046):
 //   y[t, r] = sum_kb ( sum_{c in kb} dec(W[src(r), c]) * dec(code[t, c]) ) * S[srow(r), kb] * xs[t, kb]

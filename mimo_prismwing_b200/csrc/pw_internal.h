@@ -131,9 +131,14 @@ cudaError_t launch_round_bf16(float *v, uint32_t n, uint32_t *flags, cudaStream_
 size_t router_scratch_floats(uint32_t tokens, uint32_t experts, uint32_t hidden);
 // w: [experts, hidden] router weight, f32 or bf16 bits (w_dtype = PW_ROUTER_*).
 // work: two words, zero before the first launch; the kernels leave them zero.
+// q_codes / q_scales (optional, only where router_fuses_quantize(tokens)):
+// the router's logits kernel also writes x's dynamic FP8 codes and scales,
+// byte-identical to launch_quantize.
+bool router_fuses_quantize(uint32_t tokens);
 cudaError_t launch_router(const float *x, uint32_t tokens, const void *w, uint32_t w_dtype, const float *bias,
                           uint32_t experts, uint32_t hidden, float *scratch, uint32_t *selected, float *weights,
-                          uint32_t *tie_rows, uint32_t *flags, uint32_t *work, int num_sms, cudaStream_t stream);
+                          uint32_t *tie_rows, uint32_t *flags, uint32_t *work, int num_sms, cudaStream_t stream,
+                          uint8_t *q_codes = nullptr, float *q_scales = nullptr);
 
 // Device-side schedule for a routed layer: from selected [tokens, 8] build
 // placements ordered by (expert asc, position asc) and the GEMV groups.
@@ -171,7 +176,9 @@ bool encode_weight_map(CUtensorMap *out, const void *base, uint32_t rows, uint32
 cudaError_t launch_sum_partials(const float *p, uint32_t n_parts, uint64_t n, float *y, uint32_t round,
                                 uint32_t *flags, cudaStream_t stream);
 uint32_t map_box_rows(uint32_t layout);
-// chunk: tokens per GEMV/GEMM group (8 for the GEMV, gemm_tc_tokens(2) for the GEMM)
+// chunk: tokens per GEMV/GEMM group (8 for the GEMV, gemm_tc_tokens(2) for the GEMM);
+// one launch up to 256 tokens, three above (schedule_launches)
+uint32_t schedule_launches(uint32_t tokens);
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
                             const BankTable &bank, const ScheduleOut &out, uint32_t *flags, uint32_t chunk,
                             cudaStream_t stream);

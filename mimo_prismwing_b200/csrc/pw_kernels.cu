@@ -241,6 +241,10 @@ __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w &
 // The slice sums go to the same partials as the prefill kernel.  WT is the
 // router weight's storage type: float (the checkpoint's F32 gate.weight) or
 // uint16_t (bf16 bits, widened exactly); the f32 chain is the same.
+// With q_codes, the CTAs of the first expert block also quantize the staged
+// activation slice for the experts (its two 128-column groups per token, a
+// warp per token, the same steps as k_quantize), so the decode chain has no
+// separate quantize launch.
 constexpr int kRouterTok = 8;
 constexpr uint32_t kRouterMaxSlices = 64;  // hidden <= 16384
 
@@ -250,7 +254,9 @@ __device__ __forceinline__ float router_w(uint16_t v) { return __uint_as_float((
 template <typename WT>
 __global__ void __launch_bounds__(256) k_router_slices_small(const float *__restrict__ x, uint32_t tokens,
                                                              const WT *__restrict__ w, uint32_t experts,
-                                                             uint32_t hidden, float *__restrict__ part) {
+                                                             uint32_t hidden, float *__restrict__ part,
+                                                             uint8_t *__restrict__ q_codes,
+                                                             float *__restrict__ q_scales, uint32_t *flags) {
   constexpr uint32_t kPer = 16u / sizeof(WT);  // weight values per 16-byte load
   __shared__ __align__(16) float xs[kRouterTok][kRouterSlice];
   __shared__ __align__(16) WT ws[kRouterSlice][32];
@@ -296,6 +302,25 @@ __global__ void __launch_bounds__(256) k_router_slices_small(const float *__rest
 #pragma unroll 16
   for (uint32_t i = 0; i < kRouterSlice; ++i) acc = __fmaf_rn(xs[j][i], router_w(ws[i][el]), acc);
   if (t0 + j < tokens && e0 + el < experts) part[((size_t)s * tokens + t0 + j) * experts + e0 + el] = acc;
+  if (q_codes && blockIdx.y == 0u && t0 + j < tokens) {
+    // warp j: token t0 + j, groups 2 s and 2 s + 1 (lane l holds values 4l..4l+3)
+#pragma unroll
+    for (uint32_t g = 0; g < 2u; ++g) {
+      const float4 v = reinterpret_cast<const float4 *>(&xs[j][g * 128u])[el];
+      const bool ok = finite(v.x) && finite(v.y) && finite(v.z) && finite(v.w);
+      if (!ok) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
+      float m = ok ? fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))) : 0.0f;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const Fp8GroupScale gs = Fp8GroupScale::of(m);
+      auto q = [&](float val) { return gs.quotient(val); };
+      const uint32_t lo = encode2(q(v.x), q(v.y));
+      const uint32_t hi = encode2(q(v.z), q(v.w));
+      const size_t grp = (size_t)(t0 + j) * (hidden / 128u) + 2u * s + g;
+      reinterpret_cast<uint32_t *>(q_codes + grp * 128u)[el] = lo | (hi << 16);
+      if (el == 0) q_scales[grp] = gs.scale;
+    }
+  }
 }
 
 // Prefill widths: the slice chains as a register-tiled product.  Work unit:
@@ -606,104 +631,117 @@ __device__ __forceinline__ void argmax_shfl(float &bv, uint32_t &bi, float &bs) 
   }
 }
 
+// Token t's picks and weights by one warp (lane l holds experts l + 32 k):
+// the logit (the slice sums added in slice order), score = SLEEF
+// sigmoid(logit), corrected = score + bias; 9 rounds of warp argmax (ties ->
+// lower index) give the 8 picks in canonical order and the first rejected
+// value (boundary tie detection).
+template <int NPL>
+__device__ __forceinline__ void topk_token_warp(const float *__restrict__ src, uint32_t slices,
+                                                const float (&bias_r)[NPL], uint32_t tokens, uint32_t experts,
+                                                uint32_t t, uint32_t *selected, float *weights, uint32_t *tie_rows,
+                                                uint32_t *flags) {
+  const uint32_t lane = threadIdx.x % 32u;
+  const float ninf = -__int_as_float(0x7f800000);
+  const size_t plane = (size_t)tokens * experts;
+  float score[NPL], corr[NPL];
+  bool bad = false;
+#pragma unroll
+  for (int k = 0; k < NPL; ++k) {
+    const uint32_t e = lane + 32u * k;
+    score[k] = 0.0f;
+    corr[k] = ninf;
+    if (e < experts) {
+      const float *p = src + (size_t)t * experts + e;
+      float lg;
+      if (slices <= 16u) {  // independent loads first, then the ordered sum
+        float v[16];
+#pragma unroll
+        for (uint32_t q = 0; q < 16u; ++q) v[q] = q < slices ? __ldcs(p + q * plane) : 0.0f;
+        lg = v[0];
+#pragma unroll
+        for (uint32_t q = 1; q < 16u; ++q)
+          if (q < slices) lg = __fadd_rn(lg, v[q]);
+      } else {
+        lg = p[0];
+        for (uint32_t q = 1; q < slices; ++q) lg = __fadd_rn(lg, p[q * plane]);
+      }
+      bad |= !finite(lg) || !finite(bias_r[k]);
+      score[k] = sigmoid_sleef(lg);
+      corr[k] = __fadd_rn(score[k], bias_r[k]);
+    }
+  }
+  if (bad) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
+  // 9 rounds of warp argmax (ties -> lower index): lane r keeps round r's
+  // pick (corrected value, expert, unbiased score)
+  uint32_t taken = 0;
+  float my_v = ninf, my_s = 0.0f;
+  uint32_t my_i = 0xffffffffu;
+#pragma unroll 1
+  for (uint32_t round = 0; round < 9u; ++round) {
+    float bv = ninf, bs = 0.0f;
+    uint32_t bi = 0xffffffffu;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      const uint32_t e = lane + 32u * k;
+      if (e < experts && !((taken >> k) & 1u) && better(corr[k], e, bv, bi)) {
+        bv = corr[k];
+        bi = e;
+        bs = score[k];
+      }
+    }
+    argmax_shfl(bv, bi, bs);
+    if (lane == round) {
+      my_v = bv;
+      my_i = bi;
+      my_s = bs;
+    }
+    if (round < 8u && bi != 0xffffffffu && bi % 32u == lane) taken |= 1u << (bi / 32u);
+  }
+  // weight_k = score_k / (pairwise sum of the 8 + 1e-20), src/text_endpoint.rs:4382
+  const float s4 = __shfl_down_sync(0xffffffffu, my_s, 4);  // lane k < 4: score of pick k + 4
+  const float lk = __fadd_rn(my_s, s4);                      // lane k < 4: l_k
+  const float l0 = __shfl_sync(0xffffffffu, lk, 0), l1 = __shfl_sync(0xffffffffu, lk, 1);
+  const float l2 = __shfl_sync(0xffffffffu, lk, 2), l3 = __shfl_sync(0xffffffffu, lk, 3);
+  const float den = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, l0), l1), l2), l3), 1.0e-20f);
+  const float wk = __fdiv_rn(my_s, den);
+  const bool ok_k = lane >= 8u || (finite(wk) && wk >= 0.0f && my_i < experts);
+  float sum = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, wk, k));
+  const bool all_ok = __all_sync(0xffffffffu, ok_k);
+  if (lane < 8u) {
+    selected[(size_t)t * 8 + lane] = my_i;
+    weights[(size_t)t * 8 + lane] = wk;
+  }
+  const float v7 = __shfl_sync(0xffffffffu, my_v, 7), v8 = __shfl_sync(0xffffffffu, my_v, 8);
+  if (lane == 0) {
+    if (!all_ok || fabsf(__fsub_rn(sum, 1.0f)) > 1.0e-6f) raise_flag(flags, PW_FLAG_ROUTE_WEIGHTS);
+    if (v7 == v8 && tie_rows) atomicAdd(tie_rows, 1u);
+  }
+}
+
 template <int NPL>
 __global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ src, uint32_t slices,
                                                      const float *__restrict__ bias, uint32_t tokens,
                                                      uint32_t experts, uint32_t *__restrict__ selected,
                                                      float *__restrict__ weights, uint32_t *tie_rows,
                                                      uint32_t *flags) {
-  pdl_wait();
-  pdl_launch_dependents();
   // Persistent warps loop over tokens: the code stays hot in the instruction
   // cache (a warp per token and launch ran each instruction once, and stalled
   // on instruction fetch: ~22 us per call at any token count).
   const uint32_t lane = threadIdx.x % 32u;
   const uint32_t nwarps = gridDim.x * (blockDim.x / 32u);
-  const float ninf = -__int_as_float(0x7f800000);
-  const size_t plane = (size_t)tokens * experts;
-  float bias_r[NPL];
+  float bias_r[NPL];  // the bias is no kernel's output: fetched before the wait
 #pragma unroll
   for (int k = 0; k < NPL; ++k) {
     const uint32_t e = lane + 32u * k;
     bias_r[k] = e < experts ? __ldg(bias + e) : 0.0f;
   }
-  for (uint32_t t = blockIdx.x * (blockDim.x / 32u) + threadIdx.x / 32u; t < tokens; t += nwarps) {
-    float score[NPL], corr[NPL];
-    bool bad = false;
-#pragma unroll
-    for (int k = 0; k < NPL; ++k) {
-      const uint32_t e = lane + 32u * k;
-      score[k] = 0.0f;
-      corr[k] = ninf;
-      if (e < experts) {
-        const float *p = src + (size_t)t * experts + e;
-        float lg;
-        if (slices <= 16u) {  // independent loads first, then the ordered sum
-          float v[16];
-#pragma unroll
-          for (uint32_t q = 0; q < 16u; ++q) v[q] = q < slices ? __ldcs(p + q * plane) : 0.0f;
-          lg = v[0];
-#pragma unroll
-          for (uint32_t q = 1; q < 16u; ++q)
-            if (q < slices) lg = __fadd_rn(lg, v[q]);
-        } else {
-          lg = p[0];
-          for (uint32_t q = 1; q < slices; ++q) lg = __fadd_rn(lg, p[q * plane]);
-        }
-        bad |= !finite(lg) || !finite(bias_r[k]);
-        score[k] = sigmoid_sleef(lg);
-        corr[k] = __fadd_rn(score[k], bias_r[k]);
-      }
-    }
-    if (bad) raise_flag(flags, PW_FLAG_NONFINITE_INPUT);
-    // 9 rounds of warp argmax (ties -> lower index): lane r keeps round r's
-    // pick (corrected value, expert, unbiased score)
-    uint32_t taken = 0;
-    float my_v = ninf, my_s = 0.0f;
-    uint32_t my_i = 0xffffffffu;
-#pragma unroll 1
-    for (uint32_t round = 0; round < 9u; ++round) {
-      float bv = ninf, bs = 0.0f;
-      uint32_t bi = 0xffffffffu;
-#pragma unroll
-      for (int k = 0; k < NPL; ++k) {
-        const uint32_t e = lane + 32u * k;
-        if (e < experts && !((taken >> k) & 1u) && better(corr[k], e, bv, bi)) {
-          bv = corr[k];
-          bi = e;
-          bs = score[k];
-        }
-      }
-      argmax_shfl(bv, bi, bs);
-      if (lane == round) {
-        my_v = bv;
-        my_i = bi;
-        my_s = bs;
-      }
-      if (round < 8u && bi != 0xffffffffu && bi % 32u == lane) taken |= 1u << (bi / 32u);
-    }
-    // weight_k = score_k / (pairwise sum of the 8 + 1e-20), src/text_endpoint.rs:4382
-    const float s4 = __shfl_down_sync(0xffffffffu, my_s, 4);  // lane k < 4: score of pick k + 4
-    const float lk = __fadd_rn(my_s, s4);                      // lane k < 4: l_k
-    const float l0 = __shfl_sync(0xffffffffu, lk, 0), l1 = __shfl_sync(0xffffffffu, lk, 1);
-    const float l2 = __shfl_sync(0xffffffffu, lk, 2), l3 = __shfl_sync(0xffffffffu, lk, 3);
-    const float den = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, l0), l1), l2), l3), 1.0e-20f);
-    const float wk = __fdiv_rn(my_s, den);
-    const bool ok_k = lane >= 8u || (finite(wk) && wk >= 0.0f && my_i < experts);
-    float sum = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, wk, k));
-    const bool all_ok = __all_sync(0xffffffffu, ok_k);
-    if (lane < 8u) {
-      selected[(size_t)t * 8 + lane] = my_i;
-      weights[(size_t)t * 8 + lane] = wk;
-    }
-    const float v7 = __shfl_sync(0xffffffffu, my_v, 7), v8 = __shfl_sync(0xffffffffu, my_v, 8);
-    if (lane == 0) {
-      if (!all_ok || fabsf(__fsub_rn(sum, 1.0f)) > 1.0e-6f) raise_flag(flags, PW_FLAG_ROUTE_WEIGHTS);
-      if (v7 == v8 && tie_rows) atomicAdd(tie_rows, 1u);
-    }
-  }
+  pdl_wait();
+  pdl_launch_dependents();
+  for (uint32_t t = blockIdx.x * (blockDim.x / 32u) + threadIdx.x / 32u; t < tokens; t += nwarps)
+    topk_token_warp<NPL>(src, slices, bias_r, tokens, experts, t, selected, weights, tie_rows, flags);
 }
 
 // The same selection with a whole CTA per token (experts <= 256, one expert
@@ -849,10 +887,14 @@ static cudaError_t launch_partials(const float *x, const void *w, const RouterUn
                        g, scratch, work);
 }
 
+bool router_fuses_quantize(uint32_t tokens) { return tokens < kRouterPartialMinTokens; }
+
 template <bool F32W>
 static cudaError_t launch_router_logits(const float *x, uint32_t tokens, const void *w, const RouterUnits &g,
-                                        float *scratch, uint32_t *work, int num_sms, cudaStream_t stream) {
+                                        float *scratch, uint32_t *work, int num_sms, cudaStream_t stream,
+                                        uint8_t *q_codes, float *q_scales, uint32_t *flags) {
   if (tokens >= kRouterPartialMinTokens) {
+    if (q_codes) return cudaErrorInvalidValue;  // only the decode kernel quantizes
     // The largest unit that still gives every CTA slot two or more units:
     // 64 tokens x 128 experts, then 64 x 64, then 32 x 64.  With fewer units
     // most slots run one or two whole units and the smaller ones finish first
@@ -871,19 +913,23 @@ static cudaError_t launch_router_logits(const float *x, uint32_t tokens, const v
   using WT = typename std::conditional<F32W, float, uint16_t>::type;
   return launch_kernel(k_router_slices_small<WT>,
                        dim3(g.slices, (g.experts + 31u) / 32u, (tokens + kRouterTok - 1) / kRouterTok), dim3(256), 0,
-                       stream, x, tokens, static_cast<const WT *>(w), g.experts, g.hidden, scratch);
+                       stream, x, tokens, static_cast<const WT *>(w), g.experts, g.hidden, scratch, q_codes, q_scales,
+                       flags);
 }
 
 cudaError_t launch_router(const float *x, uint32_t tokens, const void *w, uint32_t w_dtype, const float *bias,
                           uint32_t experts, uint32_t hidden, float *scratch, uint32_t *selected, float *weights,
-                          uint32_t *tie_rows, uint32_t *flags, uint32_t *work, int num_sms, cudaStream_t stream) {
+                          uint32_t *tie_rows, uint32_t *flags, uint32_t *work, int num_sms, cudaStream_t stream,
+                          uint8_t *q_codes, float *q_scales) {
   if (hidden % 512u || hidden > kRouterSlice * kRouterMaxSlices || tokens == 0 || experts <= 8 || experts > 1024u ||
       (w_dtype != PW_ROUTER_BF16 && w_dtype != PW_ROUTER_F32))
     return cudaErrorInvalidValue;
   const RouterUnits g = router_units(tokens, experts, hidden);
   cudaError_t st = w_dtype == PW_ROUTER_F32
-                       ? launch_router_logits<true>(x, tokens, w, g, scratch, work, num_sms, stream)
-                       : launch_router_logits<false>(x, tokens, w, g, scratch, work, num_sms, stream);
+                       ? launch_router_logits<true>(x, tokens, w, g, scratch, work, num_sms, stream, q_codes, q_scales,
+                                                    flags)
+                       : launch_router_logits<false>(x, tokens, w, g, scratch, work, num_sms, stream, q_codes, q_scales,
+                                                     flags);
   if (st != cudaSuccess) return st;
   if (experts <= 256u && tokens < kRouterTopkCtaMaxTokens) {
     // decode widths: a CTA per token (a shorter critical path per token; at
@@ -983,29 +1029,9 @@ __global__ void __launch_bounds__(256) k_sched_mask(const uint32_t *__restrict__
 
 __global__ void __launch_bounds__(kSchedThreads) k_sched_scan(uint32_t tokens, uint32_t experts, BankTable bank,
                                                               ScheduleOut out, uint32_t *flags, uint32_t chunk) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const uint32_t *mask = out.work;
-  uint32_t *base = out.work + experts * kSchedWords, *badw = base + experts * kSchedWords;
-  uint32_t *summary = badw + kSchedWords;
-  __shared__ uint32_t off[kSchedMaxExperts + 1], grp_off[kSchedMaxExperts + 1];
-  __shared__ uint32_t uniq, maxc, wsum_c[kSchedThreads / 32], wsum_g[kSchedThreads / 32];
-  const uint32_t words = (tokens + 31u) / 32u;
   const uint32_t tid = threadIdx.x, lane = tid % 32u, warp = tid / 32u;
-  if (tid == 0) {
-    uniq = 0;
-    maxc = 0;
-  }
-  // every global load this kernel needs is issued up front, so its latency
-  // is paid once: the per-word error flags, the mask words (four threads per
-  // expert, experts <= 256, up to 16 words each) and the expert's bank entries
-  const uint32_t ex = tid / 4u, q = tid % 4u;
-  const uint32_t per = (words + 3u) / 4u, w0 = min(words, q * per), w1 = min(words, w0 + per);
-  const bool badword = tid < words && badw[tid] != 0u;
-  uint32_t mw[kSchedWords / 4u];
-#pragma unroll
-  for (uint32_t k = 0; k < kSchedWords / 4u; ++k)
-    mw[k] = ex < experts && w0 + k < w1 ? mask[ex * kSchedWords + w0 + k] : 0u;
+  // the bank table is final before the layer's kernels start, so its entries
+  // are fetched before the programmatic-launch wait
   const bool has_bank = out.gu_groups && tid < experts;
   const uint8_t *bw[3] = {nullptr, nullptr, nullptr};
   const float *bs[3] = {nullptr, nullptr, nullptr};
@@ -1017,6 +1043,28 @@ __global__ void __launch_bounds__(kSchedThreads) k_sched_scan(uint32_t tokens, u
     bw[2] = bank.down_w[tid];
     bs[2] = bank.down_s[tid];
   }
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t *mask = out.work;
+  uint32_t *base = out.work + experts * kSchedWords, *badw = base + experts * kSchedWords;
+  uint32_t *summary = badw + kSchedWords;
+  __shared__ uint32_t off[kSchedMaxExperts + 1], grp_off[kSchedMaxExperts + 1];
+  __shared__ uint32_t uniq, maxc, wsum_c[kSchedThreads / 32], wsum_g[kSchedThreads / 32];
+  const uint32_t words = (tokens + 31u) / 32u;
+  if (tid == 0) {
+    uniq = 0;
+    maxc = 0;
+  }
+  // every other global load this kernel needs is issued up front, so its
+  // latency is paid once: the per-word error flags and the mask words (four
+  // threads per expert, experts <= 256, up to 16 words each)
+  const uint32_t ex = tid / 4u, q = tid % 4u;
+  const uint32_t per = (words + 3u) / 4u, w0 = min(words, q * per), w1 = min(words, w0 + per);
+  const bool badword = tid < words && badw[tid] != 0u;
+  uint32_t mw[kSchedWords / 4u];
+#pragma unroll
+  for (uint32_t k = 0; k < kSchedWords / 4u; ++k)
+    mw[k] = ex < experts && w0 + k < w1 ? mask[ex * kSchedWords + w0 + k] : 0u;
   const int bad = __syncthreads_or(badword);
   if (bad) {
     if (tid == 0) {
@@ -1170,12 +1218,29 @@ __global__ void __launch_bounds__(32) k_sched_place(const uint32_t *__restrict__
 constexpr uint32_t kSchedSmallTokens = 256;
 constexpr uint32_t kSchedSmallWords = kSchedSmallTokens / 32u;
 
-__global__ void __launch_bounds__(kSchedThreads) k_schedule_small(const uint32_t *__restrict__ selected,
-                                                            const float *__restrict__ weights, uint32_t tokens,
-                                                            uint32_t experts, BankTable bank, ScheduleOut out,
-                                                            uint32_t *flags, uint32_t chunk) {
-  pdl_wait();
-  pdl_launch_dependents();
+// Bank entries of expert `e` (final before the layer's kernels start, so they
+// are fetched before the programmatic-launch wait).
+struct BankEntry {
+  const uint8_t *w[3];
+  const float *s[3];
+  __device__ __forceinline__ void fetch(const BankTable &bank, uint32_t e) {
+    w[0] = bank.gate_w[e];
+    s[0] = bank.gate_s[e];
+    w[1] = bank.up_w[e];
+    s[1] = bank.up_s[e];
+    w[2] = bank.down_w[e];
+    s[2] = bank.down_s[e];
+  }
+};
+
+// The one-CTA schedule; `be` holds expert threadIdx.x's bank entries when
+// has_bank.  `selected` / `weights` carry no restrict or read-only
+// qualifiers: the fused route + schedule kernel writes them earlier in the
+// same launch.
+__device__ __forceinline__ void schedule_small_body(const uint32_t *selected, const float *weights, uint32_t tokens,
+                                                    uint32_t experts, const BankTable &bank, const ScheduleOut &out,
+                                                    uint32_t *flags, uint32_t chunk, bool has_bank,
+                                                    const BankEntry &be) {
   extern __shared__ uint32_t sm[];
   uint32_t *mask = sm;                                                            // [experts][kSchedSmallWords]
   uint16_t *prefix = reinterpret_cast<uint16_t *>(mask + experts * kSchedSmallWords);  // [experts][kSchedSmallWords]
@@ -1317,7 +1382,8 @@ __global__ void __launch_bounds__(kSchedThreads) k_schedule_small(const uint32_t
   }
   // 5. GEMV/GEMM groups: each expert's placements in chunks of <= chunk tokens
   // (skipped when the caller runs the experts elsewhere: no group arrays)
-  for (uint32_t e = tid; e < experts && out.gu_groups; e += kSchedThreads) {
+  if (has_bank) {
+    const uint32_t e = tid;
     const uint32_t c = off[e + 1] - off[e];
     for (uint32_t j = 0; j * chunk < c; ++j) {
       GemvGroup g;
@@ -1325,16 +1391,16 @@ __global__ void __launch_bounds__(kSchedThreads) k_schedule_small(const uint32_t
       g.count = min(chunk, c - chunk * j);
       g.expert = e;
       g.pad = 0;
-      g.w0 = bank.gate_w[e];
-      g.s0 = bank.gate_s[e];
-      g.w1 = bank.up_w[e];
-      g.s1 = bank.up_s[e];
+      g.w0 = be.w[0];
+      g.s0 = be.s[0];
+      g.w1 = be.w[1];
+      g.s1 = be.s[1];
       g.tm0 = bank.gate_tm + e;
       g.tm1 = bank.up_tm + e;
       out.gu_groups[grp_off[e] + j] = g;
       GemvGroup d = g;
-      d.w0 = bank.down_w[e];
-      d.s0 = bank.down_s[e];
+      d.w0 = be.w[2];
+      d.s0 = be.s[2];
       d.w1 = nullptr;
       d.s1 = nullptr;
       d.tm0 = bank.down_tm + e;
@@ -1343,6 +1409,22 @@ __global__ void __launch_bounds__(kSchedThreads) k_schedule_small(const uint32_t
     }
   }
 }
+
+
+__global__ void __launch_bounds__(kSchedThreads) k_schedule_small(const uint32_t *__restrict__ selected,
+                                                            const float *__restrict__ weights, uint32_t tokens,
+                                                            uint32_t experts, BankTable bank, ScheduleOut out,
+                                                            uint32_t *flags, uint32_t chunk) {
+  // thread e writes expert e's groups; its bank entries before the wait
+  const bool has_bank = out.gu_groups && threadIdx.x < experts;
+  BankEntry be{};
+  if (has_bank) be.fetch(bank, threadIdx.x);
+  pdl_wait();
+  pdl_launch_dependents();
+  schedule_small_body(selected, weights, tokens, experts, bank, out, flags, chunk, has_bank, be);
+}
+
+uint32_t schedule_launches(uint32_t tokens) { return tokens <= kSchedSmallTokens ? 1u : 3u; }
 
 cudaError_t launch_schedule(const uint32_t *selected, const float *weights, uint32_t tokens, uint32_t experts,
                             const BankTable &bank, const ScheduleOut &out, uint32_t *flags, uint32_t chunk,

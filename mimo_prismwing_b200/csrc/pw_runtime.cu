@@ -1592,7 +1592,10 @@ static int moe_layer_impl(pw_runtime *rt, const pw_norm *norm, const pw_router *
     CK(cudaMemsetAsync(rt->d_ties, 0, 4, rt->stream));
     // the kernel chain below runs with programmatic dependent launch
     PdlScope pdl(!rt->profiling);
-    {
+    // decode widths without a norm: the router's logits kernel quantizes x
+    // for the experts too (one launch fewer on the chain's critical path)
+    const bool fuse_quant = !norm && router_fuses_quantize(tokens);
+    if (!fuse_quant) {
       ProfScope ps(rt, P_QUANT, 1);
       if (norm)
         CK(launch_rms_quantize(dx, tokens, H, norm->weight, norm->weight_dtype, norm->epsilon, dn, xc, xs, nullptr,
@@ -1603,10 +1606,11 @@ static int moe_layer_impl(pw_runtime *rt, const pw_norm *norm, const pw_router *
     {
       ProfScope ps(rt, P_ROUTER, 2);
       CK(launch_router(dn, tokens, router->weight, router->weight_dtype, router->bias, E, H, logits, sel, wts,
-                       rt->d_ties, rt->d_flags, rt->d_router_work, rt->num_sms, rt->stream));
+                       rt->d_ties, rt->d_flags, rt->d_router_work, rt->num_sms, rt->stream, fuse_quant ? xc : nullptr,
+                       fuse_quant ? xs : nullptr));
     }
     {
-      ProfScope ps(rt, P_SCHED, 3);
+      ProfScope ps(rt, P_SCHED, schedule_launches(tokens));
       CK(launch_schedule(sel, wts, tokens, E, bank->table, so, rt->d_flags, chunk, rt->stream));
     }
     // the grid covers the worst case; CTAs read the real group count
