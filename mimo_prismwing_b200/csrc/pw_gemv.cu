@@ -47,13 +47,19 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) k_gemv_readable(const GemvAr
   const uint32_t steps = (a.K + 511u) / 512u;
   const uint8_t *wrow = grp.w0 + (size_t)r * a.K;
   const float *srow = grp.s0 + (size_t)(r / 128u) * a.scale_cols;
-  // all of this lane's weight loads first
+  // all of this lane's weight loads first.  Under programmatic dependent
+  // launch they are issued before the wait: the weights and the group record
+  // are no kernel's output (the record is cached or copied in before the
+  // launch), so the stream overlaps the previous kernel's tail; x and y wait.
+  // The next kernel is released only once this one's sums are done, so at
+  // most two of these kernels hold SMs at a time.
   uint4 q[kMaxKSteps];
 #pragma unroll
   for (uint32_t i = 0; i < kMaxKSteps; ++i) {
     const uint32_t c = 512u * i + 16u * lane;
     q[i] = (i < steps && c < a.K) ? __ldg(reinterpret_cast<const uint4 *>(wrow + c)) : make_uint4(0u, 0u, 0u, 0u);
   }
+  pdl_wait();
   float acc[CMAX];
 #pragma unroll
   for (int t = 0; t < CMAX; ++t) acc[t] = 0.0f;
@@ -84,6 +90,7 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) k_gemv_readable(const GemvAr
       }
     }
   }
+  pdl_launch_dependents();
 #pragma unroll
   for (int t = 0; t < CMAX; ++t) {
 #pragma unroll

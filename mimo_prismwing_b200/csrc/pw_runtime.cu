@@ -784,6 +784,12 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
     return fail(rt, PW_ERR_CUDA, "cuTensorMapEncodeTiled failed for a [%u, %u] weight", w->rows, w->cols);
   Call call{rt, mem, stats, 0};
   if ((s = call.begin()) != PW_OK) return s;
+  // Narrow projections run as a programmatic-dependent-launch chain: the
+  // GEMV streams its weights while the quantizer (or the previous call's
+  // kernel) finishes, and the quantizer clears the split-K counters.
+  const bool chain = !wide && !rt->profiling;
+  if (chain && kind != 1 && (s = ensure_split_ws(rt)) != PW_OK) return s;
+  PdlScope pdl(chain);
   Arena ar;
   for (int pass = 0; pass < 2; ++pass) {
     if (pass == 1) {
@@ -818,15 +824,19 @@ static int projection(pw_runtime *rt, int kind, const pw_fp8_tensor *w, uint32_t
       a.max_count = width < 8u ? width : 8u;
     } else {
       ProfScope ps(rt, P_QUANT, 1);
-      CK(launch_quantize(dx, width, K, dc, ds, rt->d_flags, rt->stream));
+      CK(launch_quantize(dx, width, K, dc, ds, rt->d_flags, rt->stream, nullptr, chain ? rt->split_cnt : nullptr,
+                         chain ? kSplitCounters : 0u));
       a.x_codes = dc;
       a.x_scales = ds;
       a.round_bf16 = round;
+      // the groups (cached, or copied in above) and the weights are final
+      a.early_weights = chain ? 1u : 0u;
     }
     {
       ProfScope ps(rt, P_PROJ, 1);
       int grid = grid_for(rt, (uint64_t)n_groups * (N / (kind == 1 ? 64u : 128u)));
-      if (!wide && kind != 1 && (s = gemv_launch_setup(rt, a, (uint64_t)n_groups * (N / 128u), 1, grid)) != PW_OK)
+      if (!wide && kind != 1 &&
+          (s = gemv_launch_setup(rt, a, (uint64_t)n_groups * (N / 128u), 1, grid, chain)) != PW_OK)
         return s;
       if (wide) {
         GemmArgs A{};
