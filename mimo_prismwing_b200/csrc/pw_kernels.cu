@@ -1466,20 +1466,20 @@ __global__ void k_combine(const T *__restrict__ down, const uint32_t *__restrict
   pdl_launch_dependents();
   const uint32_t t = blockIdx.y;
   __shared__ uint32_t pl[8];
-  __shared__ float wt[8];
-  if (threadIdx.x < 8) {
-    pl[threadIdx.x] = slot_place[t * 8u + threadIdx.x];
-    wt[threadIdx.x] = placement_w[pl[threadIdx.x]];
-  }
+  if (threadIdx.x < 8) pl[threadIdx.x] = slot_place[t * 8u + threadIdx.x];
   __syncthreads();
-  // two 4-column groups per thread: all 16 row loads in flight together
+  // two 4-column groups per thread: all 16 row loads in flight together,
+  // and the 8 route weights (L1 broadcasts) in the same round trip
   for (uint32_t c8 = blockIdx.x * blockDim.x + threadIdx.x; c8 < hidden / 8u; c8 += gridDim.x * blockDim.x) {
     float4 d[2][8];
+    float wt[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       d[0][k] = load4(down + (size_t)pl[k] * hidden, 2u * c8);
       d[1][k] = load4(down + (size_t)pl[k] * hidden, 2u * c8 + 1u);
     }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) wt[k] = __ldg(placement_w + pl[k]);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);

@@ -97,7 +97,9 @@ def router_f32(experts: int, hidden: int, seed: int, device="cuda"):
 
 
 def to_device(obj, device):
-    """Copy a WideProjectionBinding, or a tuple/list of them, to `device`."""
+    """Copy a tensor, a WideProjectionBinding, or a tuple/list of them, to `device`."""
+    if isinstance(obj, torch.Tensor):
+        return obj.to(device).contiguous()
     if isinstance(obj, WideProjectionBinding):
         return WideProjectionBinding(obj.weight.to(device).contiguous(), obj.scale.to(device).contiguous())
     return type(obj)(to_device(o, device) for o in obj)

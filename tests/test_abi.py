@@ -64,3 +64,13 @@ def test_python_mirror_keeps_reference_method_names():
     from mimo_prismwing_b200.runtime import WideMoeRuntime
     for name in ["compile", "compile_with_fused_gate_up", "execute_fp8_linear", "execute", "execute_fused_gate_up"]:
         assert hasattr(WideMoeRuntime, name)
+
+
+def test_smoke_inputs_build_on_the_host():
+    # smoke() builds its bank and router on the host and copies them over with
+    # synth.to_device: the same calls with the host as the target
+    from mimo_prismwing_b200 import synth
+    w, bias = synth.to_device(synth.router(16, 1024, 7, "cpu"), "cpu")
+    assert tuple(w.shape) == (16, 1024) and tuple(bias.shape) == (16,)
+    gate, up, down = synth.to_device(synth.expert(1024, 512, 100, "cpu"), "cpu")
+    assert tuple(gate.weight.shape) == (512, 1024) and tuple(down.weight.shape) == (1024, 512)
