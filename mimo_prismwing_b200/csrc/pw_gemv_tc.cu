@@ -212,6 +212,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_tc(const GemvArgs a, const
 
   if (warp == (uint32_t)kProducerWarp) {
     // ------------------------------------------------------------ producer
+    // Weights are read once: evict-first, so the stream does not displace
+    // what a CTA without units prefetches for the next kernel (evict-last):
+    // that CTA's share of the next groups' weights, in 32 KB pieces.
+    const uint64_t pol_stream = policy_evict_first();
+    if (a.l2_next && u_begin == u_end && total < gridDim.x) {
+      const uint64_t pol_keep = policy_evict_last();
+      const uint32_t idle_rank = blockIdx.x - u_begin, n_idle = gridDim.x - (uint32_t)total;
+      const uint64_t per = (uint64_t)a.l2_rows * a.l2_cols, pieces_per = (per + 32767u) / 32768u;
+      for (uint64_t c = (uint64_t)idle_rank * 32u + lane; c < pieces_per * n_groups; c += (uint64_t)n_idle * 32u) {
+        const uint64_t off = (c % pieces_per) * 32768u;
+        prefetch_l2_hint(a.l2_next[c / pieces_per].w0 + off, (uint32_t)min((uint64_t)32768u, per - off), pol_keep);
+      }
+    }
     uint32_t slot = 0, phase = 0, issued = 0, parity = 0;
     for (uint32_t u = u_begin; u < u_end; ++u) {
       const uint32_t tile = u / geo.splits;
@@ -229,7 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_tc(const GemvArgs a, const
         if (swait(sh, &sh.empty[slot], phase ^ 1u, a.flags)) {
           if (elect_one()) {
             mbar_arrive_expect_tx(&sh.full[slot], kStageBytes);
-            tma_load_3d(sh.ring + slot * kStageBytes, m == 0u ? m0 : m1, 0, row0, (int)(kc * 2u), &sh.full[slot]);
+            tma_load_3d_hint(sh.ring + slot * kStageBytes, m == 0u ? m0 : m1, 0, row0, (int)(kc * 2u), &sh.full[slot],
+                             pol_stream);
           }
           __syncwarp();
           issued |= 1u << slot;

@@ -93,6 +93,9 @@ struct GemvArgs {
   uint32_t splits;               // GEMV split-K over the 8-leaf K tree: 1, 2, 4 or 8
   float *split_ws;               //   partial sums [tile][split][mats][128 rows][8 tokens]
   uint32_t *split_cnt;           //   per-tile arrival counters (zero; reset by the last CTA)
+  const GemvGroup *l2_next;      // optional: the next kernel's groups (same count); CTAs with
+  uint32_t l2_rows, l2_cols;     //   no unit of their own prefetch those groups' w0 [rows, cols]
+                                 //   into L2 while the others stream
 };
 
 // Wide-width grouped GEMM (tcgen05): the GEMV arguments plus TMA maps of the

@@ -406,6 +406,8 @@ int grid_for(const pw_runtime *rt, uint64_t units) {
 // the count (the GEMV adds K in a fixed 8-leaf tree).
 constexpr size_t kSplitWsBytes = (size_t)16 << 20;
 constexpr uint32_t kSplitCounters = 1024;
+// next-kernel weights the decode GEMV may prefetch into L2 (126 MB) at once
+constexpr uint64_t kL2PrefetchBytes = (uint64_t)72 << 20;
 
 uint32_t gemv_splits(const pw_runtime *rt, uint64_t tiles, uint32_t K, uint32_t layout, int mats) {
   const uint32_t kbs = layout == PW_LAYOUT_PLAIN ? 2u : 4u;
@@ -895,6 +897,13 @@ static int enqueue_expert_chain(pw_runtime *rt, const GemvGroup *gu, const GemvG
     // under PDL the producer streams weights while the quantizer still runs
     a.early_weights = early && pdl_enabled() ? 1u : 0u;
     if ((s = gemv_launch_setup(rt, a, units_hint * (I / 128u), 2, grid_gu, early)) != PW_OK) return s;
+    // few experts (a one-token decode layer): the gate/up CTAs that get no
+    // tile prefetch the down weights into L2 while the others stream
+    if (dn && a.splits <= 1u && (uint64_t)n_groups * H * I <= kL2PrefetchBytes) {
+      a.l2_next = dn;
+      a.l2_rows = H;
+      a.l2_cols = I;
+    }
     CK(launch_gemv(2, a, grid_gu, rt->stream));
   } else {
     // gate and up as two block-scaled projections, then the staged SwiGLU
