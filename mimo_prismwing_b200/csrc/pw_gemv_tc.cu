@@ -30,7 +30,9 @@
 //    128B-swizzled K-major layout the MMA reads) and scales, promote, and run
 //    the split-K reduction, SwiGLU, hidden quantization and stores;
 //  * warp 8 (producer): one elected lane streams 32 KB TMA boxes (128 rows x
-//    2 k-blocks) of the CTA's units into the ring;
+//    2 k-blocks) of the CTA's units into the ring, evict-first in L2 (each
+//    tile is read once).  A CTA without units instead prefetches its share
+//    of the next kernel's weights (l2_next) into L2, evict-last;
 //  * warp 9 (MMA): allocates 128 TMEM columns, issues the MMAs and commits.
 // Units are (128-row tile, K split) pairs, a contiguous range per CTA; the
 // split-K publication and the last-CTA reduction are those of pw_gemv_mma.cu
