@@ -145,7 +145,8 @@ def test_dequant_all_bytes_bit_exact_on_gpu(rt):
 @pytest.mark.parametrize("width", [2, 8, 32])
 def test_dequant_all_bytes_through_fp8_mma(rt, width):
     # The block-scaled path feeds the e4m3 bytes to the tensor cores (the
-    # warp-level MMA at widths <= 8, tcgen05 from 32).  With one-hot tokens
+    # tcgen05 GEMV at widths <= 8 for this plain one-tile matrix, the tcgen05
+    # GEMM from 32).  With one-hot tokens
     # each output is a single product dec(W) * dec(code) * S * xs, rounded
     # once: bit-exact against the oracle's equation.
     from mimo_prismwing_b200.runtime import WideProjectionBinding
